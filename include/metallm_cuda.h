@@ -1,0 +1,216 @@
+/*
+ * metallm_cuda.h -- C ABI of libmetallm_cuda.so, the B200 (sm_100a)
+ * replacement for the Metal operator layer of MetalLM.
+ *
+ * The reference's operator API is the Swift singleton `MetalService`
+ * (MetalLM/Backend/Metal/MetalService.swift:48-66).  Each entry point below
+ * names the method or call site it replaces.  A Swift host binds this header
+ * through a module map; the Python package metallm_b200 binds it with ctypes.
+ *
+ * Conventions (mirroring MetalService):
+ *  - every entry point returns an int status: MLM_OK (0) or a negative
+ *    MLM_ERR_* code; the reason is kept in mlm_last_error(ctx), the way the
+ *    reference prints a reason and returns false/nil;
+ *  - op entry points only enqueue work on the context's stream (the
+ *    reference's caller-owned command buffer) and never wait; mlm_commit /
+ *    mlm_wait give the commit / waitUntilCompleted pair;
+ *  - buffers are device pointers owned by the caller (mlm_alloc or any CUDA
+ *    allocation on the context's device); ops allocate nothing;
+ *  - one context per thread / stream.  Ops on one context are not
+ *    thread-safe; the synchronous dequant helpers (mlm_dequantize_*) take a
+ *    context lock so concurrent loader tasks may share a context.
+ */
+#ifndef METALLM_CUDA_H
+#define METALLM_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MLM_ABI_VERSION 1
+
+enum mlm_status {
+  MLM_OK = 0,
+  MLM_ERR_ARG = -1,         /* null pointer or invalid argument          */
+  MLM_ERR_SHAPE = -2,       /* size / shape validation failed            */
+  MLM_ERR_ALIGN = -3,       /* pointer misaligned for the kernel         */
+  MLM_ERR_ALLOC = -4,       /* device allocation failed                  */
+  MLM_ERR_CUDA = -5,        /* CUDA runtime error (launch or execution)  */
+  MLM_ERR_NCCL = -6,        /* NCCL error                                */
+  MLM_ERR_TIMEOUT = -7,     /* bounded wait expired                      */
+  MLM_ERR_STATE = -8,       /* call out of order (e.g. KV cache full)    */
+  MLM_ERR_UNSUPPORTED = -9, /* shape / option this build does not handle */
+};
+
+typedef struct mlm_ctx mlm_ctx;
+
+/* ---------------------------------------------------------------------------
+ * Context, memory and the command-buffer stream
+ * ------------------------------------------------------------------------ */
+
+/* MetalService.init (MetalService.swift:68-163): binds `device`, creates the
+ * stream and the per-context scratch used by split-K reductions. */
+int mlm_create(int device, mlm_ctx **out);
+void mlm_destroy(mlm_ctx *ctx);
+const char *mlm_last_error(const mlm_ctx *ctx);
+const char *mlm_status_string(int status);
+int mlm_abi_version(void);
+int mlm_device_sm_count(const mlm_ctx *ctx);
+
+/* The stream ops are enqueued on (a cudaStream_t).  mlm_set_stream lets a
+ * caller run the ops on its own stream (NULL restores the context's). */
+int mlm_get_stream(mlm_ctx *ctx, void **stream);
+int mlm_set_stream(mlm_ctx *ctx, void *stream);
+
+/* device.makeBuffer / copyMemory (ModelLoader.swift:193-210) */
+int mlm_alloc(mlm_ctx *ctx, size_t bytes, void **dptr);
+int mlm_free(mlm_ctx *ctx, void *dptr);
+int mlm_memset(mlm_ctx *ctx, void *dptr, int value, size_t bytes);
+/* synchronous copies (stream-ordered, then waited) */
+int mlm_upload(mlm_ctx *ctx, void *dst, const void *src, size_t bytes);
+int mlm_download(mlm_ctx *ctx, void *dst, const void *src, size_t bytes);
+/* stream-ordered copies; host memory should be pinned (mlm_host_alloc) */
+int mlm_upload_async(mlm_ctx *ctx, void *dst, const void *src, size_t bytes);
+int mlm_download_async(mlm_ctx *ctx, void *dst, const void *src, size_t bytes);
+int mlm_host_alloc(mlm_ctx *ctx, size_t bytes, void **hptr);
+int mlm_host_free(mlm_ctx *ctx, void *hptr);
+
+/* commandBuffer.commit() / waitUntilCompleted() + commandBuffer.error
+ * (LlamaRunner.swift:1087-1093) */
+int mlm_commit(mlm_ctx *ctx);
+int mlm_wait(mlm_ctx *ctx);
+
+/* ---------------------------------------------------------------------------
+ * Seeded synthetic data (bit-identical to the CPU oracle's generators)
+ * ------------------------------------------------------------------------ */
+
+/* Q4_K blocks [first_block, first_block + nblocks) of tensor `stream` */
+int mlm_gen_q4k(mlm_ctx *ctx, uint64_t seed, uint64_t stream, uint64_t first_block,
+                uint64_t nblocks, void *out);
+int mlm_gen_f16(mlm_ctx *ctx, uint64_t seed, uint64_t stream, uint64_t first,
+                uint64_t n, float mean, float std, void *out_f16);
+int mlm_gen_f32(mlm_ctx *ctx, uint64_t seed, uint64_t stream, uint64_t first,
+                uint64_t n, float mean, float std, float *out);
+
+/* ---------------------------------------------------------------------------
+ * Q4_K super-blocks: 144 bytes = fp16 d, fp16 dmin, 12 bytes of packed
+ * 6-bit scales/mins, 128 bytes of 4-bit quants (DequantKernels.metal:20-27).
+ * Element i of a block reads qs[i/2], low nibble when i is even.
+ * ------------------------------------------------------------------------ */
+
+#define MLM_Q4K_BLOCK_ELEMS 256
+#define MLM_Q4K_BLOCK_BYTES 144
+
+/* kernel_dequantize_q4_K_f32 (DequantKernels.metal:63-92); the body of
+ * MetalService.dequantizeQ4KM_to_f32 (MetalService.swift:170-239) without
+ * its allocation and wait.  Bit-exact.  `blocks` holds ceil(n/256) blocks;
+ * blocks and out 16-byte aligned. */
+int mlm_q4k_dequant_f32(mlm_ctx *ctx, const void *blocks, float *out, uint64_t n);
+/* kernel_dequantize_q4_K_f16 (DequantKernels.metal:96-125), half arithmetic */
+int mlm_q4k_dequant_f16(mlm_ctx *ctx, const void *blocks, void *out_f16, uint64_t n);
+/* bf16 rounding of the exact fp32 dequant (no reference counterpart; feeds
+ * the tensor-core prefill path) */
+int mlm_q4k_dequant_bf16(mlm_ctx *ctx, const void *blocks, void *out_bf16, uint64_t n);
+
+/* MetalService.dequantizeQ4KM_to_f32 / _f16 (MetalService.swift:170, 243):
+ * allocate the output, run, wait.  *out receives a device pointer to free
+ * with mlm_free.  Thread-safe (the loader calls these from concurrent
+ * tasks, ModelLoaderWrapper.swift:172-201). */
+int mlm_dequantize_q4k_to_f32(mlm_ctx *ctx, const void *blocks, uint64_t n, float **out);
+int mlm_dequantize_q4k_to_f16(mlm_ctx *ctx, const void *blocks, uint64_t n, void **out);
+
+/* y[r] = sum_k W[r][k] * x[k] (+ residual[r] when residual != NULL).
+ * Replaces encodeMPSMatrixMultiply at the decode linears
+ * (MetalService.swift:797-925; LlamaRunner.swift:563-609, 954-963,
+ * 1008-1034, 1059-1068, 1169-1178) on the packed weights, with no
+ * dequantized copy.  W row-major [rows][cols/256 blocks] (GGUF ne0 = cols);
+ * x fp16 [cols]; y fp32 [rows]; fp32 accumulation.  cols % 256 == 0; W and
+ * x 16-byte aligned.  Uses the context's split-K scratch: launches on one
+ * context are stream-ordered and must not overlap. */
+int mlm_q4k_gemv(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_f16,
+                 float *y, const float *residual);
+
+/* ---------------------------------------------------------------------------
+ * Normalisation, RoPE, activations
+ * ------------------------------------------------------------------------ */
+
+/* kernel_rms_norm_f16 / encodeRMSNormF16 (NormalizationKernels.metal:9-80,
+ * MetalService.swift:544-677): y = half(x * min(1/sqrt(max(mean(x^2),1e-10)
+ * + eps), 1e6) * w), NaN/Inf weights read as 1. */
+int mlm_rmsnorm_f16(mlm_ctx *ctx, const void *x_f16, const void *w_f16, void *y_f16,
+                    int rows, int n, float eps);
+/* the same formula on an fp32 hidden state with fp32 weights; writes fp32
+ * (y_f32, may be NULL) and/or fp16 (y_f16, may be NULL; feeds the GEMV) */
+int mlm_rmsnorm_f32(mlm_ctx *ctx, const float *x, const float *w, float *y_f32,
+                    void *y_f16, int rows, int n, float eps);
+
+/* MetalRopeArgs (PositionalEmbeddingsKernels.metal:15-42) */
+typedef struct mlm_rope_args {
+  uint32_t n_dims;
+  float freq_base;   /* 500000 for Llama-3 */
+  float freq_scale;
+  int32_t pos_offset;
+  int32_t n_ctx_orig;
+  float ext_factor;  /* 0 disables the YaRN blend */
+  float attn_factor;
+  float beta_fast;
+  float beta_slow;
+  int32_t has_freq_factors;
+} mlm_rope_args;
+
+/* kernel_rope_f16_inplace / applyRoPE (PositionalEmbeddingsKernels.metal:
+ * 137-204, MetalService.swift:685-777): data [seq_len][num_heads][head_dim]
+ * fp16, adjacent pairs (i0, i0+1) rotated in place for i0 < n_dims.  freqs
+ * (n_dims/2 divisors) is read when has_freq_factors != 0. */
+int mlm_rope_f16(mlm_ctx *ctx, void *data_f16, const float *freqs,
+                 const mlm_rope_args *args, int seq_len, int num_heads, int head_dim);
+
+/* Decode-step QKV epilogue: RoPE on fp32 q [n_q_heads][d] and k
+ * [n_kv_heads][d] at position args->pos_offset, q written as fp16 q_out,
+ * rotated k and v (fp32 [n_kv_heads][d]) appended as fp16 at row `pos` of
+ * the layer's caches [max_seq][n_kv_heads][d].  Replaces applyRoPE on Q and
+ * K plus the KV-cache blit (LlamaRunner.swift:612-666). */
+int mlm_rope_qk_kv_append(mlm_ctx *ctx, const float *q, const float *k, const float *v,
+                          const float *freqs, const mlm_rope_args *args, int n_q_heads,
+                          int n_kv_heads, int head_dim, void *q_out_f16, void *k_cache_f16,
+                          void *v_cache_f16, int pos);
+
+/* kernel_silu_f16 then kernel_mul_f16 (ActivationKernels.metal:6-27,
+ * ElementwiseKernels.metal; LlamaRunner.swift:1036-1057):
+ * out_f16[i] = half(silu(gate[i]) * up[i]) from fp32 gate/up */
+int mlm_silu_mul(mlm_ctx *ctx, const float *gate, const float *up, void *out_f16, int n);
+/* kernel_add_f16 (residual adds, LlamaRunner.swift:969-980, 1074-1085), fp32 */
+int mlm_add_f32(mlm_ctx *ctx, const float *a, const float *b, float *out, int n);
+
+/* ---------------------------------------------------------------------------
+ * Attention
+ * ------------------------------------------------------------------------ */
+
+/* Decode attention for one token over an fp16 KV cache: for every query head
+ * h, out[h] = softmax(q[h] . K[0:seq_len, h/(n_heads/n_kv_heads)]^T / sqrt(d))
+ * . V[...].  Replaces applyRepeatKVHeads, the per-head MPS GEMMs and
+ * encodeMPSSoftMax (LlamaRunner.swift:669-952, AttentionKernels.metal:16-59,
+ * MetalService.swift:937-1000).  q fp16 [n_heads][d]; caches
+ * [>=seq_len][n_kv_heads][d] fp16; out fp16 [n_heads][d].  head_dim 128. */
+int mlm_attn_decode(mlm_ctx *ctx, const void *q_f16, const void *k_cache_f16,
+                    const void *v_cache_f16, int n_heads, int n_kv_heads, int head_dim,
+                    int seq_len, void *out_f16);
+
+/* ---------------------------------------------------------------------------
+ * Embedding / argmax (the greedy loop of ContentView.swift:124-146, 274-343)
+ * ------------------------------------------------------------------------ */
+
+/* out[i] = float(table[token][i]) for an fp16 [vocab][dim] table
+ * (embedding-row blit, LlamaRunner.swift:473-491) */
+int mlm_embed_f16(mlm_ctx *ctx, const void *table_f16, int vocab, int dim,
+                  const int32_t *token_dev, float *out);
+/* index of the largest logit (first on ties), written to *out_index (device) */
+int mlm_argmax_f32(mlm_ctx *ctx, const float *logits, int n, int32_t *out_index_dev);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* METALLM_CUDA_H */

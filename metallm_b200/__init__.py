@@ -1,0 +1,162 @@
+"""metallm_b200 -- B200 (sm_100a) implementation of MetalLM's Q4_K Llama-3 hot path.
+
+The product is the C-ABI shared library ``libmetallm_cuda.so`` (declared in
+``include/metallm_cuda.h``).  This package holds its CUDA sources
+(``csrc/``), the in-tree build (``build.py``) and a thin Python binding
+(``Context``/``DeviceBuffer``) used by the tests and the bench.  Every call
+goes through the C ABI; there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Sequence
+
+import numpy as np
+
+from ._lib import LIB_PATH, MLMError, RopeArgs, load, rope_args  # noqa: F401
+
+QK_K = 256
+Q4K_BLOCK_BYTES = 144
+
+
+class DeviceBuffer:
+    """A device allocation made through mlm_alloc (freed with mlm_free)."""
+
+    def __init__(self, ctx: "Context", nbytes: int):
+        self.ctx = ctx
+        self.nbytes = int(nbytes)
+        p = ctypes.c_void_p()
+        ctx._check(ctx.lib.mlm_alloc(ctx.handle, self.nbytes, ctypes.byref(p)), "mlm_alloc")
+        self.ptr = int(p.value)
+
+    def free(self) -> None:
+        if self.ptr:
+            self.ctx.lib.mlm_free(self.ctx.handle, ctypes.c_void_p(self.ptr))
+            self.ptr = 0
+
+    def __del__(self):
+        try:
+            if self.ptr and self.ctx.handle:
+                self.free()
+        except Exception:
+            pass
+
+    def upload(self, a: np.ndarray) -> "DeviceBuffer":
+        a = np.ascontiguousarray(a)
+        assert a.nbytes <= self.nbytes, (a.nbytes, self.nbytes)
+        self.ctx._check(self.ctx.lib.mlm_upload(self.ctx.handle, ctypes.c_void_p(self.ptr),
+                                                a.ctypes.data, a.nbytes), "mlm_upload")
+        return self
+
+    def download(self, dtype, count: Optional[int] = None) -> np.ndarray:
+        dtype = np.dtype(dtype)
+        n = self.nbytes // dtype.itemsize if count is None else int(count)
+        out = np.empty(n, dtype=dtype)
+        self.ctx._check(self.ctx.lib.mlm_download(self.ctx.handle, out.ctypes.data,
+                                                  ctypes.c_void_p(self.ptr), out.nbytes),
+                        "mlm_download")
+        return out
+
+    def __int__(self) -> int:
+        return self.ptr
+
+
+class Context:
+    """One mlm_ctx: a device, a stream and the kernels' scratch."""
+
+    def __init__(self, device: int = 0):
+        self.lib = load()
+        h = ctypes.c_void_p()
+        st = self.lib.mlm_create(device, ctypes.byref(h))
+        if st != 0:
+            raise MLMError(st, f"mlm_create(device={device}) failed "
+                               f"({self.lib.mlm_status_string(st).decode()})")
+        self.handle = h
+        self.device = device
+
+    def close(self) -> None:
+        if self.handle:
+            self.lib.mlm_destroy(self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # -- plumbing ------------------------------------------------------------
+    def _check(self, status: int, what: str) -> None:
+        if status != 0:
+            msg = self.lib.mlm_last_error(self.handle)
+            raise MLMError(status, f"{what}: {msg.decode() if msg else ''}")
+
+    def call(self, name: str, *args) -> None:
+        fn = getattr(self.lib, name)
+        conv = [ctypes.c_void_p(int(a)) if isinstance(a, DeviceBuffer) else a for a in args]
+        self._check(fn(self.handle, *conv), name)
+
+    def alloc(self, nbytes: int) -> DeviceBuffer:
+        return DeviceBuffer(self, nbytes)
+
+    def to_device(self, a: np.ndarray) -> DeviceBuffer:
+        a = np.ascontiguousarray(a)
+        return DeviceBuffer(self, max(a.nbytes, 16)).upload(a)
+
+    def wait(self) -> None:
+        self._check(self.lib.mlm_wait(self.handle), "mlm_wait")
+
+    def stream(self) -> int:
+        s = ctypes.c_void_p()
+        self._check(self.lib.mlm_get_stream(self.handle, ctypes.byref(s)), "mlm_get_stream")
+        return int(s.value or 0)
+
+    def set_stream(self, stream: int) -> None:
+        self._check(self.lib.mlm_set_stream(self.handle, ctypes.c_void_p(stream)),
+                    "mlm_set_stream")
+
+    @property
+    def sm_count(self) -> int:
+        return int(self.lib.mlm_device_sm_count(self.handle))
+
+    # -- generators ----------------------------------------------------------
+    def gen_q4k(self, seed: int, stream: int, nblocks: int, out: DeviceBuffer,
+                first_block: int = 0) -> DeviceBuffer:
+        self.call("mlm_gen_q4k", seed, stream, first_block, nblocks, out)
+        return out
+
+    def gen_f16(self, seed: int, stream: int, n: int, out: DeviceBuffer, mean: float = 0.0,
+                std: float = 1.0, first: int = 0) -> DeviceBuffer:
+        self.call("mlm_gen_f16", seed, stream, first, n, ctypes.c_float(mean),
+                  ctypes.c_float(std), out)
+        return out
+
+    def gen_f32(self, seed: int, stream: int, n: int, out: DeviceBuffer, mean: float = 0.0,
+                std: float = 1.0, first: int = 0) -> DeviceBuffer:
+        self.call("mlm_gen_f32", seed, stream, first, n, ctypes.c_float(mean),
+                  ctypes.c_float(std), out)
+        return out
+
+    # -- ops (thin wrappers; all stream-ordered) ------------------------------
+    def q4k_dequant_f32(self, blocks, out, n: int) -> None:
+        self.call("mlm_q4k_dequant_f32", blocks, out, n)
+
+    def q4k_dequant_f16(self, blocks, out, n: int) -> None:
+        self.call("mlm_q4k_dequant_f16", blocks, out, n)
+
+    def q4k_dequant_bf16(self, blocks, out, n: int) -> None:
+        self.call("mlm_q4k_dequant_bf16", blocks, out, n)
+
+    def q4k_gemv(self, W, rows: int, cols: int, x, y, residual=None) -> None:
+        self.call("mlm_q4k_gemv", W, rows, cols, x, y, residual)
+
+
+def exported_symbols() -> Sequence[str]:
+    from ._lib import SIGNATURES
+    return [s[0] for s in SIGNATURES]

@@ -1,0 +1,288 @@
+// attention.cu -- GQA decode attention over an fp16 KV cache, split along the
+// sequence ("flash-decoding"), plus embedding gather and device argmax.
+//
+// The reference computes one decode step's attention with a repeat-KV copy
+// (AttentionKernels.metal:16-59), 32 per-head MPS GEMMs for q.K^T scaled by
+// 1/sqrt(d), an MPS row softmax and 32 more GEMMs for P.V
+// (LlamaRunner.swift:669-952).  Here one CTA owns one KV head and one chunk
+// of positions and serves all n_heads/n_kv_heads query heads of that KV head,
+// so each K and V row is read from HBM exactly once.  Softmax is fp32 with a
+// running max; each CTA writes (max, sum, unnormalised output) for its chunk
+// and a second kernel merges the chunks.
+#include "mlm_device.cuh"
+#include "mlm_internal.h"
+
+namespace mlm {
+
+constexpr int kAttnD = 128;       // head_dim handled by this kernel
+constexpr int kAttnChunk = 64;    // positions per CTA (upper bound)
+constexpr int kAttnMaxChunks = 64;
+constexpr int kAttnThreads = 128;
+
+// partial layout per (chunk, head): [m, l, o[128]]
+constexpr int kAttnPartial = 2 + kAttnD;
+
+template <int G>
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_partial_kernel(
+    const __half *__restrict__ q, const __half *__restrict__ kc, const __half *__restrict__ vc,
+    int n_heads, int n_kv, int seq_len, int chunk_len, float scale,
+    float *__restrict__ partials) {
+  __shared__ float s_scores[G][kAttnChunk * 2];
+  __shared__ float s_out[kAttnThreads / 32][G][kAttnD];
+  const int kvh = blockIdx.x;
+  const int chunk = blockIdx.y;
+  const int p0 = chunk * chunk_len;
+  const int p1 = min(seq_len, p0 + chunk_len);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nwarp = kAttnThreads / 32;
+  const size_t row_stride = (size_t)n_kv * kAttnD;
+
+  // q of the G heads of this group, dims 4*lane .. 4*lane+3
+  float qv[G][4];
+#pragma unroll
+  for (int gh = 0; gh < G; ++gh) {
+    const __half *qh = q + (size_t)(kvh * G + gh) * kAttnD + 4 * lane;
+    const uint2 raw = *reinterpret_cast<const uint2 *>(qh);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
+    qv[gh][0] = a.x * scale;
+    qv[gh][1] = a.y * scale;
+    qv[gh][2] = b.x * scale;
+    qv[gh][3] = b.y * scale;
+  }
+
+  // scores: warp w handles positions p0 + w, p0 + w + nwarp, ...
+  for (int p = p0 + warp; p < p1; p += nwarp) {
+    const uint2 raw = *reinterpret_cast<const uint2 *>(kc + p * row_stride + kvh * kAttnD + 4 * lane);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
+#pragma unroll
+    for (int gh = 0; gh < G; ++gh) {
+      float s = qv[gh][0] * a.x + qv[gh][1] * a.y + qv[gh][2] * b.x + qv[gh][3] * b.y;
+      s = warp_sum(s);
+      if (lane == 0) s_scores[gh][p - p0] = s;
+    }
+  }
+  __syncthreads();
+
+  // chunk max and exp-sum per head (warp gh handles head gh, strided)
+  __shared__ float s_m[G], s_l[G];
+  for (int gh = warp; gh < G; gh += nwarp) {
+    float m = -INFINITY;
+    for (int i = lane; i < p1 - p0; i += 32) m = fmaxf(m, s_scores[gh][i]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (int i = lane; i < p1 - p0; i += 32) {
+      const float e = __expf(s_scores[gh][i] - m);
+      s_scores[gh][i] = e;
+      l += e;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      s_m[gh] = m;
+      s_l[gh] = l;
+    }
+  }
+  __syncthreads();
+
+  // P.V: warp w accumulates positions p0 + w (+ nwarp ...) for dims 4*lane..
+  float o[G][4];
+#pragma unroll
+  for (int gh = 0; gh < G; ++gh) o[gh][0] = o[gh][1] = o[gh][2] = o[gh][3] = 0.f;
+  for (int p = p0 + warp; p < p1; p += nwarp) {
+    const uint2 raw = *reinterpret_cast<const uint2 *>(vc + p * row_stride + kvh * kAttnD + 4 * lane);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
+#pragma unroll
+    for (int gh = 0; gh < G; ++gh) {
+      const float w = s_scores[gh][p - p0];
+      o[gh][0] += w * a.x;
+      o[gh][1] += w * a.y;
+      o[gh][2] += w * b.x;
+      o[gh][3] += w * b.y;
+    }
+  }
+#pragma unroll
+  for (int gh = 0; gh < G; ++gh)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) s_out[warp][gh][4 * lane + e] = o[gh][e];
+  __syncthreads();
+
+  for (int i = threadIdx.x; i < G * kAttnD; i += kAttnThreads) {
+    const int gh = i / kAttnD, dd = i - gh * kAttnD;
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < nwarp; ++w) acc += s_out[w][gh][dd];
+    float *pp = partials + ((size_t)chunk * n_heads + kvh * G + gh) * kAttnPartial;
+    pp[2 + dd] = acc;
+    if (dd == 0) {
+      pp[0] = s_m[gh];
+      pp[1] = s_l[gh];
+    }
+  }
+}
+
+__global__ void attn_decode_merge_kernel(const float *__restrict__ partials, int n_heads,
+                                         int nchunks, __half *__restrict__ out) {
+  const int h = blockIdx.x;
+  const int dd = threadIdx.x;  // 128 threads
+  float M = -INFINITY;
+  for (int c = 0; c < nchunks; ++c) M = fmaxf(M, partials[((size_t)c * n_heads + h) * kAttnPartial]);
+  float L = 0.f, O = 0.f;
+  for (int c = 0; c < nchunks; ++c) {
+    const float *pp = partials + ((size_t)c * n_heads + h) * kAttnPartial;
+    const float w = __expf(pp[0] - M);
+    L += pp[1] * w;
+    O += pp[2 + dd] * w;
+  }
+  out[(size_t)h * kAttnD + dd] = __float2half_rn(O / L);
+}
+
+int attn_decode_launch(mlm_ctx *ctx, const void *q, const void *kc, const void *vc, int n_heads,
+                       int n_kv, int head_dim, int seq_len, void *out, float *partials,
+                       size_t partial_floats, cudaStream_t stream) {
+  MLM_REQUIRE(ctx, head_dim == kAttnD, MLM_ERR_UNSUPPORTED,
+              "mlm_attn_decode: head_dim=%d (this build handles %d)", head_dim, kAttnD);
+  MLM_REQUIRE(ctx, n_kv > 0 && n_heads % n_kv == 0, MLM_ERR_SHAPE,
+              "mlm_attn_decode: %d query heads not a multiple of %d KV heads", n_heads, n_kv);
+  const int G = n_heads / n_kv;
+  MLM_REQUIRE(ctx, G == 1 || G == 2 || G == 4 || G == 8, MLM_ERR_UNSUPPORTED,
+              "mlm_attn_decode: GQA group %d (supported 1, 2, 4, 8)", G);
+  MLM_REQUIRE(ctx, seq_len > 0, MLM_ERR_SHAPE, "mlm_attn_decode: seq_len=%d", seq_len);
+  int nchunks = (seq_len + kAttnChunk - 1) / kAttnChunk;
+  if (nchunks > kAttnMaxChunks) nchunks = kAttnMaxChunks;
+  const int chunk_len = (seq_len + nchunks - 1) / nchunks;
+  MLM_REQUIRE(ctx, chunk_len <= 2 * kAttnChunk, MLM_ERR_SHAPE,
+              "mlm_attn_decode: seq_len=%d exceeds %d positions", seq_len,
+              2 * kAttnChunk * kAttnMaxChunks);
+  MLM_REQUIRE(ctx, (size_t)nchunks * n_heads * kAttnPartial <= partial_floats, MLM_ERR_SHAPE,
+              "mlm_attn_decode: %d heads exceed the attention scratch", n_heads);
+  const float scale = 1.0f / sqrtf((float)head_dim);
+  dim3 grid(n_kv, nchunks);
+  const __half *qh = reinterpret_cast<const __half *>(q);
+  const __half *kh = reinterpret_cast<const __half *>(kc);
+  const __half *vh = reinterpret_cast<const __half *>(vc);
+  switch (G) {
+    case 1:
+      attn_decode_partial_kernel<1><<<grid, kAttnThreads, 0, stream>>>(
+          qh, kh, vh, n_heads, n_kv, seq_len, chunk_len, scale, partials);
+      break;
+    case 2:
+      attn_decode_partial_kernel<2><<<grid, kAttnThreads, 0, stream>>>(
+          qh, kh, vh, n_heads, n_kv, seq_len, chunk_len, scale, partials);
+      break;
+    case 4:
+      attn_decode_partial_kernel<4><<<grid, kAttnThreads, 0, stream>>>(
+          qh, kh, vh, n_heads, n_kv, seq_len, chunk_len, scale, partials);
+      break;
+    default:
+      attn_decode_partial_kernel<8><<<grid, kAttnThreads, 0, stream>>>(
+          qh, kh, vh, n_heads, n_kv, seq_len, chunk_len, scale, partials);
+      break;
+  }
+  int st = check_launch(ctx, "mlm_attn_decode (partial)");
+  if (st != MLM_OK) return st;
+  attn_decode_merge_kernel<<<n_heads, kAttnD, 0, stream>>>(partials, n_heads, nchunks,
+                                                           reinterpret_cast<__half *>(out));
+  return check_launch(ctx, "mlm_attn_decode (merge)");
+}
+
+size_t attn_partial_floats_max(int max_heads) {
+  return (size_t)kAttnMaxChunks * max_heads * kAttnPartial;
+}
+
+// ---- embedding gather and argmax ------------------------------------------------
+
+__global__ void embed_f16_kernel(const __half *__restrict__ table, int vocab, int dim,
+                                 const int32_t *__restrict__ token, float *__restrict__ out) {
+  int t = *token;
+  t = t < 0 ? 0 : (t >= vocab ? vocab - 1 : t);
+  const __half *row = table + (size_t)t * dim;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x)
+    out[i] = __half2float(row[i]);
+}
+
+__global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ x, int n,
+                                                      int32_t *__restrict__ out) {
+  // first index of the maximum; NaN never wins; an all-NaN row yields 0
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = x[i];
+    if (v > best || (v == best && i < bi)) {
+      best = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ob > best || (ob == best && oi < bi)) {
+      best = ob;
+      bi = oi;
+    }
+  }
+  __shared__ float sb[32];
+  __shared__ int si[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) {
+    sb[warp] = best;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float b = sb[0];
+    int idx = si[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) {
+      if (sb[w] > b || (sb[w] == b && si[w] < idx)) {
+        b = sb[w];
+        idx = si[w];
+      }
+    }
+    *out = idx == 0x7fffffff ? 0 : idx;
+  }
+}
+
+int argmax_launch(mlm_ctx *ctx, const float *x, int n, int32_t *out, cudaStream_t stream) {
+  argmax_kernel<<<1, 1024, 0, stream>>>(x, n, out);
+  return check_launch(ctx, "mlm_argmax_f32");
+}
+
+int embed_launch(mlm_ctx *ctx, const void *table, int vocab, int dim, const int32_t *tok,
+                 float *out, cudaStream_t stream) {
+  embed_f16_kernel<<<(dim + 255) / 256, 256, 0, stream>>>(reinterpret_cast<const __half *>(table),
+                                                          vocab, dim, tok, out);
+  return check_launch(ctx, "mlm_embed_f16");
+}
+
+}  // namespace mlm
+
+using namespace mlm;
+
+extern "C" int mlm_attn_decode(mlm_ctx *ctx, const void *q, const void *kc, const void *vc,
+                               int n_heads, int n_kv_heads, int head_dim, int seq_len,
+                               void *out) {
+  MLM_CHECK_CTX(ctx);
+  MLM_REQUIRE(ctx, q && kc && vc && out, MLM_ERR_ARG, "mlm_attn_decode: null buffer");
+  MLM_REQUIRE(ctx, aligned16(q) && aligned16(kc) && aligned16(vc), MLM_ERR_ALIGN,
+              "mlm_attn_decode: q and caches must be 16-byte aligned");
+  return attn_decode_launch(ctx, q, kc, vc, n_heads, n_kv_heads, head_dim, seq_len, out,
+                            ctx->attn_partials, ctx->attn_partials_floats, ctx->stream);
+}
+
+extern "C" int mlm_embed_f16(mlm_ctx *ctx, const void *table, int vocab, int dim,
+                             const int32_t *token, float *out) {
+  MLM_CHECK_CTX(ctx);
+  MLM_REQUIRE(ctx, table && token && out, MLM_ERR_ARG, "mlm_embed_f16: null buffer");
+  MLM_REQUIRE(ctx, vocab > 0 && dim > 0, MLM_ERR_SHAPE, "mlm_embed_f16: vocab=%d dim=%d", vocab,
+              dim);
+  return embed_launch(ctx, table, vocab, dim, token, out, ctx->stream);
+}
+
+extern "C" int mlm_argmax_f32(mlm_ctx *ctx, const float *logits, int n, int32_t *out) {
+  MLM_CHECK_CTX(ctx);
+  MLM_REQUIRE(ctx, logits && out, MLM_ERR_ARG, "mlm_argmax_f32: null buffer");
+  MLM_REQUIRE(ctx, n > 0, MLM_ERR_SHAPE, "mlm_argmax_f32: n=%d", n);
+  return argmax_launch(ctx, logits, n, out, ctx->stream);
+}

@@ -1,0 +1,64 @@
+// mlm_internal.h -- context object and error plumbing shared by the CUDA
+// translation units of libmetallm_cuda.so.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "../../include/metallm_cuda.h"
+
+struct mlm_ctx {
+  int device = 0;
+  int sm_count = 0;
+  int max_smem_optin = 0;
+  cudaStream_t own_stream = nullptr;
+  cudaStream_t stream = nullptr;  // the stream ops are enqueued on
+  cudaEvent_t commit_event = nullptr;
+  std::string last_error;
+  std::mutex lock;  // serialises the synchronous helpers
+
+  // split-K scratch of the Q4_K GEMV: one partial row-tile per (warp, end)
+  // and one arrival counter per row tile; counters return to zero after
+  // every launch.
+  float *gemv_partials = nullptr;
+  int *gemv_counters = nullptr;
+  int gemv_max_warps = 0;
+  int gemv_max_tiles = 0;
+
+  // split-K scratch of decode attention
+  float *attn_partials = nullptr;
+  size_t attn_partials_floats = 0;
+};
+
+namespace mlm {
+
+int set_error(mlm_ctx *ctx, int code, const char *fmt, ...)
+    __attribute__((format(printf, 3, 4)));
+int check_launch(mlm_ctx *ctx, const char *what);
+
+inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline bool aligned4(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
+
+}  // namespace mlm
+
+#define MLM_CHECK_CTX(ctx) \
+  do {                     \
+    if (!(ctx)) return MLM_ERR_ARG; \
+  } while (0)
+
+#define MLM_REQUIRE(ctx, cond, code, ...)                   \
+  do {                                                     \
+    if (!(cond)) return mlm::set_error((ctx), (code), __VA_ARGS__); \
+  } while (0)
+
+#define MLM_CUDA_TRY(ctx, call)                                                     \
+  do {                                                                              \
+    cudaError_t e_ = (call);                                                        \
+    if (e_ != cudaSuccess)                                                          \
+      return mlm::set_error((ctx), MLM_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+  } while (0)

@@ -1,0 +1,310 @@
+// norm_rope.cu -- RMSNorm, RoPE and the small elementwise kernels of the
+// decode step.
+//
+// RMSNorm follows kernel_rms_norm_f16 (MetalLM/Backend/Metal/
+// NormalizationKernels.metal:9-80): fp32 sum of squares,
+// scale = min(1 / sqrt(max(mean, 1e-10) + eps), 1e6), y = (x*scale)*w with
+// NaN/Inf weights read as 1.  One CTA per row; the row is read once into
+// registers, reduced with warp shuffles, then scaled and written.
+//
+// RoPE follows kernel_rope_f16_inplace and its YaRN helpers
+// (PositionalEmbeddingsKernels.metal:52-125, 137-204): normal (adjacent
+// pair) mode, theta = pos * base^(-i0/n_dims) / freq_factor, optional YaRN
+// blend when ext_factor != 0.  cos/sin are evaluated in double precision so
+// large angles (pos ~ 2047 rad) keep full fp32 accuracy.
+#include "mlm_device.cuh"
+#include "mlm_internal.h"
+
+namespace mlm {
+
+// ---- RMSNorm ------------------------------------------------------------------
+
+__device__ __forceinline__ float rms_scale(float sum_sq, int n, float eps) {
+  const float mean_sq = sum_sq / (float)n;
+  const float safe = fmaxf(mean_sq, 1e-10f);
+  const float rms = sqrtf(safe + eps);
+  return fminf(1.0f / rms, 1e6f);
+}
+
+__device__ __forceinline__ float block_sum(float v, float *red) {
+  v = warp_sum(v);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  const int nw = blockDim.x >> 5;
+  float s = 0.f;
+  for (int i = 0; i < nw; ++i) s += red[i];
+  return s;
+}
+
+__device__ __forceinline__ float safe_weight(float w) {
+  return (isnan(w) || isinf(w)) ? 1.0f : w;
+}
+
+__global__ void __launch_bounds__(256) rmsnorm_f16_kernel(const __half *__restrict__ x,
+                                                         const __half *__restrict__ w,
+                                                         __half *__restrict__ y, int n,
+                                                         float eps) {
+  __shared__ float red[32];
+  const __half *xr = x + (size_t)blockIdx.x * n;
+  __half *yr = y + (size_t)blockIdx.x * n;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = __half2float(xr[i]);
+    ss += v * v;
+  }
+  const float scale = rms_scale(block_sum(ss, red), n, eps);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float wv = safe_weight(__half2float(w[i]));
+    yr[i] = __float2half_rn((__half2float(xr[i]) * scale) * wv);
+  }
+}
+
+__global__ void __launch_bounds__(512) rmsnorm_f32_kernel(const float *__restrict__ x,
+                                                         const float *__restrict__ w,
+                                                         float *__restrict__ y32,
+                                                         __half *__restrict__ y16, int n,
+                                                         float eps) {
+  __shared__ float red[32];
+  const float *xr = x + (size_t)blockIdx.x * n;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = xr[i];
+    ss += v * v;
+  }
+  const float scale = rms_scale(block_sum(ss, red), n, eps);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float o = (xr[i] * scale) * safe_weight(w[i]);
+    if (y32) y32[(size_t)blockIdx.x * n + i] = o;
+    if (y16) y16[(size_t)blockIdx.x * n + i] = __float2half_rn(o);
+  }
+}
+
+// ---- RoPE -----------------------------------------------------------------------
+
+struct RopeConsts {
+  float inv_ndims;
+  float corr0, corr1;
+};
+
+__host__ __device__ inline float yarn_corr_factor(int n_dims, int n_ctx_orig, float n_rot,
+                                                  float base) {
+  if (n_rot <= 0.0f || base <= 0.0f || n_ctx_orig <= 0) return 0.0f;
+  const float lb = logf(base);
+  if (fabsf(lb) < 1e-6f) return 0.0f;
+  const float term = (float)n_ctx_orig / (n_rot * 2.0f * 3.14159265358979323846f);
+  if (term <= 0.0f) return 0.0f;
+  return (float)n_dims * logf(term) / (2.0f * lb);
+}
+
+static RopeConsts rope_consts(const mlm_rope_args &a) {
+  RopeConsts c;
+  c.inv_ndims = -1.0f / (float)a.n_dims;
+  const float fast = yarn_corr_factor((int)a.n_dims, a.n_ctx_orig, a.beta_fast, a.freq_base);
+  const float slow = yarn_corr_factor((int)a.n_dims, a.n_ctx_orig, a.beta_slow, a.freq_base);
+  float c0 = floorf(fast);
+  if (c0 < 0.0f) c0 = 0.0f;
+  float c1 = ceilf(slow);
+  if (c1 < c0) c1 = c0;
+  if (c1 > (float)a.n_dims - 2.0f) c1 = (float)a.n_dims - 2.0f;
+  c.corr0 = c0;
+  c.corr1 = c1;
+  return c;
+}
+
+// cos/sin of pair p at position pos (calculate_rope_yarn)
+__device__ __forceinline__ void rope_cos_sin(const mlm_rope_args &a, const RopeConsts &k,
+                                             const float *freqs, int pos, int p, float &c,
+                                             float &s) {
+  const int i0 = 2 * p;
+  const float theta_extrap = (float)pos * powf(a.freq_base, k.inv_ndims * (float)i0);
+  const float ff = a.has_freq_factors ? freqs[p] : 1.0f;
+  const float theta_scaled = theta_extrap / fmaxf(0.0001f, ff);
+  const float theta_interp = a.freq_scale * theta_scaled;
+  float theta = theta_interp;
+  float mscale = a.attn_factor;
+  if (a.ext_factor != 0.0f) {
+    const float diff = fmaxf(0.001f, k.corr1 - k.corr0);
+    const float y = ((float)i0 / 2.0f - k.corr0) / diff;
+    const float ramp = 1.0f - fminf(1.0f, fmaxf(0.0f, y));
+    const float mix = ramp * a.ext_factor;
+    theta = theta_interp * (1.0f - mix) + theta_scaled * mix;
+    if (a.freq_scale > 0.0f) mscale *= (1.0f + 0.1f * logf(1.0f / a.freq_scale));
+  }
+  double sd, cd;
+  sincos((double)theta, &sd, &cd);
+  c = (float)cd * mscale;
+  s = (float)sd * mscale;
+}
+
+// grid: (ceil(n_dims/2 / 32), heads, seq) -- the reference's dispatch shape
+__global__ void rope_f16_kernel(mlm_rope_args a, RopeConsts k, const float *__restrict__ freqs,
+                                __half *__restrict__ data, int num_heads, int head_dim) {
+  const int p = blockIdx.x * blockDim.x + threadIdx.x;
+  const int h = blockIdx.y, t = blockIdx.z;
+  if (2 * p >= (int)a.n_dims || 2 * p + 1 >= head_dim) return;
+  float c, s;
+  rope_cos_sin(a, k, freqs, a.pos_offset + t, p, c, s);
+  const float hc = __half2float(__float2half_rn(c));
+  const float hs = __half2float(__float2half_rn(s));
+  __half *e = data + ((size_t)t * num_heads + h) * head_dim + 2 * p;
+  const float x0 = __half2float(e[0]), x1 = __half2float(e[1]);
+  // half operands, each rotated value formed in fp32 and rounded once
+  e[0] = __float2half_rn(__fsub_rn(__fmul_rn(x0, hc), __fmul_rn(x1, hs)));
+  e[1] = __float2half_rn(__fadd_rn(__fmul_rn(x0, hs), __fmul_rn(x1, hc)));
+}
+
+// decode: rotate fp32 q, k at position pos; q -> fp16 q_out, k and v -> fp16
+// cache rows.  One thread per rotation pair of q and k, plus v copies.
+__global__ void rope_qk_kv_kernel(mlm_rope_args a, RopeConsts k, const float *__restrict__ freqs,
+                                  const float *__restrict__ q, const float *__restrict__ kin,
+                                  const float *__restrict__ v, int nq, int nkv, int d,
+                                  __half *__restrict__ q_out, __half *__restrict__ kc,
+                                  __half *__restrict__ vc, int pos) {
+  const int pairs = d / 2;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int nqp = nq * pairs, nkp = nkv * pairs;
+  if (i < nqp + nkp) {
+    const bool is_q = i < nqp;
+    const int j = is_q ? i : i - nqp;
+    const int h = j / pairs, pp = j - h * pairs;
+    const float *src = (is_q ? q : kin) + (size_t)h * d + 2 * pp;
+    float x0 = src[0], x1 = src[1];
+    if (2 * pp < (int)a.n_dims) {
+      float c, s;
+      rope_cos_sin(a, k, freqs, a.pos_offset, pp, c, s);
+      const float r0 = x0 * c - x1 * s;
+      const float r1 = x0 * s + x1 * c;
+      x0 = r0;
+      x1 = r1;
+    }
+    __half2 o = __floats2half2_rn(x0, x1);
+    if (is_q) {
+      *reinterpret_cast<__half2 *>(q_out + (size_t)h * d + 2 * pp) = o;
+    } else {
+      *reinterpret_cast<__half2 *>(kc + ((size_t)pos * nkv + h) * d + 2 * pp) = o;
+    }
+  } else if (i < nqp + 2 * nkp) {
+    const int j = i - nqp - nkp;
+    const int h = j / pairs, pp = j - h * pairs;
+    const float *src = v + (size_t)h * d + 2 * pp;
+    *reinterpret_cast<__half2 *>(vc + ((size_t)pos * nkv + h) * d + 2 * pp) =
+        __floats2half2_rn(src[0], src[1]);
+  }
+}
+
+// ---- elementwise ------------------------------------------------------------------
+
+__global__ void silu_mul_kernel(const float *__restrict__ g, const float *__restrict__ u,
+                                __half *__restrict__ out, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float x = g[i];
+  const float sig = 1.0f / (1.0f + expf(-x));
+  out[i] = __float2half_rn(x * sig * u[i]);
+}
+
+__global__ void add_f32_kernel(const float *__restrict__ a, const float *__restrict__ b,
+                               float *__restrict__ out, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = a[i] + b[i];
+}
+
+int rope_qk_kv_launch(mlm_ctx *ctx, const float *q, const float *k, const float *v,
+                      const float *freqs, const mlm_rope_args &a, int nq, int nkv, int d,
+                      void *q_out, void *kc, void *vc, int pos, cudaStream_t stream) {
+  const RopeConsts kc_ = rope_consts(a);
+  const int total = nq * (d / 2) + 2 * nkv * (d / 2);
+  rope_qk_kv_kernel<<<(total + 255) / 256, 256, 0, stream>>>(
+      a, kc_, freqs, q, k, v, nq, nkv, d, reinterpret_cast<__half *>(q_out),
+      reinterpret_cast<__half *>(kc), reinterpret_cast<__half *>(vc), pos);
+  return check_launch(ctx, "mlm_rope_qk_kv_append");
+}
+
+int silu_mul_launch(mlm_ctx *ctx, const float *g, const float *u, void *out, int n,
+                    cudaStream_t stream) {
+  silu_mul_kernel<<<(n + 255) / 256, 256, 0, stream>>>(g, u, reinterpret_cast<__half *>(out), n);
+  return check_launch(ctx, "mlm_silu_mul");
+}
+
+int rmsnorm_f32_launch(mlm_ctx *ctx, const float *x, const float *w, float *y32, void *y16,
+                       int rows, int n, float eps, cudaStream_t stream) {
+  rmsnorm_f32_kernel<<<rows, 512, 0, stream>>>(x, w, y32, reinterpret_cast<__half *>(y16), n,
+                                                eps);
+  return check_launch(ctx, "mlm_rmsnorm_f32");
+}
+
+}  // namespace mlm
+
+using namespace mlm;
+
+extern "C" int mlm_rmsnorm_f16(mlm_ctx *ctx, const void *x, const void *w, void *y, int rows,
+                               int n, float eps) {
+  MLM_CHECK_CTX(ctx);
+  MLM_REQUIRE(ctx, x && w && y, MLM_ERR_ARG, "mlm_rmsnorm_f16: null buffer");
+  MLM_REQUIRE(ctx, rows > 0 && n > 0, MLM_ERR_SHAPE, "mlm_rmsnorm_f16: rows=%d n=%d", rows, n);
+  rmsnorm_f16_kernel<<<rows, 256, 0, ctx->stream>>>(reinterpret_cast<const __half *>(x),
+                                                     reinterpret_cast<const __half *>(w),
+                                                     reinterpret_cast<__half *>(y), n, eps);
+  return check_launch(ctx, "mlm_rmsnorm_f16");
+}
+
+extern "C" int mlm_rmsnorm_f32(mlm_ctx *ctx, const float *x, const float *w, float *y32,
+                               void *y16, int rows, int n, float eps) {
+  MLM_CHECK_CTX(ctx);
+  MLM_REQUIRE(ctx, x && w && (y32 || y16), MLM_ERR_ARG, "mlm_rmsnorm_f32: null buffer");
+  MLM_REQUIRE(ctx, rows > 0 && n > 0, MLM_ERR_SHAPE, "mlm_rmsnorm_f32: rows=%d n=%d", rows, n);
+  return rmsnorm_f32_launch(ctx, x, w, y32, y16, rows, n, eps, ctx->stream);
+}
+
+extern "C" int mlm_rope_f16(mlm_ctx *ctx, void *data, const float *freqs,
+                            const mlm_rope_args *args, int seq_len, int num_heads,
+                            int head_dim) {
+  MLM_CHECK_CTX(ctx);
+  MLM_REQUIRE(ctx, data && args, MLM_ERR_ARG, "mlm_rope_f16: null argument");
+  MLM_REQUIRE(ctx, !args->has_freq_factors || freqs, MLM_ERR_ARG,
+              "mlm_rope_f16: has_freq_factors set without a freqs buffer");
+  MLM_REQUIRE(ctx, seq_len > 0 && num_heads > 0 && head_dim > 0 && args->n_dims >= 2,
+              MLM_ERR_SHAPE, "mlm_rope_f16: invalid grid [%u, %d, %d]", args->n_dims / 2,
+              num_heads, seq_len);
+  const RopeConsts k = rope_consts(*args);
+  const int pairs = (int)args->n_dims / 2;
+  dim3 grid((pairs + 31) / 32, num_heads, seq_len);
+  rope_f16_kernel<<<grid, 32, 0, ctx->stream>>>(*args, k, freqs,
+                                                reinterpret_cast<__half *>(data), num_heads,
+                                                head_dim);
+  return check_launch(ctx, "mlm_rope_f16");
+}
+
+extern "C" int mlm_rope_qk_kv_append(mlm_ctx *ctx, const float *q, const float *k,
+                                     const float *v, const float *freqs,
+                                     const mlm_rope_args *args, int n_q_heads, int n_kv_heads,
+                                     int head_dim, void *q_out, void *k_cache, void *v_cache,
+                                     int pos) {
+  MLM_CHECK_CTX(ctx);
+  MLM_REQUIRE(ctx, q && k && v && args && q_out && k_cache && v_cache, MLM_ERR_ARG,
+              "mlm_rope_qk_kv_append: null argument");
+  MLM_REQUIRE(ctx, !args->has_freq_factors || freqs, MLM_ERR_ARG,
+              "mlm_rope_qk_kv_append: has_freq_factors set without a freqs buffer");
+  MLM_REQUIRE(ctx, n_q_heads > 0 && n_kv_heads > 0 && head_dim > 0 && head_dim % 2 == 0 &&
+                       pos >= 0,
+              MLM_ERR_SHAPE, "mlm_rope_qk_kv_append: heads=%d/%d d=%d pos=%d", n_q_heads,
+              n_kv_heads, head_dim, pos);
+  return rope_qk_kv_launch(ctx, q, k, v, freqs, *args, n_q_heads, n_kv_heads, head_dim, q_out,
+                           k_cache, v_cache, pos, ctx->stream);
+}
+
+extern "C" int mlm_silu_mul(mlm_ctx *ctx, const float *gate, const float *up, void *out, int n) {
+  MLM_CHECK_CTX(ctx);
+  MLM_REQUIRE(ctx, gate && up && out, MLM_ERR_ARG, "mlm_silu_mul: null buffer");
+  MLM_REQUIRE(ctx, n > 0, MLM_ERR_SHAPE, "mlm_silu_mul: n=%d", n);
+  return silu_mul_launch(ctx, gate, up, out, n, ctx->stream);
+}
+
+extern "C" int mlm_add_f32(mlm_ctx *ctx, const float *a, const float *b, float *out, int n) {
+  MLM_CHECK_CTX(ctx);
+  MLM_REQUIRE(ctx, a && b && out, MLM_ERR_ARG, "mlm_add_f32: null buffer");
+  MLM_REQUIRE(ctx, n > 0, MLM_ERR_SHAPE, "mlm_add_f32: n=%d", n);
+  add_f32_kernel<<<(n + 255) / 256, 256, 0, ctx->stream>>>(a, b, out, n);
+  return check_launch(ctx, "mlm_add_f32");
+}

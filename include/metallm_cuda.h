@@ -83,6 +83,19 @@ int mlm_host_free(mlm_ctx *ctx, void *hptr);
 int mlm_commit(mlm_ctx *ctx);
 int mlm_wait(mlm_ctx *ctx);
 
+/* CUDA-graph capture of the context's stream: ops enqueued between
+ * mlm_graph_begin and mlm_graph_end are recorded, not run; mlm_graph_launch
+ * replays them.  The decode step of the reference encodes the same op
+ * sequence into a fresh command buffer for every token
+ * (LlamaRunner.swift:526-1128); a captured graph replays it with one launch.
+ * Synchronous calls (mlm_wait, mlm_upload, mlm_download, the mlm_dequantize_*
+ * helpers) are not allowed while capturing. */
+typedef struct mlm_graph mlm_graph;
+int mlm_graph_begin(mlm_ctx *ctx);
+int mlm_graph_end(mlm_ctx *ctx, mlm_graph **out);
+int mlm_graph_launch(mlm_ctx *ctx, mlm_graph *graph);
+void mlm_graph_destroy(mlm_graph *graph);
+
 /* ---------------------------------------------------------------------------
  * Seeded synthetic data (bit-identical to the CPU oracle's generators)
  * ------------------------------------------------------------------------ */

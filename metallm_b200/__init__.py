@@ -121,6 +121,15 @@ class Context:
         self._check(self.lib.mlm_set_stream(self.handle, ctypes.c_void_p(stream)),
                     "mlm_set_stream")
 
+    # -- CUDA graphs -----------------------------------------------------------
+    def graph_begin(self) -> None:
+        self._check(self.lib.mlm_graph_begin(self.handle), "mlm_graph_begin")
+
+    def graph_end(self) -> "Graph":
+        g = ctypes.c_void_p()
+        self._check(self.lib.mlm_graph_end(self.handle, ctypes.byref(g)), "mlm_graph_end")
+        return Graph(self, g)
+
     @property
     def sm_count(self) -> int:
         return int(self.lib.mlm_device_sm_count(self.handle))
@@ -155,6 +164,29 @@ class Context:
 
     def q4k_gemv(self, W, rows: int, cols: int, x, y, residual=None) -> None:
         self.call("mlm_q4k_gemv", W, rows, cols, x, y, residual)
+
+
+class Graph:
+    """A captured op sequence (mlm_graph)."""
+
+    def __init__(self, ctx: Context, handle: ctypes.c_void_p):
+        self.ctx = ctx
+        self.handle = handle
+
+    def launch(self) -> None:
+        self.ctx._check(self.ctx.lib.mlm_graph_launch(self.ctx.handle, self.handle),
+                        "mlm_graph_launch")
+
+    def destroy(self) -> None:
+        if self.handle:
+            self.ctx.lib.mlm_graph_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.destroy()
+        except Exception:
+            pass
 
 
 def exported_symbols() -> Sequence[str]:

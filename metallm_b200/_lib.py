@@ -58,6 +58,10 @@ SIGNATURES = [
     ("mlm_host_alloc", c_int, [c_vp, c_size, ctypes.POINTER(c_vp)]),
     ("mlm_host_free", c_int, [c_vp, c_vp]),
     ("mlm_commit", c_int, [c_vp]),
+    ("mlm_graph_begin", c_int, [c_vp]),
+    ("mlm_graph_end", c_int, [c_vp, ctypes.POINTER(c_vp)]),
+    ("mlm_graph_launch", c_int, [c_vp, c_vp]),
+    ("mlm_graph_destroy", None, [c_vp]),
     ("mlm_wait", c_int, [c_vp]),
     ("mlm_gen_q4k", c_int, [c_vp, c_u64, c_u64, c_u64, c_u64, c_vp]),
     ("mlm_gen_f16", c_int, [c_vp, c_u64, c_u64, c_u64, c_u64, c_float, c_float, c_vp]),

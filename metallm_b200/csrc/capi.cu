@@ -19,6 +19,7 @@
 namespace mlm {
 
 int gemv_init(mlm_ctx *ctx);
+int gemv_max_ctas(int sm_count);
 size_t attn_partial_floats_max(int max_heads);
 
 int set_error(mlm_ctx *ctx, int code, const char *fmt, ...) {
@@ -41,7 +42,7 @@ int check_launch(mlm_ctx *ctx, const char *what) {
 }
 
 // Scratch limits: the GEMV needs one arrival counter per 32-row tile and two
-// 32-float partials per warp; attention needs (2 + 128) floats per head per
+// 32-float partials per CTA; attention needs (2 + 128) floats per head per
 // sequence chunk.
 constexpr int kMaxGemvRows = 1 << 20;
 constexpr int kMaxAttnHeads = 128;
@@ -106,15 +107,23 @@ extern "C" int mlm_create(int device, mlm_ctx **out) {
     return fail(MLM_ERR_CUDA);
 
   ctx->gemv_max_tiles = kMaxGemvRows / 32;
-  ctx->gemv_max_warps = ctx->sm_count * 16;
+  ctx->gemv_max_ctas = gemv_max_ctas(ctx->sm_count);
   if (cudaMalloc(&ctx->gemv_counters, sizeof(int) * ctx->gemv_max_tiles) != cudaSuccess ||
-      cudaMalloc(&ctx->gemv_partials, sizeof(float) * 64 * ctx->gemv_max_warps) != cudaSuccess)
+      cudaMalloc(&ctx->gemv_partials, sizeof(float) * 64 * ctx->gemv_max_ctas) != cudaSuccess)
     return fail(MLM_ERR_ALLOC);
   if (cudaMemset(ctx->gemv_counters, 0, sizeof(int) * ctx->gemv_max_tiles) != cudaSuccess)
     return fail(MLM_ERR_CUDA);
   ctx->attn_partials_floats = attn_partial_floats_max(kMaxAttnHeads);
   if (cudaMalloc(&ctx->attn_partials, sizeof(float) * ctx->attn_partials_floats) != cudaSuccess)
     return fail(MLM_ERR_ALLOC);
+  {
+    void *hs = nullptr;
+    if (cudaHostAlloc(&hs, sizeof(int), cudaHostAllocMapped) != cudaSuccess) return fail(MLM_ERR_ALLOC);
+    ctx->host_status = reinterpret_cast<volatile int *>(hs);
+    *ctx->host_status = 0;
+    if (cudaHostGetDevicePointer(reinterpret_cast<void **>(&ctx->dev_status), hs, 0) != cudaSuccess)
+      return fail(MLM_ERR_CUDA);
+  }
   if (gemv_init(ctx) != MLM_OK) return fail(MLM_ERR_CUDA);
   if (cudaDeviceSynchronize() != cudaSuccess) return fail(MLM_ERR_CUDA);
   *out = ctx;
@@ -128,6 +137,7 @@ extern "C" void mlm_destroy(mlm_ctx *ctx) {
   if (ctx->gemv_counters) cudaFree(ctx->gemv_counters);
   if (ctx->gemv_partials) cudaFree(ctx->gemv_partials);
   if (ctx->attn_partials) cudaFree(ctx->attn_partials);
+  if (ctx->host_status) cudaFreeHost(const_cast<int *>(ctx->host_status));
   if (ctx->commit_event) cudaEventDestroy(ctx->commit_event);
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
   delete ctx;
@@ -231,7 +241,69 @@ extern "C" int mlm_wait(mlm_ctx *ctx) {
   cudaError_t e = cudaStreamSynchronize(ctx->stream);
   if (e != cudaSuccess)
     return set_error(ctx, MLM_ERR_CUDA, "command buffer failed: %s", cudaGetErrorString(e));
+  const int dev = *ctx->host_status;
+  if (dev != 0) {
+    *ctx->host_status = 0;
+    return set_error(ctx, dev, "command buffer failed: a kernel's bounded wait expired (%s)",
+                     mlm_status_string(dev));
+  }
   return MLM_OK;
+}
+
+struct mlm_graph {
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+};
+
+extern "C" int mlm_graph_begin(mlm_ctx *ctx) {
+  MLM_CHECK_CTX(ctx);
+  MLM_CUDA_TRY(ctx, cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+  return MLM_OK;
+}
+
+extern "C" int mlm_graph_end(mlm_ctx *ctx, mlm_graph **out) {
+  MLM_CHECK_CTX(ctx);
+  MLM_REQUIRE(ctx, out, MLM_ERR_ARG, "mlm_graph_end: null output");
+  *out = nullptr;
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamEndCapture(ctx->stream, &g);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    if (g) cudaGraphDestroy(g);
+    return set_error(ctx, MLM_ERR_CUDA, "mlm_graph_end: capture failed: %s", cudaGetErrorString(e));
+  }
+  cudaGraphExec_t x = nullptr;
+  e = cudaGraphInstantiate(&x, g, 0);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    cudaGraphDestroy(g);
+    return set_error(ctx, MLM_ERR_CUDA, "mlm_graph_end: instantiate failed: %s",
+                     cudaGetErrorString(e));
+  }
+  mlm_graph *mg = new (std::nothrow) mlm_graph();
+  if (!mg) {
+    cudaGraphExecDestroy(x);
+    cudaGraphDestroy(g);
+    return set_error(ctx, MLM_ERR_ALLOC, "mlm_graph_end: out of host memory");
+  }
+  mg->graph = g;
+  mg->exec = x;
+  *out = mg;
+  return MLM_OK;
+}
+
+extern "C" int mlm_graph_launch(mlm_ctx *ctx, mlm_graph *graph) {
+  MLM_CHECK_CTX(ctx);
+  MLM_REQUIRE(ctx, graph && graph->exec, MLM_ERR_ARG, "mlm_graph_launch: null graph");
+  MLM_CUDA_TRY(ctx, cudaGraphLaunch(graph->exec, ctx->stream));
+  return MLM_OK;
+}
+
+extern "C" void mlm_graph_destroy(mlm_graph *graph) {
+  if (!graph) return;
+  if (graph->exec) cudaGraphExecDestroy(graph->exec);
+  if (graph->graph) cudaGraphDestroy(graph->graph);
+  delete graph;
 }
 
 // MetalService.dequantizeQ4KM_to_f32/_f16: allocate, run, wait.

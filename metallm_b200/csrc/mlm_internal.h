@@ -22,13 +22,18 @@ struct mlm_ctx {
   std::string last_error;
   std::mutex lock;  // serialises the synchronous helpers
 
-  // split-K scratch of the Q4_K GEMV: one partial row-tile per (warp, end)
+  // split-K scratch of the Q4_K GEMV: one partial row-tile per (CTA, end)
   // and one arrival counter per row tile; counters return to zero after
   // every launch.
   float *gemv_partials = nullptr;
   int *gemv_counters = nullptr;
-  int gemv_max_warps = 0;
+  int gemv_max_ctas = 0;
   int gemv_max_tiles = 0;
+
+  // error word written by kernels whose bounded waits ran out (mapped
+  // pinned host memory: the host reads it after a wait without a copy)
+  volatile int *host_status = nullptr;
+  int *dev_status = nullptr;
 
   // split-K scratch of decode attention
   float *attn_partials = nullptr;

@@ -120,6 +120,62 @@ __global__ void __launch_bounds__(256) q4k_dequant_kernel(const uint8_t *__restr
   }
 }
 
+// fp32 output: lane l owns elements 4l..4l+3 (qs half-word l, sub-block l/8)
+// and 128+4l..128+4l+3 (half-word 32+l, sub-block 4+l/8), so every warp store
+// covers 512 contiguous bytes.
+__global__ void __launch_bounds__(256) q4k_dequant_f32_kernel(const uint8_t *__restrict__ blocks,
+                                                              float *__restrict__ out, uint64_t n,
+                                                              uint64_t nblocks) {
+  const int lane = threadIdx.x & 31;
+  const uint64_t warp = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) >> 5;
+  const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+  const int j0 = lane >> 3, j1 = 4 + (lane >> 3);
+  constexpr int U = 4;
+
+  for (uint64_t b0 = warp; b0 < nblocks; b0 += nwarps * U) {
+    uint4 hdr[U];
+    uint32_t q0[U], q1[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint64_t b = b0 + (uint64_t)u * nwarps;
+      if (b < nblocks) {
+        const uint8_t *blk = blocks + b * kBlockBytes;
+        hdr[u] = ldg_stream(blk);
+        unsigned short a, c;
+        asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(a) : "l"(blk + 16 + 2 * lane));
+        asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(c) : "l"(blk + 80 + 2 * lane));
+        q0[u] = a;
+        q1[u] = c;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint64_t b = b0 + (uint64_t)u * nwarps;
+      if (b >= nblocks) continue;
+      const float d = half_bits_to_float(hdr[u].x);
+      const float dmin = half_bits_to_float(hdr[u].x >> 16);
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        int sc, m;
+        q4k_scale_min_regs(half ? j1 : j0, hdr[u].y, hdr[u].z, hdr[u].w, sc, m);
+        const float fs = d * (float)sc;    // exact
+        const float fm = dmin * (float)m;  // exact
+        const uint32_t q = half ? q1[u] : q0[u];
+        float v[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[e] = __fsub_rn(__fmul_rn(fs, (float)((q >> (4 * e)) & 0xF)), fm);
+        const uint64_t base = b * kQK + 128ull * half + 4ull * lane;
+        if (base + 4 <= n) {
+          stg_stream(out + base, make_float4(v[0], v[1], v[2], v[3]));
+        } else {
+          for (int e = 0; e < 4; ++e)
+            if (base + e < n) out[base + e] = v[e];
+        }
+      }
+    }
+  }
+}
+
 // ---- generators -------------------------------------------------------------
 
 __global__ void gen_q4k_kernel(uint64_t seed, uint64_t stream, uint64_t first_block,
@@ -175,8 +231,12 @@ static int launch_dequant(mlm_ctx *ctx, const void *blocks, void *out, uint64_t 
   const uint64_t cap = (uint64_t)ctx->sm_count * 8;
   if (grid > cap) grid = cap;
   if (grid < 1) grid = 1;
-  q4k_dequant_kernel<OUT><<<(unsigned)grid, threads, 0, ctx->stream>>>(
-      reinterpret_cast<const uint8_t *>(blocks), out, n, nblocks);
+  if (OUT == kOutF32)
+    q4k_dequant_f32_kernel<<<(unsigned)grid, threads, 0, ctx->stream>>>(
+        reinterpret_cast<const uint8_t *>(blocks), reinterpret_cast<float *>(out), n, nblocks);
+  else
+    q4k_dequant_kernel<OUT><<<(unsigned)grid, threads, 0, ctx->stream>>>(
+        reinterpret_cast<const uint8_t *>(blocks), out, n, nblocks);
   return check_launch(ctx, name);
 }
 

@@ -114,3 +114,34 @@ def test_gemv_rejects_bad_shapes(ctx):
     with pytest.raises(MLMError) as e:
         ctx.q4k_gemv(W.ptr + 8, 2, 256, x, y)
     assert e.value.status == -3
+
+
+def test_gemv_graph_replay_matches_eager(ctx):
+    """A captured sequence of GEMVs (with programmatic dependent launch) replays exactly."""
+    rows, cols = 14336, 4096
+    nb = rows * cols // 256
+    Ws = []
+    for c in range(3):
+        W = ctx.alloc(nb * 144)
+        ctx.gen_q4k(50 + c, 1, nb, W)
+        Ws.append(W)
+    x = ctx.alloc(2 * cols)
+    ctx.gen_f16(50, 2, cols, x)
+    ys = [ctx.alloc(4 * rows) for _ in range(3)]
+    for c in range(3):
+        ctx.q4k_gemv(Ws[c], rows, cols, x, ys[c])
+    eager = [y.download(np.uint32) for y in ys]
+    for y in ys:
+        ctx.call("mlm_memset", y, 0, y.nbytes)
+    ctx.graph_begin()
+    for c in range(3):
+        ctx.q4k_gemv(Ws[c], rows, cols, x, ys[c])
+    g = ctx.graph_end()
+    for _ in range(2):
+        g.launch()
+    ctx.wait()
+    g.destroy()
+    for c in range(3):
+        assert np.array_equal(ys[c].download(np.uint32), eager[c])
+    ref = O.q4k_matvec(O.gen_q4k(52, 1, nb), rows, cols, O.gen_f16(50, 2, cols))
+    assert rel_l2(ys[2].download(np.float32), ref) < TOL

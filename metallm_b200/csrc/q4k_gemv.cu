@@ -29,22 +29,24 @@
 // adjacent registers; threads whose B column does not match a word read a
 // zero region instead.
 //
-// Work split.  A unit is one block column of a 32-row tile (4608 bytes); a
-// segment is L consecutive units of one tile (L divides the blocks per row).
-// Each CTA owns a contiguous range of segments in tile-major order, so every
-// SM streams the same number of bytes (to one segment) whatever the shape.
-// Inside a CTA, warps pull segments from a shared-memory queue.  Each warp
-// streams its units through a ring of shared-memory stages, one TMA tensor
-// copy per unit (a 32-row x 144-byte box of W viewed as a 2D byte tensor,
-// L2 evict-first, rows past the end zero-filled by the TMA unit), each stage
-// tracked by an mbarrier; waits are bounded by a %globaltimer budget and
-// report a device error instead of hanging.  Each segment's 32 row sums go
-// to a shared-memory slot; the warp that completes a tile's last segment
-// sums the tile's slots in k order (deterministic) and stores y.  A tile
-// shared with a neighbouring CTA leaves one partial per CTA in the context
-// scratch and the last CTA to arrive (atomic counter) adds them in CTA
-// order, stores y and re-zeroes the counter.  Those boundary tiles are
-// queued first, so the cross-CTA exchange overlaps the interior work.
+// Work split.  A unit is one block column of a 32-row tile (4608 bytes).
+// Each CTA owns a contiguous range of units in tile-major order, so every SM
+// streams the same number of bytes (to one unit) whatever the shape.  The
+// CTA walks its units boundary tiles first (the tiles it shares with its
+// neighbours), so the cross-CTA exchange overlaps the interior work; each
+// warp takes a contiguous run of that sequence and advances (tile, block)
+// incrementally.  Units reach shared memory through a per-warp ring of
+// stages, one TMA tensor copy per unit (a 32-row x 144-byte box of W viewed
+// as a 2D byte tensor, L2 evict-first, rows past the end zero-filled by the
+// TMA unit), each stage tracked by an mbarrier; waits are bounded by a
+// %globaltimer budget and report a device error instead of hanging.  A warp
+// keeps its row sums in registers across the consecutive units of a tile.
+// A tile it covers alone is stored directly; a tile shared by several warps
+// leaves one part per warp in shared memory, and the last warp to finish
+// (shared-memory counter) adds the parts in warp order (deterministic).  A
+// tile shared with a neighbouring CTA leaves one partial per CTA in the
+// context scratch and the last CTA to arrive (atomic counter) adds them in
+// CTA order, stores y and re-zeroes the counter.
 #include <cuda.h>
 
 #include <algorithm>
@@ -58,8 +60,6 @@ constexpr int kGemvMaxWarps = 12;                     // warps per CTA (upper bo
 constexpr int kGemvStages = 3;                        // smem stages per warp
 constexpr int kTileRows = 32;                         // rows per tile
 constexpr int kStageBytes = kTileRows * kBlockBytes;  // 4608
-constexpr int kRing = 4;  // per-warp ring of (tile, block) entries: >= stages
-static_assert(kGemvStages <= kRing, "ring must cover the units in flight");
 constexpr unsigned long long kWaitBudgetNs = 200ull * 1000 * 1000;  // 200 ms
 
 struct GemvArgs {
@@ -70,15 +70,11 @@ struct GemvArgs {
   float *partials;  // [ctas][2][32]
   int *counters;    // [tiles]
   int *status;      // device-visible error word (0 = ok)
-  unsigned long long nbs_magic;  // ceil(2^40 / nbs): s / nbs == (s * magic) >> 40
+  unsigned long long nb_magic;  // ceil(2^40 / nb): u / nb == (u * magic) >> 40
   int rows;
-  int nb;      // blocks per row
-  int L;       // units per segment
-  int nbs;     // segments per tile
-  int tiles;   // ceil(rows / 32)
-  int nsegs;   // tiles * nbs
+  int nb;      // blocks per row = units per tile
+  int units;   // tiles * nb
   int ctas;    // grid size
-  int nslot;   // segment slots per CTA
   int ntile;   // tile counters per CTA (multiple of 4)
   uint32_t smem_bar;  // byte offset of the mbarriers
   uint32_t smem_x;    // byte offset of the x region
@@ -151,17 +147,43 @@ __device__ __forceinline__ void tma_unit(uint32_t dst, const CUtensorMap *tmap, 
       : "memory");
 }
 
-// first segment of CTA c, and the CTA whose range holds segment s
+// first unit of CTA c, and the CTA whose range holds unit u
 // (all products stay below 2^31: checked on the host)
-__device__ __forceinline__ int seg_begin(int c, const GemvArgs &p) {
-  return (c * p.nsegs) / p.ctas;
+__device__ __forceinline__ int unit_begin(int c, const GemvArgs &p) {
+  return (c * p.units) / p.ctas;
 }
-__device__ __forceinline__ int cta_of_seg(int s, const GemvArgs &p) {
-  return ((s + 1) * p.ctas - 1) / p.nsegs;
+__device__ __forceinline__ int cta_of_unit(int u, const GemvArgs &p) {
+  return ((u + 1) * p.ctas - 1) / p.units;
 }
-__device__ __forceinline__ int div_nbs(int s, const GemvArgs &p) {
-  return (int)(((unsigned long long)(unsigned)s * p.nbs_magic) >> 40);
+__device__ __forceinline__ int div_nb(int u, const GemvArgs &p) {
+  return (int)(((unsigned long long)(unsigned)u * p.nb_magic) >> 40);
 }
+
+// The CTA's units [u0, u1) in processing order: its first tile when shared
+// with the previous CTA, its last tile when shared with the next, then the
+// interior.  q is the position in that order.
+struct CtaOrder {
+  int u0, u1, S, nf, nl, t_first, t_last;
+  __device__ __forceinline__ int unit_of(int q) const {
+    if (q < nf) return u0 + q;
+    if (q < nf + nl) return u1 - nl + (q - nf);
+    return u0 + q - nl;
+  }
+  // queue positions [qa, qb) of tile t's units in this CTA
+  __device__ __forceinline__ void tile_range(int t, int nb, int &qa, int &qb) const {
+    const int a = max(u0, t * nb), b = min(u1, (t + 1) * nb);
+    if (t == t_first && nf > 0) {
+      qa = a - u0;
+      qb = b - u0;
+    } else if (t == t_last && nl > 0) {
+      qa = nf + (a - (u1 - nl));
+      qb = nf + (b - (u1 - nl));
+    } else {
+      qa = a - u0 + nl;
+      qb = b - u0 + nl;
+    }
+  }
+};
 
 __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1)
     q4k_gemv_kernel(const __grid_constant__ CUtensorMap tmap, GemvArgs p) {
@@ -172,11 +194,8 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1)
   uint4 *xzero = reinterpret_cast<uint4 *>(smem + p.smem_x);
   uint4 *xperm = xzero + 4;  // after 64 zero bytes
   float *xsum = reinterpret_cast<float *>(xperm + p.nb * 32);
-  float *slots = xsum + p.nb * 8;                                  // [nslot][32]
-  int *tile_done = reinterpret_cast<int *>(slots + p.nslot * 32);  // [ntile]
-  // [warps][kRing] (tile, first block); 16-byte aligned: ntile is a multiple of 4
-  int2 *ring = reinterpret_cast<int2 *>(tile_done + p.ntile);
-  int *sched = reinterpret_cast<int *>(ring + nwarps * kRing);
+  float *parts = xsum + p.nb * 8;                                        // [warps][2][32]
+  int *tile_done = reinterpret_cast<int *>(parts + nwarps * 2 * kTileRows);  // [ntile]
 
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -196,63 +215,58 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1)
   }
   __syncwarp();
 
-  // this CTA's segments [sb0, sb1) and its boundary tiles
-  const int sb0 = seg_begin(c, p), sb1 = seg_begin(c + 1, p);
-  const int S = sb1 - sb0;
-  const int t_first = div_nbs(sb0, p), t_last = div_nbs(sb1 - 1, p);
-  const bool first_partial = (sb0 != t_first * p.nbs) || (sb1 < (t_first + 1) * p.nbs);
-  const int nf = first_partial ? min(sb1, (t_first + 1) * p.nbs) - sb0 : 0;
-  const int nl = (t_last != t_first && sb1 != (t_last + 1) * p.nbs) ? sb1 - t_last * p.nbs : 0;
-  // queue order: first boundary tile, last boundary tile, interior tiles
-  auto seg_of_queue = [&](int qi) -> int {
-    if (qi < nf) return sb0 + qi;
-    if (qi < nf + nl) return sb1 - nl + (qi - nf);
-    return sb0 + qi - nl;
-  };
+  // this CTA's units and their order
+  CtaOrder co;
+  co.u0 = unit_begin(c, p);
+  co.u1 = unit_begin(c + 1, p);
+  co.S = co.u1 - co.u0;
+  co.t_first = div_nb(co.u0, p);
+  co.t_last = div_nb(co.u1 - 1, p);
+  const bool first_shared = (co.u0 != co.t_first * p.nb) || (co.u1 < (co.t_first + 1) * p.nb);
+  co.nf = first_shared ? min(co.u1, (co.t_first + 1) * p.nb) - co.u0 : 0;
+  co.nl = (co.t_last != co.t_first && co.u1 != (co.t_last + 1) * p.nb)
+              ? co.u1 - co.t_last * p.nb
+              : 0;
+
+  // this warp's contiguous run [q0, q1) of the order; no warp is left empty
+  const int nwe = min(nwarps, co.S);
+  const bool has_work = warp < nwe;
+  auto qstart = [&](int w) { return (w * co.S) / nwe; };
+  auto warp_of_q = [&](int q) { return ((q + 1) * nwe - 1) / co.S; };
+  const int q0 = has_work ? qstart(warp) : 0, q1 = has_work ? qstart(warp + 1) : 0;
 
   const uint64_t pol = evict_first_policy();
 
-  // ---- producer state: segments are grabbed from the queue ----------------
-  // The first kGemvStages-1 grabs of warp w are static (w, w + warps, ...),
-  // so the prologue needs no shared counter; later grabs are dynamic.
-  int grabs = 0;
-  int ti = 0, bi = 0, iu = p.L;  // segment being issued (tile, first block), units issued
-  bool issue_done = false;
-  int ring_tail = 0;
+  // ---- producer: (tile, block) of the next unit to put in flight -----------
+  int qi = q0, ti = 0, bi = 0;
+  if (has_work) {
+    const int u = co.unit_of(q0);
+    ti = div_nb(u, p);
+    bi = u - ti * p.nb;
+  }
   int st_in = 0;
-  int pending = 0;  // units issued, not yet consumed
-
-  auto issue_next = [&]() {
-    if (issue_done) return;
-    if (iu == p.L) {
-      int qi;
-      if (grabs < kGemvStages - 1) {
-        qi = warp + grabs * nwarps;
-      } else {
-        if (lane == 0) qi = atomicAdd(sched, 1);
-        qi = __shfl_sync(0xffffffffu, qi, 0);
-      }
-      ++grabs;
-      if (qi >= S) {
-        issue_done = true;
-        return;
-      }
-      const int seg = seg_of_queue(qi);
-      ti = div_nbs(seg, p);
-      bi = (seg - ti * p.nbs) * p.L;
-      if (lane == 0) ring[warp * kRing + (ring_tail & (kRing - 1))] = make_int2(ti, bi);
-      ++ring_tail;
-      iu = 0;
+  // step (q, t, b) to the next position of the order
+  auto advance = [&](int &q, int &t, int &b) {
+    ++q;
+    if (q == co.nf || q == co.nf + co.nl) {  // crossing into the next group
+      const int u = co.unit_of(q);
+      t = div_nb(u, p);
+      b = u - t * p.nb;
+    } else if (++b == p.nb) {
+      b = 0;
+      ++t;
     }
+  };
+  auto issue_next = [&]() {
+    if (qi >= q1) return;
     if (lane == 0) {
       const uint32_t bar = my_bar + 8 * st_in;
       mbar_expect_tx(bar, kStageBytes);
-      tma_unit(my_stage_addr + st_in * kStageBytes, &tmap, (bi + iu) * kBlockBytes,
-               ti * kTileRows, bar, pol);
+      tma_unit(my_stage_addr + st_in * kStageBytes, &tmap, bi * kBlockBytes, ti * kTileRows, bar,
+               pol);
     }
     st_in = (st_in + 1 == kGemvStages) ? 0 : st_in + 1;
-    ++iu;
-    ++pending;
+    advance(qi, ti, bi);
   };
 
   // The first stages only read the weights, which no preceding kernel
@@ -273,7 +287,6 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1)
     constexpr int XB = 8;           // x loads in flight per thread
     if (threadIdx.x < 4) xzero[threadIdx.x] = make_uint4(0, 0, 0, 0);
     for (int i = threadIdx.x; i < p.ntile; i += blockDim.x) tile_done[i] = 0;
-    if (threadIdx.x == 0) *sched = (kGemvStages - 1) * nwarps;
     for (int base = threadIdx.x; base < ngroups; base += XB * blockDim.x) {
       uint4 xv[XB];
 #pragma unroll
@@ -305,6 +318,7 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1)
     }
   }
   __syncthreads();
+  if (!has_work) return;
 
   // B operands: thread (g, t) carries x for words 0..3 of its slice when
   // g == 2t, for words 4..7 when g == 2t + 1, zeros otherwise.
@@ -327,82 +341,116 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1)
   const uint32_t mB = upper ? 0x3030u : 0u;
   const uint32_t shm = upper ? 4u : 0u;
 
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};  // rows g, g+8, g+16, g+24 of the segment
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};  // rows g, g+8, g+16, g+24 of the current tile
 
-  // The warp that completes a boundary tile's part of this CTA publishes it;
-  // the last CTA to arrive adds the CTAs' parts in CTA order.
-  auto boundary_finish = [&](int t, float s) {
-    const int end = (t == t_first) ? 0 : 1;
+  // store a finished row sum (lane = row in tile)
+  auto store_row = [&](int t, float s) {
+    const int r = t * kTileRows + lane;
+    if (r < p.rows) p.y[r] = s + (p.residual ? p.residual[r] : 0.f);
+  };
+
+  // A tile shared with neighbouring CTAs: publish this CTA's part; the last
+  // CTA to arrive adds the CTAs' parts in CTA order.
+  auto cta_finish = [&](int t, float s) {
+    const bool inside = (t * p.nb >= co.u0) && ((t + 1) * p.nb <= co.u1);
+    if (inside) {
+      store_row(t, s);
+      return;
+    }
+    const int end = (t == co.t_first) ? 0 : 1;
     __stcg(p.partials + ((size_t)c * 2 + end) * kTileRows + lane, s);
     __threadfence();
     __syncwarp();
     int old = 0;
     if (lane == 0) old = atomicAdd(p.counters + t, 1);
     old = __shfl_sync(0xffffffffu, old, 0);
-    const int cf = cta_of_seg(t * p.nbs, p), cl = cta_of_seg((t + 1) * p.nbs - 1, p);
+    const int cf = cta_of_unit(t * p.nb, p), cl = cta_of_unit((t + 1) * p.nb - 1, p);
     if (old == cl - cf) {
       __threadfence();
-      const int slot_cf = (seg_begin(cf, p) == t * p.nbs) ? 0 : 1;
+      const int slot_cf = (unit_begin(cf, p) == t * p.nb) ? 0 : 1;
       float tot = __ldcg(p.partials + ((size_t)cf * 2 + slot_cf) * kTileRows + lane);
       for (int cc = cf + 1; cc <= cl; ++cc)
         tot += __ldcg(p.partials + ((size_t)cc * 2) * kTileRows + lane);
-      const int r = t * kTileRows + lane;
-      if (r < p.rows) p.y[r] = tot + (p.residual ? p.residual[r] : 0.f);
+      store_row(t, tot);
       if (lane == 0) p.counters[t] = 0;
     }
   };
 
-  auto finish_segment = [&](int t, int b0) {
+  // The warp's run of tile t ended at position q_end (exclusive) after
+  // starting at q_beg: combine with the other warps' runs of the tile.
+  int my_first_tile;
+  {
+    const int u = co.unit_of(q0);
+    my_first_tile = div_nb(u, p);
+  }
+  auto finish_run = [&](int t, int q_beg, int q_end) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], 1);
       acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], 2);
     }
-    const int k = t * p.nbs + b0 / p.L - sb0;
-    if (tig == 0) {
+    int qa, qb;
+    co.tile_range(t, p.nb, qa, qb);
+    if (q_beg == qa && q_end == qb) {  // this warp holds the CTA's whole part
+      // lane r needs row r: rows g + 8i live in lane 4g (tig 0), slot i
+      float s = 0.f;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) slots[k * kTileRows + g + 8 * i] = acc[i];
+      for (int i = 0; i < 4; ++i) {
+        const float v = __shfl_sync(0xffffffffu, acc[i], (lane & 7) << 2);
+        if ((lane >> 3) == i) s = v;
+      }
+      cta_finish(t, s);
+    } else {
+      const int slot = (t == my_first_tile) ? 0 : 1;
+      float *pp = parts + (warp * 2 + slot) * kTileRows;
+      if (tig == 0) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) pp[g + 8 * i] = acc[i];
+      }
+      __syncwarp();
+      const int wa = warp_of_q(qa), wb = warp_of_q(qb - 1);
+      int old = 0;
+      if (lane == 0) {
+        __threadfence_block();
+        old = atomicAdd(tile_done + (t - co.t_first), 1);
+      }
+      old = __shfl_sync(0xffffffffu, old, 0);
+      if (old == wb - wa) {  // the last of the tile's warps
+        __threadfence_block();
+        const volatile float *vp = parts;
+        const int slot_wa = (qstart(wa) == qa) ? 0 : 1;
+        float s = vp[(wa * 2 + slot_wa) * kTileRows + lane];
+        for (int w = wa + 1; w <= wb; ++w) s += vp[(w * 2) * kTileRows + lane];
+        cta_finish(t, s);
+      }
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[i] = 0.f;
-    __syncwarp();
-    const int ks = max(sb0, t * p.nbs) - sb0;
-    const int ke = min(sb1, (t + 1) * p.nbs) - sb0;
-    int old = 0;
-    if (lane == 0) {
-      __threadfence_block();
-      old = atomicAdd(tile_done + (t - t_first), 1);
-    }
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old == ke - ks - 1) {  // this warp completed the tile's part
-      __threadfence_block();
-      const volatile float *vs = slots;
-      float s = 0.f;
-      for (int k2 = ks; k2 < ke; ++k2) s += vs[k2 * kTileRows + lane];
-      if (ks + sb0 == t * p.nbs && ke + sb0 == (t + 1) * p.nbs) {
-        const int r = t * kTileRows + lane;
-        if (r < p.rows) p.y[r] = s + (p.residual ? p.residual[r] : 0.f);
-      } else {
-        boundary_finish(t, s);
-      }
-    }
   };
 
   // ---- main loop: one unit per iteration ------------------------------------
-  int ring_head = 0, cu = 0, st_out = 0;
+  int qc = q0, tc = 0, bc = 0;  // consumer cursor
+  {
+    const int u = co.unit_of(q0);
+    tc = div_nb(u, p);
+    bc = u - tc * p.nb;
+  }
+  int run_beg = q0;
+  int st_out = 0;
   uint32_t phases = 0;  // bit s: parity of the next completion of stage s
-  while (pending > 0) {
+  bool ok = true;
+  while (qc < q1) {
     issue_next();
-    if (!mbar_wait_bounded(my_bar + 8 * st_out, (phases >> st_out) & 1, p.status)) break;
+    if (!mbar_wait_bounded(my_bar + 8 * st_out, (phases >> st_out) & 1, p.status)) {
+      ok = false;
+      break;
+    }
     phases ^= 1u << st_out;
 
-    const int2 tb = ring[warp * kRing + (ring_head & (kRing - 1))];
-    const int t = tb.x;
-    const int b = tb.y + cu;
     const uint8_t *st = my_stages + st_out * kStageBytes;
-    const uint32_t xlo = x_lo_base + b * x_lo_step;
-    const uint32_t xhi = x_hi_base + b * x_hi_step;
-    const float2 xs = *reinterpret_cast<const float2 *>(xsum + b * 8 + 2 * tig);
+    const uint32_t xlo = x_lo_base + bc * x_lo_step;
+    const uint32_t xhi = x_hi_base + bc * x_hi_step;
+    const float2 xs = *reinterpret_cast<const float2 *>(xsum + bc * 8 + 2 * tig);
 
     // quants and headers of rows g, g+8, g+16, g+24
     uint32_t q[4][8];
@@ -460,17 +508,18 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1)
     }
     __syncwarp();  // stage fully read before it is refilled
     st_out = (st_out + 1 == kGemvStages) ? 0 : st_out + 1;
-    --pending;
-    if (++cu == p.L) {
-      finish_segment(t, tb.y);
-      ++ring_head;
-      cu = 0;
+
+    const int t_now = tc;
+    advance(qc, tc, bc);
+    if (qc == q1 || tc != t_now || qc == co.nf || qc == co.nf + co.nl) {
+      finish_run(t_now, run_beg, qc);
+      run_beg = qc;
     }
   }
-  if (pending > 0) {
+  if (!ok) {
     // a stage wait ran out of budget: let the copies still in flight land
     // (bounded again) before this warp's shared memory is released
-    for (int s = 0; s < kGemvStages && pending > 0; ++s, --pending) {
+    for (int s = 0; s < kGemvStages; ++s) {
       if (!mbar_wait_bounded(my_bar + 8 * st_out, (phases >> st_out) & 1, p.status)) break;
       phases ^= 1u << st_out;
       st_out = (st_out + 1 == kGemvStages) ? 0 : st_out + 1;
@@ -489,35 +538,27 @@ int gemv_init(mlm_ctx *ctx) {
 int gemv_max_ctas(int sm_count) { return sm_count; }
 
 struct GemvPlan {
-  int warps, L, nbs, nsegs, ctas, nslot, ntile;
+  int warps, units, ctas, ntile;
   size_t smem;
   uint32_t smem_bar, smem_x;
 };
 
-// Smallest segment length (a divisor of the blocks per row) and the most
-// warps whose shared-memory footprint fits.
+// The most warps whose shared-memory footprint fits.
 static bool plan_gemv(int rows, int nb, int sm_count, size_t smem_max, GemvPlan &pl) {
   const int tiles = (rows + kTileRows - 1) / kTileRows;
-  for (int warps = kGemvMaxWarps; warps >= 4; --warps) {
-    for (int L = 1; L <= nb; ++L) {
-      if (nb % L) continue;
-      const int nbs = nb / L;
-      const long long nsegs = (long long)tiles * nbs;
-      const int ctas = (int)std::min<long long>(sm_count, nsegs);
-      if (nsegs * ctas >= (1LL << 31) || nsegs >= (1LL << 20)) continue;
-      const int segmax = (int)((nsegs + ctas - 1) / ctas);
-      // tile counters rounded to 16 bytes so the int2 ring after them is aligned
-      const int ntile = ((segmax / nbs + 2) + 3) & ~3;
-      const size_t smem_bar = (size_t)warps * kGemvStages * kStageBytes;
-      const size_t smem_x = smem_bar + (((size_t)warps * kGemvStages * 8 + 15) & ~(size_t)15);
-      const size_t smem = smem_x + 64 + (size_t)nb * 32 * 16 + (size_t)nb * 8 * 4 +
-                          (size_t)segmax * kTileRows * 4 + (size_t)ntile * 4 +
-                          (size_t)warps * kRing * sizeof(int2) + 16;
-      if (smem <= smem_max && segmax <= 4096) {
-        pl = {warps, L, nbs, (int)nsegs, ctas, segmax, ntile, smem, (uint32_t)smem_bar,
-              (uint32_t)smem_x};
-        return true;
-      }
+  const long long units = (long long)tiles * nb;
+  const int ctas = (int)std::min<long long>(sm_count, units);
+  if (units * ctas >= (1LL << 31) || units >= (1LL << 24)) return false;
+  const int umax = (int)((units + ctas - 1) / ctas);
+  const int ntile = ((umax / nb + 2) + 3) & ~3;
+  for (int warps = kGemvMaxWarps; warps >= 2; --warps) {
+    const size_t smem_bar = (size_t)warps * kGemvStages * kStageBytes;
+    const size_t smem_x = smem_bar + (((size_t)warps * kGemvStages * 8 + 15) & ~(size_t)15);
+    const size_t smem = smem_x + 64 + (size_t)nb * 32 * 16 + (size_t)nb * 8 * 4 +
+                        (size_t)warps * 2 * kTileRows * 4 + (size_t)ntile * 4;
+    if (smem <= smem_max) {
+      pl = {warps, (int)units, ctas, ntile, smem, (uint32_t)smem_bar, (uint32_t)smem_x};
+      return true;
     }
   }
   return false;
@@ -577,15 +618,11 @@ int gemv_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x, 
   a.partials = partials;
   a.counters = counters;
   a.status = ctx->dev_status;
-  a.nbs_magic = ((1ull << 40) + (unsigned long long)pl.nbs - 1) / (unsigned long long)pl.nbs;
+  a.nb_magic = ((1ull << 40) + (unsigned long long)nb - 1) / (unsigned long long)nb;
   a.rows = rows;
   a.nb = nb;
-  a.L = pl.L;
-  a.nbs = pl.nbs;
-  a.tiles = tiles;
-  a.nsegs = pl.nsegs;
+  a.units = pl.units;
   a.ctas = pl.ctas;
-  a.nslot = pl.nslot;
   a.ntile = pl.ntile;
   a.smem_bar = pl.smem_bar;
   a.smem_x = pl.smem_x;

@@ -70,9 +70,17 @@ def measured_peaks() -> dict:
             "source": "fallback"}
 
 
+# committed ncu summary of each workload's dominant kernel (named kernel + shape)
+PROFILES = {
+    "gemv_up": "q4k_gemv_14336x4096.md",
+    "gemv_down": "q4k_gemv_4096x14336.md",
+    "dequant": "q4k_dequant_f32_4096x4096.md",
+}
+
+
 def ncu_traffic(workload: str):
     """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
-    p = os.path.join(ROOT, "profiles", f"{workload}_ncu.md")
+    p = os.path.join(ROOT, "profiles", PROFILES[workload])
     if not os.path.exists(p):
         return None
     for line in open(p):

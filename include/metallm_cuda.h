@@ -146,6 +146,18 @@ int mlm_dequantize_q4k_to_f16(mlm_ctx *ctx, const void *blocks, uint64_t n, void
 int mlm_q4k_gemv(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_f16,
                  float *y, const float *residual);
 
+/* No counterpart in the reference.  mlm_q4k_gemv with its split-K scratch
+ * in a static 80 KB device array inside the library instead of the
+ * context's allocation: the call allocates nothing, for hosts that own all
+ * device memory through their own pool or enqueue from places where an
+ * allocation may not happen.  rows <= 131072 (MLM_ERR_SHAPE beyond).  The
+ * first call on a device looks up and clears the array (make it before any
+ * stream capture); later calls clear only the arrival counters, on the
+ * context stream.  All calls on a device share the array: calls that overlap
+ * on the GPU race -- keep them on one stream. */
+int mlm_q4k_gemv_static(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_f16,
+                        float *y, const float *residual);
+
 /* ---------------------------------------------------------------------------
  * Normalisation, RoPE, activations
  * ------------------------------------------------------------------------ */

@@ -72,6 +72,7 @@ SIGNATURES = [
     ("mlm_dequantize_q4k_to_f32", c_int, [c_vp, c_vp, c_u64, ctypes.POINTER(c_vp)]),
     ("mlm_dequantize_q4k_to_f16", c_int, [c_vp, c_vp, c_u64, ctypes.POINTER(c_vp)]),
     ("mlm_q4k_gemv", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_vp]),
+    ("mlm_q4k_gemv_static", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_vp]),
     ("mlm_rmsnorm_f16", c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_float]),
     ("mlm_rmsnorm_f32", c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_float]),
     ("mlm_rope_f16", c_int, [c_vp, c_vp, c_vp, ctypes.POINTER(RopeArgs), c_int, c_int, c_int]),

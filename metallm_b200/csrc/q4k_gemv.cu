@@ -667,3 +667,88 @@ extern "C" int mlm_q4k_gemv(mlm_ctx *ctx, const void *W, int rows, int cols, con
   return gemv_launch(ctx, W, rows, cols, x_f16, y, residual, ctx->gemv_partials,
                      ctx->gemv_counters, ctx->gemv_max_ctas, ctx->gemv_max_tiles, ctx->stream);
 }
+
+// ---------------------------------------------------------------------------
+// mlm_q4k_gemv_static: the same kernel with its split-K scratch in a
+// file-scope device array instead of the context's allocation.
+//
+// Who needs it: a host that owns every byte of device memory through its own
+// pool (or runs under a hard memory budget) and may not let a library
+// allocate, and code that enqueues work from a place where an allocation
+// would stall or is not allowed (a latency-critical decode loop; a region
+// that is being recorded into a graph).  This entry point allocates nothing:
+// no cudaMalloc, no cudaFree, no allocating library routine.
+//
+// Limits: at most kStaticMaxRows rows and kStaticMaxCtas CTAs (the grid is
+// capped there); larger shapes are rejected with MLM_ERR_SHAPE.  The array is
+// 80 KB per device and lives in the library image, loaded with the module.
+//
+// Set-up: the first call on a device looks up the array's device address
+// with cudaGetSymbolAddress (that device current) and clears it; calls after
+// that only read the cached address.  Make that first call before any stream
+// capture begins.
+//
+// Sharing: every call on a device uses the same array, which keeps the last
+// call's contents.  The arrival counters are cleared on the caller's stream
+// before every launch (the partials need no clearing: each is written before
+// it is read).  Calls that overlap on the GPU -- two streams, two contexts on
+// one device, two host threads -- race on the array and give wrong results;
+// order them on one stream.
+// ---------------------------------------------------------------------------
+
+namespace mlm {
+
+constexpr int kStaticMaxRows = 131072;                        // 4096 row tiles
+constexpr int kStaticMaxTiles = kStaticMaxRows / kTileRows;
+constexpr int kStaticMaxCtas = 256;
+constexpr size_t kStaticPartialBytes = (size_t)kStaticMaxCtas * 2 * kTileRows * sizeof(float);
+constexpr size_t kStaticScratchBytes = kStaticPartialBytes + (size_t)kStaticMaxTiles * sizeof(int);
+constexpr int kStaticMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_gemv_static_scratch[kStaticScratchBytes];
+
+static std::mutex g_static_mu;
+static void *g_static_addr[kStaticMaxDevices];  // set once per device, under g_static_mu
+
+static int gemv_static_scratch(mlm_ctx *ctx, void **out) {
+  int cur = -1;
+  MLM_CUDA_TRY(ctx, cudaGetDevice(&cur));
+  MLM_REQUIRE(ctx, cur == ctx->device, MLM_ERR_STATE,
+              "mlm_q4k_gemv_static: device %d is current, the context is on device %d", cur,
+              ctx->device);
+  MLM_REQUIRE(ctx, cur >= 0 && cur < kStaticMaxDevices, MLM_ERR_UNSUPPORTED,
+              "mlm_q4k_gemv_static: device %d beyond the %d-device table", cur,
+              kStaticMaxDevices);
+  std::lock_guard<std::mutex> g(g_static_mu);
+  if (!g_static_addr[cur]) {
+    void *p = nullptr;
+    MLM_CUDA_TRY(ctx, cudaGetSymbolAddress(&p, g_gemv_static_scratch));
+    MLM_REQUIRE(ctx, p != nullptr, MLM_ERR_CUDA, "mlm_q4k_gemv_static: null scratch address");
+    MLM_CUDA_TRY(ctx, cudaMemset(p, 0, kStaticScratchBytes));
+    g_static_addr[cur] = p;
+  }
+  *out = g_static_addr[cur];
+  return MLM_OK;
+}
+
+}  // namespace mlm
+
+extern "C" int mlm_q4k_gemv_static(mlm_ctx *ctx, const void *W, int rows, int cols,
+                                   const void *x_f16, float *y, const float *residual) {
+  MLM_CHECK_CTX(ctx);
+  int st = mlm::gemv_validate(ctx, W, rows, cols, x_f16, y);
+  if (st != MLM_OK) return st;
+  MLM_REQUIRE(ctx, rows <= mlm::kStaticMaxRows, MLM_ERR_SHAPE,
+              "mlm_q4k_gemv_static: rows=%d exceeds the static scratch limit of %d rows", rows,
+              mlm::kStaticMaxRows);
+  void *scratch = nullptr;
+  st = mlm::gemv_static_scratch(ctx, &scratch);
+  if (st != MLM_OK) return st;
+  float *partials = reinterpret_cast<float *>(scratch);
+  int *counters =
+      reinterpret_cast<int *>(reinterpret_cast<unsigned char *>(scratch) + mlm::kStaticPartialBytes);
+  const int tiles = (rows + mlm::kTileRows - 1) / mlm::kTileRows;
+  MLM_CUDA_TRY(ctx, cudaMemsetAsync(counters, 0, sizeof(int) * (size_t)tiles, ctx->stream));
+  return mlm::gemv_launch(ctx, W, rows, cols, x_f16, y, residual, partials, counters,
+                          mlm::kStaticMaxCtas, mlm::kStaticMaxTiles, ctx->stream);
+}

@@ -49,6 +49,27 @@ WORKLOADS = {
 }
 
 
+# decoder workloads on the Llama-3-8B shape (hidden 4096, 32/8 heads of 128,
+# FFN 14336, vocab 128256, RoPE theta 500000)
+LLAMA_WORKLOADS = {
+    "layer": "one Llama-3-8B-shape decoder layer, single-token decode at position 2047 over a "
+             "2047-token fp16 cache (BASELINE config 2)",
+    "decode": "Llama-3-8B-shape Q4_K model, batch 1: 512 prompt tokens then greedy decode "
+              "(BASELINE config 3)",
+}
+
+
+def llama_token_bytes(n_layers: int, pos: int, with_head: bool = True) -> int:
+    """Algorithmic HBM bytes of one decode step at position pos (weights read
+    once, the KV cache read up to pos, K/V written, the embedding row)."""
+    d, kvd, ffn, vocab = 4096, 1024, 14336, 128256
+    rb = d // 256 * 144
+    layer = (d + 2 * kvd) * rb + d * rb + 2 * ffn * rb + d * (ffn // 256 * 144)
+    kv = 2 * (pos + 1) * kvd * 2
+    head = vocab * rb if with_head else 0
+    return n_layers * (layer + kv) + head + 2 * d
+
+
 def gemv_bytes(rows: int, cols: int) -> int:
     return rows * (cols // 256) * 144 + 2 * cols + 4 * rows
 
@@ -309,8 +330,7 @@ def run_gpu(args, world, rank, local, pg) -> dict:
     hy = ctypes.c_void_p()
     lib.mlm_host_alloc(h, 2 * cols, ctypes.byref(hx))
     lib.mlm_host_alloc(h, 4 * out_elems, ctypes.byref(hy))
-    from oracle import oracle as O  # host input only (the x the caller owns)
-    xin = O.gen_f16(7, 2, cols)
+    xin = x.download(np.float16, cols)  # the caller's host copy of x
     ctypes.memmove(hx, xin.ctypes.data, xin.nbytes)
     h2d = 2 * cols if is_gemv else 0
     d2h = 4 * out_elems
@@ -383,9 +403,210 @@ def run_gpu(args, world, rank, local, pg) -> dict:
     return line
 
 
+def cpu_decode_rate(budget_s: float, threads: int) -> dict:
+    """The reference's Q4_K kernels compiled for the host (oracle/_ref) on one
+    decoder layer's seven linears plus the output head, at all host threads;
+    tokens/s = 1 / (32 x layer + head).  Norms, RoPE and attention (under 1 %
+    of the bytes) are left out of the sample."""
+    from oracle import oracle as O
+    shapes = [(6144, 4096), (4096, 4096), (28672, 4096), (4096, 14336)]
+    Ws = [O.gen_q4k(3, i, r * c // 256) for i, (r, c) in enumerate(shapes)]
+    head = O.gen_q4k(3, 9, 128256 * 4096 // 256)
+    xs = {c: O.gen_f16(3, 20 + c, c) for c in (4096, 14336)}
+    mv = (lambda W, r, c: O.ref_q4k_matvec(W, r, c, xs[c], threads)) if O.ref_lib() is not None \
+        else (lambda W, r, c: O.q4k_matvec(W, r, c, xs[c], acc64=False, nthreads=threads))
+    reps, t_layer, t_head = 0, 0.0, 0.0
+    t0 = time.perf_counter()
+    while reps == 0 or time.perf_counter() - t0 < budget_s:
+        a = time.perf_counter()
+        for W, (r, c) in zip(Ws, shapes):
+            mv(W, r, c)
+        b = time.perf_counter()
+        mv(head, 128256, 4096)
+        t_layer += b - a
+        t_head += time.perf_counter() - b
+        reps += 1
+    per_token = 32 * t_layer / reps + t_head / reps
+    return {"value": round(1.0 / per_token, 4), "unit": "tokens/s", "cores": threads,
+            "kind": "reference" if O.ref_lib() is not None else "port",
+            "sample": f"{reps} x (one layer's 7 Q4_K matvecs + the 128256x4096 head) in "
+                      f"{time.perf_counter() - t0:.1f} s, {threads} threads; tokens/s = "
+                      f"1 / (32 x layer + head)"}
+
+
+def run_llama(args, world, rank, local, pg) -> dict:
+    """BASELINE configs 2 (one layer) and 3 (the model: prefill, greedy decode)."""
+    import torch
+
+    from metallm_b200 import Context, Llama
+    from metallm_b200.synthetic import fill_llama, llama_config
+    ctx = Context(local)
+    torch.cuda.set_device(local)
+    tstream = torch.cuda.ExternalStream(ctx.stream(), device=f"cuda:{local}")
+    peaks = measured_peaks()
+
+    def timed(fn):
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        ev0.record(tstream)
+        fn()
+        ev1.record(tstream)
+        ev1.synchronize()
+        return ev0.elapsed_time(ev1)
+
+    extra = {}
+    if args.workload == "layer":
+        cfg = llama_config(n_layers=1, vocab=256, max_seq=2048)
+        m = Llama(ctx, cfg)
+        pos = 2047
+        fill_llama(m, 1, cache_positions=pos)
+        hidden = ctx.alloc(4 * cfg.dim)
+        ctx.gen_f32(1, 7, cfg.dim, hidden)
+        m.set_position(pos)
+        ctx.graph_begin()
+        for _ in range(args.steps):
+            m.forward_layer(0, hidden)
+        graph = ctx.graph_end()
+        for _ in range(args.warmup):
+            m.forward_layer(0, hidden)
+        ctx.wait()
+        barrier(pg, local)
+        sampler = ClockSampler(local)
+        sampler.start()
+        time.sleep(0.3)
+        dev_ms = timed(graph.launch)
+        clocks = sampler.stop()
+        graph.destroy()
+        ms_max = max_over_ranks(dev_ms, pg, local)
+        per_step_ms = ms_max / args.steps
+        alg = llama_token_bytes(1, pos, with_head=False) - 2 * 4096
+        value = alg * args.steps * world / (ms_max * 1e-3) / 1e9
+        unit, metric_value_desc = "GB/s", "one decoder layer per step"
+        launches = args.steps * 11
+        # e2e: hidden state in from pinned host memory, the layer, out again
+        lib, h = ctx.lib, ctx.handle
+        hbuf = ctypes.c_void_p()
+        lib.mlm_host_alloc(h, 4 * cfg.dim, ctypes.byref(hbuf))
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            ctx._check(lib.mlm_upload_async(h, ctypes.c_void_p(hidden.ptr), hbuf, 4 * cfg.dim), "up")
+            m.forward_layer(0, hidden)
+            ctx._check(lib.mlm_download_async(h, hbuf, ctypes.c_void_p(hidden.ptr), 4 * cfg.dim), "dn")
+            ctx.wait()
+        e2e_s = max_over_ranks(time.perf_counter() - t0, pg, local)
+        lib.mlm_host_free(h, hbuf)
+        e2e = {"value": round(alg * args.steps * world / e2e_s / 1e9, 2), "unit": "GB/s",
+               "h2d_bytes_per_step": 4 * cfg.dim, "d2h_bytes_per_step": 4 * cfg.dim}
+        config = {"workload": LLAMA_WORKLOADS["layer"], "hidden": 4096, "heads": "32/8 x 128",
+                  "ffn": 14336, "position": pos, "parallelism": "single GPU",
+                  "l2": "inputs larger than L2: 122.7 MB of Q4_K weights + 8.4 MB of KV per layer",
+                  "algorithmic_bytes_per_step": alg}
+        cpu = None
+    else:
+        prompt_len, gen_len = 512, 256
+        steps = min(args.steps, gen_len - args.warmup)
+        cfg = llama_config(n_layers=32, vocab=128256, max_seq=prompt_len + gen_len)
+        m = Llama(ctx, cfg)
+        fill_llama(m, 1)
+        prompt = np.random.default_rng(512).integers(0, 128000, size=prompt_len).tolist()
+        nxt = ctx.alloc(16)
+        ctx.wait()
+        barrier(pg, local)
+        prefill_ms = max_over_ranks(timed(lambda: m.prefill(prompt, nxt)), pg, local)
+        first = int(nxt.download(np.int32)[0])
+        out = ctx.alloc(4 * gen_len)
+        m.decode_greedy(first, args.warmup, out)  # captures the step graph
+        last = int(out.download(np.int32, args.warmup)[-1])
+        ctx.wait()
+        barrier(pg, local)
+        sampler = ClockSampler(local)
+        sampler.start()
+        time.sleep(0.3)
+        pos0 = m.position
+        dev_ms = timed(lambda: m.decode_greedy(last, steps, out))
+        clocks = sampler.stop()
+        toks = out.download(np.int32, steps)
+        ms_max = max_over_ranks(dev_ms, pg, local)
+        per_step_ms = ms_max / steps
+        value = steps * world / (ms_max * 1e-3)
+        unit = "tokens/s"
+        alg = llama_token_bytes(32, pos0 + steps // 2)
+        launches = steps * (32 * 10 + 5)
+        # e2e: forward(tokenID:) per token through the C ABI, the argmax read back
+        m.set_position(prompt_len)
+        lib, h = ctx.lib, ctx.handle
+        htok = ctypes.c_void_p()
+        lib.mlm_host_alloc(h, 16, ctypes.byref(htok))
+        tok_dev = ctx.alloc(16)
+        logits = ctx.alloc(4 * cfg.vocab)
+        tok = first
+        e2e_steps = min(steps, 32)
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            m.forward(tok, logits)
+            ctx.call("mlm_argmax_f32", logits, cfg.vocab, tok_dev)
+            ctx._check(lib.mlm_download_async(h, htok, ctypes.c_void_p(tok_dev.ptr), 4), "dn")
+            ctx.wait()
+            tok = ctypes.c_int32.from_address(htok.value).value
+        e2e_s = max_over_ranks(time.perf_counter() - t0, pg, local)
+        lib.mlm_host_free(h, htok)
+        e2e = {"value": round(e2e_steps * world / e2e_s, 2), "unit": "tokens/s",
+               "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 4}
+        config = {"workload": LLAMA_WORKLOADS["decode"], "layers": 32, "hidden": 4096,
+                  "heads": "32/8 x 128", "ffn": 14336, "vocab": 128256, "batch": 1,
+                  "prompt_tokens": prompt_len, "decode_steps_timed": steps,
+                  "parallelism": "single GPU",
+                  "l2": "inputs larger than L2: 4.2 GB of Q4_K weights per token",
+                  "algorithmic_bytes_per_step": alg}
+        extra = {"prefill": {"value": round(prompt_len / (prefill_ms * 1e-3), 2),
+                             "unit": "tokens/s",
+                             "path": "prompt run as sequential decode steps (no tensor-core "
+                                     "prefill GEMM yet)"},
+                 "first_tokens": [int(t) for t in toks[:8]]}
+        cpu = "decode"
+    kernel_gbs = alg / (per_step_ms * 1e-3) / 1e9
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": unit, "n_gpus": world,
+        "steps": steps if args.workload == "decode" else args.steps, "warmup": args.warmup,
+        "ms_per_step": round(per_step_ms, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "q4k x f16 -> f32 (fp16 KV cache)",
+        "data": "synthetic (seeded Q4_K weights, fp16 embedding, fp32 norms generated on "
+                "device, as BASELINE configs 2/3)",
+        "config": config, "e2e": e2e, "gpu_launches": launches,
+        "launch": "CUDA graph (one decode step captured, replayed per token)",
+        "roofline": {"bound": "hbm", "achieved": round(kernel_gbs, 1), "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": round(kernel_gbs / peaks["hbm_gbs"], 4),
+                     "peak_source": peaks["source"], "traffic": None},
+        "clocks": clocks,
+    }
+    line.update(extra)
+    if rank == 0 and world == 1 and not args.no_cpu and cpu == "decode":
+        line["cpu_baseline"] = cpu_decode_rate(args.cpu_seconds, host_threads())
+    ctx.close()
+    return line
+
+
 def run_reference(args, world, rank) -> dict | None:
     if rank != 0:
         return None
+    if args.workload in LLAMA_WORKLOADS:
+        th = host_threads()
+        r = cpu_decode_rate(args.cpu_seconds, th)
+        if args.workload == "decode":
+            v, unit, alg = r["value"], "tokens/s", llama_token_bytes(32, 640)
+            ms = 1e3 / v
+        else:  # one layer: its bytes over a 32nd of the token time without the head
+            alg = llama_token_bytes(1, 2047, with_head=False) - 2 * 4096
+            ms = 1e3 / r["value"] / 33.0
+            v, unit = round(alg / (ms * 1e-3) / 1e9, 3), "GB/s"
+        return {"impl": "reference", "metric": METRIC, "value": v, "unit": unit, "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "q4k x f16 -> f32", "data": "synthetic (seeded Q4_K blocks)",
+                "config": {"workload": LLAMA_WORKLOADS[args.workload]},
+                "cpu_baseline": dict(r, value=v, unit=unit),
+                "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
     rows, cols, desc = WORKLOADS[args.workload]
     is_gemv = args.workload.startswith("gemv")
     th = host_threads()
@@ -422,7 +643,8 @@ def main() -> None:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--workload", default="gemv_up", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="gemv_up",
+                    choices=sorted(WORKLOADS) + sorted(LLAMA_WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--copies", type=int, default=6, help="rotating weight copies (> L2)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -440,7 +662,8 @@ def main() -> None:
 
     world, rank, local, pg = dist_setup(args)
     try:
-        line = run_gpu(args, world, rank, local, pg)
+        line = (run_llama if args.workload in LLAMA_WORKLOADS else run_gpu)(
+            args, world, rank, local, pg)
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:

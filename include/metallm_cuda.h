@@ -146,6 +146,12 @@ int mlm_dequantize_q4k_to_f16(mlm_ctx *ctx, const void *blocks, uint64_t n, void
 int mlm_q4k_gemv(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_f16,
                  float *y, const float *residual);
 
+/* mlm_q4k_gemv on an x given as fp16 values times one fp32 scale per 32
+ * elements (x[k] = x_f16[k] * x_scale[k/32]), as mlm_silu_mul_scaled writes
+ * it: the down projection of the decode FFN (LlamaRunner.swift:1059-1068). */
+int mlm_q4k_gemv_xs(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_f16,
+                    const float *x_scale, float *y, const float *residual);
+
 /* Tiled Q4_K layout: the same 144-byte blocks, reordered once after upload
  * so that the decode GEMV streams them as contiguous 4608-byte units (32
  * rows of one block column, laid out in the GEMV's register order; rows past
@@ -223,6 +229,13 @@ int mlm_rope_qk_kv_append(mlm_ctx *ctx, const float *q, const float *k, const fl
  * ElementwiseKernels.metal; LlamaRunner.swift:1036-1057):
  * out_f16[i] = half(silu(gate[i]) * up[i]) from fp32 gate/up */
 int mlm_silu_mul(mlm_ctx *ctx, const float *gate, const float *up, void *out_f16, int n);
+/* No counterpart in the reference (its SiLU and multiply store fp16, which
+ * overflows on large activations): the same product stored as fp16 with one
+ * power-of-two scale per 32 elements, out_f16[i] * scale[i/32] being the fp16
+ * rounding of the product scaled to below 2^15 (a power-of-two scale is
+ * exact).  n % 32 == 0; feeds mlm_q4k_gemv_xs. */
+int mlm_silu_mul_scaled(mlm_ctx *ctx, const float *gate, const float *up, void *out_f16,
+                        float *scale, int n);
 /* kernel_add_f16 (residual adds, LlamaRunner.swift:969-980, 1074-1085), fp32 */
 int mlm_add_f32(mlm_ctx *ctx, const float *a, const float *b, float *out, int n);
 
@@ -250,6 +263,84 @@ int mlm_embed_f16(mlm_ctx *ctx, const void *table_f16, int vocab, int dim,
                   const int32_t *token_dev, float *out);
 /* index of the largest logit (first on ties), written to *out_index (device) */
 int mlm_argmax_f32(mlm_ctx *ctx, const float *logits, int n, int32_t *out_index_dev);
+
+/* ---------------------------------------------------------------------------
+ * Llama decode runner: class LlamaRunner (LlamaRunner.swift:22-1210)
+ * ------------------------------------------------------------------------ */
+
+/* LlamaConfig (the fields LlamaRunner.swift:38-48 and forward() read) */
+typedef struct mlm_llama_config {
+  int32_t n_layers;
+  int32_t dim;        /* embeddingDim */
+  int32_t n_heads;
+  int32_t n_kv_heads; /* numKeyValueHeads */
+  int32_t head_dim;   /* 128 */
+  int32_t ffn_dim;    /* hiddenDim */
+  int32_t vocab;
+  int32_t max_seq;    /* sequenceLength: KV-cache capacity, <= 8192 */
+  float rms_eps;
+  mlm_rope_args rope; /* freq_base (theta), YaRN parameters, n_dims */
+} mlm_llama_config;
+
+/* Device pointers of one layer's tensors inside the runner's buffers; a
+ * loader uploads the GGUF tensors straight into them (LlamaModel's blocks,
+ * ModelLoader.swift:104-219).  Q4_K tensors in GGUF layout [rows][cols/256]
+ * (wq/wk/wv rows are contiguous, as are w_gate/w_up).  k_cache / v_cache are
+ * this layer's fp16 [max_seq][n_kv_heads][head_dim] caches. */
+typedef struct mlm_llama_layer {
+  float *attn_norm; /* fp32 [dim] */
+  void *wq, *wk, *wv, *wo;
+  float *ffn_norm; /* fp32 [dim] */
+  void *w_gate, *w_up, *w_down;
+  void *k_cache, *v_cache;
+} mlm_llama_layer;
+
+typedef struct mlm_llama_globals {
+  void *tok_embd;     /* fp16 [vocab][dim] */
+  float *output_norm; /* fp32 [dim] */
+  void *output;       /* Q4_K [vocab][dim/256] */
+  float *rope_freqs;  /* fp32 [head_dim/2], read when rope.has_freq_factors */
+} mlm_llama_globals;
+
+typedef struct mlm_llama mlm_llama;
+
+/* LlamaRunner.init: allocates the weights, the KV caches (2 x n_layers x
+ * max_seq x n_kv_heads x head_dim fp16) and the activations of one decode
+ * step on ctx's device.  The runner enqueues on ctx's stream. */
+int mlm_llama_create(mlm_ctx *ctx, const mlm_llama_config *cfg, mlm_llama **out);
+void mlm_llama_destroy(mlm_llama *m);
+int mlm_llama_layer_tensors(mlm_llama *m, int layer, mlm_llama_layer *out);
+int mlm_llama_global_tensors(mlm_llama *m, mlm_llama_globals *out);
+
+/* LlamaRunner.resetState / currentPosition.  mlm_llama_set_position lets a
+ * caller that filled the caches itself continue at `pos`. */
+int mlm_llama_reset(mlm_llama *m);
+int mlm_llama_set_position(mlm_llama *m, int pos);
+int mlm_llama_position(const mlm_llama *m);
+
+/* One decoder layer of forward() at the current position (the body of the
+ * layer loop, LlamaRunner.swift:537-1085): hidden fp32 [dim] in place,
+ * K and V appended at the current position.  Does not advance. */
+int mlm_llama_forward_layer(mlm_llama *m, int layer, float *hidden);
+
+/* LlamaRunner.forward(tokenID:) (LlamaRunner.swift:320-1210): embedding,
+ * all layers, final norm, output head; fp32 logits [vocab] (device) written
+ * to `logits` (NULL: kept inside the runner).  Advances the position.
+ * MLM_ERR_STATE when the cache is full, MLM_ERR_ARG for a bad token id. */
+int mlm_llama_forward(mlm_llama *m, int token, float *logits);
+
+/* The prompt: forward() over tokens[0..n) (host array) without the output
+ * head except for the last token; its greedy next token goes to
+ * *next_token_dev (device, may be NULL). */
+int mlm_llama_prefill(mlm_llama *m, const int32_t *tokens, int n, int32_t *next_token_dev);
+
+/* Greedy generation (the sampling loop of ContentView.swift:124-146 with the
+ * argmax on the device): starting from `token` at the current position,
+ * `steps` decode steps, each feeding back its argmax; tokens_out_dev[i]
+ * receives the i-th generated token.  One decode step is captured once as a
+ * CUDA graph and replayed; the first call captures it (make it outside any
+ * other capture on ctx's stream). */
+int mlm_llama_decode_greedy(mlm_llama *m, int token, int steps, int32_t *tokens_out_dev);
 
 #ifdef __cplusplus
 }

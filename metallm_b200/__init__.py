@@ -13,7 +13,8 @@ from typing import Optional, Sequence
 
 import numpy as np
 
-from ._lib import LIB_PATH, MLMError, RopeArgs, load, rope_args  # noqa: F401
+from ._lib import (LIB_PATH, LlamaConfig, LlamaGlobals, LlamaLayer, MLMError,  # noqa: F401
+                   RopeArgs, load, rope_args)
 
 QK_K = 256
 Q4K_BLOCK_BYTES = 144
@@ -194,6 +195,81 @@ class Graph:
     def __del__(self):
         try:
             self.destroy()
+        except Exception:
+            pass
+
+
+class Llama:
+    """mlm_llama: the decode runner (LlamaRunner.swift) on one context.
+
+    Tensors live in the runner's own device buffers; ``layer_tensors`` and
+    ``global_tensors`` give their device addresses (as ints) so a loader can
+    write the raw GGUF blocks straight into them.
+    """
+
+    def __init__(self, ctx: Context, cfg: LlamaConfig):
+        self.ctx = ctx
+        self.cfg = cfg
+        h = ctypes.c_void_p()
+        ctx._check(ctx.lib.mlm_llama_create(ctx.handle, ctypes.byref(cfg), ctypes.byref(h)),
+                   "mlm_llama_create")
+        self.handle = h
+
+    def _check(self, st: int, what: str) -> None:
+        self.ctx._check(st, what)
+
+    def layer_tensors(self, layer: int) -> dict:
+        t = LlamaLayer()
+        self._check(self.ctx.lib.mlm_llama_layer_tensors(self.handle, layer, ctypes.byref(t)),
+                    "mlm_llama_layer_tensors")
+        return {name: int(getattr(t, name)) for name, _ in LlamaLayer._fields_}
+
+    def global_tensors(self) -> dict:
+        t = LlamaGlobals()
+        self._check(self.ctx.lib.mlm_llama_global_tensors(self.handle, ctypes.byref(t)),
+                    "mlm_llama_global_tensors")
+        return {name: int(getattr(t, name)) for name, _ in LlamaGlobals._fields_}
+
+    def reset(self) -> None:
+        self._check(self.ctx.lib.mlm_llama_reset(self.handle), "mlm_llama_reset")
+
+    def set_position(self, pos: int) -> None:
+        self._check(self.ctx.lib.mlm_llama_set_position(self.handle, pos), "mlm_llama_set_position")
+
+    @property
+    def position(self) -> int:
+        return int(self.ctx.lib.mlm_llama_position(self.handle))
+
+    def forward_layer(self, layer: int, hidden) -> None:
+        self._check(self.ctx.lib.mlm_llama_forward_layer(self.handle, layer,
+                                                         ctypes.c_void_p(int(hidden))),
+                    "mlm_llama_forward_layer")
+
+    def forward(self, token: int, logits=None) -> None:
+        self._check(self.ctx.lib.mlm_llama_forward(
+            self.handle, token, ctypes.c_void_p(int(logits)) if logits is not None else None),
+            "mlm_llama_forward")
+
+    def prefill(self, tokens: Sequence[int], next_token=None) -> None:
+        arr = (ctypes.c_int32 * len(tokens))(*[int(t) for t in tokens])
+        self._check(self.ctx.lib.mlm_llama_prefill(
+            self.handle, arr, len(tokens),
+            ctypes.c_void_p(int(next_token)) if next_token is not None else None),
+            "mlm_llama_prefill")
+
+    def decode_greedy(self, token: int, steps: int, tokens_out) -> None:
+        self._check(self.ctx.lib.mlm_llama_decode_greedy(self.handle, token, steps,
+                                                         ctypes.c_void_p(int(tokens_out))),
+                    "mlm_llama_decode_greedy")
+
+    def close(self) -> None:
+        if self.handle:
+            self.ctx.lib.mlm_llama_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
         except Exception:
             pass
 

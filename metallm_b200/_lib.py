@@ -38,6 +38,25 @@ def rope_args(n_dims=128, freq_base=500000.0, freq_scale=1.0, pos_offset=0, n_ct
                     attn_factor, beta_fast, beta_slow, int(has_freq_factors))
 
 
+class LlamaConfig(ctypes.Structure):
+    """mlm_llama_config (LlamaConfig as LlamaRunner.swift reads it)."""
+    _fields_ = [("n_layers", ctypes.c_int32), ("dim", ctypes.c_int32), ("n_heads", ctypes.c_int32),
+                ("n_kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+                ("ffn_dim", ctypes.c_int32), ("vocab", ctypes.c_int32), ("max_seq", ctypes.c_int32),
+                ("rms_eps", c_float), ("rope", RopeArgs)]
+
+
+class LlamaLayer(ctypes.Structure):
+    """mlm_llama_layer: device pointers of one layer's tensors."""
+    _fields_ = [(n, ctypes.c_void_p) for n in ("attn_norm", "wq", "wk", "wv", "wo", "ffn_norm",
+                                               "w_gate", "w_up", "w_down", "k_cache", "v_cache")]
+
+
+class LlamaGlobals(ctypes.Structure):
+    """mlm_llama_globals."""
+    _fields_ = [(n, ctypes.c_void_p) for n in ("tok_embd", "output_norm", "output", "rope_freqs")]
+
+
 # (name, restype, argtypes) of every exported entry point
 SIGNATURES = [
     ("mlm_abi_version", c_int, []),
@@ -72,6 +91,7 @@ SIGNATURES = [
     ("mlm_dequantize_q4k_to_f32", c_int, [c_vp, c_vp, c_u64, ctypes.POINTER(c_vp)]),
     ("mlm_dequantize_q4k_to_f16", c_int, [c_vp, c_vp, c_u64, ctypes.POINTER(c_vp)]),
     ("mlm_q4k_gemv", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_vp]),
+    ("mlm_q4k_gemv_xs", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_vp]),
     ("mlm_q4k_gemv_static", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_vp]),
     ("mlm_q4k_tiled_bytes", ctypes.c_size_t, [c_int, c_int]),
     ("mlm_q4k_tile", c_int, [c_vp, c_vp, c_int, c_int, c_vp]),
@@ -82,10 +102,22 @@ SIGNATURES = [
     ("mlm_rope_qk_kv_append", c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.POINTER(RopeArgs),
                                       c_int, c_int, c_int, c_vp, c_vp, c_vp, c_int]),
     ("mlm_silu_mul", c_int, [c_vp, c_vp, c_vp, c_vp, c_int]),
+    ("mlm_silu_mul_scaled", c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int]),
     ("mlm_add_f32", c_int, [c_vp, c_vp, c_vp, c_vp, c_int]),
     ("mlm_attn_decode", c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp]),
     ("mlm_embed_f16", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp]),
     ("mlm_argmax_f32", c_int, [c_vp, c_vp, c_int, c_vp]),
+    ("mlm_llama_create", c_int, [c_vp, ctypes.POINTER(LlamaConfig), ctypes.POINTER(c_vp)]),
+    ("mlm_llama_destroy", None, [c_vp]),
+    ("mlm_llama_layer_tensors", c_int, [c_vp, c_int, ctypes.POINTER(LlamaLayer)]),
+    ("mlm_llama_global_tensors", c_int, [c_vp, ctypes.POINTER(LlamaGlobals)]),
+    ("mlm_llama_reset", c_int, [c_vp]),
+    ("mlm_llama_set_position", c_int, [c_vp, c_int]),
+    ("mlm_llama_position", c_int, [c_vp]),
+    ("mlm_llama_forward_layer", c_int, [c_vp, c_int, c_vp]),
+    ("mlm_llama_forward", c_int, [c_vp, c_int, c_vp]),
+    ("mlm_llama_prefill", c_int, [c_vp, ctypes.POINTER(ctypes.c_int32), c_int, c_vp]),
+    ("mlm_llama_decode_greedy", c_int, [c_vp, c_int, c_int, c_vp]),
 ]
 
 _lib: Optional[ctypes.CDLL] = None

@@ -26,12 +26,16 @@ template <int G>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_partial_kernel(
     const __half *__restrict__ q, const __half *__restrict__ kc, const __half *__restrict__ vc,
     int n_heads, int n_kv, int seq_len, int chunk_len, float scale,
-    float *__restrict__ partials) {
+    float *__restrict__ partials, const int *__restrict__ pos_dev) {
   __shared__ float s_scores[G][kAttnChunk * 2];
   __shared__ float s_out[kAttnThreads / 32][G][kAttnD];
   const int kvh = blockIdx.x;
   const int chunk = blockIdx.y;
   const int p0 = chunk * chunk_len;
+  // graph-replayed decode: the position lives in device memory and the grid
+  // covers the cache's capacity; chunks past the sequence do nothing
+  if (pos_dev) seq_len = *pos_dev + 1;
+  if (p0 >= seq_len) return;
   const int p1 = min(seq_len, p0 + chunk_len);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nwarp = kAttnThreads / 32;
@@ -123,9 +127,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_partial_kernel(
 }
 
 __global__ void attn_decode_merge_kernel(const float *__restrict__ partials, int n_heads,
-                                         int nchunks, __half *__restrict__ out) {
+                                         int nchunks, __half *__restrict__ out,
+                                         const int *__restrict__ pos_dev, int chunk_len) {
   const int h = blockIdx.x;
   const int dd = threadIdx.x;  // 128 threads
+  if (pos_dev) nchunks = (*pos_dev + chunk_len) / chunk_len;
   float M = -INFINITY;
   for (int c = 0; c < nchunks; ++c) M = fmaxf(M, partials[((size_t)c * n_heads + h) * kAttnPartial]);
   float L = 0.f, O = 0.f;
@@ -138,9 +144,12 @@ __global__ void attn_decode_merge_kernel(const float *__restrict__ partials, int
   out[(size_t)h * kAttnD + dd] = __float2half_rn(O / L);
 }
 
+// seq_len positions, or, when pos_dev is set, *pos_dev + 1 positions read on
+// the device out of a cache of capacity seq_len (a launch a captured graph can
+// replay at every step): fixed 128-position chunks covering the capacity.
 int attn_decode_launch(mlm_ctx *ctx, const void *q, const void *kc, const void *vc, int n_heads,
                        int n_kv, int head_dim, int seq_len, void *out, float *partials,
-                       size_t partial_floats, cudaStream_t stream) {
+                       size_t partial_floats, cudaStream_t stream, const int *pos_dev) {
   MLM_REQUIRE(ctx, head_dim == kAttnD, MLM_ERR_UNSUPPORTED,
               "mlm_attn_decode: head_dim=%d (this build handles %d)", head_dim, kAttnD);
   MLM_REQUIRE(ctx, n_kv > 0 && n_heads % n_kv == 0, MLM_ERR_SHAPE,
@@ -149,9 +158,18 @@ int attn_decode_launch(mlm_ctx *ctx, const void *q, const void *kc, const void *
   MLM_REQUIRE(ctx, G == 1 || G == 2 || G == 4 || G == 8, MLM_ERR_UNSUPPORTED,
               "mlm_attn_decode: GQA group %d (supported 1, 2, 4, 8)", G);
   MLM_REQUIRE(ctx, seq_len > 0, MLM_ERR_SHAPE, "mlm_attn_decode: seq_len=%d", seq_len);
-  int nchunks = (seq_len + kAttnChunk - 1) / kAttnChunk;
-  if (nchunks > kAttnMaxChunks) nchunks = kAttnMaxChunks;
-  const int chunk_len = (seq_len + nchunks - 1) / nchunks;
+  int nchunks, chunk_len;
+  if (pos_dev) {
+    chunk_len = 2 * kAttnChunk;
+    nchunks = (seq_len + chunk_len - 1) / chunk_len;
+    MLM_REQUIRE(ctx, nchunks <= kAttnMaxChunks, MLM_ERR_SHAPE,
+                "mlm_attn_decode: cache capacity %d exceeds %d positions", seq_len,
+                2 * kAttnChunk * kAttnMaxChunks);
+  } else {
+    nchunks = (seq_len + kAttnChunk - 1) / kAttnChunk;
+    if (nchunks > kAttnMaxChunks) nchunks = kAttnMaxChunks;
+    chunk_len = (seq_len + nchunks - 1) / nchunks;
+  }
   MLM_REQUIRE(ctx, chunk_len <= 2 * kAttnChunk, MLM_ERR_SHAPE,
               "mlm_attn_decode: seq_len=%d exceeds %d positions", seq_len,
               2 * kAttnChunk * kAttnMaxChunks);
@@ -165,25 +183,25 @@ int attn_decode_launch(mlm_ctx *ctx, const void *q, const void *kc, const void *
   switch (G) {
     case 1:
       attn_decode_partial_kernel<1><<<grid, kAttnThreads, 0, stream>>>(
-          qh, kh, vh, n_heads, n_kv, seq_len, chunk_len, scale, partials);
+          qh, kh, vh, n_heads, n_kv, seq_len, chunk_len, scale, partials, pos_dev);
       break;
     case 2:
       attn_decode_partial_kernel<2><<<grid, kAttnThreads, 0, stream>>>(
-          qh, kh, vh, n_heads, n_kv, seq_len, chunk_len, scale, partials);
+          qh, kh, vh, n_heads, n_kv, seq_len, chunk_len, scale, partials, pos_dev);
       break;
     case 4:
       attn_decode_partial_kernel<4><<<grid, kAttnThreads, 0, stream>>>(
-          qh, kh, vh, n_heads, n_kv, seq_len, chunk_len, scale, partials);
+          qh, kh, vh, n_heads, n_kv, seq_len, chunk_len, scale, partials, pos_dev);
       break;
     default:
       attn_decode_partial_kernel<8><<<grid, kAttnThreads, 0, stream>>>(
-          qh, kh, vh, n_heads, n_kv, seq_len, chunk_len, scale, partials);
+          qh, kh, vh, n_heads, n_kv, seq_len, chunk_len, scale, partials, pos_dev);
       break;
   }
   int st = check_launch(ctx, "mlm_attn_decode (partial)");
   if (st != MLM_OK) return st;
-  attn_decode_merge_kernel<<<n_heads, kAttnD, 0, stream>>>(partials, n_heads, nchunks,
-                                                           reinterpret_cast<__half *>(out));
+  attn_decode_merge_kernel<<<n_heads, kAttnD, 0, stream>>>(
+      partials, n_heads, nchunks, reinterpret_cast<__half *>(out), pos_dev, chunk_len);
   return check_launch(ctx, "mlm_attn_decode (merge)");
 }
 
@@ -268,7 +286,7 @@ extern "C" int mlm_attn_decode(mlm_ctx *ctx, const void *q, const void *kc, cons
   MLM_REQUIRE(ctx, aligned16(q) && aligned16(kc) && aligned16(vc), MLM_ERR_ALIGN,
               "mlm_attn_decode: q and caches must be 16-byte aligned");
   return attn_decode_launch(ctx, q, kc, vc, n_heads, n_kv_heads, head_dim, seq_len, out,
-                            ctx->attn_partials, ctx->attn_partials_floats, ctx->stream);
+                            ctx->attn_partials, ctx->attn_partials_floats, ctx->stream, nullptr);
 }
 
 extern "C" int mlm_embed_f16(mlm_ctx *ctx, const void *table, int vocab, int dim,

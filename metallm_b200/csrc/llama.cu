@@ -1,0 +1,355 @@
+// llama.cu -- the decode runner: LlamaRunner (MetalLM/Backend/LlamaRunner.swift)
+// on this library's kernels.
+//
+// The reference encodes every decode step op by op: a blit for the
+// embedding row, then per layer RMSNorm, three MPS GEMMs on fp16 weights
+// dequantized at load, RoPE, a KV-cache blit, repeat-KV plus 32 per-head
+// GEMM / softmax / GEMM triples, the output projection, a residual add,
+// RMSNorm, gate/up GEMMs, SiLU, multiply, the down GEMM and a residual add;
+// then the final norm, the output GEMM and a CPU argmax
+// (LlamaRunner.swift:320-1210, ContentView.swift:124-146).
+//
+// Here the runner owns the weights in Q4_K GGUF layout, with wq/wk/wv and
+// w_gate/w_up stored as one row-concatenated matrix each so that they run as
+// one GEMV; residual adds are fused into the GEMVs that produce them; RoPE
+// and the cache append are one kernel; attention is one split-sequence
+// kernel pair over the fp16 cache.  A decode step is 10 launches per layer
+// plus 6.  The hidden state stays fp32 between layers (the reference keeps
+// fp16); GEMV inputs are fp16 as in the reference, the SiLU-gated product
+// with a power-of-two scale per 32 elements (a plain fp16 store overflows
+// there on large activations; the reference's does).  Token, position and
+// step counter live in device memory, so a step is captured once as a CUDA
+// graph and replayed for every generated token.
+#include <cuda_runtime.h>
+
+#include <new>
+#include <vector>
+
+#include "mlm_device.cuh"
+#include "mlm_internal.h"
+
+namespace mlm {
+namespace {
+
+struct LayerBuf {
+  float *attn_norm, *ffn_norm;
+  uint8_t *qkv, *wo, *gu, *down;  // Q4_K
+  __half *kc, *vc;
+};
+
+// device step state
+enum { kToken = 0, kPos = 1, kStep = 2, kStateInts = 4 };
+
+__global__ void set_state_kernel(int *st, int token, int pos, int step) {
+  st[kToken] = token;
+  st[kPos] = pos;
+  st[kStep] = step;
+}
+
+// after the argmax of a step: record its token, move to the next position
+__global__ void advance_kernel(int *st, int32_t *tokens) {
+  tokens[st[kStep]] = st[kToken];
+  st[kStep] += 1;
+  st[kPos] += 1;
+}
+
+inline size_t q4k_row_bytes(int cols) { return (size_t)(cols / kQK) * kBlockBytes; }
+
+}  // namespace
+}  // namespace mlm
+
+using namespace mlm;
+
+struct mlm_llama {
+  mlm_ctx *ctx = nullptr;
+  mlm_llama_config cfg{};
+  int pos = 0;
+  std::vector<LayerBuf> layers;
+  __half *tok_embd = nullptr;
+  float *out_norm = nullptr;
+  uint8_t *output = nullptr;
+  float *rope_freqs = nullptr;
+  // activations of one step
+  float *hidden = nullptr, *qkv_out = nullptr, *gu_out = nullptr, *logits = nullptr;
+  __half *xn = nullptr, *q16 = nullptr, *attn_out = nullptr, *h16 = nullptr;
+  float *h_scale = nullptr;  // [ffn_dim / 32]
+  int *state = nullptr;
+  int32_t *gen_tokens = nullptr;  // [max_seq] tokens of the captured greedy loop
+  cudaGraph_t step_graph = nullptr;
+  cudaGraphExec_t step_exec = nullptr;
+  std::vector<void *> allocs;
+
+  int kvdim() const { return cfg.n_kv_heads * cfg.head_dim; }
+  int qkv_rows() const { return cfg.dim + 2 * kvdim(); }
+
+  template <class T>
+  int alloc(T **p, size_t bytes) {
+    void *q = nullptr;
+    if (cudaMalloc(&q, bytes ? bytes : 16) != cudaSuccess) {
+      cudaGetLastError();
+      return set_error(ctx, MLM_ERR_ALLOC, "mlm_llama_create: cudaMalloc(%zu) failed", bytes);
+    }
+    allocs.push_back(q);
+    *p = reinterpret_cast<T *>(q);
+    return MLM_OK;
+  }
+
+  int gemv(const uint8_t *W, int rows, int cols, const __half *x, float *y, const float *res,
+           const float *x_scale = nullptr) {
+    return gemv_launch(ctx, W, rows, cols, x, y, res, ctx->gemv_partials, ctx->gemv_counters,
+                       ctx->gemv_max_ctas, ctx->gemv_max_tiles, ctx->stream, x_scale);
+  }
+
+  // one decoder layer at the device position state[kPos]
+  int layer(int l, float *h) {
+    const LayerBuf &L = layers[l];
+    const mlm_llama_config &c = cfg;
+    cudaStream_t s = ctx->stream;
+    const int kvd = kvdim();
+    int st;
+    if ((st = rmsnorm_f32_launch(ctx, h, L.attn_norm, nullptr, xn, 1, c.dim, c.rms_eps, s))) return st;
+    if ((st = gemv(L.qkv, qkv_rows(), c.dim, xn, qkv_out, nullptr))) return st;
+    if ((st = rope_qk_kv_launch(ctx, qkv_out, qkv_out + c.dim, qkv_out + c.dim + kvd, rope_freqs,
+                                c.rope, c.n_heads, c.n_kv_heads, c.head_dim, q16, L.kc, L.vc, 0,
+                                s, state + kPos)))
+      return st;
+    if ((st = attn_decode_launch(ctx, q16, L.kc, L.vc, c.n_heads, c.n_kv_heads, c.head_dim,
+                                 c.max_seq, attn_out, ctx->attn_partials,
+                                 ctx->attn_partials_floats, s, state + kPos)))
+      return st;
+    if ((st = gemv(L.wo, c.dim, c.dim, attn_out, h, h))) return st;  // + residual
+    if ((st = rmsnorm_f32_launch(ctx, h, L.ffn_norm, nullptr, xn, 1, c.dim, c.rms_eps, s))) return st;
+    if ((st = gemv(L.gu, 2 * c.ffn_dim, c.dim, xn, gu_out, nullptr))) return st;
+    // SiLU-gated product as fp16 with per-32 power-of-two scales (it exceeds
+    // the fp16 range on large activations)
+    if ((st = silu_mul_scaled_launch(ctx, gu_out, gu_out + c.ffn_dim, h16, h_scale, c.ffn_dim, s)))
+      return st;
+    return gemv(L.down, c.dim, c.ffn_dim, h16, h, h, h_scale);  // + residual
+  }
+
+  // embedding of state[kToken], all layers; then, when `head`, the final
+  // norm, the output GEMV into `lg` and the argmax into state[kToken]
+  int step(bool head, float *lg) {
+    int st;
+    if ((st = embed_launch(ctx, tok_embd, cfg.vocab, cfg.dim, state + kToken, hidden,
+                           ctx->stream)))
+      return st;
+    for (int l = 0; l < cfg.n_layers; ++l)
+      if ((st = layer(l, hidden))) return st;
+    if (!head) return MLM_OK;
+    if ((st = rmsnorm_f32_launch(ctx, hidden, out_norm, nullptr, xn, 1, cfg.dim, cfg.rms_eps,
+                                 ctx->stream)))
+      return st;
+    if ((st = gemv(output, cfg.vocab, cfg.dim, xn, lg, nullptr))) return st;
+    return argmax_launch(ctx, lg, cfg.vocab, state + kToken, ctx->stream);
+  }
+
+  int set_state(int token, int p, int stp) {
+    set_state_kernel<<<1, 1, 0, ctx->stream>>>(state, token, p, stp);
+    return check_launch(ctx, "mlm_llama (state)");
+  }
+
+  void destroy() {
+    if (step_exec) cudaGraphExecDestroy(step_exec);
+    if (step_graph) cudaGraphDestroy(step_graph);
+    for (void *p : allocs) cudaFree(p);
+    allocs.clear();
+  }
+};
+
+extern "C" int mlm_llama_create(mlm_ctx *ctx, const mlm_llama_config *cfg, mlm_llama **out) {
+  MLM_CHECK_CTX(ctx);
+  MLM_REQUIRE(ctx, cfg && out, MLM_ERR_ARG, "mlm_llama_create: null argument");
+  *out = nullptr;
+  const mlm_llama_config &c = *cfg;
+  MLM_REQUIRE(ctx, c.n_layers > 0 && c.vocab > 0 && c.max_seq > 0 && c.max_seq <= 8192,
+              MLM_ERR_SHAPE, "mlm_llama_create: layers=%d vocab=%d max_seq=%d (max 8192)",
+              c.n_layers, c.vocab, c.max_seq);
+  MLM_REQUIRE(ctx, c.head_dim == 128 && c.n_heads * c.head_dim == c.dim, MLM_ERR_UNSUPPORTED,
+              "mlm_llama_create: head_dim=%d n_heads=%d dim=%d (head_dim 128, n_heads*head_dim "
+              "== dim)",
+              c.head_dim, c.n_heads, c.dim);
+  MLM_REQUIRE(ctx, c.dim % kQK == 0 && c.ffn_dim % kQK == 0, MLM_ERR_SHAPE,
+              "mlm_llama_create: dim=%d ffn=%d must be multiples of 256", c.dim, c.ffn_dim);
+  MLM_REQUIRE(ctx, c.n_kv_heads > 0 && c.n_heads % c.n_kv_heads == 0, MLM_ERR_SHAPE,
+              "mlm_llama_create: %d heads, %d KV heads", c.n_heads, c.n_kv_heads);
+  MLM_REQUIRE(ctx, c.rope.n_dims >= 2 && (int)c.rope.n_dims <= c.head_dim, MLM_ERR_SHAPE,
+              "mlm_llama_create: rope n_dims=%d", (int)c.rope.n_dims);
+  MLM_REQUIRE(ctx, 2 * c.ffn_dim <= ctx->gemv_max_tiles * 32 && c.vocab <= ctx->gemv_max_tiles * 32,
+              MLM_ERR_SHAPE, "mlm_llama_create: matrices exceed the GEMV row limit");
+
+  mlm_llama *m = new (std::nothrow) mlm_llama();
+  if (!m) return MLM_ERR_ALLOC;
+  m->ctx = ctx;
+  m->cfg = c;
+  auto fail = [&](int code) {
+    m->destroy();
+    delete m;
+    return code;
+  };
+  const size_t rb_dim = q4k_row_bytes(c.dim), rb_ffn = q4k_row_bytes(c.ffn_dim);
+  const size_t cache_bytes = (size_t)c.max_seq * c.n_kv_heads * c.head_dim * sizeof(__half);
+  m->layers.resize(c.n_layers);
+  for (int l = 0; l < c.n_layers; ++l) {
+    LayerBuf &L = m->layers[l];
+    if (m->alloc(&L.attn_norm, sizeof(float) * c.dim) || m->alloc(&L.ffn_norm, sizeof(float) * c.dim) ||
+        m->alloc(&L.qkv, (size_t)m->qkv_rows() * rb_dim) || m->alloc(&L.wo, (size_t)c.dim * rb_dim) ||
+        m->alloc(&L.gu, (size_t)2 * c.ffn_dim * rb_dim) || m->alloc(&L.down, (size_t)c.dim * rb_ffn) ||
+        m->alloc(&L.kc, cache_bytes) || m->alloc(&L.vc, cache_bytes))
+      return fail(MLM_ERR_ALLOC);
+  }
+  if (m->alloc(&m->tok_embd, (size_t)c.vocab * c.dim * sizeof(__half)) ||
+      m->alloc(&m->out_norm, sizeof(float) * c.dim) ||
+      m->alloc(&m->output, (size_t)c.vocab * rb_dim) ||
+      m->alloc(&m->rope_freqs, sizeof(float) * (c.head_dim / 2)) ||
+      m->alloc(&m->hidden, sizeof(float) * c.dim) ||
+      m->alloc(&m->qkv_out, sizeof(float) * m->qkv_rows()) ||
+      m->alloc(&m->gu_out, sizeof(float) * 2 * c.ffn_dim) ||
+      m->alloc(&m->logits, sizeof(float) * c.vocab) ||
+      m->alloc(&m->xn, sizeof(__half) * c.dim) || m->alloc(&m->q16, sizeof(__half) * c.dim) ||
+      m->alloc(&m->attn_out, sizeof(__half) * c.dim) ||
+      m->alloc(&m->h16, sizeof(__half) * c.ffn_dim) ||
+      m->alloc(&m->h_scale, sizeof(float) * (c.ffn_dim / 32)) ||
+      m->alloc(&m->state, sizeof(int) * kStateInts) ||
+      m->alloc(&m->gen_tokens, sizeof(int32_t) * c.max_seq))
+    return fail(MLM_ERR_ALLOC);
+  if (cudaMemsetAsync(m->state, 0, sizeof(int) * kStateInts, ctx->stream) != cudaSuccess)
+    return fail(set_error(ctx, MLM_ERR_CUDA, "mlm_llama_create: memset failed"));
+  *out = m;
+  return MLM_OK;
+}
+
+extern "C" void mlm_llama_destroy(mlm_llama *m) {
+  if (!m) return;
+  cudaStreamSynchronize(m->ctx->stream);
+  m->destroy();
+  delete m;
+}
+
+extern "C" int mlm_llama_layer_tensors(mlm_llama *m, int layer, mlm_llama_layer *out) {
+  if (!m) return MLM_ERR_ARG;
+  MLM_REQUIRE(m->ctx, out && layer >= 0 && layer < m->cfg.n_layers, MLM_ERR_ARG,
+              "mlm_llama_layer_tensors: layer %d of %d", layer, m->cfg.n_layers);
+  const LayerBuf &L = m->layers[layer];
+  const size_t rb = q4k_row_bytes(m->cfg.dim);
+  out->attn_norm = L.attn_norm;
+  out->ffn_norm = L.ffn_norm;
+  out->wq = L.qkv;
+  out->wk = L.qkv + (size_t)m->cfg.dim * rb;
+  out->wv = L.qkv + (size_t)(m->cfg.dim + m->kvdim()) * rb;
+  out->wo = L.wo;
+  out->w_gate = L.gu;
+  out->w_up = L.gu + (size_t)m->cfg.ffn_dim * rb;
+  out->w_down = L.down;
+  out->k_cache = L.kc;
+  out->v_cache = L.vc;
+  return MLM_OK;
+}
+
+extern "C" int mlm_llama_global_tensors(mlm_llama *m, mlm_llama_globals *out) {
+  if (!m) return MLM_ERR_ARG;
+  MLM_REQUIRE(m->ctx, out, MLM_ERR_ARG, "mlm_llama_global_tensors: null output");
+  out->tok_embd = m->tok_embd;
+  out->output_norm = m->out_norm;
+  out->output = m->output;
+  out->rope_freqs = m->rope_freqs;
+  return MLM_OK;
+}
+
+extern "C" int mlm_llama_reset(mlm_llama *m) {
+  if (!m) return MLM_ERR_ARG;
+  m->pos = 0;
+  return MLM_OK;
+}
+
+extern "C" int mlm_llama_set_position(mlm_llama *m, int pos) {
+  if (!m) return MLM_ERR_ARG;
+  MLM_REQUIRE(m->ctx, pos >= 0 && pos <= m->cfg.max_seq, MLM_ERR_ARG,
+              "mlm_llama_set_position: %d outside [0, %d]", pos, m->cfg.max_seq);
+  m->pos = pos;
+  return MLM_OK;
+}
+
+extern "C" int mlm_llama_position(const mlm_llama *m) { return m ? m->pos : -1; }
+
+extern "C" int mlm_llama_forward_layer(mlm_llama *m, int layer, float *hidden) {
+  if (!m) return MLM_ERR_ARG;
+  MLM_REQUIRE(m->ctx, hidden && layer >= 0 && layer < m->cfg.n_layers, MLM_ERR_ARG,
+              "mlm_llama_forward_layer: layer %d of %d", layer, m->cfg.n_layers);
+  MLM_REQUIRE(m->ctx, m->pos < m->cfg.max_seq, MLM_ERR_STATE,
+              "mlm_llama_forward_layer: KV cache full (pos=%d, max=%d)", m->pos, m->cfg.max_seq);
+  int st = m->set_state(0, m->pos, 0);
+  if (st != MLM_OK) return st;
+  return m->layer(layer, hidden);
+}
+
+extern "C" int mlm_llama_forward(mlm_llama *m, int token, float *logits) {
+  if (!m) return MLM_ERR_ARG;
+  MLM_REQUIRE(m->ctx, m->pos < m->cfg.max_seq, MLM_ERR_STATE,
+              "mlm_llama_forward: KV cache full (pos=%d, max=%d)", m->pos, m->cfg.max_seq);
+  MLM_REQUIRE(m->ctx, token >= 0 && token < m->cfg.vocab, MLM_ERR_ARG,
+              "mlm_llama_forward: invalid token id %d (vocab %d)", token, m->cfg.vocab);
+  int st = m->set_state(token, m->pos, 0);
+  if (st == MLM_OK) st = m->step(true, logits ? logits : m->logits);
+  if (st == MLM_OK) m->pos += 1;
+  return st;
+}
+
+extern "C" int mlm_llama_prefill(mlm_llama *m, const int32_t *tokens, int n, int32_t *next) {
+  if (!m) return MLM_ERR_ARG;
+  MLM_REQUIRE(m->ctx, tokens && n > 0, MLM_ERR_ARG, "mlm_llama_prefill: no tokens");
+  MLM_REQUIRE(m->ctx, m->pos + n <= m->cfg.max_seq, MLM_ERR_STATE,
+              "mlm_llama_prefill: %d tokens at position %d exceed the cache (%d)", n, m->pos,
+              m->cfg.max_seq);
+  for (int i = 0; i < n; ++i)
+    MLM_REQUIRE(m->ctx, tokens[i] >= 0 && tokens[i] < m->cfg.vocab, MLM_ERR_ARG,
+                "mlm_llama_prefill: invalid token id %d at %d", tokens[i], i);
+  for (int i = 0; i < n; ++i) {
+    int st = m->set_state(tokens[i], m->pos, 0);
+    if (st == MLM_OK) st = m->step(i == n - 1, m->logits);
+    if (st != MLM_OK) return st;
+    m->pos += 1;
+  }
+  if (next)
+    MLM_CUDA_TRY(m->ctx, cudaMemcpyAsync(next, m->state + kToken, sizeof(int32_t),
+                                         cudaMemcpyDeviceToDevice, m->ctx->stream));
+  return MLM_OK;
+}
+
+extern "C" int mlm_llama_decode_greedy(mlm_llama *m, int token, int steps, int32_t *tokens_out) {
+  if (!m) return MLM_ERR_ARG;
+  mlm_ctx *ctx = m->ctx;
+  MLM_REQUIRE(ctx, tokens_out && steps > 0, MLM_ERR_ARG, "mlm_llama_decode_greedy: no output");
+  MLM_REQUIRE(ctx, token >= 0 && token < m->cfg.vocab, MLM_ERR_ARG,
+              "mlm_llama_decode_greedy: invalid token id %d", token);
+  MLM_REQUIRE(ctx, m->pos + steps <= m->cfg.max_seq, MLM_ERR_STATE,
+              "mlm_llama_decode_greedy: %d steps at position %d exceed the cache (%d)", steps,
+              m->pos, m->cfg.max_seq);
+  if (!m->step_exec) {
+    // capture one step: embedding .. argmax, then record the token and move on
+    MLM_CUDA_TRY(ctx, cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+    int st = m->step(true, m->logits);
+    if (st == MLM_OK) {
+      advance_kernel<<<1, 1, 0, ctx->stream>>>(m->state, m->gen_tokens);
+      st = check_launch(ctx, "mlm_llama_decode_greedy (advance)");
+    }
+    cudaGraph_t g = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(ctx->stream, &g);
+    if (st != MLM_OK || e != cudaSuccess) {
+      if (g) cudaGraphDestroy(g);
+      cudaGetLastError();
+      return st != MLM_OK ? st
+                          : set_error(ctx, MLM_ERR_CUDA, "mlm_llama_decode_greedy: capture: %s",
+                                      cudaGetErrorString(e));
+    }
+    m->step_graph = g;
+    MLM_CUDA_TRY(ctx, cudaGraphInstantiate(&m->step_exec, g, 0));
+  }
+  int st = m->set_state(token, m->pos, 0);
+  if (st != MLM_OK) return st;
+  for (int i = 0; i < steps; ++i) MLM_CUDA_TRY(ctx, cudaGraphLaunch(m->step_exec, ctx->stream));
+  MLM_CUDA_TRY(ctx, cudaMemcpyAsync(tokens_out, m->gen_tokens, sizeof(int32_t) * steps,
+                                    cudaMemcpyDeviceToDevice, ctx->stream));
+  m->pos += steps;
+  return MLM_OK;
+}

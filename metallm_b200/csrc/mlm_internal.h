@@ -46,6 +46,29 @@ int set_error(mlm_ctx *ctx, int code, const char *fmt, ...)
     __attribute__((format(printf, 3, 4)));
 int check_launch(mlm_ctx *ctx, const char *what);
 
+// Kernel launchers shared between translation units (stream-ordered; each
+// returns an MLM_* status and records the reason in ctx on failure).
+int gemv_validate(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x, float *y);
+int gemv_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x, float *y,
+                const float *residual, float *partials, int *counters, int max_ctas,
+                int max_tiles, cudaStream_t stream, const float *x_scale);
+int rmsnorm_f32_launch(mlm_ctx *ctx, const float *x, const float *w, float *y32, void *y16,
+                       int rows, int n, float eps, cudaStream_t stream);
+int rope_qk_kv_launch(mlm_ctx *ctx, const float *q, const float *k, const float *v,
+                      const float *freqs, const mlm_rope_args &a, int nq, int nkv, int d,
+                      void *q_out, void *kc, void *vc, int pos, cudaStream_t stream,
+                      const int *pos_dev);
+int attn_decode_launch(mlm_ctx *ctx, const void *q, const void *kc, const void *vc, int n_heads,
+                       int n_kv, int head_dim, int seq_len, void *out, float *partials,
+                       size_t partial_floats, cudaStream_t stream, const int *pos_dev);
+int silu_mul_launch(mlm_ctx *ctx, const float *g, const float *u, void *out, int n,
+                    cudaStream_t stream);
+int silu_mul_scaled_launch(mlm_ctx *ctx, const float *g, const float *u, void *out, float *scale,
+                           int n, cudaStream_t stream);
+int argmax_launch(mlm_ctx *ctx, const float *x, int n, int32_t *out, cudaStream_t stream);
+int embed_launch(mlm_ctx *ctx, const void *table, int vocab, int dim, const int32_t *tok,
+                 float *out, cudaStream_t stream);
+
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline bool aligned4(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
 

@@ -160,7 +160,12 @@ __global__ void rope_qk_kv_kernel(mlm_rope_args a, RopeConsts k, const float *__
                                   const float *__restrict__ q, const float *__restrict__ kin,
                                   const float *__restrict__ v, int nq, int nkv, int d,
                                   __half *__restrict__ q_out, __half *__restrict__ kc,
-                                  __half *__restrict__ vc, int pos) {
+                                  __half *__restrict__ vc, int pos,
+                                  const int *__restrict__ pos_dev) {
+  // graph-replayed decode reads the position from device memory: it is both
+  // the rotation angle's position and the cache row
+  const int apos = pos_dev ? *pos_dev : a.pos_offset;
+  if (pos_dev) pos = apos;
   const int pairs = d / 2;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   const int nqp = nq * pairs, nkp = nkv * pairs;
@@ -172,7 +177,7 @@ __global__ void rope_qk_kv_kernel(mlm_rope_args a, RopeConsts k, const float *__
     float x0 = src[0], x1 = src[1];
     if (2 * pp < (int)a.n_dims) {
       float c, s;
-      rope_cos_sin(a, k, freqs, a.pos_offset, pp, c, s);
+      rope_cos_sin(a, k, freqs, apos, pp, c, s);
       const float r0 = x0 * c - x1 * s;
       const float r1 = x0 * s + x1 * c;
       x0 = r0;
@@ -204,6 +209,25 @@ __global__ void silu_mul_kernel(const float *__restrict__ g, const float *__rest
   out[i] = __float2half_rn(x * sig * u[i]);
 }
 
+// The same product stored as fp16 with one power-of-two scale per 32
+// elements: out[i] * scale[i / 32] is fp16 rounding of the product, with the
+// scale chosen so that the sub-block's largest magnitude stays below 2^15.
+// (A plain fp16 store overflows for large products; scaling by a power of
+// two is exact.)  n is a multiple of 32.
+__global__ void silu_mul_scaled_kernel(const float *__restrict__ g, const float *__restrict__ u,
+                                       __half *__restrict__ out, float *__restrict__ scale,
+                                       int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;  // whole warps: n % 32 == 0
+  const float x = g[i];
+  const float sig = 1.0f / (1.0f + expf(-x));
+  const float h = x * sig * u[i];
+  const float m = warp_max(fabsf(h));
+  const int e = max(0, (int)((__float_as_uint(m) >> 23) & 0xFF) - 127 - 14);
+  out[i] = __float2half_rn(h * __uint_as_float((uint32_t)(127 - e) << 23));
+  if ((threadIdx.x & 31) == 0) scale[i >> 5] = __uint_as_float((uint32_t)(127 + e) << 23);
+}
+
 __global__ void add_f32_kernel(const float *__restrict__ a, const float *__restrict__ b,
                                float *__restrict__ out, int n) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -212,12 +236,13 @@ __global__ void add_f32_kernel(const float *__restrict__ a, const float *__restr
 
 int rope_qk_kv_launch(mlm_ctx *ctx, const float *q, const float *k, const float *v,
                       const float *freqs, const mlm_rope_args &a, int nq, int nkv, int d,
-                      void *q_out, void *kc, void *vc, int pos, cudaStream_t stream) {
+                      void *q_out, void *kc, void *vc, int pos, cudaStream_t stream,
+                      const int *pos_dev) {
   const RopeConsts kc_ = rope_consts(a);
   const int total = nq * (d / 2) + 2 * nkv * (d / 2);
   rope_qk_kv_kernel<<<(total + 255) / 256, 256, 0, stream>>>(
       a, kc_, freqs, q, k, v, nq, nkv, d, reinterpret_cast<__half *>(q_out),
-      reinterpret_cast<__half *>(kc), reinterpret_cast<__half *>(vc), pos);
+      reinterpret_cast<__half *>(kc), reinterpret_cast<__half *>(vc), pos, pos_dev);
   return check_launch(ctx, "mlm_rope_qk_kv_append");
 }
 
@@ -225,6 +250,13 @@ int silu_mul_launch(mlm_ctx *ctx, const float *g, const float *u, void *out, int
                     cudaStream_t stream) {
   silu_mul_kernel<<<(n + 255) / 256, 256, 0, stream>>>(g, u, reinterpret_cast<__half *>(out), n);
   return check_launch(ctx, "mlm_silu_mul");
+}
+
+int silu_mul_scaled_launch(mlm_ctx *ctx, const float *g, const float *u, void *out, float *scale,
+                           int n, cudaStream_t stream) {
+  silu_mul_scaled_kernel<<<(n + 255) / 256, 256, 0, stream>>>(
+      g, u, reinterpret_cast<__half *>(out), scale, n);
+  return check_launch(ctx, "mlm_silu_mul_scaled");
 }
 
 int rmsnorm_f32_launch(mlm_ctx *ctx, const float *x, const float *w, float *y32, void *y16,
@@ -291,7 +323,7 @@ extern "C" int mlm_rope_qk_kv_append(mlm_ctx *ctx, const float *q, const float *
               MLM_ERR_SHAPE, "mlm_rope_qk_kv_append: heads=%d/%d d=%d pos=%d", n_q_heads,
               n_kv_heads, head_dim, pos);
   return rope_qk_kv_launch(ctx, q, k, v, freqs, *args, n_q_heads, n_kv_heads, head_dim, q_out,
-                           k_cache, v_cache, pos, ctx->stream);
+                           k_cache, v_cache, pos, ctx->stream, nullptr);
 }
 
 extern "C" int mlm_silu_mul(mlm_ctx *ctx, const float *gate, const float *up, void *out, int n) {
@@ -299,6 +331,15 @@ extern "C" int mlm_silu_mul(mlm_ctx *ctx, const float *gate, const float *up, vo
   MLM_REQUIRE(ctx, gate && up && out, MLM_ERR_ARG, "mlm_silu_mul: null buffer");
   MLM_REQUIRE(ctx, n > 0, MLM_ERR_SHAPE, "mlm_silu_mul: n=%d", n);
   return silu_mul_launch(ctx, gate, up, out, n, ctx->stream);
+}
+
+extern "C" int mlm_silu_mul_scaled(mlm_ctx *ctx, const float *gate, const float *up,
+                                   void *out_f16, float *scale, int n) {
+  MLM_CHECK_CTX(ctx);
+  MLM_REQUIRE(ctx, gate && up && out_f16 && scale, MLM_ERR_ARG, "mlm_silu_mul_scaled: null buffer");
+  MLM_REQUIRE(ctx, n > 0 && n % 32 == 0, MLM_ERR_SHAPE,
+              "mlm_silu_mul_scaled: n=%d is not a positive multiple of 32", n);
+  return silu_mul_scaled_launch(ctx, gate, up, out_f16, scale, n, ctx->stream);
 }
 
 extern "C" int mlm_add_f32(mlm_ctx *ctx, const float *a, const float *b, float *out, int n) {

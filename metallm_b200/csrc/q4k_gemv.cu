@@ -63,6 +63,7 @@ constexpr int kStageBytes = kTileRows * kBlockBytes;  // 4608
 struct GemvArgs {
   const uint8_t *W;
   const __half *x;
+  const float *x_scale;  // per 32-element sub-block of x (NULL: 1)
   float *y;
   const float *residual;
   float *partials;  // [ctas][2][32]
@@ -97,8 +98,9 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1)
   const int nwarps = blockDim.x >> 5;
   uint4 *xzero = reinterpret_cast<uint4 *>(smem + p.smem_x);
   uint4 *xperm = xzero + 4;  // after 64 zero bytes
-  float *xsum = reinterpret_cast<float *>(xperm + p.nb * 32);
-  float *parts = xsum + p.nb * 8;                                        // [warps][2][32]
+  float *xsum = reinterpret_cast<float *>(xperm + p.nb * 32);  // [nb][8]
+  float *xscl = xsum + p.nb * 8;                               // [nb][8]
+  float *parts = xscl + p.nb * 8;                                        // [warps][2][32]
   int *tile_done = reinterpret_cast<int *>(parts + nwarps * 2 * kTileRows);  // [ntile]
 
   const int lane = threadIdx.x & 31;
@@ -216,7 +218,11 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1)
           float sx = ((f0.x + f0.y) + (f1.x + f1.y)) + ((f2.x + f2.y) + (f3.x + f3.y));
           sx += __shfl_xor_sync(0xffffffffu, sx, 1);
           sx += __shfl_xor_sync(0xffffffffu, sx, 2);
-          if ((i & 3) == 0) xsum[i >> 2] = sx;
+          if ((i & 3) == 0) {
+            const float sc = p.x_scale ? p.x_scale[i >> 2] : 1.0f;
+            xsum[i >> 2] = sx * sc;
+            xscl[i >> 2] = sc;
+          }
         }
       }
     }
@@ -355,6 +361,7 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1)
     const uint32_t xlo = x_lo_base + bc * x_lo_step;
     const uint32_t xhi = x_hi_base + bc * x_hi_step;
     const float2 xs = *reinterpret_cast<const float2 *>(xsum + bc * 8 + 2 * tig);
+    const float2 xsc = *reinterpret_cast<const float2 *>(xscl + bc * 8 + 2 * tig);
 
     // quants and headers of rows g, g+8, g+16, g+24
     uint32_t q[4][8];
@@ -398,8 +405,9 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1)
     for (int i = 0; i < 4; ++i) {
       const int mt = i >> 1, hr = i & 1;
       const uint4 h = hd[i];
-      const float cs0 = fmaf(0.0625f, cacc[mt][1][2 * hr], cacc[mt][0][2 * hr]);
-      const float cs1 = fmaf(0.0625f, cacc[mt][1][2 * hr + 1], cacc[mt][0][2 * hr + 1]);
+      // sub-block sums of the stored x, times the x scale of each sub-block
+      const float cs0 = fmaf(0.0625f, cacc[mt][1][2 * hr], cacc[mt][0][2 * hr]) * xsc.x;
+      const float cs1 = fmaf(0.0625f, cacc[mt][1][2 * hr + 1], cacc[mt][0][2 * hr + 1]) * xsc.y;
       const uint32_t P = __byte_perm(h.y, h.w, psel);
       const uint32_t Q = __byte_perm(h.z, h.w, psel);
       const uint32_t scp = (P & mA) | ((P >> 18) & mB);
@@ -458,7 +466,7 @@ static bool plan_gemv(int rows, int nb, int sm_count, size_t smem_max, GemvPlan 
   for (int warps = kGemvMaxWarps; warps >= 2; --warps) {
     const size_t smem_bar = (size_t)warps * kGemvStages * kStageBytes;
     const size_t smem_x = smem_bar + (((size_t)warps * kGemvStages * 8 + 15) & ~(size_t)15);
-    const size_t smem = smem_x + 64 + (size_t)nb * 32 * 16 + (size_t)nb * 8 * 4 +
+    const size_t smem = smem_x + 64 + (size_t)nb * 32 * 16 + (size_t)nb * 8 * 4 * 2 +
                         (size_t)warps * 2 * kTileRows * 4 + (size_t)ntile * 4;
     if (smem <= smem_max) {
       pl = {warps, (int)units, ctas, ntile, smem, (uint32_t)smem_bar, (uint32_t)smem_x};
@@ -500,7 +508,7 @@ static int encode_weight_map(mlm_ctx *ctx, const void *W, int rows, int nb, CUte
 
 int gemv_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x, float *y,
                 const float *residual, float *partials, int *counters, int max_ctas,
-                int max_tiles, cudaStream_t stream) {
+                int max_tiles, cudaStream_t stream, const float *x_scale) {
   const int nb = cols / kQK;
   const int tiles = (rows + kTileRows - 1) / kTileRows;
   MLM_REQUIRE(ctx, tiles <= max_tiles, MLM_ERR_SHAPE,
@@ -517,6 +525,7 @@ int gemv_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x, 
   GemvArgs a;
   a.W = reinterpret_cast<const uint8_t *>(W);
   a.x = reinterpret_cast<const __half *>(x);
+  a.x_scale = x_scale;
   a.y = y;
   a.residual = residual;
   a.partials = partials;
@@ -569,7 +578,19 @@ extern "C" int mlm_q4k_gemv(mlm_ctx *ctx, const void *W, int rows, int cols, con
   int st = gemv_validate(ctx, W, rows, cols, x_f16, y);
   if (st != MLM_OK) return st;
   return gemv_launch(ctx, W, rows, cols, x_f16, y, residual, ctx->gemv_partials,
-                     ctx->gemv_counters, ctx->gemv_max_ctas, ctx->gemv_max_tiles, ctx->stream);
+                     ctx->gemv_counters, ctx->gemv_max_ctas, ctx->gemv_max_tiles, ctx->stream,
+                     nullptr);
+}
+
+extern "C" int mlm_q4k_gemv_xs(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_f16,
+                               const float *x_scale, float *y, const float *residual) {
+  MLM_CHECK_CTX(ctx);
+  int st = gemv_validate(ctx, W, rows, cols, x_f16, y);
+  if (st != MLM_OK) return st;
+  MLM_REQUIRE(ctx, x_scale, MLM_ERR_ARG, "mlm_q4k_gemv_xs: null x_scale");
+  return gemv_launch(ctx, W, rows, cols, x_f16, y, residual, ctx->gemv_partials,
+                     ctx->gemv_counters, ctx->gemv_max_ctas, ctx->gemv_max_tiles, ctx->stream,
+                     x_scale);
 }
 
 // ---------------------------------------------------------------------------
@@ -654,5 +675,5 @@ extern "C" int mlm_q4k_gemv_static(mlm_ctx *ctx, const void *W, int rows, int co
   const int tiles = (rows + mlm::kTileRows - 1) / mlm::kTileRows;
   MLM_CUDA_TRY(ctx, cudaMemsetAsync(counters, 0, sizeof(int) * (size_t)tiles, ctx->stream));
   return mlm::gemv_launch(ctx, W, rows, cols, x_f16, y, residual, partials, counters,
-                          mlm::kStaticMaxCtas, mlm::kStaticMaxTiles, ctx->stream);
+                          mlm::kStaticMaxCtas, mlm::kStaticMaxTiles, ctx->stream, nullptr);
 }

@@ -1,0 +1,66 @@
+"""Seeded synthetic Llama weights and caches for the decode runner.
+
+No checkpoint is used anywhere: a model of a named shape is filled on the
+device by the counter-based generators of the C ABI (mlm_gen_q4k / _f16 /
+_f32), which the CPU oracle reproduces bit for bit.  Every tensor has its
+own generator stream, given here, so a CPU restatement can rebuild any
+tensor on its own.
+
+Distributions (the benchmark configurations): Q4_K blocks with d, dmin =
+fp16(|N(0,1)| * 0.01), 6-bit scales/mins uniform, nibbles uniform; RMSNorm
+weights 1 + N(0, 0.02) fp32; token embedding N(0, 0.02) fp16; KV-cache
+entries N(0, 1) fp16.
+"""
+from __future__ import annotations
+
+from typing import Dict
+
+from ._lib import LlamaConfig, rope_args
+
+LAYER_TENSORS = ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down", "attn_norm", "ffn_norm",
+                 "k_cache", "v_cache")
+GLOBAL_TENSORS = ("tok_embd", "output_norm", "output")
+
+
+def layer_stream(layer: int, name: str) -> int:
+    return 1000 + 100 * layer + LAYER_TENSORS.index(name)
+
+
+def global_stream(name: str) -> int:
+    return 500 + GLOBAL_TENSORS.index(name)
+
+
+def llama_config(n_layers: int = 32, dim: int = 4096, n_heads: int = 32, n_kv_heads: int = 8,
+                 ffn_dim: int = 14336, vocab: int = 128256, max_seq: int = 2048,
+                 rms_eps: float = 1e-5, rope_theta: float = 500000.0) -> LlamaConfig:
+    """Llama-3-8B shape by default (head_dim 128, RoPE theta 500000, YaRN off)."""
+    return LlamaConfig(n_layers, dim, n_heads, n_kv_heads, 128, ffn_dim, vocab, max_seq, rms_eps,
+                       rope_args(n_dims=128, freq_base=rope_theta))
+
+
+def q4k_shapes(cfg: LlamaConfig) -> Dict[str, tuple]:
+    """(rows, cols) of each Q4_K tensor of a layer (GGUF: cols = ne0)."""
+    kvd = cfg.n_kv_heads * cfg.head_dim
+    return {"wq": (cfg.dim, cfg.dim), "wk": (kvd, cfg.dim), "wv": (kvd, cfg.dim),
+            "wo": (cfg.dim, cfg.dim), "w_gate": (cfg.ffn_dim, cfg.dim),
+            "w_up": (cfg.ffn_dim, cfg.dim), "w_down": (cfg.dim, cfg.ffn_dim)}
+
+
+def fill_llama(llama, seed: int, cache_positions: int = 0, layers=None) -> None:
+    """Fill the runner's weights (and the first `cache_positions` rows of
+    every layer's KV cache) on the device."""
+    ctx, cfg = llama.ctx, llama.cfg
+    kvd = cfg.n_kv_heads * cfg.head_dim
+    for layer in (range(cfg.n_layers) if layers is None else layers):
+        t = llama.layer_tensors(layer)
+        for name, (rows, cols) in q4k_shapes(cfg).items():
+            ctx.gen_q4k(seed, layer_stream(layer, name), rows * cols // 256, t[name])
+        for name in ("attn_norm", "ffn_norm"):
+            ctx.gen_f32(seed, layer_stream(layer, name), cfg.dim, t[name], 1.0, 0.02)
+        if cache_positions:
+            for name in ("k_cache", "v_cache"):
+                ctx.gen_f16(seed, layer_stream(layer, name), cache_positions * kvd, t[name])
+    g = llama.global_tensors()
+    ctx.gen_f16(seed, global_stream("tok_embd"), cfg.vocab * cfg.dim, g["tok_embd"], 0.0, 0.02)
+    ctx.gen_f32(seed, global_stream("output_norm"), cfg.dim, g["output_norm"], 1.0, 0.02)
+    ctx.gen_q4k(seed, global_stream("output"), cfg.vocab * cfg.dim // 256, g["output"])

@@ -1,0 +1,62 @@
+"""CPU restatement of one Llama decode step -- test infrastructure only.
+
+The op order of LlamaRunner.forward (MetalLM/Backend/LlamaRunner.swift:
+537-1085 per layer, 1130-1184 for the final norm and the output head),
+composed from the oracle's pinned pieces (q4k_oracle.c): the bit-exact Q4_K
+dequantizer in an fp64-accumulated matvec, RMSNorm (NormalizationKernels.metal:
+31-79), RoPE (PositionalEmbeddingsKernels.metal:159-203) and softmax
+attention in fp64.  Weights are applied in W[out][in] orientation (the
+reference's MPS call reads them transposed; that is a known reference bug,
+not reproduced).  Everything is fp32 (matvec sums in fp64) except the KV
+cache, which is fp16 as in the reference: the reference's own fp16
+activations overflow on the synthetic benchmark weights (the SiLU-gated
+product exceeds 65504), so this is the fp32 composition the parity bar is
+stated against.
+
+Weights are plain numpy arrays: Q4_K tensors as uint8 block bytes
+[rows * cols / 256 * 144], norms as fp32.  This module is only imported by
+the tests; the product never calls it.
+"""
+from __future__ import annotations
+
+from typing import Dict
+
+import numpy as np
+
+from . import oracle as O
+
+
+def layer_decode(w: Dict[str, np.ndarray], hidden: np.ndarray, kcache: np.ndarray,
+                 vcache: np.ndarray, pos: int, cfg: dict) -> np.ndarray:
+    """One decoder layer at position `pos`; appends K/V at row `pos` of the
+    fp16 caches [max_seq][n_kv][head_dim] and returns the new fp32 hidden."""
+    d, hd, nh, nkv, ffn, eps = (cfg[k] for k in ("dim", "head_dim", "n_heads", "n_kv_heads",
+                                                 "ffn_dim", "rms_eps"))
+    kvd = nkv * hd
+    xn = O.rmsnorm_f32(hidden, w["attn_norm"], 1, d, eps)
+    q = O.q4k_matvec_f32x(w["wq"], d, d, xn)
+    k = O.q4k_matvec_f32x(w["wk"], kvd, d, xn)
+    v = O.q4k_matvec_f32x(w["wv"], kvd, d, xn)
+    ra = O.rope_args(n_dims=hd, freq_base=cfg["rope_theta"], pos_offset=pos)
+    q = O.rope_f32(ra, q, 1, nh, hd)
+    k = O.rope_f32(ra, k, 1, nkv, hd)
+    kcache[pos] = k.astype(np.float16).reshape(nkv, hd)
+    vcache[pos] = v.astype(np.float16).reshape(nkv, hd)
+    attn = O.attn_decode(q, kcache[: pos + 1], vcache[: pos + 1], nh, nkv, hd, pos + 1)
+    hidden = hidden + O.q4k_matvec_f32x(w["wo"], d, d, attn)
+    xn2 = O.rmsnorm_f32(hidden, w["ffn_norm"], 1, d, eps)
+    g = O.q4k_matvec_f32x(w["w_gate"], ffn, d, xn2)
+    u = O.q4k_matvec_f32x(w["w_up"], ffn, d, xn2)
+    return hidden + O.q4k_matvec_f32x(w["w_down"], d, ffn, O.silu_mul(g, u))
+
+
+def model_forward(layers, glob: Dict[str, np.ndarray], caches, token: int, pos: int,
+                  cfg: dict) -> np.ndarray:
+    """forward(tokenID:): embedding row, every layer, final norm, output head;
+    returns fp32 logits [vocab].  caches[l] = (kcache, vcache), updated."""
+    d = cfg["dim"]
+    hidden = glob["tok_embd"][token * d:(token + 1) * d].astype(np.float32)
+    for w, (kc, vc) in zip(layers, caches):
+        hidden = layer_decode(w, hidden, kc, vc, pos, cfg)
+    xn = O.rmsnorm_f32(hidden, glob["output_norm"], 1, d, cfg["rms_eps"])
+    return O.q4k_matvec_f32x(glob["output"], cfg["vocab"], d, xn)

@@ -145,3 +145,20 @@ def test_gemv_graph_replay_matches_eager(ctx):
         assert np.array_equal(ys[c].download(np.uint32), eager[c])
     ref = O.q4k_matvec(O.gen_q4k(52, 1, nb), rows, cols, O.gen_f16(50, 2, cols))
     assert rel_l2(ys[2].download(np.float32), ref) < TOL
+
+
+def test_gemv_scaled_x(ctx):
+    """x = x_f16 * x_scale[k/32]: the down projection's input format."""
+    rows, cols = 1000, 14336
+    nb = rows * cols // 256
+    W = ctx.alloc(nb * 144)
+    ctx.gen_q4k(21, 1, nb, W)
+    x16 = O.gen_f16(21, 2, cols)
+    scale = (2.0 ** (np.arange(cols // 32) % 9)).astype(np.float32)
+    y = ctx.alloc(4 * rows)
+    r = ctx.alloc(4 * rows)
+    ctx.gen_f32(21, 3, rows, r)
+    ctx.call("mlm_q4k_gemv_xs", W, rows, cols, ctx.to_device(x16), ctx.to_device(scale), y, r)
+    xtrue = x16.astype(np.float32) * np.repeat(scale, 32)
+    ref = O.q4k_matvec_f32x(O.gen_q4k(21, 1, nb), rows, cols, xtrue) + O.gen_f32(21, 3, rows)
+    assert rel_l2(y.download(np.float32), ref) < TOL

@@ -1,0 +1,174 @@
+"""The decode runner (mlm_llama_*) against the oracle's restatement of
+LlamaRunner.forward, through the C ABI.
+
+Bar: layer output and logits within relative L2 1e-2 of the fp32/fp64
+oracle composed from the bit-exact dequantizer, identical greedy argmax.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from metallm_b200 import Llama, MLMError
+from metallm_b200.synthetic import global_stream, layer_stream, llama_config, q4k_shapes
+from oracle import llama_oracle as LO
+from oracle import oracle as O
+from tests.conftest import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+SEED = 2024
+
+
+def cfg_dict(cfg) -> dict:
+    return {"dim": cfg.dim, "head_dim": cfg.head_dim, "n_heads": cfg.n_heads,
+            "n_kv_heads": cfg.n_kv_heads, "ffn_dim": cfg.ffn_dim, "rms_eps": cfg.rms_eps,
+            "rope_theta": cfg.rope.freq_base, "vocab": cfg.vocab}
+
+
+def oracle_layer(cfg, layer: int) -> dict:
+    w = {name: O.gen_q4k(SEED, layer_stream(layer, name), rows * cols // 256)
+         for name, (rows, cols) in q4k_shapes(cfg).items()}
+    for name in ("attn_norm", "ffn_norm"):
+        w[name] = O.gen_f32(SEED, layer_stream(layer, name), cfg.dim, 1.0, 0.02)
+    return w
+
+
+def oracle_cache(cfg, layer: int, filled: int):
+    kvd = cfg.n_kv_heads * cfg.head_dim
+    caches = []
+    for name in ("k_cache", "v_cache"):
+        c = np.zeros((cfg.max_seq, cfg.n_kv_heads, cfg.head_dim), dtype=np.float16)
+        if filled:
+            c[:filled] = O.gen_f16(SEED, layer_stream(layer, name), filled * kvd).reshape(
+                filled, cfg.n_kv_heads, cfg.head_dim)
+        caches.append(c)
+    return caches
+
+
+def oracle_globals(cfg) -> dict:
+    return {"tok_embd": O.gen_f16(SEED, global_stream("tok_embd"), cfg.vocab * cfg.dim, 0.0, 0.02),
+            "output_norm": O.gen_f32(SEED, global_stream("output_norm"), cfg.dim, 1.0, 0.02),
+            "output": O.gen_q4k(SEED, global_stream("output"), cfg.vocab * cfg.dim // 256)}
+
+
+def test_layer_decode_llama8b_shape(ctx):
+    """One Llama-3-8B-shape layer, single-token decode at position 2047 over
+    a 2047-token fp16 cache ~ N(0,1), fp32 input ~ N(0,1)."""
+    from metallm_b200.synthetic import fill_llama
+    cfg = llama_config(n_layers=1, vocab=256, max_seq=2048)
+    m = Llama(ctx, cfg)
+    pos = 2047
+    fill_llama(m, SEED, cache_positions=pos)
+    hidden = ctx.alloc(4 * cfg.dim)
+    ctx.gen_f32(SEED, 7, cfg.dim, hidden)
+    m.set_position(pos)
+    m.forward_layer(0, hidden)
+    got = hidden.download(np.float32)
+    t = m.layer_tensors(0)
+    kvd = cfg.n_kv_heads * cfg.head_dim
+    k_row = np.empty(kvd, dtype=np.float16)
+    ctx._check(ctx.lib.mlm_download(ctx.handle, k_row.ctypes.data,
+                                    __import__("ctypes").c_void_p(t["k_cache"] + pos * kvd * 2),
+                                    k_row.nbytes), "download")
+
+    kc, vc = oracle_cache(cfg, 0, pos)
+    want = LO.layer_decode(oracle_layer(cfg, 0), O.gen_f32(SEED, 7, cfg.dim), kc, vc, pos,
+                           cfg_dict(cfg))
+    assert np.all(np.isfinite(got))
+    err = rel_l2(got, want)
+    assert err < TOL, err
+    assert rel_l2(k_row.astype(np.float32), kc[pos].reshape(-1).astype(np.float32)) < 1e-3
+    m.close()
+
+
+def _small_cfg():
+    return llama_config(n_layers=2, dim=1024, n_heads=8, n_kv_heads=2, ffn_dim=2816,
+                        vocab=4096, max_seq=64)
+
+
+def test_model_forward_and_greedy(ctx):
+    from metallm_b200.synthetic import fill_llama
+    cfg = _small_cfg()
+    m = Llama(ctx, cfg)
+    fill_llama(m, SEED)
+    cd = cfg_dict(cfg)
+    layers = [oracle_layer(cfg, l) for l in range(cfg.n_layers)]
+    glob = oracle_globals(cfg)
+    caches = [oracle_cache(cfg, l, 0) for l in range(cfg.n_layers)]
+
+    prompt = [17, 4000, 3, 999, 2048]
+    logits = ctx.alloc(4 * cfg.vocab)
+    for pos, tok in enumerate(prompt):
+        m.forward(tok, logits)
+        got = logits.download(np.float32)
+        want = LO.model_forward(layers, glob, caches, tok, pos, cd)
+        assert rel_l2(got, want) < TOL, (pos, rel_l2(got, want))
+        assert int(np.argmax(got)) == int(np.argmax(want)), pos
+    assert m.position == len(prompt)
+
+    # greedy continuation on the device vs the oracle's argmax loop
+    steps = 8
+    first = int(np.argmax(want))
+    out = ctx.alloc(4 * steps)
+    m.decode_greedy(first, steps, out)
+    got_tokens = out.download(np.int32).tolist()
+    tok, pos, ref_tokens = first, len(prompt), []
+    for _ in range(steps):
+        lg = LO.model_forward(layers, glob, caches, tok, pos, cd)
+        tok = int(np.argmax(lg))
+        ref_tokens.append(tok)
+        pos += 1
+    assert got_tokens == ref_tokens
+    assert m.position == len(prompt) + steps
+
+    # a second greedy call replays the captured step graph
+    out2 = ctx.alloc(4 * 2)
+    m.decode_greedy(ref_tokens[-1], 2, out2)
+    for i, g2 in enumerate(out2.download(np.int32).tolist()):
+        lg = LO.model_forward(layers, glob, caches, tok, pos, cd)
+        tok = int(np.argmax(lg))
+        pos += 1
+        assert g2 == tok, i
+    m.close()
+
+
+def test_prefill_matches_forward(ctx):
+    from metallm_b200.synthetic import fill_llama
+    cfg = _small_cfg()
+    m = Llama(ctx, cfg)
+    fill_llama(m, SEED)
+    prompt = [5, 6, 7, 8, 9, 10]
+    nxt = ctx.alloc(16)
+    m.prefill(prompt, nxt)
+    a = int(nxt.download(np.int32)[0])
+    m.reset()
+    logits = ctx.alloc(4 * cfg.vocab)
+    for tok in prompt:
+        m.forward(tok, logits)
+    assert a == int(np.argmax(logits.download(np.float32)))
+    m.close()
+
+
+def test_llama_errors(ctx):
+    from metallm_b200.synthetic import llama_config as lc
+    with pytest.raises(MLMError) as e:
+        Llama(ctx, lc(n_layers=1, dim=1000))
+    assert e.value.status in (-2, -9)
+    cfg = lc(n_layers=1, dim=1024, n_heads=8, n_kv_heads=2, ffn_dim=1024, vocab=512, max_seq=2)
+    m = Llama(ctx, cfg)
+    with pytest.raises(MLMError) as e:
+        m.forward(512)
+    assert e.value.status == -1
+    m.forward(1)
+    m.forward(2)
+    with pytest.raises(MLMError) as e:
+        m.forward(3)
+    assert e.value.status == -8
+    out = ctx.alloc(16)
+    m.reset()
+    with pytest.raises(MLMError) as e:
+        m.decode_greedy(1, 3, out)
+    assert e.value.status == -8
+    m.close()

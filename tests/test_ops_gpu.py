@@ -142,3 +142,28 @@ def test_argmax_first_max_and_embed(ctx):
     ctx.call("mlm_embed_f16", ctx.to_device(table), vocab, dim, tok, out)
     assert np.array_equal(out.download(np.float32),
                           table.reshape(vocab, dim)[321].astype(np.float32))
+
+
+def test_silu_mul_scaled(ctx):
+    """fp16 x per-32 power-of-two scale: finite where plain fp16 overflows,
+    and equal to the fp16 rounding of the scaled product."""
+    n = 14336
+    g = O.gen_f32(41, 1, n, 0.0, 300.0)
+    u = O.gen_f32(41, 2, n, 0.0, 300.0)
+    gd, ud = ctx.to_device(g), ctx.to_device(u)
+    out, sc = ctx.alloc(2 * n), ctx.alloc(4 * (n // 32))
+    ctx.call("mlm_silu_mul_scaled", gd, ud, out, sc, n)
+    h16 = out.download(np.float16)[:n]
+    s = sc.download(np.float32)[: n // 32]
+    ref = O.silu_mul(g, u).astype(np.float64)
+    assert np.all(np.isfinite(h16))
+    assert np.any(np.abs(ref) > 65504.0)  # the case a plain fp16 store overflows
+    e = np.log2(s)
+    assert np.all(e == np.round(e)) and np.all(e >= 0)
+    blocks = np.abs(h16.astype(np.float32)).reshape(-1, 32).max(axis=1)
+    assert np.all(blocks <= 32768.0)  # fp16 rounding may reach 2^15 exactly
+    got = h16.astype(np.float64) * np.repeat(s, 32)
+    # fp16 rounding of the scaled value: half an ulp, or the subnormal spacing
+    # 2^-24 (times the scale) near zero
+    bound = np.maximum(2.0 ** -11 * np.abs(ref), 2.0 ** -24 * np.repeat(s, 32))
+    assert np.all(np.abs(got - ref) <= bound)

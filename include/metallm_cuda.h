@@ -152,6 +152,21 @@ int mlm_q4k_gemv(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_
 int mlm_q4k_gemv_xs(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_f16,
                     const float *x_scale, float *y, const float *residual);
 
+/* The GEMV with its input normalised on the fly: x = RMSNorm(hidden) as
+ * mlm_rmsnorm_f32 computes it (NormalizationKernels.metal:31-79; fp32 hidden
+ * and weights, the product rounded to fp16), each CTA reducing the sum of
+ * squares itself -- the encodeRMSNormF16 + encodeMPSMatrixMultiply pairs of
+ * LlamaRunner.swift:547-609 and 992-1034 in one launch.  hidden and norm_w
+ * 16-byte aligned. */
+int mlm_q4k_gemv_rmsnorm(mlm_ctx *ctx, const void *W, int rows, int cols, const float *hidden,
+                         const float *norm_w, float eps, float *y, const float *residual);
+/* The GEMV on x = silu(gate) * up formed on the fly (fp32 in, stored as fp16
+ * with per-32 power-of-two scales as mlm_silu_mul_scaled does): applySILU,
+ * applyElementWiseMul and the down projection of LlamaRunner.swift:1036-1068
+ * in one launch. */
+int mlm_q4k_gemv_swiglu(mlm_ctx *ctx, const void *W, int rows, int cols, const float *gate,
+                        const float *up, float *y, const float *residual);
+
 /* Tiled Q4_K layout: the same 144-byte blocks, reordered once after upload
  * so that the decode GEMV streams them as contiguous 4608-byte units (32
  * rows of one block column, laid out in the GEMV's register order; rows past

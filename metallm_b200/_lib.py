@@ -92,6 +92,8 @@ SIGNATURES = [
     ("mlm_dequantize_q4k_to_f16", c_int, [c_vp, c_vp, c_u64, ctypes.POINTER(c_vp)]),
     ("mlm_q4k_gemv", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_vp]),
     ("mlm_q4k_gemv_xs", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_vp]),
+    ("mlm_q4k_gemv_rmsnorm", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_float, c_vp, c_vp]),
+    ("mlm_q4k_gemv_swiglu", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_vp]),
     ("mlm_q4k_gemv_static", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_vp]),
     ("mlm_q4k_tiled_bytes", ctypes.c_size_t, [c_int, c_int]),
     ("mlm_q4k_tile", c_int, [c_vp, c_vp, c_int, c_int, c_vp]),

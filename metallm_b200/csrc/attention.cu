@@ -21,6 +21,12 @@ constexpr int kAttnThreads = 128;
 
 // partial layout per (chunk, head): [m, l, o[128]]
 constexpr int kAttnPartial = 2 + kAttnD;
+// K and V rows of one chunk staged in shared memory (dynamic)
+constexpr int kAttnStageBytes = 2 * (2 * kAttnChunk) * kAttnD * (int)sizeof(__half);
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
 
 template <int G>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_partial_kernel(
@@ -41,6 +47,30 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_partial_kernel(
   const int nwarp = kAttnThreads / 32;
   const size_t row_stride = (size_t)n_kv * kAttnD;
 
+  // Stage the chunk's K rows, then its V rows, into shared memory: every
+  // 16-byte piece is requested up front (~64 KB in flight per CTA), so the
+  // loops below never wait on HBM one position at a time.
+  extern __shared__ __align__(16) __half s_kv[];  // [2][2 * kAttnChunk][kAttnD]
+  __half *s_k = s_kv, *s_v = s_kv + 2 * kAttnChunk * kAttnD;
+  {
+    constexpr int kPiecesPerRow = kAttnD * (int)sizeof(__half) / 16;  // 16
+    const int pieces = (p1 - p0) * kPiecesPerRow;
+    const uint32_t sk = (uint32_t)__cvta_generic_to_shared(s_k);
+    const uint32_t sv = (uint32_t)__cvta_generic_to_shared(s_v);
+    for (int j = threadIdx.x; j < pieces; j += kAttnThreads) {
+      const int r = j / kPiecesPerRow, c = j - r * kPiecesPerRow;
+      cp_async16(sk + (uint32_t)(r * kAttnD + c * 8) * 2,
+                 kc + (size_t)(p0 + r) * row_stride + kvh * kAttnD + c * 8);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    for (int j = threadIdx.x; j < pieces; j += kAttnThreads) {
+      const int r = j / kPiecesPerRow, c = j - r * kPiecesPerRow;
+      cp_async16(sv + (uint32_t)(r * kAttnD + c * 8) * 2,
+                 vc + (size_t)(p0 + r) * row_stride + kvh * kAttnD + c * 8);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+
   // q of the G heads of this group, dims 4*lane .. 4*lane+3
   float qv[G][4];
 #pragma unroll
@@ -55,9 +85,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_partial_kernel(
     qv[gh][3] = b.y * scale;
   }
 
+  asm volatile("cp.async.wait_group 1;" ::: "memory");  // K landed
+  __syncthreads();
+
   // scores: warp w handles positions p0 + w, p0 + w + nwarp, ...
   for (int p = p0 + warp; p < p1; p += nwarp) {
-    const uint2 raw = *reinterpret_cast<const uint2 *>(kc + p * row_stride + kvh * kAttnD + 4 * lane);
+    const uint2 raw = *reinterpret_cast<const uint2 *>(s_k + (p - p0) * kAttnD + 4 * lane);
     const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
     const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
 #pragma unroll
@@ -87,6 +120,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_partial_kernel(
       s_l[gh] = l;
     }
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");  // V landed
   __syncthreads();
 
   // P.V: warp w accumulates positions p0 + w (+ nwarp ...) for dims 4*lane..
@@ -94,7 +128,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_partial_kernel(
 #pragma unroll
   for (int gh = 0; gh < G; ++gh) o[gh][0] = o[gh][1] = o[gh][2] = o[gh][3] = 0.f;
   for (int p = p0 + warp; p < p1; p += nwarp) {
-    const uint2 raw = *reinterpret_cast<const uint2 *>(vc + p * row_stride + kvh * kAttnD + 4 * lane);
+    const uint2 raw = *reinterpret_cast<const uint2 *>(s_v + (p - p0) * kAttnD + 4 * lane);
     const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
     const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
 #pragma unroll
@@ -182,19 +216,19 @@ int attn_decode_launch(mlm_ctx *ctx, const void *q, const void *kc, const void *
   const __half *vh = reinterpret_cast<const __half *>(vc);
   switch (G) {
     case 1:
-      attn_decode_partial_kernel<1><<<grid, kAttnThreads, 0, stream>>>(
+      attn_decode_partial_kernel<1><<<grid, kAttnThreads, kAttnStageBytes, stream>>>(
           qh, kh, vh, n_heads, n_kv, seq_len, chunk_len, scale, partials, pos_dev);
       break;
     case 2:
-      attn_decode_partial_kernel<2><<<grid, kAttnThreads, 0, stream>>>(
+      attn_decode_partial_kernel<2><<<grid, kAttnThreads, kAttnStageBytes, stream>>>(
           qh, kh, vh, n_heads, n_kv, seq_len, chunk_len, scale, partials, pos_dev);
       break;
     case 4:
-      attn_decode_partial_kernel<4><<<grid, kAttnThreads, 0, stream>>>(
+      attn_decode_partial_kernel<4><<<grid, kAttnThreads, kAttnStageBytes, stream>>>(
           qh, kh, vh, n_heads, n_kv, seq_len, chunk_len, scale, partials, pos_dev);
       break;
     default:
-      attn_decode_partial_kernel<8><<<grid, kAttnThreads, 0, stream>>>(
+      attn_decode_partial_kernel<8><<<grid, kAttnThreads, kAttnStageBytes, stream>>>(
           qh, kh, vh, n_heads, n_kv, seq_len, chunk_len, scale, partials, pos_dev);
       break;
   }
@@ -203,6 +237,19 @@ int attn_decode_launch(mlm_ctx *ctx, const void *q, const void *kc, const void *
   attn_decode_merge_kernel<<<n_heads, kAttnD, 0, stream>>>(
       partials, n_heads, nchunks, reinterpret_cast<__half *>(out), pos_dev, chunk_len);
   return check_launch(ctx, "mlm_attn_decode (merge)");
+}
+
+// called once per context, with its device current
+int attn_init(mlm_ctx *ctx) {
+  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_partial_kernel<1>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnStageBytes));
+  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_partial_kernel<2>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnStageBytes));
+  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_partial_kernel<4>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnStageBytes));
+  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_partial_kernel<8>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnStageBytes));
+  return MLM_OK;
 }
 
 size_t attn_partial_floats_max(int max_heads) {

@@ -13,8 +13,9 @@
 // w_gate/w_up stored as one row-concatenated matrix each so that they run as
 // one GEMV; residual adds are fused into the GEMVs that produce them; RoPE
 // and the cache append are one kernel; attention is one split-sequence
-// kernel pair over the fp16 cache.  A decode step is 10 launches per layer
-// plus 6.  The hidden state stays fp32 between layers (the reference keeps
+// kernel pair over the fp16 cache; the RMSNorms and the SiLU-gated product
+// are computed inside the x staging of the GEMVs that consume them.  A
+// decode step is 6 launches per layer plus 4.  The hidden state stays fp32 between layers (the reference keeps
 // fp16); GEMV inputs are fp16 as in the reference, the SiLU-gated product
 // with a power-of-two scale per 32 elements (a plain fp16 store overflows
 // there on large activations; the reference's does).  Token, position and
@@ -71,8 +72,7 @@ struct mlm_llama {
   float *rope_freqs = nullptr;
   // activations of one step
   float *hidden = nullptr, *qkv_out = nullptr, *gu_out = nullptr, *logits = nullptr;
-  __half *xn = nullptr, *q16 = nullptr, *attn_out = nullptr, *h16 = nullptr;
-  float *h_scale = nullptr;  // [ffn_dim / 32]
+  __half *q16 = nullptr, *attn_out = nullptr;
   int *state = nullptr;
   int32_t *gen_tokens = nullptr;  // [max_seq] tokens of the captured greedy loop
   cudaGraph_t step_graph = nullptr;
@@ -94,10 +94,17 @@ struct mlm_llama {
     return MLM_OK;
   }
 
-  int gemv(const uint8_t *W, int rows, int cols, const __half *x, float *y, const float *res,
-           const float *x_scale = nullptr) {
-    return gemv_launch(ctx, W, rows, cols, x, y, res, ctx->gemv_partials, ctx->gemv_counters,
-                       ctx->gemv_max_ctas, ctx->gemv_max_tiles, ctx->stream, x_scale);
+  int gemv(const uint8_t *W, int rows, int cols, const GemvInput &in, float *y, const float *res) {
+    return gemv_launch(ctx, W, rows, cols, in, y, res, ctx->gemv_partials, ctx->gemv_counters,
+                       ctx->gemv_max_ctas, ctx->gemv_max_tiles, ctx->stream);
+  }
+  GemvInput normed(const float *h, const float *w) const {
+    GemvInput in;
+    in.mode = GemvInput::kRmsNorm;
+    in.a = h;
+    in.b = w;
+    in.eps = cfg.rms_eps;
+    return in;
   }
 
   // one decoder layer at the device position state[kPos]
@@ -107,8 +114,8 @@ struct mlm_llama {
     cudaStream_t s = ctx->stream;
     const int kvd = kvdim();
     int st;
-    if ((st = rmsnorm_f32_launch(ctx, h, L.attn_norm, nullptr, xn, 1, c.dim, c.rms_eps, s))) return st;
-    if ((st = gemv(L.qkv, qkv_rows(), c.dim, xn, qkv_out, nullptr))) return st;
+    // RMSNorm runs inside the GEMV's x staging
+    if ((st = gemv(L.qkv, qkv_rows(), c.dim, normed(h, L.attn_norm), qkv_out, nullptr))) return st;
     if ((st = rope_qk_kv_launch(ctx, qkv_out, qkv_out + c.dim, qkv_out + c.dim + kvd, rope_freqs,
                                 c.rope, c.n_heads, c.n_kv_heads, c.head_dim, q16, L.kc, L.vc, 0,
                                 s, state + kPos)))
@@ -117,14 +124,16 @@ struct mlm_llama {
                                  c.max_seq, attn_out, ctx->attn_partials,
                                  ctx->attn_partials_floats, s, state + kPos)))
       return st;
-    if ((st = gemv(L.wo, c.dim, c.dim, attn_out, h, h))) return st;  // + residual
-    if ((st = rmsnorm_f32_launch(ctx, h, L.ffn_norm, nullptr, xn, 1, c.dim, c.rms_eps, s))) return st;
-    if ((st = gemv(L.gu, 2 * c.ffn_dim, c.dim, xn, gu_out, nullptr))) return st;
-    // SiLU-gated product as fp16 with per-32 power-of-two scales (it exceeds
-    // the fp16 range on large activations)
-    if ((st = silu_mul_scaled_launch(ctx, gu_out, gu_out + c.ffn_dim, h16, h_scale, c.ffn_dim, s)))
-      return st;
-    return gemv(L.down, c.dim, c.ffn_dim, h16, h, h, h_scale);  // + residual
+    if ((st = gemv(L.wo, c.dim, c.dim, gemv_half(attn_out), h, h))) return st;  // + residual
+    if ((st = gemv(L.gu, 2 * c.ffn_dim, c.dim, normed(h, L.ffn_norm), gu_out, nullptr))) return st;
+    // the SiLU-gated product is formed in the down projection's x staging,
+    // as fp16 with per-32 power-of-two scales (it exceeds the fp16 range on
+    // large activations)
+    GemvInput sw;
+    sw.mode = GemvInput::kSwiGLU;
+    sw.a = gu_out;
+    sw.b = gu_out + c.ffn_dim;
+    return gemv(L.down, c.dim, c.ffn_dim, sw, h, h);  // + residual
   }
 
   // embedding of state[kToken], all layers; then, when `head`, the final
@@ -137,10 +146,7 @@ struct mlm_llama {
     for (int l = 0; l < cfg.n_layers; ++l)
       if ((st = layer(l, hidden))) return st;
     if (!head) return MLM_OK;
-    if ((st = rmsnorm_f32_launch(ctx, hidden, out_norm, nullptr, xn, 1, cfg.dim, cfg.rms_eps,
-                                 ctx->stream)))
-      return st;
-    if ((st = gemv(output, cfg.vocab, cfg.dim, xn, lg, nullptr))) return st;
+    if ((st = gemv(output, cfg.vocab, cfg.dim, normed(hidden, out_norm), lg, nullptr))) return st;
     return argmax_launch(ctx, lg, cfg.vocab, state + kToken, ctx->stream);
   }
 
@@ -206,10 +212,9 @@ extern "C" int mlm_llama_create(mlm_ctx *ctx, const mlm_llama_config *cfg, mlm_l
       m->alloc(&m->qkv_out, sizeof(float) * m->qkv_rows()) ||
       m->alloc(&m->gu_out, sizeof(float) * 2 * c.ffn_dim) ||
       m->alloc(&m->logits, sizeof(float) * c.vocab) ||
-      m->alloc(&m->xn, sizeof(__half) * c.dim) || m->alloc(&m->q16, sizeof(__half) * c.dim) ||
+      m->alloc(&m->q16, sizeof(__half) * c.dim) ||
       m->alloc(&m->attn_out, sizeof(__half) * c.dim) ||
-      m->alloc(&m->h16, sizeof(__half) * c.ffn_dim) ||
-      m->alloc(&m->h_scale, sizeof(float) * (c.ffn_dim / 32)) ||
+
       m->alloc(&m->state, sizeof(int) * kStateInts) ||
       m->alloc(&m->gen_tokens, sizeof(int32_t) * c.max_seq))
     return fail(MLM_ERR_ALLOC);

@@ -83,6 +83,24 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// ---- RMSNorm pieces (NormalizationKernels.metal:31-79) ---------------------
+// scale = min(1 / sqrt(max(mean(x^2), 1e-10) + eps), 1e6)
+__device__ __forceinline__ float rms_scale(float sum_sq, int n, float eps) {
+  const float mean_sq = sum_sq / (float)n;
+  const float safe = fmaxf(mean_sq, 1e-10f);
+  const float rms = sqrtf(safe + eps);
+  return fminf(1.0f / rms, 1e6f);
+}
+// NaN / Inf weights read as 1
+__device__ __forceinline__ float safe_weight(float w) {
+  return (isnan(w) || isinf(w)) ? 1.0f : w;
+}
+// SiLU-gated product of the decode FFN (kernel_silu_f16 then kernel_mul_f16,
+// ActivationKernels.metal:6-27, in fp32)
+__device__ __forceinline__ float swiglu(float g, float u) {
+  return g * (1.0f / (1.0f + expf(-g))) * u;
+}
+
 // 128-bit streaming load that does not allocate in L1 (weights are read once)
 __device__ __forceinline__ uint4 ldg_stream(const void *p) {
   uint4 r;

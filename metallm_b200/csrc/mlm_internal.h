@@ -48,10 +48,34 @@ int check_launch(mlm_ctx *ctx, const char *what);
 
 // Kernel launchers shared between translation units (stream-ordered; each
 // returns an MLM_* status and records the reason in ctx on failure).
-int gemv_validate(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x, float *y);
-int gemv_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x, float *y,
+// The x of a Q4_K GEMV, staged by the kernel into fp16 values with one scale
+// per 32-element sub-block:
+//  kHalf     x = x_f16 (times x_scale[k/32] when x_scale is set);
+//  kRmsNorm  x = fp16(a * rms_scale(a) * w): the RMSNorm of an fp32 hidden
+//            state a with fp32 weights b (NormalizationKernels.metal:31-79),
+//            computed by every CTA, so no separate norm kernel runs;
+//  kSwiGLU   x = silu(a) * b from fp32 gate a and up b, stored with a
+//            power-of-two scale per 32 elements.
+struct GemvInput {
+  enum Mode { kHalf = 0, kRmsNorm = 1, kSwiGLU = 2 };
+  int mode = kHalf;
+  const void *x_f16 = nullptr;
+  const float *x_scale = nullptr;
+  const float *a = nullptr;
+  const float *b = nullptr;
+  float eps = 0.f;
+};
+inline GemvInput gemv_half(const void *x, const float *x_scale = nullptr) {
+  GemvInput in;
+  in.x_f16 = x;
+  in.x_scale = x_scale;
+  return in;
+}
+int gemv_validate(mlm_ctx *ctx, const void *W, int rows, int cols, const GemvInput &in,
+                  float *y);
+int gemv_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const GemvInput &in, float *y,
                 const float *residual, float *partials, int *counters, int max_ctas,
-                int max_tiles, cudaStream_t stream, const float *x_scale);
+                int max_tiles, cudaStream_t stream);
 int rmsnorm_f32_launch(mlm_ctx *ctx, const float *x, const float *w, float *y32, void *y16,
                        int rows, int n, float eps, cudaStream_t stream);
 int rope_qk_kv_launch(mlm_ctx *ctx, const float *q, const float *k, const float *v,

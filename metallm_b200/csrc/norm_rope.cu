@@ -19,13 +19,6 @@ namespace mlm {
 
 // ---- RMSNorm ------------------------------------------------------------------
 
-__device__ __forceinline__ float rms_scale(float sum_sq, int n, float eps) {
-  const float mean_sq = sum_sq / (float)n;
-  const float safe = fmaxf(mean_sq, 1e-10f);
-  const float rms = sqrtf(safe + eps);
-  return fminf(1.0f / rms, 1e6f);
-}
-
 __device__ __forceinline__ float block_sum(float v, float *red) {
   v = warp_sum(v);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -35,10 +28,6 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
   float s = 0.f;
   for (int i = 0; i < nw; ++i) s += red[i];
   return s;
-}
-
-__device__ __forceinline__ float safe_weight(float w) {
-  return (isnan(w) || isinf(w)) ? 1.0f : w;
 }
 
 __global__ void __launch_bounds__(256) rmsnorm_f16_kernel(const __half *__restrict__ x,
@@ -204,9 +193,7 @@ __global__ void silu_mul_kernel(const float *__restrict__ g, const float *__rest
                                 __half *__restrict__ out, int n) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
-  const float x = g[i];
-  const float sig = 1.0f / (1.0f + expf(-x));
-  out[i] = __float2half_rn(x * sig * u[i]);
+  out[i] = __float2half_rn(swiglu(g[i], u[i]));
 }
 
 // The same product stored as fp16 with one power-of-two scale per 32
@@ -219,9 +206,7 @@ __global__ void silu_mul_scaled_kernel(const float *__restrict__ g, const float 
                                        int n) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;  // whole warps: n % 32 == 0
-  const float x = g[i];
-  const float sig = 1.0f / (1.0f + expf(-x));
-  const float h = x * sig * u[i];
+  const float h = swiglu(g[i], u[i]);
   const float m = warp_max(fabsf(h));
   const int e = max(0, (int)((__float_as_uint(m) >> 23) & 0xFF) - 127 - 14);
   out[i] = __float2half_rn(h * __uint_as_float((uint32_t)(127 - e) << 23));

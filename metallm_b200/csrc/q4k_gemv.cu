@@ -64,6 +64,9 @@ struct GemvArgs {
   const uint8_t *W;
   const __half *x;
   const float *x_scale;  // per 32-element sub-block of x (NULL: 1)
+  const float *xa, *xb;  // fp32 sources of x in the kRmsNorm / kSwiGLU modes
+  float eps;
+  int x_mode;            // GemvInput::Mode
   float *y;
   const float *residual;
   float *partials;  // [ctas][2][32]
@@ -187,43 +190,105 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1)
   asm volatile("griddepcontrol.launch_dependents;");
 
   // ---- x -> shared memory, permuted, plus per-sub-block sums ---------------
+  // Group i = elements 8i .. 8i+7 of x as eight fp16 values v and the scale
+  // sc of its sub-block (x = v * sc).  Four consecutive lanes hold the four
+  // groups of a sub-block; ngroups is a multiple of 32, so whole warps take
+  // part in the shuffles.
   {
-    const uint4 *xg = reinterpret_cast<const uint4 *>(p.x);
-    const int ngroups = p.nb * 32;  // multiple of 32: whole warps stay converged
-    constexpr int XB = 8;           // x loads in flight per thread
+    const int ngroups = p.nb * 32;
     if (threadIdx.x < 4) xzero[threadIdx.x] = make_uint4(0, 0, 0, 0);
     for (int i = threadIdx.x; i < p.ntile; i += blockDim.x) tile_done[i] = 0;
-    for (int base = threadIdx.x; base < ngroups; base += XB * blockDim.x) {
-      uint4 xv[XB];
-#pragma unroll
-      for (int u = 0; u < XB; ++u) {
-        const int i = base + u * blockDim.x;
-        if (i < ngroups) xv[u] = __ldg(xg + i);
+    auto stage = [&](int i, const uint4 v, float sc) {
+      uint4 o;
+      o.x = __byte_perm(v.x, v.z, 0x5410);  // (x0, x4)
+      o.y = __byte_perm(v.y, v.w, 0x5410);  // (x2, x6)
+      o.z = __byte_perm(v.x, v.z, 0x7632);  // (x1, x5)
+      o.w = __byte_perm(v.y, v.w, 0x7632);  // (x3, x7)
+      xperm[i] = o;
+      const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&v.x));
+      const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&v.y));
+      const float2 f2 = __half22float2(*reinterpret_cast<const __half2 *>(&v.z));
+      const float2 f3 = __half22float2(*reinterpret_cast<const __half2 *>(&v.w));
+      float sx = ((f0.x + f0.y) + (f1.x + f1.y)) + ((f2.x + f2.y) + (f3.x + f3.y));
+      sx += __shfl_xor_sync(0xffffffffu, sx, 1);
+      sx += __shfl_xor_sync(0xffffffffu, sx, 2);
+      if ((i & 3) == 0) {
+        xsum[i >> 2] = sx * sc;
+        xscl[i >> 2] = sc;
       }
+    };
+    auto pack = [](const float (&f)[8]) {
+      uint4 v;
+      __half2 h;
+      h = __floats2half2_rn(f[0], f[1]); v.x = *reinterpret_cast<uint32_t *>(&h);
+      h = __floats2half2_rn(f[2], f[3]); v.y = *reinterpret_cast<uint32_t *>(&h);
+      h = __floats2half2_rn(f[4], f[5]); v.z = *reinterpret_cast<uint32_t *>(&h);
+      h = __floats2half2_rn(f[6], f[7]); v.w = *reinterpret_cast<uint32_t *>(&h);
+      return v;
+    };
+    auto load8 = [](const float *src, int i, float (&f)[8]) {
+      const float4 a = __ldg(reinterpret_cast<const float4 *>(src) + 2 * i);
+      const float4 b = __ldg(reinterpret_cast<const float4 *>(src) + 2 * i + 1);
+      f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+      f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+    };
+    if (p.x_mode == GemvInput::kHalf) {
+      const uint4 *xg = reinterpret_cast<const uint4 *>(p.x);
+      constexpr int XB = 8;  // x loads in flight per thread
+      for (int base = threadIdx.x; base < ngroups; base += XB * blockDim.x) {
+        uint4 xv[XB];
 #pragma unroll
-      for (int u = 0; u < XB; ++u) {
-        const int i = base + u * blockDim.x;
-        if (i < ngroups) {
-          const uint4 v = xv[u];
-          uint4 o;
-          o.x = __byte_perm(v.x, v.z, 0x5410);  // (x0, x4)
-          o.y = __byte_perm(v.y, v.w, 0x5410);  // (x2, x6)
-          o.z = __byte_perm(v.x, v.z, 0x7632);  // (x1, x5)
-          o.w = __byte_perm(v.y, v.w, 0x7632);  // (x3, x7)
-          xperm[i] = o;
-          const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&v.x));
-          const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&v.y));
-          const float2 f2 = __half22float2(*reinterpret_cast<const __half2 *>(&v.z));
-          const float2 f3 = __half22float2(*reinterpret_cast<const __half2 *>(&v.w));
-          float sx = ((f0.x + f0.y) + (f1.x + f1.y)) + ((f2.x + f2.y) + (f3.x + f3.y));
-          sx += __shfl_xor_sync(0xffffffffu, sx, 1);
-          sx += __shfl_xor_sync(0xffffffffu, sx, 2);
-          if ((i & 3) == 0) {
-            const float sc = p.x_scale ? p.x_scale[i >> 2] : 1.0f;
-            xsum[i >> 2] = sx * sc;
-            xscl[i >> 2] = sc;
-          }
+        for (int u = 0; u < XB; ++u) {
+          const int i = base + u * blockDim.x;
+          if (i < ngroups) xv[u] = __ldg(xg + i);
         }
+#pragma unroll
+        for (int u = 0; u < XB; ++u) {
+          const int i = base + u * blockDim.x;
+          if (i < ngroups) stage(i, xv[u], p.x_scale ? p.x_scale[i >> 2] : 1.0f);
+        }
+      }
+    } else if (p.x_mode == GemvInput::kRmsNorm) {
+      // every CTA reduces the sum of squares of the whole hidden state itself
+      float ss = 0.f;
+      const float4 *a4 = reinterpret_cast<const float4 *>(p.xa);
+      for (int k = threadIdx.x; k < ngroups * 2; k += blockDim.x) {
+        const float4 v = __ldg(a4 + k);
+        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+      }
+      ss = warp_sum(ss);
+      float *red = parts;  // free until the main loop
+      if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+      __syncthreads();
+      float tot = 0.f;
+      for (int w = 0; w < nwarps; ++w) tot += red[w];
+      const float scale = rms_scale(tot, ngroups * 8, p.eps);
+      for (int i = threadIdx.x; i < ngroups; i += blockDim.x) {
+        float a[8], w[8];
+        load8(p.xa, i, a);
+        load8(p.xb, i, w);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) a[e] = (a[e] * scale) * safe_weight(w[e]);
+        stage(i, pack(a), 1.0f);
+      }
+    } else {  // kSwiGLU, with a power-of-two scale per sub-block
+      for (int i = threadIdx.x; i < ngroups; i += blockDim.x) {
+        float g[8], u[8];
+        load8(p.xa, i, g);
+        load8(p.xb, i, u);
+        float m = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          g[e] = swiglu(g[e], u[e]);
+          m = fmaxf(m, fabsf(g[e]));
+        }
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+        const int ex = max(0, (int)((__float_as_uint(m) >> 23) & 0xFF) - 127 - 14);
+        const float inv = __uint_as_float((uint32_t)(127 - ex) << 23);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) g[e] *= inv;
+        stage(i, pack(g), __uint_as_float((uint32_t)(127 + ex) << 23));
       }
     }
   }
@@ -506,9 +571,9 @@ static int encode_weight_map(mlm_ctx *ctx, const void *W, int rows, int nb, CUte
   return MLM_OK;
 }
 
-int gemv_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x, float *y,
+int gemv_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const GemvInput &in, float *y,
                 const float *residual, float *partials, int *counters, int max_ctas,
-                int max_tiles, cudaStream_t stream, const float *x_scale) {
+                int max_tiles, cudaStream_t stream) {
   const int nb = cols / kQK;
   const int tiles = (rows + kTileRows - 1) / kTileRows;
   MLM_REQUIRE(ctx, tiles <= max_tiles, MLM_ERR_SHAPE,
@@ -524,8 +589,12 @@ int gemv_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x, 
   if (st != MLM_OK) return st;
   GemvArgs a;
   a.W = reinterpret_cast<const uint8_t *>(W);
-  a.x = reinterpret_cast<const __half *>(x);
-  a.x_scale = x_scale;
+  a.x = reinterpret_cast<const __half *>(in.x_f16);
+  a.x_scale = in.x_scale;
+  a.xa = in.a;
+  a.xb = in.b;
+  a.eps = in.eps;
+  a.x_mode = in.mode;
   a.y = y;
   a.residual = residual;
   a.partials = partials;
@@ -557,13 +626,18 @@ int gemv_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x, 
   return MLM_OK;
 }
 
-int gemv_validate(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x, float *y) {
-  MLM_REQUIRE(ctx, W && x && y, MLM_ERR_ARG, "mlm_q4k_gemv: null buffer");
+int gemv_validate(mlm_ctx *ctx, const void *W, int rows, int cols, const GemvInput &in,
+                  float *y) {
+  const bool half = in.mode == GemvInput::kHalf;
+  const void *x = half ? in.x_f16 : in.a;
+  MLM_REQUIRE(ctx, W && x && y && (half || in.b), MLM_ERR_ARG, "mlm_q4k_gemv: null buffer");
+  MLM_REQUIRE(ctx, half || (aligned16(in.a) && aligned16(in.b)), MLM_ERR_ALIGN,
+              "mlm_q4k_gemv: fp32 inputs must be 16-byte aligned");
   MLM_REQUIRE(ctx, rows > 0 && cols > 0, MLM_ERR_SHAPE, "mlm_q4k_gemv: rows=%d cols=%d", rows,
               cols);
   MLM_REQUIRE(ctx, cols % kQK == 0, MLM_ERR_SHAPE,
               "mlm_q4k_gemv: cols=%d is not a multiple of the 256-element super-block", cols);
-  MLM_REQUIRE(ctx, aligned16(W) && aligned16(x), MLM_ERR_ALIGN,
+  MLM_REQUIRE(ctx, aligned16(W) && (!half || aligned16(x)), MLM_ERR_ALIGN,
               "mlm_q4k_gemv: W and x must be 16-byte aligned");
   return MLM_OK;
 }
@@ -572,25 +646,45 @@ int gemv_validate(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x
 
 using namespace mlm;
 
+static int gemv_entry(mlm_ctx *ctx, const void *W, int rows, int cols, const GemvInput &in,
+                      float *y, const float *residual) {
+  MLM_CHECK_CTX(ctx);
+  int st = gemv_validate(ctx, W, rows, cols, in, y);
+  if (st != MLM_OK) return st;
+  return gemv_launch(ctx, W, rows, cols, in, y, residual, ctx->gemv_partials,
+                     ctx->gemv_counters, ctx->gemv_max_ctas, ctx->gemv_max_tiles, ctx->stream);
+}
+
 extern "C" int mlm_q4k_gemv(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_f16,
                             float *y, const float *residual) {
-  MLM_CHECK_CTX(ctx);
-  int st = gemv_validate(ctx, W, rows, cols, x_f16, y);
-  if (st != MLM_OK) return st;
-  return gemv_launch(ctx, W, rows, cols, x_f16, y, residual, ctx->gemv_partials,
-                     ctx->gemv_counters, ctx->gemv_max_ctas, ctx->gemv_max_tiles, ctx->stream,
-                     nullptr);
+  return gemv_entry(ctx, W, rows, cols, gemv_half(x_f16), y, residual);
 }
 
 extern "C" int mlm_q4k_gemv_xs(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_f16,
                                const float *x_scale, float *y, const float *residual) {
-  MLM_CHECK_CTX(ctx);
-  int st = gemv_validate(ctx, W, rows, cols, x_f16, y);
-  if (st != MLM_OK) return st;
-  MLM_REQUIRE(ctx, x_scale, MLM_ERR_ARG, "mlm_q4k_gemv_xs: null x_scale");
-  return gemv_launch(ctx, W, rows, cols, x_f16, y, residual, ctx->gemv_partials,
-                     ctx->gemv_counters, ctx->gemv_max_ctas, ctx->gemv_max_tiles, ctx->stream,
-                     x_scale);
+  if (ctx && !x_scale) return set_error(ctx, MLM_ERR_ARG, "mlm_q4k_gemv_xs: null x_scale");
+  return gemv_entry(ctx, W, rows, cols, gemv_half(x_f16, x_scale), y, residual);
+}
+
+extern "C" int mlm_q4k_gemv_rmsnorm(mlm_ctx *ctx, const void *W, int rows, int cols,
+                                    const float *hidden, const float *norm_w, float eps,
+                                    float *y, const float *residual) {
+  GemvInput in;
+  in.mode = GemvInput::kRmsNorm;
+  in.a = hidden;
+  in.b = norm_w;
+  in.eps = eps;
+  return gemv_entry(ctx, W, rows, cols, in, y, residual);
+}
+
+extern "C" int mlm_q4k_gemv_swiglu(mlm_ctx *ctx, const void *W, int rows, int cols,
+                                   const float *gate, const float *up, float *y,
+                                   const float *residual) {
+  GemvInput in;
+  in.mode = GemvInput::kSwiGLU;
+  in.a = gate;
+  in.b = up;
+  return gemv_entry(ctx, W, rows, cols, in, y, residual);
 }
 
 // ---------------------------------------------------------------------------
@@ -661,7 +755,7 @@ static int gemv_static_scratch(mlm_ctx *ctx, void **out) {
 extern "C" int mlm_q4k_gemv_static(mlm_ctx *ctx, const void *W, int rows, int cols,
                                    const void *x_f16, float *y, const float *residual) {
   MLM_CHECK_CTX(ctx);
-  int st = mlm::gemv_validate(ctx, W, rows, cols, x_f16, y);
+  int st = mlm::gemv_validate(ctx, W, rows, cols, mlm::gemv_half(x_f16), y);
   if (st != MLM_OK) return st;
   MLM_REQUIRE(ctx, rows <= mlm::kStaticMaxRows, MLM_ERR_SHAPE,
               "mlm_q4k_gemv_static: rows=%d exceeds the static scratch limit of %d rows", rows,
@@ -674,6 +768,6 @@ extern "C" int mlm_q4k_gemv_static(mlm_ctx *ctx, const void *W, int rows, int co
       reinterpret_cast<int *>(reinterpret_cast<unsigned char *>(scratch) + mlm::kStaticPartialBytes);
   const int tiles = (rows + mlm::kTileRows - 1) / mlm::kTileRows;
   MLM_CUDA_TRY(ctx, cudaMemsetAsync(counters, 0, sizeof(int) * (size_t)tiles, ctx->stream));
-  return mlm::gemv_launch(ctx, W, rows, cols, x_f16, y, residual, partials, counters,
-                          mlm::kStaticMaxCtas, mlm::kStaticMaxTiles, ctx->stream, nullptr);
+  return mlm::gemv_launch(ctx, W, rows, cols, mlm::gemv_half(x_f16), y, residual, partials,
+                          counters, mlm::kStaticMaxCtas, mlm::kStaticMaxTiles, ctx->stream);
 }

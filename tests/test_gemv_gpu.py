@@ -6,6 +6,8 @@ dequantized weights).
 """
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
 import pytest
 
@@ -162,3 +164,37 @@ def test_gemv_scaled_x(ctx):
     xtrue = x16.astype(np.float32) * np.repeat(scale, 32)
     ref = O.q4k_matvec_f32x(O.gen_q4k(21, 1, nb), rows, cols, xtrue) + O.gen_f32(21, 3, rows)
     assert rel_l2(y.download(np.float32), ref) < TOL
+
+
+def test_gemv_rmsnorm_input(ctx):
+    """x = fp16(RMSNorm(hidden)) formed inside the GEMV."""
+    rows, cols = 6144, 4096
+    nb = rows * cols // 256
+    W = ctx.alloc(nb * 144)
+    ctx.gen_q4k(23, 1, nb, W)
+    h = O.gen_f32(23, 2, cols, 0.0, 3.0)
+    w = O.gen_f32(23, 3, cols, 1.0, 0.02)
+    y = ctx.alloc(4 * rows)
+    ctx.call("mlm_q4k_gemv_rmsnorm", W, rows, cols, ctx.to_device(h), ctx.to_device(w),
+             ctypes.c_float(1e-5), y, None)
+    xn = O.rmsnorm_f32(h, w, 1, cols, 1e-5).astype(np.float16)
+    ref = O.q4k_matvec(O.gen_q4k(23, 1, nb), rows, cols, xn, acc64=True)
+    assert rel_l2(y.download(np.float32), ref) < TOL
+
+
+def test_gemv_swiglu_input(ctx):
+    """x = silu(gate) * up formed inside the GEMV (large values: scaled fp16)."""
+    rows, cols = 4096, 14336
+    nb = rows * cols // 256
+    W = ctx.alloc(nb * 144)
+    ctx.gen_q4k(24, 1, nb, W)
+    g = O.gen_f32(24, 2, cols, 0.0, 200.0)
+    u = O.gen_f32(24, 3, cols, 0.0, 200.0)
+    r = O.gen_f32(24, 4, rows)
+    y = ctx.alloc(4 * rows)
+    ctx.call("mlm_q4k_gemv_swiglu", W, rows, cols, ctx.to_device(g), ctx.to_device(u), y,
+             ctx.to_device(r))
+    ref = O.q4k_matvec_f32x(O.gen_q4k(24, 1, nb), rows, cols, O.silu_mul(g, u)) + r
+    got = y.download(np.float32)
+    assert np.all(np.isfinite(got))
+    assert rel_l2(got, ref) < 1e-3  # x rounded to fp16 (2^-11 per element)

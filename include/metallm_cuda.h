@@ -167,6 +167,17 @@ int mlm_q4k_gemv_rmsnorm(mlm_ctx *ctx, const void *W, int rows, int cols, const 
 int mlm_q4k_gemv_swiglu(mlm_ctx *ctx, const void *W, int rows, int cols, const float *gate,
                         const float *up, float *y, const float *residual);
 
+/* Prefill GEMM on packed Q4_K weights: y[t][n] = sum_k x[t][k] * W[n][k] for
+ * `tokens` rows of x at once (bf16 [tokens][cols] row-major; y fp32
+ * [tokens][rows]).  The reference has no batched prefill: it runs forward()
+ * per prompt token with encodeMPSMatrixMultiply on fp16 weights
+ * (MetalService.swift:797-925).  W (GGUF layout) is dequantized tile by tile
+ * to bf16 in shared memory and multiplied on the tensor cores (tcgen05, fp32
+ * accumulation).  cols % 256 == 0; W and x 16-byte aligned.  Narrow weights
+ * split K over CTAs and add into y with fp32 atomics (y is zeroed first). */
+int mlm_q4k_gemm(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_bf16,
+                 int tokens, float *y);
+
 /* Tiled Q4_K layout: the same 144-byte blocks, reordered once after upload
  * so that the decode GEMV streams them as contiguous 4608-byte units (32
  * rows of one block column, laid out in the GEMV's register order; rows past

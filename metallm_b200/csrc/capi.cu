@@ -21,6 +21,7 @@ namespace mlm {
 int gemv_init(mlm_ctx *ctx);
 int gemv_tiled_init(mlm_ctx *ctx);
 int attn_init(mlm_ctx *ctx);
+int gemm_init(mlm_ctx *ctx);
 int gemv_max_ctas(int sm_count);
 size_t attn_partial_floats_max(int max_heads);
 
@@ -126,7 +127,8 @@ extern "C" int mlm_create(int device, mlm_ctx **out) {
     if (cudaHostGetDevicePointer(reinterpret_cast<void **>(&ctx->dev_status), hs, 0) != cudaSuccess)
       return fail(MLM_ERR_CUDA);
   }
-  if (gemv_init(ctx) != MLM_OK || gemv_tiled_init(ctx) != MLM_OK || attn_init(ctx) != MLM_OK)
+  if (gemv_init(ctx) != MLM_OK || gemv_tiled_init(ctx) != MLM_OK || attn_init(ctx) != MLM_OK ||
+      gemm_init(ctx) != MLM_OK)
     return fail(MLM_ERR_CUDA);
   if (cudaDeviceSynchronize() != cudaSuccess) return fail(MLM_ERR_CUDA);
   *out = ctx;

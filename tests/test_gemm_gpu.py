@@ -1,0 +1,61 @@
+"""Prefill Q4_K GEMM on the tensor cores (mlm_q4k_gemm), through the C ABI.
+
+Bar: relative L2 <= 2e-3 against a float64 product of the same bf16
+operands (the exact fp32 dequantization rounded to bf16, x in bf16).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tests.conftest import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-3
+
+
+def bf16_bits(x: np.ndarray) -> np.ndarray:
+    """fp32 -> bf16 (round to nearest even), as uint16 bit patterns."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    u = u + 0x7FFF + ((u >> 16) & 1)
+    return (u >> 16).astype(np.uint16)
+
+
+def bf16_value(bits: np.ndarray) -> np.ndarray:
+    return (bits.astype(np.uint32) << 16).view(np.float32)
+
+
+def _run(ctx, rows, cols, tokens, seed=5):
+    nb = rows * cols // 256
+    blocks = O.gen_q4k(seed, 1, nb)
+    xb = bf16_bits(O.gen_f32(seed, 2, tokens * cols))
+    y = ctx.alloc(4 * rows * tokens)
+    ctx.call("mlm_q4k_gemm", ctx.to_device(blocks), rows, cols, ctx.to_device(xb), tokens, y)
+    got = y.download(np.float32, rows * tokens).reshape(tokens, rows)
+    w = bf16_value(bf16_bits(O.q4k_dequant_f32(blocks, rows * cols))).reshape(rows, cols)
+    x = bf16_value(xb).reshape(tokens, cols)
+    ref = x.astype(np.float64) @ w.astype(np.float64).T
+    return got, ref
+
+
+@pytest.mark.parametrize("rows,cols,tokens", [(128, 256, 512), (256, 1024, 512), (200, 768, 100),
+                                              (4096, 4096, 512), (1000, 2048, 1300),
+                                              (6144, 4096, 64)])
+def test_gemm_shapes(ctx, rows, cols, tokens):
+    got, ref = _run(ctx, rows, cols, tokens)
+    assert np.all(np.isfinite(got))
+    err = rel_l2(got, ref)
+    assert err < TOL, (rows, cols, tokens, err)
+
+
+def test_gemm_bad_args(ctx):
+    from metallm_b200 import MLMError
+    buf = ctx.alloc(1 << 16)
+    with pytest.raises(MLMError) as e:
+        ctx.call("mlm_q4k_gemm", buf, 128, 300, buf, 16, buf)
+    assert e.value.status == -2
+    with pytest.raises(MLMError) as e:
+        ctx.call("mlm_q4k_gemm", buf.ptr + 8, 128, 256, buf, 16, buf)
+    assert e.value.status == -3

@@ -174,9 +174,11 @@ int mlm_q4k_gemv_swiglu(mlm_ctx *ctx, const void *W, int rows, int cols, const f
  * (MetalService.swift:797-925).  W (GGUF layout) is dequantized tile by tile
  * to bf16 in shared memory and multiplied on the tensor cores (tcgen05, fp32
  * accumulation).  cols % 256 == 0; W and x 16-byte aligned.  Narrow weights
- * split K over CTAs and add into y with fp32 atomics (y is zeroed first). */
+ * split K over CTAs and add into y with fp32 atomics (y starts from the
+ * residual, or zero).  residual (fp32 [tokens][rows], may be y itself) is
+ * added when not NULL. */
 int mlm_q4k_gemm(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_bf16,
-                 int tokens, float *y);
+                 int tokens, float *y, const float *residual);
 
 /* Tiled Q4_K layout: the same 144-byte blocks, reordered once after upload
  * so that the decode GEMV streams them as contiguous 4608-byte units (32
@@ -355,10 +357,14 @@ int mlm_llama_forward_layer(mlm_llama *m, int layer, float *hidden);
  * MLM_ERR_STATE when the cache is full, MLM_ERR_ARG for a bad token id. */
 int mlm_llama_forward(mlm_llama *m, int token, float *logits);
 
-/* The prompt: forward() over tokens[0..n) (host array) without the output
- * head except for the last token; its greedy next token goes to
- * *next_token_dev (device, may be NULL). */
-int mlm_llama_prefill(mlm_llama *m, const int32_t *tokens, int n, int32_t *next_token_dev);
+/* The prompt (the reference calls forward() once per token): tokens[0..n)
+ * (host array) at the current position, run batched on the tensor-core GEMM
+ * (mlm_q4k_gemm; bf16 activations) in chunks of up to 1024 tokens, the KV
+ * caches filled; then the output head on the last token: its fp32 logits go
+ * to `logits` (device, may be NULL) and its greedy next token to
+ * *next_token_dev (device, may be NULL).  Advances the position by n. */
+int mlm_llama_prefill(mlm_llama *m, const int32_t *tokens, int n, float *logits,
+                      int32_t *next_token_dev);
 
 /* Greedy generation (the sampling loop of ContentView.swift:124-146 with the
  * argmax on the device): starting from `token` at the current position,

@@ -9,6 +9,7 @@ goes through the C ABI; there is no CPU fallback.
 from __future__ import annotations
 
 import ctypes
+import weakref
 from typing import Optional, Sequence
 
 import numpy as np
@@ -74,9 +75,14 @@ class Context:
                                f"({self.lib.mlm_status_string(st).decode()})")
         self.handle = h
         self.device = device
+        # runners made on this context; closed before the context itself so
+        # that no runner outlives the stream and scratch it uses
+        self._runners = weakref.WeakSet()
 
     def close(self) -> None:
         if self.handle:
+            for r in list(self._runners):
+                r.close()
             self.lib.mlm_destroy(self.handle)
             self.handle = None
 
@@ -214,6 +220,7 @@ class Llama:
         ctx._check(ctx.lib.mlm_llama_create(ctx.handle, ctypes.byref(cfg), ctypes.byref(h)),
                    "mlm_llama_create")
         self.handle = h
+        ctx._runners.add(self)
 
     def _check(self, st: int, what: str) -> None:
         self.ctx._check(st, what)
@@ -250,10 +257,11 @@ class Llama:
             self.handle, token, ctypes.c_void_p(int(logits)) if logits is not None else None),
             "mlm_llama_forward")
 
-    def prefill(self, tokens: Sequence[int], next_token=None) -> None:
+    def prefill(self, tokens: Sequence[int], next_token=None, logits=None) -> None:
         arr = (ctypes.c_int32 * len(tokens))(*[int(t) for t in tokens])
         self._check(self.ctx.lib.mlm_llama_prefill(
             self.handle, arr, len(tokens),
+            ctypes.c_void_p(int(logits)) if logits is not None else None,
             ctypes.c_void_p(int(next_token)) if next_token is not None else None),
             "mlm_llama_prefill")
 
@@ -263,9 +271,9 @@ class Llama:
                     "mlm_llama_decode_greedy")
 
     def close(self) -> None:
-        if self.handle:
+        if self.handle and self.ctx.handle:
             self.ctx.lib.mlm_llama_destroy(self.handle)
-            self.handle = None
+        self.handle = None
 
     def __del__(self):
         try:

@@ -94,7 +94,7 @@ SIGNATURES = [
     ("mlm_q4k_gemv_xs", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_vp]),
     ("mlm_q4k_gemv_rmsnorm", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_float, c_vp, c_vp]),
     ("mlm_q4k_gemv_swiglu", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_vp]),
-    ("mlm_q4k_gemm", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_int, c_vp]),
+    ("mlm_q4k_gemm", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_int, c_vp, c_vp]),
     ("mlm_q4k_gemv_static", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_vp]),
     ("mlm_q4k_tiled_bytes", ctypes.c_size_t, [c_int, c_int]),
     ("mlm_q4k_tile", c_int, [c_vp, c_vp, c_int, c_int, c_vp]),
@@ -119,7 +119,7 @@ SIGNATURES = [
     ("mlm_llama_position", c_int, [c_vp]),
     ("mlm_llama_forward_layer", c_int, [c_vp, c_int, c_vp]),
     ("mlm_llama_forward", c_int, [c_vp, c_int, c_vp]),
-    ("mlm_llama_prefill", c_int, [c_vp, ctypes.POINTER(ctypes.c_int32), c_int, c_vp]),
+    ("mlm_llama_prefill", c_int, [c_vp, ctypes.POINTER(ctypes.c_int32), c_int, c_vp, c_vp]),
     ("mlm_llama_decode_greedy", c_int, [c_vp, c_int, c_int, c_vp]),
 ]
 

@@ -20,9 +20,14 @@
 // with a power-of-two scale per 32 elements (a plain fp16 store overflows
 // there on large activations; the reference's does).  Token, position and
 // step counter live in device memory, so a step is captured once as a CUDA
-// graph and replayed for every generated token.
+// graph and replayed for every generated token.  The prompt runs batched:
+// per layer, RMSNorm rows, the tensor-core Q4_K GEMM for the fused QKV, RoPE
+// with the cache append, causal attention over the cache, the GEMM for the
+// output projection (residual added), RMSNorm, the gate/up GEMM, SiLU-gated
+// product and the down GEMM (residual added), in chunks of up to 1024 tokens.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <new>
 #include <vector>
 
@@ -75,6 +80,11 @@ struct mlm_llama {
   __half *q16 = nullptr, *attn_out = nullptr;
   int *state = nullptr;
   int32_t *gen_tokens = nullptr;  // [max_seq] tokens of the captured greedy loop
+  // batched prompt pass: activations of up to pf_chunk tokens
+  int pf_chunk = 0;
+  float *pf_hidden = nullptr, *pf_qkv = nullptr, *pf_gu = nullptr;
+  void *pf_x = nullptr, *pf_q16 = nullptr, *pf_attn = nullptr;  // bf16 / fp16 / bf16
+  int32_t *pf_tokens = nullptr;
   cudaGraph_t step_graph = nullptr;
   cudaGraphExec_t step_exec = nullptr;
   std::vector<void *> allocs;
@@ -150,6 +160,35 @@ struct mlm_llama {
     return argmax_launch(ctx, lg, cfg.vocab, state + kToken, ctx->stream);
   }
 
+  // T prompt tokens (device ids in pf_tokens) at positions pos .. pos+T-1:
+  // every layer on the tensor-core GEMM; leaves the hidden rows in pf_hidden
+  int prefill_chunk(int T) {
+    const mlm_llama_config &c = cfg;
+    cudaStream_t s = ctx->stream;
+    int st;
+    if ((st = embed_rows_launch(ctx, tok_embd, c.vocab, c.dim, pf_tokens, T, pf_hidden, s))) return st;
+    for (int l = 0; l < c.n_layers; ++l) {
+      const LayerBuf &L = layers[l];
+      if ((st = rmsnorm_rows_bf16_launch(ctx, pf_hidden, L.attn_norm, pf_x, T, c.dim, c.rms_eps, s)))
+        return st;
+      if ((st = gemm_launch(ctx, L.qkv, qkv_rows(), c.dim, pf_x, T, pf_qkv, nullptr, s))) return st;
+      if ((st = rope_kv_rows_launch(ctx, pf_qkv, rope_freqs, c.rope, c.n_heads, c.n_kv_heads,
+                                    c.head_dim, pos, T, pf_q16, L.kc, L.vc, s)))
+        return st;
+      if ((st = attn_prefill_launch(ctx, pf_q16, L.kc, L.vc, pos, T, c.n_heads, c.n_kv_heads,
+                                    c.head_dim, pf_attn, s)))
+        return st;
+      if ((st = gemm_launch(ctx, L.wo, c.dim, c.dim, pf_attn, T, pf_hidden, pf_hidden, s))) return st;
+      if ((st = rmsnorm_rows_bf16_launch(ctx, pf_hidden, L.ffn_norm, pf_x, T, c.dim, c.rms_eps, s)))
+        return st;
+      if ((st = gemm_launch(ctx, L.gu, 2 * c.ffn_dim, c.dim, pf_x, T, pf_gu, nullptr, s))) return st;
+      if ((st = swiglu_rows_bf16_launch(ctx, pf_gu, c.ffn_dim, T, pf_x, s))) return st;
+      if ((st = gemm_launch(ctx, L.down, c.dim, c.ffn_dim, pf_x, T, pf_hidden, pf_hidden, s)))
+        return st;
+    }
+    return MLM_OK;
+  }
+
   int set_state(int token, int p, int stp) {
     set_state_kernel<<<1, 1, 0, ctx->stream>>>(state, token, p, stp);
     return check_launch(ctx, "mlm_llama (state)");
@@ -218,6 +257,17 @@ extern "C" int mlm_llama_create(mlm_ctx *ctx, const mlm_llama_config *cfg, mlm_l
       m->alloc(&m->state, sizeof(int) * kStateInts) ||
       m->alloc(&m->gen_tokens, sizeof(int32_t) * c.max_seq))
     return fail(MLM_ERR_ALLOC);
+  m->pf_chunk = std::min(c.max_seq, 1024);
+  {
+    const size_t T = m->pf_chunk;
+    const size_t xw = std::max(c.dim, c.ffn_dim);
+    if (m->alloc(&m->pf_hidden, sizeof(float) * T * c.dim) ||
+        m->alloc(&m->pf_qkv, sizeof(float) * T * m->qkv_rows()) ||
+        m->alloc(&m->pf_gu, sizeof(float) * T * 2 * c.ffn_dim) ||
+        m->alloc(&m->pf_x, 2 * T * xw) || m->alloc(&m->pf_q16, 2 * T * c.dim) ||
+        m->alloc(&m->pf_attn, 2 * T * c.dim) || m->alloc(&m->pf_tokens, sizeof(int32_t) * T))
+      return fail(MLM_ERR_ALLOC);
+  }
   if (cudaMemsetAsync(m->state, 0, sizeof(int) * kStateInts, ctx->stream) != cudaSuccess)
     return fail(set_error(ctx, MLM_ERR_CUDA, "mlm_llama_create: memset failed"));
   *out = m;
@@ -300,24 +350,35 @@ extern "C" int mlm_llama_forward(mlm_llama *m, int token, float *logits) {
   return st;
 }
 
-extern "C" int mlm_llama_prefill(mlm_llama *m, const int32_t *tokens, int n, int32_t *next) {
+extern "C" int mlm_llama_prefill(mlm_llama *m, const int32_t *tokens, int n, float *logits,
+                                 int32_t *next) {
   if (!m) return MLM_ERR_ARG;
-  MLM_REQUIRE(m->ctx, tokens && n > 0, MLM_ERR_ARG, "mlm_llama_prefill: no tokens");
-  MLM_REQUIRE(m->ctx, m->pos + n <= m->cfg.max_seq, MLM_ERR_STATE,
+  mlm_ctx *ctx = m->ctx;
+  MLM_REQUIRE(ctx, tokens && n > 0, MLM_ERR_ARG, "mlm_llama_prefill: no tokens");
+  MLM_REQUIRE(ctx, m->pos + n <= m->cfg.max_seq, MLM_ERR_STATE,
               "mlm_llama_prefill: %d tokens at position %d exceed the cache (%d)", n, m->pos,
               m->cfg.max_seq);
   for (int i = 0; i < n; ++i)
-    MLM_REQUIRE(m->ctx, tokens[i] >= 0 && tokens[i] < m->cfg.vocab, MLM_ERR_ARG,
+    MLM_REQUIRE(ctx, tokens[i] >= 0 && tokens[i] < m->cfg.vocab, MLM_ERR_ARG,
                 "mlm_llama_prefill: invalid token id %d at %d", tokens[i], i);
-  for (int i = 0; i < n; ++i) {
-    int st = m->set_state(tokens[i], m->pos, 0);
-    if (st == MLM_OK) st = m->step(i == n - 1, m->logits);
+  int T = 0;
+  for (int c0 = 0; c0 < n; c0 += T) {
+    T = std::min(m->pf_chunk, n - c0);
+    MLM_CUDA_TRY(ctx, cudaMemcpyAsync(m->pf_tokens, tokens + c0, sizeof(int32_t) * T,
+                                      cudaMemcpyHostToDevice, ctx->stream));
+    int st = m->prefill_chunk(T);
     if (st != MLM_OK) return st;
-    m->pos += 1;
+    m->pos += T;
   }
+  // the output head on the last token, as a decode step ends
+  const float *last = m->pf_hidden + (size_t)(T - 1) * m->cfg.dim;
+  float *lg = logits ? logits : m->logits;
+  int st = m->gemv(m->output, m->cfg.vocab, m->cfg.dim, m->normed(last, m->out_norm), lg, nullptr);
+  if (st == MLM_OK) st = argmax_launch(ctx, lg, m->cfg.vocab, m->state + kToken, ctx->stream);
+  if (st != MLM_OK) return st;
   if (next)
-    MLM_CUDA_TRY(m->ctx, cudaMemcpyAsync(next, m->state + kToken, sizeof(int32_t),
-                                         cudaMemcpyDeviceToDevice, m->ctx->stream));
+    MLM_CUDA_TRY(ctx, cudaMemcpyAsync(next, m->state + kToken, sizeof(int32_t),
+                                      cudaMemcpyDeviceToDevice, ctx->stream));
   return MLM_OK;
 }
 

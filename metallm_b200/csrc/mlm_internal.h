@@ -87,6 +87,20 @@ int attn_decode_launch(mlm_ctx *ctx, const void *q, const void *kc, const void *
                        size_t partial_floats, cudaStream_t stream, const int *pos_dev);
 int silu_mul_launch(mlm_ctx *ctx, const float *g, const float *u, void *out, int n,
                     cudaStream_t stream);
+// batched prompt pass (prefill.cu, q4k_gemm.cu)
+int gemm_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_bf16, int tokens,
+                float *y, const float *residual, cudaStream_t stream);
+int embed_rows_launch(mlm_ctx *ctx, const void *table, int vocab, int dim, const int32_t *tokens,
+                      int T, float *out, cudaStream_t stream);
+int rmsnorm_rows_bf16_launch(mlm_ctx *ctx, const float *x, const float *w, void *y, int rows,
+                             int n, float eps, cudaStream_t stream);
+int rope_kv_rows_launch(mlm_ctx *ctx, const float *qkv, const float *freqs, const mlm_rope_args &a,
+                        int nq, int nkv, int d, int pos0, int T, void *q_out, void *kc, void *vc,
+                        cudaStream_t stream);
+int attn_prefill_launch(mlm_ctx *ctx, const void *q16, const void *kc, const void *vc, int pos0,
+                        int T, int n_heads, int n_kv, int head_dim, void *out, cudaStream_t stream);
+int swiglu_rows_bf16_launch(mlm_ctx *ctx, const float *gu, int ffn, int T, void *out,
+                            cudaStream_t stream);
 int silu_mul_scaled_launch(mlm_ctx *ctx, const float *g, const float *u, void *out, float *scale,
                            int n, cudaStream_t stream);
 int argmax_launch(mlm_ctx *ctx, const float *x, int n, int32_t *out, cudaStream_t stream);

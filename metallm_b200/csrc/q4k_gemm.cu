@@ -23,8 +23,8 @@
 //              of their 32-lane quarter of the accumulator, stores to Y.
 // Stages are tracked by mbarriers (full: TMA bytes / dequant warps, empty:
 // the MMA commit); every wait is bounded and reports a device error.  K may
-// be split across CTAs (grid z) for narrow weights, the parts then added into
-// a zeroed Y with fp32 atomics.
+// be split across CTAs (grid z) for narrow weights, the parts then added with
+// fp32 atomics into a Y that starts from the residual (or zero).
 #include <cuda.h>
 
 #include <algorithm>
@@ -69,6 +69,7 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
 
 struct GemmArgs {
   float *y;      // [T][N] fp32
+  const float *residual;  // [T][N] or NULL (the atomic path starts y from it)
   int *status;   // device-visible error word
   int N, K, T;
   int kb_per_split;  // Q4_K block columns per split
@@ -265,7 +266,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               if (p.atomic)
                 atomicAdd(dst, __uint_as_float(v[i]));
               else
-                *dst = __uint_as_float(v[i]);
+                *dst = __uint_as_float(v[i]) + (p.residual ? p.residual[(size_t)t * p.N + n] : 0.f);
             }
           }
         }
@@ -315,8 +316,9 @@ int gemm_init(mlm_ctx *ctx) {
 
 using namespace mlm;
 
-extern "C" int mlm_q4k_gemm(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_bf16,
-                            int tokens, float *y) {
+namespace mlm {
+int gemm_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_bf16, int tokens,
+                float *y, const float *residual, cudaStream_t stream) {
   MLM_CHECK_CTX(ctx);
   MLM_REQUIRE(ctx, W && x_bf16 && y, MLM_ERR_ARG, "mlm_q4k_gemm: null buffer");
   MLM_REQUIRE(ctx, rows > 0 && cols > 0 && tokens > 0 && cols % kQK == 0, MLM_ERR_SHAPE,
@@ -358,15 +360,31 @@ extern "C" int mlm_q4k_gemm(mlm_ctx *ctx, const void *W, int rows, int cols, con
   while (splits < 8 && tiles * splits * 2 <= ctx->sm_count && nb % (splits * 2) == 0) splits *= 2;
   GemmArgs a;
   a.y = y;
+  a.residual = residual;
   a.status = ctx->dev_status;
   a.N = rows;
   a.K = cols;
   a.T = tokens;
   a.kb_per_split = nb / splits;
   a.atomic = splits > 1;
-  if (splits > 1)
-    MLM_CUDA_TRY(ctx, cudaMemsetAsync(y, 0, sizeof(float) * (size_t)rows * tokens, ctx->stream));
+  if (splits > 1) {  // the parts are added into y, which starts from the residual or zero
+    const size_t bytes = sizeof(float) * (size_t)rows * tokens;
+    if (residual) {
+      if (residual != y)
+        MLM_CUDA_TRY(ctx, cudaMemcpyAsync(y, residual, bytes, cudaMemcpyDeviceToDevice, stream));
+    } else {
+      MLM_CUDA_TRY(ctx, cudaMemsetAsync(y, 0, bytes, stream));
+    }
+  }
   dim3 grid((rows + kGemmRows - 1) / kGemmRows, (tokens + kGemmTok - 1) / kGemmTok, splits);
-  q4k_gemm_kernel<<<grid, kGemmThreads, kGemmSmem, ctx->stream>>>(mw, mx, a);
+  q4k_gemm_kernel<<<grid, kGemmThreads, kGemmSmem, stream>>>(mw, mx, a);
   return check_launch(ctx, "mlm_q4k_gemm");
+}
+}  // namespace mlm
+
+extern "C" int mlm_q4k_gemm(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_bf16,
+                            int tokens, float *y, const float *residual) {
+  MLM_CHECK_CTX(ctx);
+  MLM_REQUIRE(ctx, !residual || aligned4(residual), MLM_ERR_ALIGN, "mlm_q4k_gemm: residual");
+  return gemm_launch(ctx, W, rows, cols, x_bf16, tokens, y, residual, ctx->stream);
 }

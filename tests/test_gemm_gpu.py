@@ -32,7 +32,7 @@ def _run(ctx, rows, cols, tokens, seed=5):
     blocks = O.gen_q4k(seed, 1, nb)
     xb = bf16_bits(O.gen_f32(seed, 2, tokens * cols))
     y = ctx.alloc(4 * rows * tokens)
-    ctx.call("mlm_q4k_gemm", ctx.to_device(blocks), rows, cols, ctx.to_device(xb), tokens, y)
+    ctx.call("mlm_q4k_gemm", ctx.to_device(blocks), rows, cols, ctx.to_device(xb), tokens, y, None)
     got = y.download(np.float32, rows * tokens).reshape(tokens, rows)
     w = bf16_value(bf16_bits(O.q4k_dequant_f32(blocks, rows * cols))).reshape(rows, cols)
     x = bf16_value(xb).reshape(tokens, cols)
@@ -50,12 +50,28 @@ def test_gemm_shapes(ctx, rows, cols, tokens):
     assert err < TOL, (rows, cols, tokens, err)
 
 
+@pytest.mark.parametrize("rows,cols,tokens", [(4096, 4096, 512), (1000, 2048, 1300)])
+def test_gemm_residual_in_place(ctx, rows, cols, tokens):
+    """y = x W^T + y (the residual stream updated in place), split and unsplit."""
+    nb = rows * cols // 256
+    blocks = O.gen_q4k(6, 1, nb)
+    xb = bf16_bits(O.gen_f32(6, 2, tokens * cols))
+    r = O.gen_f32(6, 3, tokens * rows, 0.0, 100.0)
+    y = ctx.to_device(r)
+    ctx.call("mlm_q4k_gemm", ctx.to_device(blocks), rows, cols, ctx.to_device(xb), tokens, y, y)
+    got = y.download(np.float32, rows * tokens).reshape(tokens, rows)
+    w = bf16_value(bf16_bits(O.q4k_dequant_f32(blocks, rows * cols))).reshape(rows, cols)
+    ref = bf16_value(xb).reshape(tokens, cols).astype(np.float64) @ w.astype(np.float64).T
+    ref += r.reshape(tokens, rows)
+    assert rel_l2(got, ref) < TOL
+
+
 def test_gemm_bad_args(ctx):
     from metallm_b200 import MLMError
     buf = ctx.alloc(1 << 16)
     with pytest.raises(MLMError) as e:
-        ctx.call("mlm_q4k_gemm", buf, 128, 300, buf, 16, buf)
+        ctx.call("mlm_q4k_gemm", buf, 128, 300, buf, 16, buf, None)
     assert e.value.status == -2
     with pytest.raises(MLMError) as e:
-        ctx.call("mlm_q4k_gemm", buf.ptr + 8, 128, 256, buf, 16, buf)
+        ctx.call("mlm_q4k_gemm", buf.ptr + 8, 128, 256, buf, 16, buf, None)
     assert e.value.status == -3

@@ -134,20 +134,103 @@ def test_model_forward_and_greedy(ctx):
     m.close()
 
 
-def test_prefill_matches_forward(ctx):
+def _oracle_model(cfg):
+    layers = [oracle_layer(cfg, l) for l in range(cfg.n_layers)]
+    return layers, oracle_globals(cfg), [oracle_cache(cfg, l, 0) for l in range(cfg.n_layers)]
+
+
+def _layer0_top2_gap(cfg, w0, glob, kcache, prompt, t: int) -> float:
+    """Smallest relative gap between the two largest layer-0 attention scores
+    of token t over its heads, in the oracle's fp64 arithmetic."""
+    d, hd = cfg.dim, cfg.head_dim
+    h = glob["tok_embd"][prompt[t] * d:(prompt[t] + 1) * d].astype(np.float32)
+    xn = O.rmsnorm_f32(h, w0["attn_norm"], 1, d, cfg.rms_eps)
+    q = O.q4k_matvec_f32x(w0["wq"], d, d, xn)
+    q = O.rope_f32(O.rope_args(n_dims=hd, freq_base=cfg.rope.freq_base, pos_offset=t),
+                   q, 1, cfg.n_heads, hd).reshape(cfg.n_heads, hd).astype(np.float64)
+    k = kcache[:t + 1].astype(np.float64)
+    group = cfg.n_heads // cfg.n_kv_heads
+    gap = 1.0
+    for hh in range(cfg.n_heads):
+        s = np.sort(k[:, hh // group] @ q[hh])[::-1]
+        if t > 0:
+            gap = min(gap, (s[0] - s[1]) / abs(s[0]))
+    return gap
+
+
+@pytest.mark.parametrize("max_seq,n", [(64, 40), (1100, 1030)])
+def test_prefill_vs_oracle(ctx, max_seq, n):
+    """Batched prompt pass (tensor-core GEMM, bf16 activations) vs the oracle's
+    token-by-token forward: last-token logits and the KV cache it leaves;
+    1030 tokens cross the 1024-token chunk boundary.
+
+    The synthetic weights give attention scores of order 1e4, so softmax is
+    close to an argmax: where the two best keys of a layer-0 head are within a
+    relative 2e-2 of each other, bf16 rounding of the prompt pass can pick the
+    other key and that token's hidden state -- hence its layer-1 K/V row --
+    differs from the fp32 oracle's.  Every layer-0 row must be within 1e-2;
+    layer-1 rows carry two layers of bf16 rounding (about 8x the fp16 decode
+    path's error on the same row) and must be within 2e-2 except at such
+    near-tied tokens, at most 1% of them; the layer-1 cache over the other
+    rows is within 1e-2.
+    """
+    from metallm_b200.synthetic import fill_llama
+    cfg = llama_config(n_layers=2, dim=1024, n_heads=8, n_kv_heads=2, ffn_dim=2816,
+                       vocab=4096, max_seq=max_seq)
+    m = Llama(ctx, cfg)
+    fill_llama(m, SEED)
+    prompt = np.random.default_rng(n).integers(0, cfg.vocab, size=n).tolist()
+    logits = ctx.alloc(4 * cfg.vocab)
+    nxt = ctx.alloc(16)
+    m.prefill(prompt, nxt, logits)
+    got = logits.download(np.float32)
+    layers, glob, caches = _oracle_model(cfg)
+    for pos, tok in enumerate(prompt):
+        want = LO.model_forward(layers, glob, caches, tok, pos, cfg_dict(cfg))
+    assert rel_l2(got, want) < TOL, rel_l2(got, want)
+    assert int(nxt.download(np.int32)[0]) == int(np.argmax(want))
+    assert m.position == n
+    kvd = cfg.n_kv_heads * cfg.head_dim
+    for layer in range(cfg.n_layers):
+        t = m.layer_tensors(layer)
+        for name, idx in (("k_cache", 0), ("v_cache", 1)):
+            g = np.empty(n * kvd, dtype=np.float16)
+            ctx._check(ctx.lib.mlm_download(ctx.handle, g.ctypes.data,
+                                            __import__("ctypes").c_void_p(t[name]), g.nbytes),
+                       "dl")
+            g = g.astype(np.float32).reshape(n, kvd)
+            r = caches[layer][idx][:n].reshape(n, kvd).astype(np.float32)
+            err = np.linalg.norm(g - r, axis=1) / np.maximum(np.linalg.norm(r, axis=1), 1e-30)
+            if layer == 0:
+                assert err.max() < TOL, (name, int(err.argmax()), err.max())
+                continue
+            bad = np.nonzero(err >= 2 * TOL)[0].tolist()
+            assert len(bad) <= n // 100, (name, bad)
+            for row in bad:
+                gap = _layer0_top2_gap(cfg, layers[0], glob, caches[0][0], prompt, row)
+                assert gap < 2e-2, (name, row, err[row], gap)
+            keep = np.setdiff1d(np.arange(n), bad)
+            assert rel_l2(g[keep], r[keep]) < TOL, name
+    m.close()
+
+
+def test_prefill_then_decode_matches_forward(ctx):
+    """Prefill followed by greedy decode agrees with running forward() per token."""
     from metallm_b200.synthetic import fill_llama
     cfg = _small_cfg()
     m = Llama(ctx, cfg)
     fill_llama(m, SEED)
     prompt = [5, 6, 7, 8, 9, 10]
-    nxt = ctx.alloc(16)
-    m.prefill(prompt, nxt)
-    a = int(nxt.download(np.int32)[0])
+    la = ctx.alloc(4 * cfg.vocab)
+    m.prefill(prompt, None, la)
+    a = la.download(np.float32)
     m.reset()
-    logits = ctx.alloc(4 * cfg.vocab)
+    lb = ctx.alloc(4 * cfg.vocab)
     for tok in prompt:
-        m.forward(tok, logits)
-    assert a == int(np.argmax(logits.download(np.float32)))
+        m.forward(tok, lb)
+    b = lb.download(np.float32)
+    assert rel_l2(a, b) < TOL
+    assert int(np.argmax(a)) == int(np.argmax(b))
     m.close()
 
 

@@ -56,7 +56,19 @@ LLAMA_WORKLOADS = {
              "2047-token fp16 cache (BASELINE config 2)",
     "decode": "Llama-3-8B-shape Q4_K model, batch 1: 512 prompt tokens then greedy decode "
               "(BASELINE config 3)",
+    "prefill": "Llama-3-8B-shape Q4_K model, batch 1: the 512-token prompt pass (tcgen05 Q4_K "
+               "GEMM, bf16 activations) up to the first generated token (BASELINE config 3)",
 }
+
+
+def llama_prefill_flops(n_layers: int, T: int) -> int:
+    """Algorithmic FLOPs of a T-token prompt pass from position 0: every linear
+    on every token, causal attention (QK^T and PV over the keys at or before
+    each query), the output head on the last token."""
+    d, kvd, ffn, vocab, heads, hd = 4096, 1024, 14336, 128256, 32, 128
+    linear = 2 * T * (d * (d + 2 * kvd) + d * d + 2 * ffn * d + ffn * d)
+    attn = 2 * 2 * heads * hd * (T * (T + 1) // 2)
+    return n_layers * (linear + attn) + 2 * vocab * d
 
 
 def llama_token_bytes(n_layers: int, pos: int, with_head: bool = True) -> int:
@@ -96,6 +108,8 @@ PROFILES = {
     "gemv_up": "q4k_gemv_14336x4096.md",
     "gemv_down": "q4k_gemv_4096x14336.md",
     "dequant": "q4k_dequant_f32_4096x4096.md",
+    "prefill": "q4k_gemm_28672x4096x512.md",
+    "gemm": "q4k_gemm_28672x4096x512.md",
 }
 
 
@@ -428,10 +442,133 @@ def cpu_decode_rate(budget_s: float, threads: int) -> dict:
         reps += 1
     per_token = 32 * t_layer / reps + t_head / reps
     return {"value": round(1.0 / per_token, 4), "unit": "tokens/s", "cores": threads,
+            "layer_s": t_layer / reps, "head_s": t_head / reps,
             "kind": "reference" if O.ref_lib() is not None else "port",
             "sample": f"{reps} x (one layer's 7 Q4_K matvecs + the 128256x4096 head) in "
                       f"{time.perf_counter() - t0:.1f} s, {threads} threads; tokens/s = "
                       f"1 / (32 x layer + head)"}
+
+
+GEMM_SHAPE = (28672, 4096, 512)
+GEMM_DESC = ("Q4_K x bf16 GEMM on tcgen05: the fused gate/up weights of a Llama-3-8B layer "
+             "(28672 x 4096 Q4_K) on a 512-token prompt (BASELINE config 3 prefill)")
+
+
+def cpu_gemm_rate(budget_s: float, threads: int) -> dict:
+    """CPU matvec rate on the GEMM's weights, as TFLOP/s: the GEMM is T
+    independent matvecs, so a bounded sample of them gives its rate."""
+    rows, cols, _ = GEMM_SHAPE
+    r = cpu_gemv_rate(rows, cols, budget_s, threads, "reference")
+    tflops = r["value"] * 1e9 / gemv_bytes(rows, cols) * 2 * rows * cols / 1e12
+    return {"value": round(tflops, 6), "unit": "TFLOP/s", "cores": threads, "kind": r["kind"],
+            "sample": r["sample"] + "; TFLOP/s = 2 x rows x cols per matvec"}
+
+
+def run_gemm(args, world, rank, local, pg) -> dict:
+    """The prefill GEMM alone: each step is one 28672 x 4096 x 512 launch,
+    rotating over weight copies larger than L2 together."""
+    import torch
+
+    from metallm_b200 import Context
+    rows, cols, T = GEMM_SHAPE
+    ctx = Context(local)
+    torch.cuda.set_device(local)
+    tstream = torch.cuda.ExternalStream(ctx.stream(), device=f"cuda:{local}")
+    peaks = measured_peaks()
+    nb = rows * cols // 256
+    copies = max(2, min(args.copies, 4))  # 4 x 66 MB > L2
+    Ws = []
+    for c in range(copies):
+        W = ctx.alloc(nb * 144)
+        ctx.gen_q4k(1000 + c, 1, nb, W)
+        Ws.append(W)
+    x = ctx.alloc(2 * T * cols)
+    ctx.gen_f16(7, 2, T * cols, x)  # fp16 normals read as bf16: finite, small
+    y = ctx.alloc(4 * T * rows)
+    step = lambda i: ctx.call("mlm_q4k_gemm", Ws[i % copies], rows, cols, x, T, y, None)
+    for i in range(args.warmup):
+        step(i)
+    ctx.wait()
+    barrier(pg, local)
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(tstream)
+    for i in range(args.steps):
+        step(i)
+    ev1.record(tstream)
+    ev1.synchronize()
+    dev_ms = ev0.elapsed_time(ev1)
+    clocks = sampler.stop()
+    ms_max = max_over_ranks(dev_ms, pg, local)
+    per_ms = ms_max / args.steps
+    flops = 2 * rows * cols * T
+    tflops = flops / (per_ms * 1e-3) / 1e12
+    # e2e: X from pinned host memory, the GEMM, Y back to pinned host memory
+    lib, h = ctx.lib, ctx.handle
+    hx, hy = ctypes.c_void_p(), ctypes.c_void_p()
+    lib.mlm_host_alloc(h, 2 * T * cols, ctypes.byref(hx))
+    lib.mlm_host_alloc(h, 4 * T * rows, ctypes.byref(hy))
+    e2e_steps = min(args.steps, 20)
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        ctx._check(lib.mlm_upload_async(h, ctypes.c_void_p(x.ptr), hx, 2 * T * cols), "up")
+        step(i)
+        ctx._check(lib.mlm_download_async(h, hy, ctypes.c_void_p(y.ptr), 4 * T * rows), "dn")
+        ctx.wait()
+    e2e_s = max_over_ranks(time.perf_counter() - t0, pg, local)
+    lib.mlm_host_free(h, hx)
+    lib.mlm_host_free(h, hy)
+    line = {
+        "metric": METRIC, "value": round(tflops * world, 2), "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_ms, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "q4k -> bf16 x bf16 -> f32 (tcgen05)",
+        "data": "synthetic (seeded Q4_K blocks, fp16 normals read as bf16, generated on device)",
+        "config": {"workload": GEMM_DESC, "rows": rows, "cols": cols, "tokens": T,
+                   "parallelism": "replicas" if world > 1 else "single GPU",
+                   "l2": f"{copies} rotating weight copies ({copies * nb * 144 / 1e6:.0f} MB > L2)",
+                   "algorithmic_flops_per_step": flops},
+        "e2e": {"value": round(flops * e2e_steps * world / e2e_s / 1e12, 3), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": 2 * T * cols, "d2h_bytes_per_step": 4 * T * rows},
+        "gpu_launches": args.steps,
+        "roofline": {"bound": "tensor", "achieved": round(tflops, 1),
+                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": round(tflops / peaks["bf16_tflops"], 4),
+                     "peak_source": peaks["source"] + " (bf16 burst)",
+                     "traffic": ncu_traffic("gemm")},
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_gemm_rate(args.cpu_seconds, host_threads())
+    ctx.close()
+    return line
+
+
+def gemm_kernel_time(ctx, m, n_layers: int, T: int, reps: int, tstream) -> dict:
+    """Device time of the dominant prefill kernel alone: the fused gate/up
+    Q4_K GEMM (28672 x 4096) on T bf16 tokens, rotating over the layers'
+    weights (66 MB each) so every launch streams its weights from HBM."""
+    import torch
+    x = ctx.alloc(2 * T * 4096)
+    ctx.gen_f16(1, 11, T * 4096, x)  # fp16 normals read as bf16: finite, small
+    y = ctx.alloc(4 * T * 28672)
+    ws = [m.layer_tensors(l)["w_gate"] for l in range(n_layers)]
+    call = lambda i: ctx.call("mlm_q4k_gemm", ws[i % n_layers], 28672, 4096, x, T, y, None)
+    for i in range(3):
+        call(i)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(tstream)
+    for i in range(reps):
+        call(i)
+    ev1.record(tstream)
+    ev1.synchronize()
+    ms = ev0.elapsed_time(ev1) / reps
+    flops = 2 * 28672 * 4096 * T
+    return {"ms": ms, "flops": flops, "tflops": flops / (ms * 1e-3) / 1e12}
 
 
 def run_llama(args, world, rank, local, pg) -> dict:
@@ -502,6 +639,68 @@ def run_llama(args, world, rank, local, pg) -> dict:
                   "l2": "inputs larger than L2: 122.7 MB of Q4_K weights + 8.4 MB of KV per layer",
                   "algorithmic_bytes_per_step": alg}
         cpu = None
+    elif args.workload == "prefill":
+        T = 512
+        steps = min(args.steps, 16)
+        cfg = llama_config(n_layers=32, vocab=128256, max_seq=T)
+        m = Llama(ctx, cfg)
+        fill_llama(m, 1)
+        prompt = np.random.default_rng(512).integers(0, 128000, size=T).tolist()
+        nxt = ctx.alloc(16)
+        for _ in range(args.warmup):
+            m.reset()
+            m.prefill(prompt, nxt)
+        ctx.wait()
+        barrier(pg, local)
+        sampler = ClockSampler(local)
+        sampler.start()
+        time.sleep(0.3)
+
+        def passes():
+            for _ in range(steps):
+                m.reset()
+                m.prefill(prompt, nxt)
+        dev_ms = timed(passes)
+        clocks = sampler.stop()
+        ms_max = max_over_ranks(dev_ms, pg, local)
+        per_step_ms = ms_max / steps
+        value = T * steps * world / (ms_max * 1e-3)
+        unit = "tokens/s"
+        flops = llama_prefill_flops(32, T)
+        alg = llama_token_bytes(32, 0)  # weights streamed once per pass
+        launches = steps * (1 + 32 * 9 + 3)
+        # e2e: the prompt ids from host memory through mlm_llama_prefill, the
+        # first generated token read back
+        lib, h = ctx.lib, ctx.handle
+        htok = ctypes.c_void_p()
+        lib.mlm_host_alloc(h, 16, ctypes.byref(htok))
+        e2e_steps = min(steps, 4)
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            m.reset()
+            m.prefill(prompt, nxt)
+            ctx._check(lib.mlm_download_async(h, htok, ctypes.c_void_p(nxt.ptr), 4), "dn")
+            ctx.wait()
+        e2e_s = max_over_ranks(time.perf_counter() - t0, pg, local)
+        lib.mlm_host_free(h, htok)
+        e2e = {"value": round(T * e2e_steps * world / e2e_s, 2), "unit": "tokens/s",
+               "h2d_bytes_per_step": 4 * T, "d2h_bytes_per_step": 4}
+        gk = gemm_kernel_time(ctx, m, 32, T, 64, tstream)
+        config = {"workload": LLAMA_WORKLOADS["prefill"], "layers": 32, "hidden": 4096,
+                  "heads": "32/8 x 128", "ffn": 14336, "vocab": 128256, "batch": 1,
+                  "prompt_tokens": T, "parallelism": "single GPU",
+                  "l2": "inputs larger than L2: 4.2 GB of Q4_K weights per pass",
+                  "algorithmic_flops_per_step": flops}
+        extra = {"tflops": round(flops / (per_step_ms * 1e-3) / 1e12, 1),
+                 "roofline": {"bound": "tensor", "achieved": round(gk["tflops"], 1),
+                              "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                              "frac": round(gk["tflops"] / peaks["bf16_tflops"], 4),
+                              "peak_source": peaks["source"] + " (bf16 burst)",
+                              "traffic": ncu_traffic("prefill"),
+                              "kernel": "q4k_gemm_kernel, gate/up 28672x4096 x 512 tokens",
+                              "kernel_ms": round(gk["ms"], 4),
+                              "algorithmic_flops_per_launch": gk["flops"]}}
+        cpu = None
     else:
         prompt_len, gen_len = 512, 256
         steps = min(args.steps, gen_len - args.warmup)
@@ -512,6 +711,8 @@ def run_llama(args, world, rank, local, pg) -> dict:
         nxt = ctx.alloc(16)
         ctx.wait()
         barrier(pg, local)
+        m.prefill(prompt, nxt)  # first pass loads the kernels
+        m.reset()
         prefill_ms = max_over_ranks(timed(lambda: m.prefill(prompt, nxt)), pg, local)
         first = int(nxt.download(np.int32)[0])
         out = ctx.alloc(4 * gen_len)
@@ -560,26 +761,28 @@ def run_llama(args, world, rank, local, pg) -> dict:
                   "algorithmic_bytes_per_step": alg}
         extra = {"prefill": {"value": round(prompt_len / (prefill_ms * 1e-3), 2),
                              "unit": "tokens/s",
-                             "path": "prompt run as sequential decode steps (no tensor-core "
-                                     "prefill GEMM yet)"},
+                             "path": "batched prompt pass: tcgen05 Q4_K GEMM, bf16 activations"},
                  "first_tokens": [int(t) for t in toks[:8]]}
         cpu = "decode"
     kernel_gbs = alg / (per_step_ms * 1e-3) / 1e9
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": unit, "n_gpus": world,
-        "steps": steps if args.workload == "decode" else args.steps, "warmup": args.warmup,
+        "steps": args.steps if args.workload == "layer" else steps, "warmup": args.warmup,
         "ms_per_step": round(per_step_ms, 5), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "q4k x f16 -> f32 (fp16 KV cache)",
         "data": "synthetic (seeded Q4_K weights, fp16 embedding, fp32 norms generated on "
                 "device, as BASELINE configs 2/3)",
         "config": config, "e2e": e2e, "gpu_launches": launches,
-        "launch": "CUDA graph (one decode step captured, replayed per token)",
+        "launch": ("stream-ordered launches, one per kernel" if args.workload == "prefill" else
+                   "CUDA graph (one decode step captured, replayed per token)"),
         "roofline": {"bound": "hbm", "achieved": round(kernel_gbs, 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(kernel_gbs / peaks["hbm_gbs"], 4),
                      "peak_source": peaks["source"], "traffic": None},
         "clocks": clocks,
     }
     line.update(extra)
+    if args.workload == "prefill":
+        line["dtype"] = "q4k -> bf16 x bf16 -> f32 (tcgen05), fp16 KV cache"
     if rank == 0 and world == 1 and not args.no_cpu and cpu == "decode":
         line["cpu_baseline"] = cpu_decode_rate(args.cpu_seconds, host_threads())
     ctx.close()
@@ -589,12 +792,30 @@ def run_llama(args, world, rank, local, pg) -> dict:
 def run_reference(args, world, rank) -> dict | None:
     if rank != 0:
         return None
+    if args.workload == "gemm":
+        r = cpu_gemm_rate(args.cpu_seconds, host_threads())
+        rows, cols, T = GEMM_SHAPE
+        v = r["value"]
+        return {"impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(2 * rows * cols * T / (v * 1e12) * 1e3, 3),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "q4k x f16 -> f32", "data": "synthetic (seeded Q4_K blocks)",
+                "config": {"workload": GEMM_DESC, "rows": rows, "cols": cols, "tokens": T},
+                "cpu_baseline": r,
+                "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
     if args.workload in LLAMA_WORKLOADS:
         th = host_threads()
         r = cpu_decode_rate(args.cpu_seconds, th)
         if args.workload == "decode":
             v, unit, alg = r["value"], "tokens/s", llama_token_bytes(32, 640)
             ms = 1e3 / v
+        elif args.workload == "prefill":  # every prompt token through 32 layers, one head
+            T = 512
+            ms = (T * 32 * r["layer_s"] + r["head_s"]) * 1e3
+            v, unit = round(T / (ms * 1e-3), 4), "tokens/s"
+            r = dict(r, sample=r["sample"] + "; prompt tokens/s = 512 / (512 x 32 x layer + head)")
         else:  # one layer: its bytes over a 32nd of the token time without the head
             alg = llama_token_bytes(1, 2047, with_head=False) - 2 * 4096
             ms = 1e3 / r["value"] / 33.0
@@ -644,7 +865,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--workload", default="gemv_up",
-                    choices=sorted(WORKLOADS) + sorted(LLAMA_WORKLOADS))
+                    choices=sorted(WORKLOADS) + sorted(LLAMA_WORKLOADS) + ["gemm"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--copies", type=int, default=6, help="rotating weight copies (> L2)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -662,8 +883,9 @@ def main() -> None:
 
     world, rank, local, pg = dist_setup(args)
     try:
-        line = (run_llama if args.workload in LLAMA_WORKLOADS else run_gpu)(
-            args, world, rank, local, pg)
+        run = run_gemm if args.workload == "gemm" else \
+            run_llama if args.workload in LLAMA_WORKLOADS else run_gpu
+        line = run(args, world, rank, local, pg)
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:

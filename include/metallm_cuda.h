@@ -173,10 +173,12 @@ int mlm_q4k_gemv_swiglu(mlm_ctx *ctx, const void *W, int rows, int cols, const f
  * per prompt token with encodeMPSMatrixMultiply on fp16 weights
  * (MetalService.swift:797-925).  W (GGUF layout) is dequantized tile by tile
  * to bf16 in shared memory and multiplied on the tensor cores (tcgen05, fp32
- * accumulation).  cols % 256 == 0; W and x 16-byte aligned.  Narrow weights
- * split K over CTAs and add into y with fp32 atomics (y starts from the
- * residual, or zero).  residual (fp32 [tokens][rows], may be y itself) is
- * added when not NULL. */
+ * accumulation).  cols % 256 == 0; W and x 16-byte aligned; at most 65536
+ * output tiles of 256 rows x 256 tokens.  One persistent CTA per SM; where a
+ * tile's K range is shared by several CTAs, the parts after the first are
+ * added into y with fp32 atomics (summation order may then differ from run
+ * to run in the last bits).  residual (fp32 [tokens][rows], may be y
+ * itself) is added when not NULL. */
 int mlm_q4k_gemm(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_bf16,
                  int tokens, float *y, const float *residual);
 

@@ -38,6 +38,11 @@ struct mlm_ctx {
   // split-K scratch of decode attention
   float *attn_partials = nullptr;
   size_t attn_partials_floats = 0;
+
+  // stream-K hand-off flags of the prefill GEMM, one per output tile; zero
+  // between launches (each launch's waiters count them back down)
+  int *gemm_flags = nullptr;
+  int gemm_max_tiles = 0;
 };
 
 namespace mlm {

@@ -103,6 +103,11 @@ void mlm_graph_destroy(mlm_graph *graph);
 /* Q4_K blocks [first_block, first_block + nblocks) of tensor `stream` */
 int mlm_gen_q4k(mlm_ctx *ctx, uint64_t seed, uint64_t stream, uint64_t first_block,
                 uint64_t nblocks, void *out);
+/* rows row0 .. row0+rows, block columns kb0 .. kb0+nkb of tensor `stream`
+ * (nb_full block columns in all), stored densely as [rows][nkb] blocks: the
+ * shard of a tensor whose input columns are split over ranks */
+int mlm_gen_q4k_sub(mlm_ctx *ctx, uint64_t seed, uint64_t stream, uint64_t nb_full, uint64_t row0,
+                    uint64_t rows, uint64_t kb0, uint64_t nkb, void *out);
 int mlm_gen_f16(mlm_ctx *ctx, uint64_t seed, uint64_t stream, uint64_t first,
                 uint64_t n, float mean, float std, void *out_f16);
 int mlm_gen_f32(mlm_ctx *ctx, uint64_t seed, uint64_t stream, uint64_t first,
@@ -295,6 +300,25 @@ int mlm_embed_f16(mlm_ctx *ctx, const void *table_f16, int vocab, int dim,
 int mlm_argmax_f32(mlm_ctx *ctx, const float *logits, int n, int32_t *out_index_dev);
 
 /* ---------------------------------------------------------------------------
+ * Tensor parallelism over NCCL, one context (one process) per GPU.  No
+ * counterpart in the reference, which runs on one Metal device.  NCCL is
+ * loaded at run time (libnccl.so.2; a copy already in the process is
+ * reused).  Collectives are enqueued on the context's stream.
+ * ------------------------------------------------------------------------ */
+
+/* a fresh NCCL unique id (NCCL_UNIQUE_ID_BYTES = 128 bytes) for rank 0 to
+ * hand to the other ranks */
+int mlm_tp_unique_id(mlm_ctx *ctx, void *out, size_t bytes);
+/* join the group: every rank calls this with the same id (a collective) */
+int mlm_tp_init(mlm_ctx *ctx, int nranks, int rank, const void *unique_id);
+/* this context's rank and group size (size 0 when it has no group) */
+int mlm_tp_info(const mlm_ctx *ctx, int *rank, int *size);
+/* recv = sum over ranks of send (fp32, count elements; may be in place) */
+int mlm_tp_allreduce_f32(mlm_ctx *ctx, const float *send, float *recv, size_t count);
+/* recv = the ranks' `bytes`-byte send buffers, rank order */
+int mlm_tp_allgather(mlm_ctx *ctx, const void *send, void *recv, size_t bytes);
+
+/* ---------------------------------------------------------------------------
  * Llama decode runner: class LlamaRunner (LlamaRunner.swift:22-1210)
  * ------------------------------------------------------------------------ */
 
@@ -336,7 +360,13 @@ typedef struct mlm_llama mlm_llama;
 
 /* LlamaRunner.init: allocates the weights, the KV caches (2 x n_layers x
  * max_seq x n_kv_heads x head_dim fp16) and the activations of one decode
- * step on ctx's device.  The runner enqueues on ctx's stream. */
+ * step on ctx's device.  The runner enqueues on ctx's stream.  When ctx has
+ * a tensor-parallel group of R ranks (mlm_tp_init), this rank r holds only
+ * its shard: heads [r H/R, (r+1) H/R) and KV heads likewise (wq/wk/wv rows,
+ * caches), FFN rows [r F/R, (r+1) F/R) of w_gate / w_up, the same input
+ * columns of wo / w_down (stored [dim][cols/R]), and vocabulary rows
+ * [r V/R, (r+1) V/R) of the output head; cfg stays the whole model's.  Each
+ * of these must divide evenly (MLM_ERR_SHAPE). */
 int mlm_llama_create(mlm_ctx *ctx, const mlm_llama_config *cfg, mlm_llama **out);
 void mlm_llama_destroy(mlm_llama *m);
 int mlm_llama_layer_tensors(mlm_llama *m, int layer, mlm_llama_layer *out);

@@ -128,6 +128,23 @@ class Context:
         self._check(self.lib.mlm_set_stream(self.handle, ctypes.c_void_p(stream)),
                     "mlm_set_stream")
 
+    # -- tensor parallelism (one context per rank) ------------------------------
+    def tp_unique_id(self) -> bytes:
+        buf = ctypes.create_string_buffer(128)
+        self._check(self.lib.mlm_tp_unique_id(self.handle, buf, 128), "mlm_tp_unique_id")
+        return buf.raw
+
+    def tp_init(self, nranks: int, rank: int, unique_id: bytes) -> None:
+        buf = ctypes.create_string_buffer(bytes(unique_id), 128)
+        self._check(self.lib.mlm_tp_init(self.handle, nranks, rank, buf), "mlm_tp_init")
+
+    def tp_info(self) -> tuple:
+        """(rank, size) of this context's group; size 0 without one."""
+        r, n = ctypes.c_int(), ctypes.c_int()
+        self._check(self.lib.mlm_tp_info(self.handle, ctypes.byref(r), ctypes.byref(n)),
+                    "mlm_tp_info")
+        return r.value, n.value
+
     # -- CUDA graphs -----------------------------------------------------------
     def graph_begin(self) -> None:
         self._check(self.lib.mlm_graph_begin(self.handle), "mlm_graph_begin")
@@ -146,6 +163,12 @@ class Context:
                 first_block: int = 0) -> DeviceBuffer:
         self.call("mlm_gen_q4k", seed, stream, first_block, nblocks, out)
         return out
+
+    def gen_q4k_sub(self, seed: int, stream: int, nb_full: int, row0: int, rows: int, kb0: int,
+                    nkb: int, out) -> None:
+        """Rows row0.. and block columns kb0.. of generated tensor `stream`."""
+        self.call("mlm_gen_q4k_sub", seed, stream, nb_full, row0, rows, kb0, nkb,
+                  ctypes.c_void_p(int(out)))
 
     def gen_f16(self, seed: int, stream: int, n: int, out: DeviceBuffer, mean: float = 0.0,
                 std: float = 1.0, first: int = 0) -> DeviceBuffer:

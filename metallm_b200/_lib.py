@@ -83,6 +83,7 @@ SIGNATURES = [
     ("mlm_graph_destroy", None, [c_vp]),
     ("mlm_wait", c_int, [c_vp]),
     ("mlm_gen_q4k", c_int, [c_vp, c_u64, c_u64, c_u64, c_u64, c_vp]),
+    ("mlm_gen_q4k_sub", c_int, [c_vp, c_u64, c_u64, c_u64, c_u64, c_u64, c_u64, c_u64, c_vp]),
     ("mlm_gen_f16", c_int, [c_vp, c_u64, c_u64, c_u64, c_u64, c_float, c_float, c_vp]),
     ("mlm_gen_f32", c_int, [c_vp, c_u64, c_u64, c_u64, c_u64, c_float, c_float, c_vp]),
     ("mlm_q4k_dequant_f32", c_int, [c_vp, c_vp, c_vp, c_u64]),
@@ -121,6 +122,11 @@ SIGNATURES = [
     ("mlm_llama_forward", c_int, [c_vp, c_int, c_vp]),
     ("mlm_llama_prefill", c_int, [c_vp, ctypes.POINTER(ctypes.c_int32), c_int, c_vp, c_vp]),
     ("mlm_llama_decode_greedy", c_int, [c_vp, c_int, c_int, c_vp]),
+    ("mlm_tp_unique_id", c_int, [c_vp, c_vp, c_size]),
+    ("mlm_tp_init", c_int, [c_vp, c_int, c_int, c_vp]),
+    ("mlm_tp_info", c_int, [c_vp, ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
+    ("mlm_tp_allreduce_f32", c_int, [c_vp, c_vp, c_vp, c_size]),
+    ("mlm_tp_allgather", c_int, [c_vp, c_vp, c_vp, c_size]),
 ]
 
 _lib: Optional[ctypes.CDLL] = None

@@ -267,51 +267,83 @@ __global__ void embed_f16_kernel(const __half *__restrict__ table, int vocab, in
     out[i] = __half2float(row[i]);
 }
 
-__global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ x, int n,
-                                                      int32_t *__restrict__ out) {
-  // first index of the maximum; NaN never wins; an all-NaN row yields 0
-  float best = -INFINITY;
-  int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+// Argmax as one 64-bit maximum: the high word orders the float values, the
+// low word is ~index so that equal values (-0 and +0 included) resolve to
+// the first index.  NaN never wins; an all-NaN row yields 0 (key 0).
+__device__ __forceinline__ unsigned long long argmax_key(float v, int i) {
+  const uint32_t b = __float_as_uint(__fadd_rn(v, 0.0f));  // -0 -> +0: equal values tie
+  const uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return ((unsigned long long)ord << 32) | (uint32_t)(~(uint32_t)i);
+}
+
+constexpr int kArgmaxThreads = 256;
+
+// grid-stride partial maxima, combined with atomicMax in scratch[0]; the
+// last CTA to finish (ticket in scratch[1]) writes the index and zeroes the
+// scratch for the next call
+// (with key_out set, the last CTA stores the key of the maximum, indices
+// counted from `offset`, instead of the index)
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(
+    const float *__restrict__ x, int n, int offset, unsigned long long *scratch,
+    int32_t *__restrict__ out, unsigned long long *key_out) {
+  unsigned long long best = 0;
+  const int stride = gridDim.x * blockDim.x;
+#pragma unroll 8
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
     const float v = x[i];
-    if (v > best || (v == best && i < bi)) {
-      best = v;
-      bi = i;
-    }
+    if (v == v) best = max(best, argmax_key(v, i + offset));
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (ob > best || (ob == best && oi < bi)) {
-      best = ob;
-      bi = oi;
-    }
-  }
-  __shared__ float sb[32];
-  __shared__ int si[32];
+  for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+  __shared__ unsigned long long sb[kArgmaxThreads / 32];
+  __shared__ bool last;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (lane == 0) {
-    sb[warp] = best;
-    si[warp] = bi;
-  }
+  if (lane == 0) sb[warp] = best;
   __syncthreads();
   if (threadIdx.x == 0) {
-    float b = sb[0];
-    int idx = si[0];
-    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) {
-      if (sb[w] > b || (sb[w] == b && si[w] < idx)) {
-        b = sb[w];
-        idx = si[w];
-      }
-    }
-    *out = idx == 0x7fffffff ? 0 : idx;
+    unsigned long long b = sb[0];
+    for (int w = 1; w < kArgmaxThreads / 32; ++w) b = max(b, sb[w]);
+    if (b) atomicMax(scratch, b);
+    __threadfence();
+    last = atomicAdd(scratch + 1, 1ull) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (last && threadIdx.x == 0) {
+    const unsigned long long k = atomicExch(scratch, 0ull);
+    scratch[1] = 0;
+    if (key_out)
+      *key_out = k;
+    else
+      *out = k ? (int32_t)~(uint32_t)(k & 0xFFFFFFFFull) : 0;
   }
 }
 
+__global__ void argmax_keys_kernel(const unsigned long long *keys, int nkeys, int32_t *out) {
+  unsigned long long k = 0;
+  for (int i = 0; i < nkeys; ++i) k = max(k, keys[i]);
+  *out = k ? (int32_t)~(uint32_t)(k & 0xFFFFFFFFull) : 0;
+}
+
 int argmax_launch(mlm_ctx *ctx, const float *x, int n, int32_t *out, cudaStream_t stream) {
-  argmax_kernel<<<1, 1024, 0, stream>>>(x, n, out);
+  const int ctas = std::max(1, std::min(ctx->sm_count, (n + 8 * kArgmaxThreads - 1) /
+                                                           (8 * kArgmaxThreads)));
+  argmax_kernel<<<ctas, kArgmaxThreads, 0, stream>>>(x, n, 0, ctx->argmax_scratch, out, nullptr);
   return check_launch(ctx, "mlm_argmax_f32");
+}
+
+int argmax_key_launch(mlm_ctx *ctx, const float *x, int n, int offset, unsigned long long *key,
+                      cudaStream_t stream) {
+  const int ctas = std::max(1, std::min(ctx->sm_count, (n + 8 * kArgmaxThreads - 1) /
+                                                           (8 * kArgmaxThreads)));
+  argmax_kernel<<<ctas, kArgmaxThreads, 0, stream>>>(x, n, offset, ctx->argmax_scratch, nullptr,
+                                                      key);
+  return check_launch(ctx, "argmax (key)");
+}
+
+int argmax_keys_launch(mlm_ctx *ctx, const unsigned long long *keys, int nkeys, int32_t *out,
+                       cudaStream_t stream) {
+  argmax_keys_kernel<<<1, 1, 0, stream>>>(keys, nkeys, out);
+  return check_launch(ctx, "argmax (keys)");
 }
 
 int embed_launch(mlm_ctx *ctx, const void *table, int vocab, int dim, const int32_t *tok,

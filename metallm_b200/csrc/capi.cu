@@ -120,6 +120,10 @@ extern "C" int mlm_create(int device, mlm_ctx **out) {
   ctx->attn_partials_floats = attn_partial_floats_max(kMaxAttnHeads);
   if (cudaMalloc(&ctx->attn_partials, sizeof(float) * ctx->attn_partials_floats) != cudaSuccess)
     return fail(MLM_ERR_ALLOC);
+  if (cudaMalloc(&ctx->argmax_scratch, 2 * sizeof(unsigned long long)) != cudaSuccess)
+    return fail(MLM_ERR_ALLOC);
+  if (cudaMemset(ctx->argmax_scratch, 0, 2 * sizeof(unsigned long long)) != cudaSuccess)
+    return fail(MLM_ERR_CUDA);
   {
     void *hs = nullptr;
     if (cudaHostAlloc(&hs, sizeof(int), cudaHostAllocMapped) != cudaSuccess) return fail(MLM_ERR_ALLOC);
@@ -140,10 +144,12 @@ extern "C" void mlm_destroy(mlm_ctx *ctx) {
   if (!ctx) return;
   cudaSetDevice(ctx->device);
   if (ctx->own_stream) cudaStreamSynchronize(ctx->own_stream);
+  tp_destroy(ctx);
   if (ctx->gemv_counters) cudaFree(ctx->gemv_counters);
   if (ctx->gemv_partials) cudaFree(ctx->gemv_partials);
   if (ctx->attn_partials) cudaFree(ctx->attn_partials);
   if (ctx->gemm_flags) cudaFree(ctx->gemm_flags);
+  if (ctx->argmax_scratch) cudaFree(ctx->argmax_scratch);
   if (ctx->host_status) cudaFreeHost(const_cast<int *>(ctx->host_status));
   if (ctx->commit_event) cudaEventDestroy(ctx->commit_event);
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);

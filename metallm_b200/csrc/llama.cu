@@ -25,6 +25,16 @@
 // with the cache append, causal attention over the cache, the GEMM for the
 // output projection (residual added), RMSNorm, the gate/up GEMM, SiLU-gated
 // product and the down GEMM (residual added), in chunks of up to 1024 tokens.
+//
+// Tensor parallelism (when the context has an NCCL group, mlm_tp_init): each
+// rank holds its share of the heads (QKV rows, KV cache, attention), of the
+// FFN rows (gate/up) and of the vocabulary (output head), and the matching
+// input columns of the output and down projections, which therefore produce
+// partial sums: rank 0 adds the residual into its partial and one NCCL sum
+// all-reduce lands the new hidden state on every rank, twice per layer.  The
+// greedy token is the maximum of the ranks' argmax keys (one 8-byte
+// all-gather).  Everything stays on the context's stream, so the sharded
+// decode step is captured as one CUDA graph like the single-GPU one.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -88,9 +98,19 @@ struct mlm_llama {
   cudaGraph_t step_graph = nullptr;
   cudaGraphExec_t step_exec = nullptr;
   std::vector<void *> allocs;
+  // tensor parallelism: this rank's share (tp == 1 and !tp_on: one GPU)
+  bool tp_on = false;
+  int tp = 1, rank = 0;
+  float *part = nullptr, *pf_part = nullptr, *logits_l = nullptr;  // partial sums, local logits
+  unsigned long long *key_l = nullptr, *keys = nullptr;            // argmax keys: own, all ranks
 
-  int kvdim() const { return cfg.n_kv_heads * cfg.head_dim; }
-  int qkv_rows() const { return cfg.dim + 2 * kvdim(); }
+  int nh() const { return cfg.n_heads / tp; }
+  int nkv() const { return cfg.n_kv_heads / tp; }
+  int ffn() const { return cfg.ffn_dim / tp; }
+  int vocab_l() const { return cfg.vocab / tp; }
+  int qdim() const { return nh() * cfg.head_dim; }
+  int kvdim() const { return nkv() * cfg.head_dim; }
+  int qkv_rows() const { return qdim() + 2 * kvdim(); }
 
   template <class T>
   int alloc(T **p, size_t bytes) {
@@ -126,38 +146,68 @@ struct mlm_llama {
     int st;
     // RMSNorm runs inside the GEMV's x staging
     if ((st = gemv(L.qkv, qkv_rows(), c.dim, normed(h, L.attn_norm), qkv_out, nullptr))) return st;
-    if ((st = rope_qk_kv_launch(ctx, qkv_out, qkv_out + c.dim, qkv_out + c.dim + kvd, rope_freqs,
-                                c.rope, c.n_heads, c.n_kv_heads, c.head_dim, q16, L.kc, L.vc, 0,
-                                s, state + kPos)))
+    if ((st = rope_qk_kv_launch(ctx, qkv_out, qkv_out + qdim(), qkv_out + qdim() + kvd, rope_freqs,
+                                c.rope, nh(), nkv(), c.head_dim, q16, L.kc, L.vc, 0, s,
+                                state + kPos)))
       return st;
-    if ((st = attn_decode_launch(ctx, q16, L.kc, L.vc, c.n_heads, c.n_kv_heads, c.head_dim,
-                                 c.max_seq, attn_out, ctx->attn_partials,
-                                 ctx->attn_partials_floats, s, state + kPos)))
+    if ((st = attn_decode_launch(ctx, q16, L.kc, L.vc, nh(), nkv(), c.head_dim, c.max_seq,
+                                 attn_out, ctx->attn_partials, ctx->attn_partials_floats, s,
+                                 state + kPos)))
       return st;
-    if ((st = gemv(L.wo, c.dim, c.dim, gemv_half(attn_out), h, h))) return st;  // + residual
-    if ((st = gemv(L.gu, 2 * c.ffn_dim, c.dim, normed(h, L.ffn_norm), gu_out, nullptr))) return st;
+    if ((st = row_parallel(L.wo, qdim(), gemv_half(attn_out), h))) return st;  // + residual
+    if ((st = gemv(L.gu, 2 * ffn(), c.dim, normed(h, L.ffn_norm), gu_out, nullptr))) return st;
     // the SiLU-gated product is formed in the down projection's x staging,
     // as fp16 with per-32 power-of-two scales (it exceeds the fp16 range on
     // large activations)
     GemvInput sw;
     sw.mode = GemvInput::kSwiGLU;
     sw.a = gu_out;
-    sw.b = gu_out + c.ffn_dim;
-    return gemv(L.down, c.dim, c.ffn_dim, sw, h, h);  // + residual
+    sw.b = gu_out + ffn();
+    return row_parallel(L.down, ffn(), sw, h);  // + residual
   }
 
-  // embedding of state[kToken], all layers; then, when `head`, the final
-  // norm, the output GEMV into `lg` and the argmax into state[kToken]
-  int step(bool head, float *lg) {
+  // h += W x for a projection whose input columns are split over the ranks:
+  // in place on one GPU; with TP, rank 0's partial carries the residual and
+  // the sum all-reduce writes h on every rank
+  int row_parallel(const uint8_t *W, int cols, const GemvInput &in, float *h) {
+    if (!tp_on) return gemv(W, cfg.dim, cols, in, h, h);
+    int st = gemv(W, cfg.dim, cols, in, part, rank == 0 ? h : nullptr);
+    if (st != MLM_OK) return st;
+    return tp_allreduce_sum(ctx, part, h, cfg.dim, ctx->stream);
+  }
+
+  // final norm, the output GEMV and the greedy token into state[kToken];
+  // the full logits also land in lg_out when it is given
+  int head(const float *h, float *lg_out) {
+    int st;
+    if (!tp_on) {
+      float *lg = lg_out ? lg_out : logits;
+      if ((st = gemv(output, cfg.vocab, cfg.dim, normed(h, out_norm), lg, nullptr))) return st;
+      return argmax_launch(ctx, lg, cfg.vocab, state + kToken, ctx->stream);
+    }
+    if ((st = gemv(output, vocab_l(), cfg.dim, normed(h, out_norm), logits_l, nullptr))) return st;
+    if ((st = argmax_key_launch(ctx, logits_l, vocab_l(), rank * vocab_l(), key_l, ctx->stream)))
+      return st;
+    if ((st = tp_allgather_bytes(ctx, key_l, keys, sizeof(unsigned long long), ctx->stream)))
+      return st;
+    if ((st = argmax_keys_launch(ctx, keys, tp, state + kToken, ctx->stream))) return st;
+    if (lg_out)
+      return tp_allgather_bytes(ctx, logits_l, lg_out, sizeof(float) * vocab_l(), ctx->stream);
+    return MLM_OK;
+  }
+
+  // embedding of state[kToken], all layers; then, when `with_head`, the
+  // final norm, the output GEMV (logits into lg when given) and the argmax
+  // into state[kToken]
+  int step(bool with_head, float *lg) {
     int st;
     if ((st = embed_launch(ctx, tok_embd, cfg.vocab, cfg.dim, state + kToken, hidden,
                            ctx->stream)))
       return st;
     for (int l = 0; l < cfg.n_layers; ++l)
       if ((st = layer(l, hidden))) return st;
-    if (!head) return MLM_OK;
-    if ((st = gemv(output, cfg.vocab, cfg.dim, normed(hidden, out_norm), lg, nullptr))) return st;
-    return argmax_launch(ctx, lg, cfg.vocab, state + kToken, ctx->stream);
+    if (!with_head) return MLM_OK;
+    return head(hidden, lg);
   }
 
   // T prompt tokens (device ids in pf_tokens) at positions pos .. pos+T-1:
@@ -172,21 +222,30 @@ struct mlm_llama {
       if ((st = rmsnorm_rows_bf16_launch(ctx, pf_hidden, L.attn_norm, pf_x, T, c.dim, c.rms_eps, s)))
         return st;
       if ((st = gemm_launch(ctx, L.qkv, qkv_rows(), c.dim, pf_x, T, pf_qkv, nullptr, s))) return st;
-      if ((st = rope_kv_rows_launch(ctx, pf_qkv, rope_freqs, c.rope, c.n_heads, c.n_kv_heads,
-                                    c.head_dim, pos, T, pf_q16, L.kc, L.vc, s)))
+      if ((st = rope_kv_rows_launch(ctx, pf_qkv, rope_freqs, c.rope, nh(), nkv(), c.head_dim, pos,
+                                    T, pf_q16, L.kc, L.vc, s)))
         return st;
-      if ((st = attn_prefill_launch(ctx, pf_q16, L.kc, L.vc, pos, T, c.n_heads, c.n_kv_heads,
-                                    c.head_dim, pf_attn, s)))
+      if ((st = attn_prefill_launch(ctx, pf_q16, L.kc, L.vc, pos, T, nh(), nkv(), c.head_dim,
+                                    pf_attn, s)))
         return st;
-      if ((st = gemm_launch(ctx, L.wo, c.dim, c.dim, pf_attn, T, pf_hidden, pf_hidden, s))) return st;
+      if ((st = row_parallel_rows(L.wo, qdim(), pf_attn, T))) return st;
       if ((st = rmsnorm_rows_bf16_launch(ctx, pf_hidden, L.ffn_norm, pf_x, T, c.dim, c.rms_eps, s)))
         return st;
-      if ((st = gemm_launch(ctx, L.gu, 2 * c.ffn_dim, c.dim, pf_x, T, pf_gu, nullptr, s))) return st;
-      if ((st = swiglu_rows_bf16_launch(ctx, pf_gu, c.ffn_dim, T, pf_x, s))) return st;
-      if ((st = gemm_launch(ctx, L.down, c.dim, c.ffn_dim, pf_x, T, pf_hidden, pf_hidden, s)))
-        return st;
+      if ((st = gemm_launch(ctx, L.gu, 2 * ffn(), c.dim, pf_x, T, pf_gu, nullptr, s))) return st;
+      if ((st = swiglu_rows_bf16_launch(ctx, pf_gu, ffn(), T, pf_x, s))) return st;
+      if ((st = row_parallel_rows(L.down, ffn(), pf_x, T))) return st;
     }
     return MLM_OK;
+  }
+
+  // pf_hidden += X W^T over T rows for a projection with split input
+  // columns (see row_parallel)
+  int row_parallel_rows(const uint8_t *W, int cols, const void *x, int T) {
+    if (!tp_on) return gemm_launch(ctx, W, cfg.dim, cols, x, T, pf_hidden, pf_hidden, ctx->stream);
+    int st = gemm_launch(ctx, W, cfg.dim, cols, x, T, pf_part, rank == 0 ? pf_hidden : nullptr,
+                         ctx->stream);
+    if (st != MLM_OK) return st;
+    return tp_allreduce_sum(ctx, pf_part, pf_hidden, (size_t)T * cfg.dim, ctx->stream);
   }
 
   int set_state(int token, int p, int stp) {
@@ -222,50 +281,73 @@ extern "C" int mlm_llama_create(mlm_ctx *ctx, const mlm_llama_config *cfg, mlm_l
               "mlm_llama_create: rope n_dims=%d", (int)c.rope.n_dims);
   MLM_REQUIRE(ctx, 2 * c.ffn_dim <= ctx->gemv_max_tiles * 32 && c.vocab <= ctx->gemv_max_tiles * 32,
               MLM_ERR_SHAPE, "mlm_llama_create: matrices exceed the GEMV row limit");
+  const int tp = ctx->tp_comm ? ctx->tp_size : 1;
+  if (ctx->tp_comm) {
+    // heads, FFN rows and the vocabulary split evenly; the split input
+    // columns of the output and down projections stay whole Q4_K blocks
+    MLM_REQUIRE(ctx,
+                c.n_heads % tp == 0 && c.n_kv_heads % tp == 0 && c.vocab % tp == 0 &&
+                    (c.ffn_dim / tp) % kQK == 0 && c.ffn_dim % tp == 0 &&
+                    (c.n_heads / tp * c.head_dim) % kQK == 0,
+                MLM_ERR_SHAPE,
+                "mlm_llama_create: %d ranks do not divide heads %d / KV heads %d / FFN %d / vocab "
+                "%d into whole shards",
+                tp, c.n_heads, c.n_kv_heads, c.ffn_dim, c.vocab);
+  }
 
   mlm_llama *m = new (std::nothrow) mlm_llama();
   if (!m) return MLM_ERR_ALLOC;
   m->ctx = ctx;
   m->cfg = c;
+  m->tp_on = ctx->tp_comm != nullptr;
+  m->tp = tp;
+  m->rank = ctx->tp_comm ? ctx->tp_rank : 0;
   auto fail = [&](int code) {
     m->destroy();
     delete m;
     return code;
   };
-  const size_t rb_dim = q4k_row_bytes(c.dim), rb_ffn = q4k_row_bytes(c.ffn_dim);
-  const size_t cache_bytes = (size_t)c.max_seq * c.n_kv_heads * c.head_dim * sizeof(__half);
+  const size_t rb_dim = q4k_row_bytes(c.dim), rb_ffn = q4k_row_bytes(m->ffn()),
+               rb_q = q4k_row_bytes(m->qdim());
+  const size_t cache_bytes = (size_t)c.max_seq * m->kvdim() * sizeof(__half);
   m->layers.resize(c.n_layers);
   for (int l = 0; l < c.n_layers; ++l) {
     LayerBuf &L = m->layers[l];
     if (m->alloc(&L.attn_norm, sizeof(float) * c.dim) || m->alloc(&L.ffn_norm, sizeof(float) * c.dim) ||
-        m->alloc(&L.qkv, (size_t)m->qkv_rows() * rb_dim) || m->alloc(&L.wo, (size_t)c.dim * rb_dim) ||
-        m->alloc(&L.gu, (size_t)2 * c.ffn_dim * rb_dim) || m->alloc(&L.down, (size_t)c.dim * rb_ffn) ||
+        m->alloc(&L.qkv, (size_t)m->qkv_rows() * rb_dim) || m->alloc(&L.wo, (size_t)c.dim * rb_q) ||
+        m->alloc(&L.gu, (size_t)2 * m->ffn() * rb_dim) || m->alloc(&L.down, (size_t)c.dim * rb_ffn) ||
         m->alloc(&L.kc, cache_bytes) || m->alloc(&L.vc, cache_bytes))
       return fail(MLM_ERR_ALLOC);
   }
   if (m->alloc(&m->tok_embd, (size_t)c.vocab * c.dim * sizeof(__half)) ||
       m->alloc(&m->out_norm, sizeof(float) * c.dim) ||
-      m->alloc(&m->output, (size_t)c.vocab * rb_dim) ||
+      m->alloc(&m->output, (size_t)m->vocab_l() * rb_dim) ||
       m->alloc(&m->rope_freqs, sizeof(float) * (c.head_dim / 2)) ||
       m->alloc(&m->hidden, sizeof(float) * c.dim) ||
       m->alloc(&m->qkv_out, sizeof(float) * m->qkv_rows()) ||
-      m->alloc(&m->gu_out, sizeof(float) * 2 * c.ffn_dim) ||
+      m->alloc(&m->gu_out, sizeof(float) * 2 * m->ffn()) ||
       m->alloc(&m->logits, sizeof(float) * c.vocab) ||
-      m->alloc(&m->q16, sizeof(__half) * c.dim) ||
-      m->alloc(&m->attn_out, sizeof(__half) * c.dim) ||
-
+      m->alloc(&m->q16, sizeof(__half) * m->qdim()) ||
+      m->alloc(&m->attn_out, sizeof(__half) * m->qdim()) ||
       m->alloc(&m->state, sizeof(int) * kStateInts) ||
       m->alloc(&m->gen_tokens, sizeof(int32_t) * c.max_seq))
     return fail(MLM_ERR_ALLOC);
   m->pf_chunk = std::min(c.max_seq, 1024);
   {
     const size_t T = m->pf_chunk;
-    const size_t xw = std::max(c.dim, c.ffn_dim);
+    const size_t xw = std::max(c.dim, m->ffn());
     if (m->alloc(&m->pf_hidden, sizeof(float) * T * c.dim) ||
         m->alloc(&m->pf_qkv, sizeof(float) * T * m->qkv_rows()) ||
-        m->alloc(&m->pf_gu, sizeof(float) * T * 2 * c.ffn_dim) ||
-        m->alloc(&m->pf_x, 2 * T * xw) || m->alloc(&m->pf_q16, 2 * T * c.dim) ||
-        m->alloc(&m->pf_attn, 2 * T * c.dim) || m->alloc(&m->pf_tokens, sizeof(int32_t) * T))
+        m->alloc(&m->pf_gu, sizeof(float) * T * 2 * m->ffn()) ||
+        m->alloc(&m->pf_x, 2 * T * xw) || m->alloc(&m->pf_q16, 2 * T * m->qdim()) ||
+        m->alloc(&m->pf_attn, 2 * T * m->qdim()) || m->alloc(&m->pf_tokens, sizeof(int32_t) * T))
+      return fail(MLM_ERR_ALLOC);
+    if (m->tp_on &&
+        (m->alloc(&m->part, sizeof(float) * c.dim) ||
+         m->alloc(&m->pf_part, sizeof(float) * T * c.dim) ||
+         m->alloc(&m->logits_l, sizeof(float) * m->vocab_l()) ||
+         m->alloc(&m->key_l, sizeof(unsigned long long)) ||
+         m->alloc(&m->keys, sizeof(unsigned long long) * tp)))
       return fail(MLM_ERR_ALLOC);
   }
   if (cudaMemsetAsync(m->state, 0, sizeof(int) * kStateInts, ctx->stream) != cudaSuccess)
@@ -290,11 +372,11 @@ extern "C" int mlm_llama_layer_tensors(mlm_llama *m, int layer, mlm_llama_layer 
   out->attn_norm = L.attn_norm;
   out->ffn_norm = L.ffn_norm;
   out->wq = L.qkv;
-  out->wk = L.qkv + (size_t)m->cfg.dim * rb;
-  out->wv = L.qkv + (size_t)(m->cfg.dim + m->kvdim()) * rb;
+  out->wk = L.qkv + (size_t)m->qdim() * rb;
+  out->wv = L.qkv + (size_t)(m->qdim() + m->kvdim()) * rb;
   out->wo = L.wo;
   out->w_gate = L.gu;
-  out->w_up = L.gu + (size_t)m->cfg.ffn_dim * rb;
+  out->w_up = L.gu + (size_t)m->ffn() * rb;
   out->w_down = L.down;
   out->k_cache = L.kc;
   out->v_cache = L.vc;
@@ -345,7 +427,7 @@ extern "C" int mlm_llama_forward(mlm_llama *m, int token, float *logits) {
   MLM_REQUIRE(m->ctx, token >= 0 && token < m->cfg.vocab, MLM_ERR_ARG,
               "mlm_llama_forward: invalid token id %d (vocab %d)", token, m->cfg.vocab);
   int st = m->set_state(token, m->pos, 0);
-  if (st == MLM_OK) st = m->step(true, logits ? logits : m->logits);
+  if (st == MLM_OK) st = m->step(true, logits);
   if (st == MLM_OK) m->pos += 1;
   return st;
 }
@@ -372,9 +454,7 @@ extern "C" int mlm_llama_prefill(mlm_llama *m, const int32_t *tokens, int n, flo
   }
   // the output head on the last token, as a decode step ends
   const float *last = m->pf_hidden + (size_t)(T - 1) * m->cfg.dim;
-  float *lg = logits ? logits : m->logits;
-  int st = m->gemv(m->output, m->cfg.vocab, m->cfg.dim, m->normed(last, m->out_norm), lg, nullptr);
-  if (st == MLM_OK) st = argmax_launch(ctx, lg, m->cfg.vocab, m->state + kToken, ctx->stream);
+  int st = m->head(last, logits);
   if (st != MLM_OK) return st;
   if (next)
     MLM_CUDA_TRY(ctx, cudaMemcpyAsync(next, m->state + kToken, sizeof(int32_t),
@@ -394,7 +474,7 @@ extern "C" int mlm_llama_decode_greedy(mlm_llama *m, int token, int steps, int32
   if (!m->step_exec) {
     // capture one step: embedding .. argmax, then record the token and move on
     MLM_CUDA_TRY(ctx, cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
-    int st = m->step(true, m->logits);
+    int st = m->step(true, nullptr);
     if (st == MLM_OK) {
       advance_kernel<<<1, 1, 0, ctx->stream>>>(m->state, m->gen_tokens);
       st = check_launch(ctx, "mlm_llama_decode_greedy (advance)");

@@ -43,6 +43,14 @@ struct mlm_ctx {
   // between launches (each launch's waiters count them back down)
   int *gemm_flags = nullptr;
   int gemm_max_tiles = 0;
+
+  // device-wide argmax: the running 64-bit key and the CTA ticket, zero
+  // between launches
+  unsigned long long *argmax_scratch = nullptr;
+  // tensor parallelism (mlm_tp_init): an NCCL communicator over the ranks,
+  // one context per rank
+  void *tp_comm = nullptr;  // ncclComm_t
+  int tp_rank = 0, tp_size = 1;
 };
 
 namespace mlm {
@@ -109,6 +117,19 @@ int swiglu_rows_bf16_launch(mlm_ctx *ctx, const float *gu, int ffn, int T, void 
 int silu_mul_scaled_launch(mlm_ctx *ctx, const float *g, const float *u, void *out, float *scale,
                            int n, cudaStream_t stream);
 int argmax_launch(mlm_ctx *ctx, const float *x, int n, int32_t *out, cudaStream_t stream);
+// argmax of x[0..n) as a 64-bit key (value order, then ~(index + offset)),
+// for combining the argmaxes of vocabulary shards; argmax_keys_launch then
+// writes the index of the largest of `nkeys` keys
+int argmax_key_launch(mlm_ctx *ctx, const float *x, int n, int offset, unsigned long long *key,
+                      cudaStream_t stream);
+int argmax_keys_launch(mlm_ctx *ctx, const unsigned long long *keys, int nkeys, int32_t *out,
+                       cudaStream_t stream);
+// NCCL collectives on ctx->tp_comm (tp.cu)
+int tp_allreduce_sum(mlm_ctx *ctx, const float *send, float *recv, size_t count,
+                     cudaStream_t stream);
+int tp_allgather_bytes(mlm_ctx *ctx, const void *send, void *recv, size_t bytes,
+                       cudaStream_t stream);
+void tp_destroy(mlm_ctx *ctx);
 int embed_launch(mlm_ctx *ctx, const void *table, int vocab, int dim, const int32_t *tok,
                  float *out, cudaStream_t stream);
 

@@ -178,11 +178,8 @@ __global__ void __launch_bounds__(256) q4k_dequant_f32_kernel(const uint8_t *__r
 
 // ---- generators -------------------------------------------------------------
 
-__global__ void gen_q4k_kernel(uint64_t seed, uint64_t stream, uint64_t first_block,
-                               uint64_t nblocks, uint8_t *__restrict__ out) {
-  const uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
-  if (i >= nblocks) return;
-  const uint64_t b = first_block + i;
+// block b of a generated tensor, written to o (144 bytes, 16-byte aligned)
+__device__ void gen_q4k_block(uint64_t seed, uint64_t stream, uint64_t b, uint8_t *out_blk) {
   const float d = (float)fabs(rng_normal(seed, stream, 2 * b));
   const float dm = (float)fabs(rng_normal(seed, stream, 2 * b + 1));
   const uint32_t hd = __half_as_ushort(__float2half_rn(__fmul_rn(d, 0.01f)));
@@ -195,9 +192,27 @@ __global__ void gen_q4k_kernel(uint64_t seed, uint64_t stream, uint64_t first_bl
     if (2 * k + 1 < 36) w[2 * k + 1] = (uint32_t)r;
     if (2 * k + 2 < 36) w[2 * k + 2] = (uint32_t)(r >> 32);
   }
-  uint4 *o = reinterpret_cast<uint4 *>(out + i * kBlockBytes);
+  uint4 *o = reinterpret_cast<uint4 *>(out_blk);
 #pragma unroll
   for (int c = 0; c < 9; ++c) o[c] = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+}
+
+__global__ void gen_q4k_kernel(uint64_t seed, uint64_t stream, uint64_t first_block,
+                               uint64_t nblocks, uint8_t *__restrict__ out) {
+  const uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  if (i >= nblocks) return;
+  gen_q4k_block(seed, stream, first_block + i, out + i * kBlockBytes);
+}
+
+// the sub-matrix rows row0.., block columns kb0 .. kb0+nkb of a generated
+// tensor with nb_full block columns, stored densely ([rows][nkb] blocks)
+__global__ void gen_q4k_sub_kernel(uint64_t seed, uint64_t stream, uint64_t nb_full,
+                                   uint64_t row0, uint64_t rows, uint64_t kb0, uint64_t nkb,
+                                   uint8_t *__restrict__ out) {
+  const uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  if (i >= rows * nkb) return;
+  const uint64_t r = i / nkb, c = i % nkb;
+  gen_q4k_block(seed, stream, (row0 + r) * nb_full + kb0 + c, out + i * kBlockBytes);
 }
 
 __global__ void gen_f16_kernel(uint64_t seed, uint64_t stream, uint64_t first, uint64_t n,
@@ -266,6 +281,22 @@ extern "C" int mlm_gen_q4k(mlm_ctx *ctx, uint64_t seed, uint64_t stream, uint64_
   gen_q4k_kernel<<<grid, 128, 0, ctx->stream>>>(seed, stream, first_block, nblocks,
                                                 reinterpret_cast<uint8_t *>(out));
   return check_launch(ctx, "mlm_gen_q4k");
+}
+
+extern "C" int mlm_gen_q4k_sub(mlm_ctx *ctx, uint64_t seed, uint64_t stream, uint64_t nb_full,
+                               uint64_t row0, uint64_t rows, uint64_t kb0, uint64_t nkb,
+                               void *out) {
+  MLM_CHECK_CTX(ctx);
+  if (rows == 0 || nkb == 0) return MLM_OK;
+  MLM_REQUIRE(ctx, out, MLM_ERR_ARG, "mlm_gen_q4k_sub: null output");
+  MLM_REQUIRE(ctx, kb0 + nkb <= nb_full, MLM_ERR_SHAPE,
+              "mlm_gen_q4k_sub: block columns %llu..%llu of %llu", (unsigned long long)kb0,
+              (unsigned long long)(kb0 + nkb), (unsigned long long)nb_full);
+  MLM_REQUIRE(ctx, aligned16(out), MLM_ERR_ALIGN, "mlm_gen_q4k_sub: output must be 16-byte aligned");
+  const uint64_t n = rows * nkb;
+  gen_q4k_sub_kernel<<<(unsigned)((n + 127) / 128), 128, 0, ctx->stream>>>(
+      seed, stream, nb_full, row0, rows, kb0, nkb, reinterpret_cast<uint8_t *>(out));
+  return check_launch(ctx, "mlm_gen_q4k_sub");
 }
 
 extern "C" int mlm_gen_f16(mlm_ctx *ctx, uint64_t seed, uint64_t stream, uint64_t first,

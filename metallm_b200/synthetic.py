@@ -46,15 +46,31 @@ def q4k_shapes(cfg: LlamaConfig) -> Dict[str, tuple]:
             "w_up": (cfg.ffn_dim, cfg.dim), "w_down": (cfg.dim, cfg.ffn_dim)}
 
 
+def _fill_q4k(ctx, seed: int, stream: int, sh: dict, out) -> None:
+    """The (row0, rows, kb0, nkb) part of generated tensor `stream`."""
+    if sh["kb0"] == 0 and sh["nkb"] == sh["nb"]:
+        ctx.gen_q4k(seed, stream, sh["rows"] * sh["nb"], out, first_block=sh["row0"] * sh["nb"])
+    else:
+        ctx.gen_q4k_sub(seed, stream, sh["nb"], sh["row0"], sh["rows"], sh["kb0"], sh["nkb"], out)
+
+
 def fill_llama(llama, seed: int, cache_positions: int = 0, layers=None) -> None:
     """Fill the runner's weights (and the first `cache_positions` rows of
-    every layer's KV cache) on the device."""
+    every layer's KV cache) on the device.  Under tensor parallelism each
+    rank fills exactly its shard of the same whole model (metallm_b200.tp),
+    so every group size computes the same network."""
+    from .tp import Shard, layer_shards, output_shard
     ctx, cfg = llama.ctx, llama.cfg
+    rank, size = ctx.tp_info()
+    shard = Shard(rank, max(size, 1))
+    if size and cache_positions:
+        raise ValueError("prefilled caches are not generated under tensor parallelism")
     kvd = cfg.n_kv_heads * cfg.head_dim
+    shards = layer_shards(cfg, shard)
     for layer in (range(cfg.n_layers) if layers is None else layers):
         t = llama.layer_tensors(layer)
-        for name, (rows, cols) in q4k_shapes(cfg).items():
-            ctx.gen_q4k(seed, layer_stream(layer, name), rows * cols // 256, t[name])
+        for name in q4k_shapes(cfg):
+            _fill_q4k(ctx, seed, layer_stream(layer, name), shards[name], t[name])
         for name in ("attn_norm", "ffn_norm"):
             ctx.gen_f32(seed, layer_stream(layer, name), cfg.dim, t[name], 1.0, 0.02)
         if cache_positions:
@@ -63,4 +79,4 @@ def fill_llama(llama, seed: int, cache_positions: int = 0, layers=None) -> None:
     g = llama.global_tensors()
     ctx.gen_f16(seed, global_stream("tok_embd"), cfg.vocab * cfg.dim, g["tok_embd"], 0.0, 0.02)
     ctx.gen_f32(seed, global_stream("output_norm"), cfg.dim, g["output_norm"], 1.0, 0.02)
-    ctx.gen_q4k(seed, global_stream("output"), cfg.vocab * cfg.dim // 256, g["output"])
+    _fill_q4k(ctx, seed, global_stream("output"), output_shard(cfg, shard), g["output"])

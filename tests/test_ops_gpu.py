@@ -144,6 +144,40 @@ def test_argmax_first_max_and_embed(ctx):
                           table.reshape(vocab, dim)[321].astype(np.float32))
 
 
+def _argmax_ref(x: np.ndarray) -> int:
+    """First index of the maximum with NaN never winning; all-NaN -> 0."""
+    v = np.where(np.isnan(x), -np.inf, x)
+    if np.all(np.isnan(x)):
+        return 0
+    m = v.max()
+    if m == -np.inf:  # only -inf and NaN: the first -inf
+        return int(np.nonzero(x == -np.inf)[0][0])
+    return int(np.argmax(v == m))
+
+
+@pytest.mark.parametrize("n", [1, 7, 1000, 4097, 128256, 1 << 20])
+def test_argmax_sizes_ties_nan(ctx, n):
+    """Device-wide argmax over several CTAs: ties resolve to the first index,
+    NaN never wins, negative values and -inf order correctly; repeated calls
+    (the running key is reset by the last CTA of each call)."""
+    rng = np.random.default_rng(n)
+    idx = ctx.alloc(16)
+    cases = [rng.standard_normal(n).astype(np.float32) - 5.0]
+    x = rng.standard_normal(n).astype(np.float32)
+    x[rng.integers(0, n, size=max(1, n // 50))] = np.nan
+    if n > 3:
+        x[n - 2] = x[n // 3] = np.float32(50.0)  # tie: the earlier index wins
+    cases.append(x)
+    cases.append(np.full(n, np.nan, dtype=np.float32))
+    y = np.full(n, -np.inf, dtype=np.float32)
+    y[: n // 2] = np.nan
+    cases.append(y)
+    for x in cases:
+        for _ in range(2):
+            ctx.call("mlm_argmax_f32", ctx.to_device(x), n, idx)
+            assert int(idx.download(np.int32, 1)[0]) == _argmax_ref(x)
+
+
 def test_silu_mul_scaled(ctx):
     """fp16 x per-32 power-of-two scale: finite where plain fp16 overflows,
     and equal to the fp16 rounding of the scaled product."""

@@ -58,7 +58,25 @@ LLAMA_WORKLOADS = {
               "(BASELINE config 3)",
     "prefill": "Llama-3-8B-shape Q4_K model, batch 1: the 512-token prompt pass (tcgen05 Q4_K "
                "GEMM, bf16 activations) up to the first generated token (BASELINE config 3)",
+    "tp70b": "Llama-3-70B-shape Q4_K model (80 layers, hidden 8192, 64/8 heads of 128, FFN 28672, "
+             "vocab 128256), one sequence: 2048-token prompt then greedy decode, tensor-parallel "
+             "over the N GPUs (BASELINE config 4 shape, batch 1)",
 }
+
+L70 = dict(n_layers=80, dim=8192, n_heads=64, n_kv_heads=8, ffn_dim=28672, vocab=128256)
+
+
+def llama70_rank_bytes(tp: int, pos: int) -> int:
+    """Algorithmic HBM bytes one rank reads and writes in a decode step of the
+    70B shape at position pos: its shard of every weight once, its KV heads
+    up to pos, the appended K/V row."""
+    d, hd, ffn, vocab = 8192, 128, 28672, 128256
+    nh, nkv = 64 // tp, 8 // tp
+    blk = lambda rows, cols: rows * (cols // 256) * 144
+    layer = (blk((nh + 2 * nkv) * hd, d) + blk(d, nh * hd) + blk(2 * ffn // tp, d)
+             + blk(d, ffn // tp))
+    kv = 2 * (pos + 1) * nkv * hd * 2
+    return 80 * (layer + kv) + blk(vocab // tp, d) + 2 * d
 
 
 def llama_prefill_flops(n_layers: int, T: int) -> int:
@@ -417,16 +435,20 @@ def run_gpu(args, world, rank, local, pg) -> dict:
     return line
 
 
-def cpu_decode_rate(budget_s: float, threads: int) -> dict:
+def cpu_decode_rate(budget_s: float, threads: int, big: bool = False) -> dict:
     """The reference's Q4_K kernels compiled for the host (oracle/_ref) on one
     decoder layer's seven linears plus the output head, at all host threads;
-    tokens/s = 1 / (32 x layer + head).  Norms, RoPE and attention (under 1 %
-    of the bytes) are left out of the sample."""
+    tokens/s = 1 / (L x layer + head) with L = 32 (the 8B shape) or 80 (the
+    70B shape, big=True).  Norms, RoPE and attention (under 1 % of the
+    bytes) are left out of the sample."""
     from oracle import oracle as O
-    shapes = [(6144, 4096), (4096, 4096), (28672, 4096), (4096, 14336)]
+    if big:
+        nl, d, shapes = 80, 8192, [(10240, 8192), (8192, 8192), (57344, 8192), (8192, 28672)]
+    else:
+        nl, d, shapes = 32, 4096, [(6144, 4096), (4096, 4096), (28672, 4096), (4096, 14336)]
     Ws = [O.gen_q4k(3, i, r * c // 256) for i, (r, c) in enumerate(shapes)]
-    head = O.gen_q4k(3, 9, 128256 * 4096 // 256)
-    xs = {c: O.gen_f16(3, 20 + c, c) for c in (4096, 14336)}
+    head = O.gen_q4k(3, 9, 128256 * d // 256)
+    xs = {c: O.gen_f16(3, 20 + c, c) for c in {c for _, c in shapes}}
     mv = (lambda W, r, c: O.ref_q4k_matvec(W, r, c, xs[c], threads)) if O.ref_lib() is not None \
         else (lambda W, r, c: O.q4k_matvec(W, r, c, xs[c], acc64=False, nthreads=threads))
     reps, t_layer, t_head = 0, 0.0, 0.0
@@ -436,17 +458,17 @@ def cpu_decode_rate(budget_s: float, threads: int) -> dict:
         for W, (r, c) in zip(Ws, shapes):
             mv(W, r, c)
         b = time.perf_counter()
-        mv(head, 128256, 4096)
+        mv(head, 128256, d)
         t_layer += b - a
         t_head += time.perf_counter() - b
         reps += 1
-    per_token = 32 * t_layer / reps + t_head / reps
+    per_token = nl * t_layer / reps + t_head / reps
     return {"value": round(1.0 / per_token, 4), "unit": "tokens/s", "cores": threads,
             "layer_s": t_layer / reps, "head_s": t_head / reps,
             "kind": "reference" if O.ref_lib() is not None else "port",
-            "sample": f"{reps} x (one layer's 7 Q4_K matvecs + the 128256x4096 head) in "
+            "sample": f"{reps} x (one layer's 7 Q4_K matvecs + the 128256x{d} head) in "
                       f"{time.perf_counter() - t0:.1f} s, {threads} threads; tokens/s = "
-                      f"1 / (32 x layer + head)"}
+                      f"1 / ({nl} x layer + head)"}
 
 
 GEMM_SHAPE = (28672, 4096, 512)
@@ -619,7 +641,7 @@ def run_llama(args, world, rank, local, pg) -> dict:
         alg = llama_token_bytes(1, pos, with_head=False) - 2 * 4096
         value = alg * args.steps * world / (ms_max * 1e-3) / 1e9
         unit, metric_value_desc = "GB/s", "one decoder layer per step"
-        launches = args.steps * 11
+        launches = args.steps * 8  # state + QKV GEMV, RoPE, 2 attention, 3 GEMVs
         # e2e: hidden state in from pinned host memory, the layer, out again
         lib, h = ctx.lib, ctx.handle
         hbuf = ctypes.c_void_p()
@@ -668,7 +690,7 @@ def run_llama(args, world, rank, local, pg) -> dict:
         unit = "tokens/s"
         flops = llama_prefill_flops(32, T)
         alg = llama_token_bytes(32, 0)  # weights streamed once per pass
-        launches = steps * (1 + 32 * 9 + 3)
+        launches = steps * (1 + 32 * 9 + 2)  # embed, 9 per layer, head GEMV + argmax
         # e2e: the prompt ids from host memory through mlm_llama_prefill, the
         # first generated token read back
         lib, h = ctx.lib, ctx.handle
@@ -732,7 +754,7 @@ def run_llama(args, world, rank, local, pg) -> dict:
         value = steps * world / (ms_max * 1e-3)
         unit = "tokens/s"
         alg = llama_token_bytes(32, pos0 + steps // 2)
-        launches = steps * (32 * 10 + 5)
+        launches = steps * (1 + 32 * 7 + 3)  # embed, 7 per layer, head, argmax, advance
         # e2e: forward(tokenID:) per token through the C ABI, the argmax read back
         m.set_position(prompt_len)
         lib, h = ctx.lib, ctx.handle
@@ -789,6 +811,111 @@ def run_llama(args, world, rank, local, pg) -> dict:
     return line
 
 
+def run_tp70b(args, world, rank, local, pg) -> dict:
+    """The 70B shape tensor-parallel over the launch's ranks (one process and
+    one NCCL rank per GPU): prompt pass, then timed greedy decode."""
+    import torch
+
+    from metallm_b200 import Context, Llama
+    from metallm_b200.synthetic import fill_llama, llama_config
+    from metallm_b200.tp import bootstrap
+    ctx = Context(local)
+    torch.cuda.set_device(local)
+    tstream = torch.cuda.ExternalStream(ctx.stream(), device=f"cuda:{local}")
+    peaks = measured_peaks()
+    if world > 1:
+        bootstrap(ctx)
+    prompt_len, gen_len = 2048, 128
+    steps = min(args.steps, gen_len - args.warmup)
+    cfg = llama_config(max_seq=prompt_len + gen_len, **L70)
+    m = Llama(ctx, cfg)
+    fill_llama(m, 1)
+    prompt = np.random.default_rng(2048).integers(0, 128000, size=prompt_len).tolist()
+    nxt = ctx.alloc(16)
+
+    def timed(fn):
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        ev0.record(tstream)
+        fn()
+        ev1.record(tstream)
+        ev1.synchronize()
+        return ev0.elapsed_time(ev1)
+
+    m.prefill(prompt[:256], nxt)  # loads the kernels
+    m.reset()
+    ctx.wait()
+    barrier(pg, local)
+    prefill_ms = max_over_ranks(timed(lambda: m.prefill(prompt, nxt)), pg, local)
+    first = int(nxt.download(np.int32)[0])
+    out = ctx.alloc(4 * gen_len)
+    m.decode_greedy(first, args.warmup, out)  # captures the step graph
+    last = int(out.download(np.int32, args.warmup)[-1])
+    ctx.wait()
+    barrier(pg, local)
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    pos0 = m.position
+    dev_ms = timed(lambda: m.decode_greedy(last, steps, out))
+    clocks = sampler.stop()
+    toks = out.download(np.int32, steps)
+    ms_max = max_over_ranks(dev_ms, pg, local)
+    per_step_ms = ms_max / steps
+    alg = llama70_rank_bytes(world, pos0 + steps // 2)
+    kernel_gbs = alg / (per_step_ms * 1e-3) / 1e9
+    # e2e: forward(tokenID:) per token through the C ABI, the token read back
+    lib, h = ctx.lib, ctx.handle
+    htok = ctypes.c_void_p()
+    lib.mlm_host_alloc(h, 16, ctypes.byref(htok))
+    logits = ctx.alloc(4 * cfg.vocab)
+    tok_dev = ctx.alloc(16)
+    m.set_position(prompt_len)
+    tok, e2e_steps = first, min(steps, 16)
+    barrier(pg, local)
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        m.forward(tok, logits)
+        ctx.call("mlm_argmax_f32", logits, cfg.vocab, tok_dev)
+        ctx._check(lib.mlm_download_async(h, htok, ctypes.c_void_p(tok_dev.ptr), 4), "dn")
+        ctx.wait()
+        tok = ctypes.c_int32.from_address(htok.value).value
+    e2e_s = max_over_ranks(time.perf_counter() - t0, pg, local)
+    lib.mlm_host_free(h, htok)
+    line = {
+        "metric": METRIC, "value": round(steps / (ms_max * 1e-3), 2), "unit": "tokens/s",
+        "n_gpus": world, "steps": steps, "warmup": args.warmup,
+        "ms_per_step": round(per_step_ms, 5), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "q4k x f16 -> f32 (fp16 KV cache)",
+        "data": "synthetic (seeded Q4_K weights, fp16 embedding, fp32 norms generated on device; "
+                "every rank its shard of one model)",
+        "config": {"workload": LLAMA_WORKLOADS["tp70b"], "batch": 1, "prompt_tokens": prompt_len,
+                   "decode_steps_timed": steps, "parallelism": f"tp{world}",
+                   "l2": "inputs larger than L2: Q4_K weights of 39.1 GB / N per token",
+                   "algorithmic_bytes_per_step_per_rank": alg},
+        "e2e": {"value": round(e2e_steps / e2e_s, 2), "unit": "tokens/s",
+                "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 4},
+        # embed; per layer 7 kernels (+ 2 one-shot all-reduces with TP); head
+        # GEMV, argmax (key + key reduce with TP), advance
+        "gpu_launches": steps * (1 + 80 * (9 if world > 1 else 7) + (4 if world > 1 else 3)),
+        "launch": "CUDA graph (one decode step, NCCL all-reduces included, replayed per token)",
+        "roofline": {"bound": "hbm", "achieved": round(kernel_gbs, 1), "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": round(kernel_gbs / peaks["hbm_gbs"], 4),
+                     "peak_source": peaks["source"], "traffic": None,
+                     "note": "per rank: its weight shard and KV heads per step"},
+        "prefill": {"value": round(prompt_len / (prefill_ms * 1e-3), 2), "unit": "tokens/s",
+                    "path": "batched prompt pass: tcgen05 Q4_K GEMM, NCCL all-reduce per "
+                            "projection"},
+        "first_tokens": [int(t) for t in toks[:8]],
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_decode_rate(args.cpu_seconds, host_threads(), big=True)
+    m.close()
+    ctx.close()
+    return line
+
+
 def run_reference(args, world, rank) -> dict | None:
     if rank != 0:
         return None
@@ -807,9 +934,9 @@ def run_reference(args, world, rank) -> dict | None:
                         "d2h_bytes_per_step": 0}}
     if args.workload in LLAMA_WORKLOADS:
         th = host_threads()
-        r = cpu_decode_rate(args.cpu_seconds, th)
-        if args.workload == "decode":
-            v, unit, alg = r["value"], "tokens/s", llama_token_bytes(32, 640)
+        r = cpu_decode_rate(args.cpu_seconds, th, big=args.workload == "tp70b")
+        if args.workload in ("decode", "tp70b"):
+            v, unit = r["value"], "tokens/s"
             ms = 1e3 / v
         elif args.workload == "prefill":  # every prompt token through 32 layers, one head
             T = 512
@@ -883,8 +1010,8 @@ def main() -> None:
 
     world, rank, local, pg = dist_setup(args)
     try:
-        run = run_gemm if args.workload == "gemm" else \
-            run_llama if args.workload in LLAMA_WORKLOADS else run_gpu
+        run = run_gemm if args.workload == "gemm" else run_tp70b if args.workload == "tp70b" \
+            else run_llama if args.workload in LLAMA_WORKLOADS else run_gpu
         line = run(args, world, rank, local, pg)
         if rank == 0:
             print(json.dumps(line), flush=True)

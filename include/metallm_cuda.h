@@ -302,8 +302,12 @@ int mlm_argmax_f32(mlm_ctx *ctx, const float *logits, int n, int32_t *out_index_
 /* ---------------------------------------------------------------------------
  * Tensor parallelism over NCCL, one context (one process) per GPU.  No
  * counterpart in the reference, which runs on one Metal device.  NCCL is
- * loaded at run time (libnccl.so.2; a copy already in the process is
- * reused).  Collectives are enqueued on the context's stream.
+ * loaded at run time by its soname, libnccl.so.2: a copy already in the
+ * process is reused, else the system's is loaded -- a process that will also
+ * load another NCCL build (PyTorch's, say) must load that one first.
+ * Collectives are enqueued on the context's stream; small fp32 sums run as
+ * one kernel over NVLink peer memory mapped at mlm_tp_init (CUDA IPC), the
+ * rest through NCCL.
  * ------------------------------------------------------------------------ */
 
 /* a fresh NCCL unique id (NCCL_UNIQUE_ID_BYTES = 128 bytes) for rank 0 to

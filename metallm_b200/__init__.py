@@ -129,12 +129,24 @@ class Context:
                     "mlm_set_stream")
 
     # -- tensor parallelism (one context per rank) ------------------------------
+    @staticmethod
+    def _nccl_first() -> None:
+        """The library binds the NCCL already in the process when there is one.
+        PyTorch links its own NCCL build; loading it now, before the library
+        would fall back to the system's copy, keeps a single NCCL per process."""
+        try:
+            import torch.distributed  # noqa: F401
+        except ImportError:
+            pass
+
     def tp_unique_id(self) -> bytes:
+        self._nccl_first()
         buf = ctypes.create_string_buffer(128)
         self._check(self.lib.mlm_tp_unique_id(self.handle, buf, 128), "mlm_tp_unique_id")
         return buf.raw
 
     def tp_init(self, nranks: int, rank: int, unique_id: bytes) -> None:
+        self._nccl_first()
         buf = ctypes.create_string_buffer(bytes(unique_id), 128)
         self._check(self.lib.mlm_tp_init(self.handle, nranks, rank, buf), "mlm_tp_init")
 

@@ -51,6 +51,13 @@ struct mlm_ctx {
   // one context per rank
   void *tp_comm = nullptr;  // ncclComm_t
   int tp_rank = 0, tp_size = 1;
+  // one-shot all-reduce over NVLink peer memory (tp.cu): every rank's
+  // receive area (its own, then the other ranks' IPC mappings), each CTA's
+  // epoch counter
+  bool ar_ready = false;
+  float *ar_peer[8] = {};
+  void *ar_own = nullptr;
+  int *ar_epoch = nullptr;
 };
 
 namespace mlm {

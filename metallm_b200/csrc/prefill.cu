@@ -94,141 +94,181 @@ __global__ void swiglu_rows_bf16_kernel(const float *__restrict__ gu, int ffn,
 }
 
 // ---- causal GQA attention of T queries over the cache ----------------------
-// CTA = one query head x kPfQ consecutive query tokens (8 per warp); keys in
-// blocks of kPfK staged in shared memory (K rows with their 16-byte chunks
-// rotated by the row index, so lanes reading different rows hit different
-// banks); fp32 online softmax; lane l holds output dims 4l .. 4l+3.
-constexpr int kPfQ = 32;
-constexpr int kPfK = 64;
-constexpr int kPfD = 128;
-constexpr int kPfThreads = 128;
-constexpr int kPfSmem = kPfQ * kPfD * 4 + 2 * kPfK * kPfD * 2;  // 48 KB
+// Flash attention on the tensor cores (mma.sync m16n8k16, fp16 in, fp32
+// accumulate).  CTA = one query head x 64 consecutive query tokens, warp =
+// 16 of them, their Q fragments held in registers for the whole key loop.
+// Keys in blocks of 64 staged in shared memory: K rows as stored (padded to
+// 272 bytes, so the 8 rows a fragment load touches fall in distinct banks)
+// and V transposed (dims as rows, padded to 144 bytes), so both MMA operands
+// are single 32-bit loads.  Per block: S = Q K^T (64 MMAs per warp), the
+// causal mask (key position > query position), the online softmax in base 2
+// with the 1/sqrt(128) scale folded in, then O += P V (64 MMAs) with P taken
+// straight from the S accumulators as fp16 A fragments.  The reference runs
+// the same softmax(q k^T / sqrt(d)) v per token with MPS (LlamaRunner.swift:
+// 669-952); GQA head h reads KV head h / (n_heads / n_kv)
+// (AttentionKernels.metal:43).
+constexpr int kFaQ = 64;                // queries per CTA (16 per warp)
+constexpr int kFaK = 64;                // keys per block
+constexpr int kFaD = 128;               // head dim
+constexpr int kFaThreads = 128;
+constexpr int kKs = kFaD + 8;           // K row stride in halves (272 bytes)
+constexpr int kVs = kFaK + 8;           // transposed V row stride in halves (144 bytes)
 
-__global__ void __launch_bounds__(kPfThreads) attn_prefill_kernel(
+__device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
+                                          uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+__global__ void __launch_bounds__(kFaThreads) attn_prefill_kernel(
     const __half *__restrict__ q16, const __half *__restrict__ kc, const __half *__restrict__ vc,
-    int pos0, int T, int n_heads, int n_kv, float scale, __nv_bfloat16 *__restrict__ out) {
-  extern __shared__ __align__(16) uint8_t pf_smem[];
-  float *sq = reinterpret_cast<float *>(pf_smem);               // [kPfQ][128], scaled
-  uint4 *sk = reinterpret_cast<uint4 *>(sq + kPfQ * kPfD);      // [kPfK][16], rotated
-  uint4 *sv = sk + kPfK * 16;                                   // [kPfK][16]
+    int pos0, int T, int n_heads, int n_kv, float scale_log2, __nv_bfloat16 *__restrict__ out) {
+  __shared__ __align__(16) __half ks[kFaK * kKs];
+  __shared__ __align__(16) __half vt[kFaD * kVs];
   const int h = blockIdx.x, kvh = h / (n_heads / n_kv);
-  const int qt0 = blockIdx.y * kPfQ;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int i = threadIdx.x; i < kPfQ * kPfD; i += kPfThreads) {
-    const int t = qt0 + i / kPfD;
-    sq[i] = (t < T) ? __half2float(q16[((size_t)t * n_heads + h) * kPfD + (i % kPfD)]) * scale
-                    : 0.f;
-  }
-  const int qi0 = warp * 8;
-  float m[8], l[8], o[8][4];
+  const int qb = blockIdx.y * kFaQ;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int q0 = qb + warp * 16;  // first query token of the warp
+  const int r0 = q0 + g, r1 = q0 + g + 8;
+
+  // Q fragments (rows g, g+8; dims 16 ks + 2t, +1 and + 8)
+  uint32_t qa[8][4];
+  {
+    const __half *qr0 = q16 + ((size_t)min(r0, T - 1) * n_heads + h) * kFaD;
+    const __half *qr1 = q16 + ((size_t)min(r1, T - 1) * n_heads + h) * kFaD;
 #pragma unroll
-  for (int qi = 0; qi < 8; ++qi) {
-    m[qi] = -INFINITY;
-    l[qi] = 0.f;
-    o[qi][0] = o[qi][1] = o[qi][2] = o[qi][3] = 0.f;
+    for (int k = 0; k < 8; ++k) {
+      qa[k][0] = r0 < T ? *reinterpret_cast<const uint32_t *>(qr0 + 16 * k + 2 * t) : 0u;
+      qa[k][1] = r1 < T ? *reinterpret_cast<const uint32_t *>(qr1 + 16 * k + 2 * t) : 0u;
+      qa[k][2] = r0 < T ? *reinterpret_cast<const uint32_t *>(qr0 + 16 * k + 8 + 2 * t) : 0u;
+      qa[k][3] = r1 < T ? *reinterpret_cast<const uint32_t *>(qr1 + 16 * k + 8 + 2 * t) : 0u;
+    }
   }
-  const int kmax = pos0 + min(qt0 + kPfQ, T);  // keys [0, kmax) are needed
-  const size_t row_stride = (size_t)n_kv * kPfD;
-  for (int kbase = 0; kbase < kmax; kbase += kPfK) {
-    const int rows = min(kPfK, kmax - kbase);
-    __syncthreads();  // previous block fully used (and q staged on the first pass)
-    for (int i = threadIdx.x; i < rows * 16; i += kPfThreads) {
-      const int j = i >> 4, c = i & 15;
-      const size_t g = (size_t)(kbase + j) * row_stride + kvh * kPfD + c * 8;
-      sk[j * 16 + ((c + j) & 15)] = *reinterpret_cast<const uint4 *>(kc + g);
-      sv[j * 16 + c] = *reinterpret_cast<const uint4 *>(vc + g);
+  const int qp0 = pos0 + r0, qp1 = pos0 + r1;  // query positions
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+  float o[16][4];
+#pragma unroll
+  for (int d = 0; d < 16; ++d) o[d][0] = o[d][1] = o[d][2] = o[d][3] = 0.f;
+
+  // keys 0 .. kend-1: up to the CTA's last query position
+  const int kend = pos0 + min(qb + kFaQ, T);
+  for (int kb = 0; kb < kend; kb += kFaK) {
+    __syncthreads();  // the previous block is no longer read
+    for (int i = threadIdx.x; i < kFaK * 16; i += kFaThreads) {
+      const int key = i % kFaK, chunk = i / kFaK;  // consecutive keys per warp
+      uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+      if (kb + key < kend) {
+        const size_t off = ((size_t)(kb + key) * n_kv + kvh) * kFaD + chunk * 8;
+        kv = *reinterpret_cast<const uint4 *>(kc + off);
+        vv = *reinterpret_cast<const uint4 *>(vc + off);
+      }
+      *reinterpret_cast<uint4 *>(ks + key * kKs + chunk * 8) = kv;
+      const __half *ve = reinterpret_cast<const __half *>(&vv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) vt[(chunk * 8 + e) * kVs + key] = ve[e];
     }
     __syncthreads();
-    // scores of keys lane and lane + 32 for the warp's 8 queries
-    float s[8][2];
+
+    // S = Q K^T: 16 queries x 64 keys per warp
+    float sc[8][4];
 #pragma unroll
-    for (int jj = 0; jj < 2; ++jj) {
-      const int j = lane + 32 * jj;
-      float acc[8];
+    for (int j = 0; j < 8; ++j) {
+      sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+      const __half *kr = ks + (8 * j + g) * kKs + 2 * t;
 #pragma unroll
-      for (int qi = 0; qi < 8; ++qi) acc[qi] = 0.f;
-      if (j < rows) {
-        for (int c = 0; c < 16; ++c) {
-          const uint4 kv = sk[j * 16 + ((c + j) & 15)];
-          const __half2 *kh = reinterpret_cast<const __half2 *>(&kv);
-          float kf[8];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = __half22float2(kh[e]);
-            kf[2 * e] = f.x;
-            kf[2 * e + 1] = f.y;
-          }
-#pragma unroll
-          for (int qi = 0; qi < 8; ++qi) {
-            const float4 qa = *reinterpret_cast<const float4 *>(sq + (qi0 + qi) * kPfD + c * 8);
-            const float4 qb = *reinterpret_cast<const float4 *>(sq + (qi0 + qi) * kPfD + c * 8 + 4);
-            acc[qi] += qa.x * kf[0] + qa.y * kf[1] + qa.z * kf[2] + qa.w * kf[3] + qb.x * kf[4] +
-                       qb.y * kf[5] + qb.z * kf[6] + qb.w * kf[7];
-          }
-        }
-      }
-#pragma unroll
-      for (int qi = 0; qi < 8; ++qi) {
-        const int tq = qt0 + qi0 + qi;
-        const bool ok = j < rows && tq < T && kbase + j <= pos0 + tq;
-        s[qi][jj] = ok ? acc[qi] : -INFINITY;
+      for (int k = 0; k < 8; ++k) {
+        const uint32_t b0 = *reinterpret_cast<const uint32_t *>(kr + 16 * k);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t *>(kr + 16 * k + 8);
+        mma_16816(sc[j], qa[k], b0, b1);
       }
     }
-    // online softmax update
+    // mask, scale (base 2), row maxima
+    float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-    for (int qi = 0; qi < 8; ++qi) {
-      const float mx = warp_max(fmaxf(s[qi][0], s[qi][1]));
-      const float mnew = fmaxf(m[qi], mx);
-      if (mnew == -INFINITY) {  // no visible key yet for this query
-        s[qi][0] = s[qi][1] = 0.f;
-        continue;
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int kp = kb + 8 * j + 2 * t + (c & 1);
+        const int qp = (c < 2) ? qp0 : qp1;
+        const float v = (kp <= qp && kp < kend) ? sc[j][c] * scale_log2 : -INFINITY;
+        sc[j][c] = v;
+        mx[c >> 1] = fmaxf(mx[c >> 1], v);
       }
-      const float alpha = __expf(m[qi] - mnew);
-      s[qi][0] = __expf(s[qi][0] - mnew);
-      s[qi][1] = __expf(s[qi][1] - mnew);
-      l[qi] = l[qi] * alpha + warp_sum(s[qi][0] + s[qi][1]);
-#pragma unroll
-      for (int d = 0; d < 4; ++d) o[qi][d] *= alpha;
-      m[qi] = mnew;
     }
-    // P . V: lane l accumulates dims 4l .. 4l+3
+    float corr[2];
 #pragma unroll
-    for (int jj = 0; jj < 2; ++jj) {
-      for (int jl = 0; jl < 32 && 32 * jj + jl < rows; ++jl) {
-        const int j = 32 * jj + jl;
-        const uint2 vv = *reinterpret_cast<const uint2 *>(reinterpret_cast<const __half *>(sv) +
-                                                          j * kPfD + 4 * lane);
-        const float2 va = __half22float2(*reinterpret_cast<const __half2 *>(&vv.x));
-        const float2 vb = __half22float2(*reinterpret_cast<const __half2 *>(&vv.y));
+    for (int rr = 0; rr < 2; ++rr) {
+      mx[rr] = fmaxf(mx[rr], __shfl_xor_sync(0xffffffffu, mx[rr], 1));
+      mx[rr] = fmaxf(mx[rr], __shfl_xor_sync(0xffffffffu, mx[rr], 2));
+      const float mn = fmaxf(m[rr], mx[rr]);
+      corr[rr] = (mn == -INFINITY) ? 1.f : exp2f(m[rr] - mn);
+      m[rr] = mn;
+      l[rr] *= corr[rr];
+    }
 #pragma unroll
-        for (int qi = 0; qi < 8; ++qi) {
-          const float p = __shfl_sync(0xffffffffu, s[qi][jj], jl);
-          o[qi][0] += p * va.x;
-          o[qi][1] += p * va.y;
-          o[qi][2] += p * vb.x;
-          o[qi][3] += p * vb.y;
-        }
+    for (int d = 0; d < 16; ++d) {
+      o[d][0] *= corr[0];
+      o[d][1] *= corr[0];
+      o[d][2] *= corr[1];
+      o[d][3] *= corr[1];
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float mm = m[c >> 1];
+        const float p = (sc[j][c] == -INFINITY) ? 0.f : exp2f(sc[j][c] - mm);
+        sc[j][c] = p;
+        l[c >> 1] += p;
+      }
+    }
+    // O += P V: P from the S accumulators (keys 16 kk .. 16 kk + 15)
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      const uint32_t pa[4] = {pack_half2(sc[2 * kk][0], sc[2 * kk][1]),
+                              pack_half2(sc[2 * kk][2], sc[2 * kk][3]),
+                              pack_half2(sc[2 * kk + 1][0], sc[2 * kk + 1][1]),
+                              pack_half2(sc[2 * kk + 1][2], sc[2 * kk + 1][3])};
+#pragma unroll
+      for (int d = 0; d < 16; ++d) {
+        const __half *vr = vt + (8 * d + g) * kVs + 16 * kk + 2 * t;
+        const uint32_t b0 = *reinterpret_cast<const uint32_t *>(vr);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t *>(vr + 8);
+        mma_16816(o[d], pa, b0, b1);
       }
     }
   }
+  // normalise and store (bf16, the output projection's GEMM input)
 #pragma unroll
-  for (int qi = 0; qi < 8; ++qi) {
-    const int tq = qt0 + qi0 + qi;
-    if (tq < T) {
-      const float inv = 1.0f / l[qi];
-      __nv_bfloat16 *dst = out + ((size_t)tq * n_heads + h) * kPfD + 4 * lane;
-      *reinterpret_cast<__nv_bfloat162 *>(dst) = __floats2bfloat162_rn(o[qi][0] * inv, o[qi][1] * inv);
-      *reinterpret_cast<__nv_bfloat162 *>(dst + 2) =
-          __floats2bfloat162_rn(o[qi][2] * inv, o[qi][3] * inv);
-    }
+  for (int rr = 0; rr < 2; ++rr) {
+    l[rr] += __shfl_xor_sync(0xffffffffu, l[rr], 1);
+    l[rr] += __shfl_xor_sync(0xffffffffu, l[rr], 2);
+  }
+  const float inv0 = 1.f / l[0], inv1 = 1.f / l[1];
+#pragma unroll
+  for (int d = 0; d < 16; ++d) {
+    const int col = h * kFaD + 8 * d + 2 * t;
+    if (r0 < T)
+      *reinterpret_cast<__nv_bfloat162 *>(out + (size_t)r0 * n_heads * kFaD + col) =
+          __floats2bfloat162_rn(o[d][0] * inv0, o[d][1] * inv0);
+    if (r1 < T)
+      *reinterpret_cast<__nv_bfloat162 *>(out + (size_t)r1 * n_heads * kFaD + col) =
+          __floats2bfloat162_rn(o[d][2] * inv1, o[d][3] * inv1);
   }
 }
 
 }  // namespace
 
 int prefill_init(mlm_ctx *ctx) {
-  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_prefill_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem));
   return MLM_OK;
 }
 
@@ -259,11 +299,13 @@ int rope_kv_rows_launch(mlm_ctx *ctx, const float *qkv, const float *freqs, cons
 
 int attn_prefill_launch(mlm_ctx *ctx, const void *q16, const void *kc, const void *vc, int pos0,
                         int T, int n_heads, int n_kv, int head_dim, void *out, cudaStream_t stream) {
-  MLM_REQUIRE(ctx, head_dim == kPfD && n_kv > 0 && n_heads % n_kv == 0, MLM_ERR_UNSUPPORTED,
+  MLM_REQUIRE(ctx, head_dim == kFaD && n_kv > 0 && n_heads % n_kv == 0, MLM_ERR_UNSUPPORTED,
               "prefill attention: head_dim=%d heads=%d/%d", head_dim, n_heads, n_kv);
-  attn_prefill_kernel<<<dim3(n_heads, (T + kPfQ - 1) / kPfQ), kPfThreads, kPfSmem, stream>>>(
+  // log2(e) / sqrt(head_dim): the softmax runs in base 2
+  const float scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
+  attn_prefill_kernel<<<dim3(n_heads, (T + kFaQ - 1) / kFaQ), kFaThreads, 0, stream>>>(
       reinterpret_cast<const __half *>(q16), reinterpret_cast<const __half *>(kc),
-      reinterpret_cast<const __half *>(vc), pos0, T, n_heads, n_kv, 1.0f / sqrtf((float)head_dim),
+      reinterpret_cast<const __half *>(vc), pos0, T, n_heads, n_kv, scale_log2,
       reinterpret_cast<__nv_bfloat16 *>(out));
   return check_launch(ctx, "prefill (attention)");
 }

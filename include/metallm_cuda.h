@@ -410,6 +410,27 @@ int mlm_llama_prefill(mlm_llama *m, const int32_t *tokens, int n, float *logits,
  * other capture on ctx's stream). */
 int mlm_llama_decode_greedy(mlm_llama *m, int token, int steps, int32_t *tokens_out_dev);
 
+/* A batch of independent sequences on one runner (the reference decodes one
+ * conversation at a time).  mlm_llama_create_batch allocates `batch`
+ * (1 .. min(64, max_seq)) sets of KV caches; the calls above act on
+ * sequence 0.  Each sequence's prompt goes through mlm_llama_prefill_seq
+ * (as mlm_llama_prefill, on that sequence's caches and position).  A
+ * batched step runs the batch's tokens together through the tensor-core
+ * GEMM (the weights are streamed once for all of them, bf16 activations) and
+ * attends per sequence: mlm_llama_forward_batch takes one host token per
+ * sequence and writes fp32 logits [batch][vocab] (device, may be NULL);
+ * mlm_llama_decode_greedy_batch runs `steps` greedy steps from one host
+ * token per sequence, tokens_out_dev[i * batch + b] receiving sequence b's
+ * i-th token (one batched step captured once as a CUDA graph and replayed).
+ * Every sequence advances by one position per step. */
+int mlm_llama_create_batch(mlm_ctx *ctx, const mlm_llama_config *cfg, int batch, mlm_llama **out);
+int mlm_llama_prefill_seq(mlm_llama *m, int seq, const int32_t *tokens, int n, float *logits,
+                          int32_t *next_token_dev);
+int mlm_llama_seq_position(const mlm_llama *m, int seq);
+int mlm_llama_forward_batch(mlm_llama *m, const int32_t *tokens, float *logits);
+int mlm_llama_decode_greedy_batch(mlm_llama *m, const int32_t *tokens, int steps,
+                                  int32_t *tokens_out_dev);
+
 #ifdef __cplusplus
 }
 #endif

@@ -248,12 +248,17 @@ class Llama:
     write the raw GGUF blocks straight into them.
     """
 
-    def __init__(self, ctx: Context, cfg: LlamaConfig):
+    def __init__(self, ctx: Context, cfg: LlamaConfig, batch: int = 1):
         self.ctx = ctx
         self.cfg = cfg
+        self.batch = batch
         h = ctypes.c_void_p()
-        ctx._check(ctx.lib.mlm_llama_create(ctx.handle, ctypes.byref(cfg), ctypes.byref(h)),
-                   "mlm_llama_create")
+        if batch == 1:
+            st = ctx.lib.mlm_llama_create(ctx.handle, ctypes.byref(cfg), ctypes.byref(h))
+        else:
+            st = ctx.lib.mlm_llama_create_batch(ctx.handle, ctypes.byref(cfg), batch,
+                                                ctypes.byref(h))
+        ctx._check(st, "mlm_llama_create")
         self.handle = h
         ctx._runners.add(self)
 
@@ -292,13 +297,32 @@ class Llama:
             self.handle, token, ctypes.c_void_p(int(logits)) if logits is not None else None),
             "mlm_llama_forward")
 
-    def prefill(self, tokens: Sequence[int], next_token=None, logits=None) -> None:
+    def prefill(self, tokens: Sequence[int], next_token=None, logits=None, seq: int = 0) -> None:
         arr = (ctypes.c_int32 * len(tokens))(*[int(t) for t in tokens])
-        self._check(self.ctx.lib.mlm_llama_prefill(
-            self.handle, arr, len(tokens),
-            ctypes.c_void_p(int(logits)) if logits is not None else None,
-            ctypes.c_void_p(int(next_token)) if next_token is not None else None),
-            "mlm_llama_prefill")
+        lg = ctypes.c_void_p(int(logits)) if logits is not None else None
+        nx = ctypes.c_void_p(int(next_token)) if next_token is not None else None
+        if seq == 0:
+            st = self.ctx.lib.mlm_llama_prefill(self.handle, arr, len(tokens), lg, nx)
+        else:
+            st = self.ctx.lib.mlm_llama_prefill_seq(self.handle, seq, arr, len(tokens), lg, nx)
+        self._check(st, "mlm_llama_prefill")
+
+    def seq_position(self, seq: int) -> int:
+        return int(self.ctx.lib.mlm_llama_seq_position(self.handle, seq))
+
+    def forward_batch(self, tokens: Sequence[int], logits=None) -> None:
+        """One step of every sequence; logits fp32 [batch][vocab] on the device."""
+        arr = (ctypes.c_int32 * self.batch)(*[int(t) for t in tokens])
+        self._check(self.ctx.lib.mlm_llama_forward_batch(
+            self.handle, arr, ctypes.c_void_p(int(logits)) if logits is not None else None),
+            "mlm_llama_forward_batch")
+
+    def decode_greedy_batch(self, tokens: Sequence[int], steps: int, tokens_out) -> None:
+        """`steps` greedy steps of every sequence; tokens_out int32 [steps][batch]."""
+        arr = (ctypes.c_int32 * self.batch)(*[int(t) for t in tokens])
+        self._check(self.ctx.lib.mlm_llama_decode_greedy_batch(
+            self.handle, arr, steps, ctypes.c_void_p(int(tokens_out))),
+            "mlm_llama_decode_greedy_batch")
 
     def decode_greedy(self, token: int, steps: int, tokens_out) -> None:
         self._check(self.ctx.lib.mlm_llama_decode_greedy(self.handle, token, steps,

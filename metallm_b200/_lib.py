@@ -122,6 +122,11 @@ SIGNATURES = [
     ("mlm_llama_forward", c_int, [c_vp, c_int, c_vp]),
     ("mlm_llama_prefill", c_int, [c_vp, ctypes.POINTER(ctypes.c_int32), c_int, c_vp, c_vp]),
     ("mlm_llama_decode_greedy", c_int, [c_vp, c_int, c_int, c_vp]),
+    ("mlm_llama_create_batch", c_int, [c_vp, c_vp, c_int, ctypes.POINTER(c_vp)]),
+    ("mlm_llama_prefill_seq", c_int, [c_vp, c_int, c_vp, c_int, c_vp, c_vp]),
+    ("mlm_llama_seq_position", c_int, [c_vp, c_int]),
+    ("mlm_llama_forward_batch", c_int, [c_vp, c_vp, c_vp]),
+    ("mlm_llama_decode_greedy_batch", c_int, [c_vp, c_vp, c_int, c_vp]),
     ("mlm_tp_unique_id", c_int, [c_vp, c_vp, c_size]),
     ("mlm_tp_init", c_int, [c_vp, c_int, c_int, c_vp]),
     ("mlm_tp_info", c_int, [c_vp, ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),

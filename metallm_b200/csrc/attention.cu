@@ -32,15 +32,22 @@ template <int G>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_partial_kernel(
     const __half *__restrict__ q, const __half *__restrict__ kc, const __half *__restrict__ vc,
     int n_heads, int n_kv, int seq_len, int chunk_len, float scale,
-    float *__restrict__ partials, const int *__restrict__ pos_dev) {
+    float *__restrict__ partials, const int *__restrict__ pos_dev, size_t q_bs, size_t kv_bs,
+    size_t part_bs) {
   __shared__ float s_scores[G][kAttnChunk * 2];
   __shared__ float s_out[kAttnThreads / 32][G][kAttnD];
   const int kvh = blockIdx.x;
   const int chunk = blockIdx.y;
   const int p0 = chunk * chunk_len;
+  // sequence blockIdx.z of a batch: its query, cache and scratch
+  const int bz = blockIdx.z;
+  q += bz * q_bs;
+  kc += bz * kv_bs;
+  vc += bz * kv_bs;
+  partials += bz * part_bs;
   // graph-replayed decode: the position lives in device memory and the grid
   // covers the cache's capacity; chunks past the sequence do nothing
-  if (pos_dev) seq_len = *pos_dev + 1;
+  if (pos_dev) seq_len = pos_dev[bz] + 1;
   if (p0 >= seq_len) return;
   const int p1 = min(seq_len, p0 + chunk_len);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -160,12 +167,17 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_partial_kernel(
   }
 }
 
+template <class OutT>
 __global__ void attn_decode_merge_kernel(const float *__restrict__ partials, int n_heads,
-                                         int nchunks, __half *__restrict__ out,
-                                         const int *__restrict__ pos_dev, int chunk_len) {
+                                         int nchunks, OutT *__restrict__ out,
+                                         const int *__restrict__ pos_dev, int chunk_len,
+                                         size_t part_bs, size_t out_bs) {
   const int h = blockIdx.x;
   const int dd = threadIdx.x;  // 128 threads
-  if (pos_dev) nchunks = (*pos_dev + chunk_len) / chunk_len;
+  const int bz = blockIdx.y;   // sequence of a batch
+  partials += bz * part_bs;
+  out += bz * out_bs;
+  if (pos_dev) nchunks = (pos_dev[bz] + chunk_len) / chunk_len;
   float M = -INFINITY;
   for (int c = 0; c < nchunks; ++c) M = fmaxf(M, partials[((size_t)c * n_heads + h) * kAttnPartial]);
   float L = 0.f, O = 0.f;
@@ -175,15 +187,20 @@ __global__ void attn_decode_merge_kernel(const float *__restrict__ partials, int
     L += pp[1] * w;
     O += pp[2 + dd] * w;
   }
-  out[(size_t)h * kAttnD + dd] = __float2half_rn(O / L);
+  out[(size_t)h * kAttnD + dd] = from_float<OutT>(O / L);
 }
 
-// seq_len positions, or, when pos_dev is set, *pos_dev + 1 positions read on
-// the device out of a cache of capacity seq_len (a launch a captured graph can
-// replay at every step): fixed 128-position chunks covering the capacity.
-int attn_decode_launch(mlm_ctx *ctx, const void *q, const void *kc, const void *vc, int n_heads,
-                       int n_kv, int head_dim, int seq_len, void *out, float *partials,
-                       size_t partial_floats, cudaStream_t stream, const int *pos_dev) {
+// seq_len positions, or, when pos_dev is set, pos_dev[b] + 1 positions read
+// on the device out of a cache of capacity seq_len (a launch a captured graph
+// can replay at every step): fixed 128-position chunks covering the capacity.
+// `batch` sequences (grid z): sequence b reads q + b q_bs, caches + b kv_bs,
+// uses partials + b part_bs and writes out + b out_bs (as OutT).
+template <class OutT>
+static int attn_decode_impl(mlm_ctx *ctx, const void *q, const void *kc, const void *vc,
+                            int n_heads, int n_kv, int head_dim, int seq_len, OutT *out,
+                            float *partials, size_t partial_floats, cudaStream_t stream,
+                            const int *pos_dev, int batch, size_t q_bs, size_t kv_bs,
+                            size_t out_bs) {
   MLM_REQUIRE(ctx, head_dim == kAttnD, MLM_ERR_UNSUPPORTED,
               "mlm_attn_decode: head_dim=%d (this build handles %d)", head_dim, kAttnD);
   MLM_REQUIRE(ctx, n_kv > 0 && n_heads % n_kv == 0, MLM_ERR_SHAPE,
@@ -191,7 +208,8 @@ int attn_decode_launch(mlm_ctx *ctx, const void *q, const void *kc, const void *
   const int G = n_heads / n_kv;
   MLM_REQUIRE(ctx, G == 1 || G == 2 || G == 4 || G == 8, MLM_ERR_UNSUPPORTED,
               "mlm_attn_decode: GQA group %d (supported 1, 2, 4, 8)", G);
-  MLM_REQUIRE(ctx, seq_len > 0, MLM_ERR_SHAPE, "mlm_attn_decode: seq_len=%d", seq_len);
+  MLM_REQUIRE(ctx, seq_len > 0 && batch > 0, MLM_ERR_SHAPE, "mlm_attn_decode: seq_len=%d batch=%d",
+              seq_len, batch);
   int nchunks, chunk_len;
   if (pos_dev) {
     chunk_len = 2 * kAttnChunk;
@@ -207,36 +225,64 @@ int attn_decode_launch(mlm_ctx *ctx, const void *q, const void *kc, const void *
   MLM_REQUIRE(ctx, chunk_len <= 2 * kAttnChunk, MLM_ERR_SHAPE,
               "mlm_attn_decode: seq_len=%d exceeds %d positions", seq_len,
               2 * kAttnChunk * kAttnMaxChunks);
-  MLM_REQUIRE(ctx, (size_t)nchunks * n_heads * kAttnPartial <= partial_floats, MLM_ERR_SHAPE,
-              "mlm_attn_decode: %d heads exceed the attention scratch", n_heads);
+  const size_t part_bs = (size_t)nchunks * n_heads * kAttnPartial;
+  MLM_REQUIRE(ctx, part_bs * batch <= partial_floats, MLM_ERR_SHAPE,
+              "mlm_attn_decode: %d heads x %d sequences exceed the attention scratch", n_heads,
+              batch);
   const float scale = 1.0f / sqrtf((float)head_dim);
-  dim3 grid(n_kv, nchunks);
+  dim3 grid(n_kv, nchunks, batch);
   const __half *qh = reinterpret_cast<const __half *>(q);
   const __half *kh = reinterpret_cast<const __half *>(kc);
   const __half *vh = reinterpret_cast<const __half *>(vc);
   switch (G) {
     case 1:
       attn_decode_partial_kernel<1><<<grid, kAttnThreads, kAttnStageBytes, stream>>>(
-          qh, kh, vh, n_heads, n_kv, seq_len, chunk_len, scale, partials, pos_dev);
+          qh, kh, vh, n_heads, n_kv, seq_len, chunk_len, scale, partials, pos_dev, q_bs, kv_bs,
+          part_bs);
       break;
     case 2:
       attn_decode_partial_kernel<2><<<grid, kAttnThreads, kAttnStageBytes, stream>>>(
-          qh, kh, vh, n_heads, n_kv, seq_len, chunk_len, scale, partials, pos_dev);
+          qh, kh, vh, n_heads, n_kv, seq_len, chunk_len, scale, partials, pos_dev, q_bs, kv_bs,
+          part_bs);
       break;
     case 4:
       attn_decode_partial_kernel<4><<<grid, kAttnThreads, kAttnStageBytes, stream>>>(
-          qh, kh, vh, n_heads, n_kv, seq_len, chunk_len, scale, partials, pos_dev);
+          qh, kh, vh, n_heads, n_kv, seq_len, chunk_len, scale, partials, pos_dev, q_bs, kv_bs,
+          part_bs);
       break;
     default:
       attn_decode_partial_kernel<8><<<grid, kAttnThreads, kAttnStageBytes, stream>>>(
-          qh, kh, vh, n_heads, n_kv, seq_len, chunk_len, scale, partials, pos_dev);
+          qh, kh, vh, n_heads, n_kv, seq_len, chunk_len, scale, partials, pos_dev, q_bs, kv_bs,
+          part_bs);
       break;
   }
   int st = check_launch(ctx, "mlm_attn_decode (partial)");
   if (st != MLM_OK) return st;
-  attn_decode_merge_kernel<<<n_heads, kAttnD, 0, stream>>>(
-      partials, n_heads, nchunks, reinterpret_cast<__half *>(out), pos_dev, chunk_len);
+  attn_decode_merge_kernel<OutT><<<dim3(n_heads, batch), kAttnD, 0, stream>>>(
+      partials, n_heads, nchunks, out, pos_dev, chunk_len, part_bs, out_bs);
   return check_launch(ctx, "mlm_attn_decode (merge)");
+}
+
+int attn_decode_launch(mlm_ctx *ctx, const void *q, const void *kc, const void *vc, int n_heads,
+                       int n_kv, int head_dim, int seq_len, void *out, float *partials,
+                       size_t partial_floats, cudaStream_t stream, const int *pos_dev) {
+  return attn_decode_impl(ctx, q, kc, vc, n_heads, n_kv, head_dim, seq_len,
+                          reinterpret_cast<__half *>(out), partials, partial_floats, stream,
+                          pos_dev, 1, 0, 0, 0);
+}
+
+int attn_decode_batch_launch(mlm_ctx *ctx, const void *q, const void *kc, const void *vc,
+                             int n_heads, int n_kv, int head_dim, int capacity, int batch,
+                             size_t kv_bs, void *out_bf16, float *partials,
+                             size_t partial_floats, cudaStream_t stream, const int *pos_dev) {
+  const size_t qd = (size_t)n_heads * head_dim;
+  return attn_decode_impl(ctx, q, kc, vc, n_heads, n_kv, head_dim, capacity,
+                          reinterpret_cast<__nv_bfloat16 *>(out_bf16), partials, partial_floats,
+                          stream, pos_dev, batch, qd, kv_bs, qd);
+}
+
+size_t attn_decode_partial_floats(int n_heads, int capacity) {
+  return (size_t)((capacity + 2 * kAttnChunk - 1) / (2 * kAttnChunk)) * n_heads * kAttnPartial;
 }
 
 // called once per context, with its device current
@@ -318,6 +364,17 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(
   }
 }
 
+// rows of keys laid out [nkeys][rows] (an all-gather of every rank's row
+// keys): out[b] = the index of the largest key of row b
+__global__ void argmax_keys_rows_kernel(const unsigned long long *keys, int nkeys, int rows,
+                                        int32_t *out) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= rows) return;
+  unsigned long long k = 0;
+  for (int i = 0; i < nkeys; ++i) k = max(k, keys[(size_t)i * rows + b]);
+  out[b] = k ? (int32_t)~(uint32_t)(k & 0xFFFFFFFFull) : 0;
+}
+
 __global__ void argmax_keys_kernel(const unsigned long long *keys, int nkeys, int32_t *out) {
   unsigned long long k = 0;
   for (int i = 0; i < nkeys; ++i) k = max(k, keys[i]);
@@ -329,6 +386,12 @@ int argmax_launch(mlm_ctx *ctx, const float *x, int n, int32_t *out, cudaStream_
                                                            (8 * kArgmaxThreads)));
   argmax_kernel<<<ctas, kArgmaxThreads, 0, stream>>>(x, n, 0, ctx->argmax_scratch, out, nullptr);
   return check_launch(ctx, "mlm_argmax_f32");
+}
+
+int argmax_keys_rows_launch(mlm_ctx *ctx, const unsigned long long *keys, int nkeys, int rows,
+                            int32_t *out, cudaStream_t stream) {
+  argmax_keys_rows_kernel<<<(rows + 127) / 128, 128, 0, stream>>>(keys, nkeys, rows, out);
+  return check_launch(ctx, "argmax (row keys)");
 }
 
 int argmax_key_launch(mlm_ctx *ctx, const float *x, int n, int offset, unsigned long long *key,

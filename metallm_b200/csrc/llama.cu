@@ -69,6 +69,18 @@ __global__ void advance_kernel(int *st, int32_t *tokens) {
   st[kPos] += 1;
 }
 
+// the same for a batch of sequences: gen[step][b] = tok[b], positions + 1
+__global__ void advance_batch_kernel(int *st, int *pos, const int32_t *tok, int32_t *gen,
+                                     int batch) {
+  const int step = st[kStep];
+  for (int b = threadIdx.x; b < batch; b += blockDim.x) {
+    gen[(size_t)step * batch + b] = tok[b];
+    pos[b] += 1;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) st[kStep] = step + 1;
+}
+
 inline size_t q4k_row_bytes(int cols) { return (size_t)(cols / kQK) * kBlockBytes; }
 
 }  // namespace
@@ -103,6 +115,23 @@ struct mlm_llama {
   int tp = 1, rank = 0;
   float *part = nullptr, *pf_part = nullptr, *logits_l = nullptr;  // partial sums, local logits
   unsigned long long *key_l = nullptr, *keys = nullptr;            // argmax keys: own, all ranks
+  // a batch of sequences (mlm_llama_create_batch): sequence b's KV caches
+  // start b * seq_elems() elements into each layer's; `pos` is sequence 0's
+  // position (and, inside mlm_llama_prefill_seq, that of the sequence cur)
+  int batch = 1, cur = 0;
+  std::vector<int> seq_pos;                     // positions of sequences 1.. (0: pos)
+  int *pos_b = nullptr;                         // device positions [batch]
+  int32_t *tok_b = nullptr;                     // device tokens [batch]
+  int32_t *gen_b = nullptr;                     // [max_seq][batch] greedy tokens
+  float *b_logits = nullptr;                    // [batch][vocab / tp]
+  float *b_partials = nullptr;                  // attention scratch of the batch
+  size_t b_partial_floats = 0;
+  unsigned long long *b_keys_l = nullptr, *b_keys = nullptr;  // [batch], [tp][batch]
+  cudaGraph_t bstep_graph = nullptr;
+  cudaGraphExec_t bstep_exec = nullptr;
+
+  size_t seq_elems() const { return (size_t)cfg.max_seq * kvdim(); }
+  int position(int b) const { return b == 0 ? pos : seq_pos[b]; }
 
   int nh() const { return cfg.n_heads / tp; }
   int nkv() const { return cfg.n_kv_heads / tp; }
@@ -222,10 +251,11 @@ struct mlm_llama {
       if ((st = rmsnorm_rows_bf16_launch(ctx, pf_hidden, L.attn_norm, pf_x, T, c.dim, c.rms_eps, s)))
         return st;
       if ((st = gemm_launch(ctx, L.qkv, qkv_rows(), c.dim, pf_x, T, pf_qkv, nullptr, s))) return st;
+      __half *kc = L.kc + cur * seq_elems(), *vc = L.vc + cur * seq_elems();
       if ((st = rope_kv_rows_launch(ctx, pf_qkv, rope_freqs, c.rope, nh(), nkv(), c.head_dim, pos,
-                                    T, pf_q16, L.kc, L.vc, s)))
+                                    T, pf_q16, kc, vc, s)))
         return st;
-      if ((st = attn_prefill_launch(ctx, pf_q16, L.kc, L.vc, pos, T, nh(), nkv(), c.head_dim,
+      if ((st = attn_prefill_launch(ctx, pf_q16, kc, vc, pos, T, nh(), nkv(), c.head_dim,
                                     pf_attn, s)))
         return st;
       if ((st = row_parallel_rows(L.wo, qdim(), pf_attn, T))) return st;
@@ -234,6 +264,64 @@ struct mlm_llama {
       if ((st = gemm_launch(ctx, L.gu, 2 * ffn(), c.dim, pf_x, T, pf_gu, nullptr, s))) return st;
       if ((st = swiglu_rows_bf16_launch(ctx, pf_gu, ffn(), T, pf_x, s))) return st;
       if ((st = row_parallel_rows(L.down, ffn(), pf_x, T))) return st;
+    }
+    return MLM_OK;
+  }
+
+  // one decode step of every sequence of the batch (token tok_b[b] at
+  // position pos_b[b]): the prompt pass's row kernels and tensor-core GEMMs
+  // over the batch's B rows, attention per sequence over its own cache; the
+  // greedy tokens land in tok_b; logits (all rows, [B][vocab]) in lg_out
+  // when it is given
+  int step_batch(float *lg_out) {
+    const mlm_llama_config &c = cfg;
+    cudaStream_t s = ctx->stream;
+    const int B = batch;
+    int st;
+    if ((st = embed_rows_launch(ctx, tok_embd, c.vocab, c.dim, tok_b, B, pf_hidden, s))) return st;
+    for (int l = 0; l < c.n_layers; ++l) {
+      const LayerBuf &L = layers[l];
+      if ((st = rmsnorm_rows_bf16_launch(ctx, pf_hidden, L.attn_norm, pf_x, B, c.dim, c.rms_eps, s)))
+        return st;
+      if ((st = gemm_launch(ctx, L.qkv, qkv_rows(), c.dim, pf_x, B, pf_qkv, nullptr, s))) return st;
+      if ((st = rope_kv_batch_launch(ctx, pf_qkv, rope_freqs, c.rope, nh(), nkv(), c.head_dim, B,
+                                     pos_b, seq_elems(), pf_q16, L.kc, L.vc, s)))
+        return st;
+      if ((st = attn_decode_batch_launch(ctx, pf_q16, L.kc, L.vc, nh(), nkv(), c.head_dim,
+                                         c.max_seq, B, seq_elems(), pf_attn, b_partials,
+                                         b_partial_floats, s, pos_b)))
+        return st;
+      if ((st = row_parallel_rows(L.wo, qdim(), pf_attn, B))) return st;
+      if ((st = rmsnorm_rows_bf16_launch(ctx, pf_hidden, L.ffn_norm, pf_x, B, c.dim, c.rms_eps, s)))
+        return st;
+      if ((st = gemm_launch(ctx, L.gu, 2 * ffn(), c.dim, pf_x, B, pf_gu, nullptr, s))) return st;
+      if ((st = swiglu_rows_bf16_launch(ctx, pf_gu, ffn(), B, pf_x, s))) return st;
+      if ((st = row_parallel_rows(L.down, ffn(), pf_x, B))) return st;
+    }
+    if ((st = rmsnorm_rows_bf16_launch(ctx, pf_hidden, out_norm, pf_x, B, c.dim, c.rms_eps, s)))
+      return st;
+    if ((st = gemm_launch(ctx, output, vocab_l(), c.dim, pf_x, B, b_logits, nullptr, s))) return st;
+    for (int b = 0; b < B; ++b) {
+      st = tp_on ? argmax_key_launch(ctx, b_logits + (size_t)b * vocab_l(), vocab_l(),
+                                     rank * vocab_l(), b_keys_l + b, s)
+                 : argmax_launch(ctx, b_logits + (size_t)b * c.vocab, c.vocab, tok_b + b, s);
+      if (st != MLM_OK) return st;
+    }
+    if (tp_on) {
+      if ((st = tp_allgather_bytes(ctx, b_keys_l, b_keys, sizeof(unsigned long long) * B, s)))
+        return st;
+      if ((st = argmax_keys_rows_launch(ctx, b_keys, tp, B, tok_b, s))) return st;
+    }
+    if (lg_out) {
+      if (!tp_on)
+        MLM_CUDA_TRY(ctx, cudaMemcpyAsync(lg_out, b_logits, sizeof(float) * B * c.vocab,
+                                          cudaMemcpyDeviceToDevice, s));
+      else
+        for (int b = 0; b < B; ++b)  // row b: rank r's slice lands at [b][r V/R ..)
+          if ((st = tp_allgather_bytes(ctx, b_logits + (size_t)b * vocab_l(),
+                                       lg_out + (size_t)b * c.vocab, sizeof(float) * vocab_l(),
+                                       s)))
+            return st;
     }
     return MLM_OK;
   }
@@ -256,16 +344,20 @@ struct mlm_llama {
   void destroy() {
     if (step_exec) cudaGraphExecDestroy(step_exec);
     if (step_graph) cudaGraphDestroy(step_graph);
+    if (bstep_exec) cudaGraphExecDestroy(bstep_exec);
+    if (bstep_graph) cudaGraphDestroy(bstep_graph);
     for (void *p : allocs) cudaFree(p);
     allocs.clear();
   }
 };
 
-extern "C" int mlm_llama_create(mlm_ctx *ctx, const mlm_llama_config *cfg, mlm_llama **out) {
+static int llama_create(mlm_ctx *ctx, const mlm_llama_config *cfg, int batch, mlm_llama **out) {
   MLM_CHECK_CTX(ctx);
   MLM_REQUIRE(ctx, cfg && out, MLM_ERR_ARG, "mlm_llama_create: null argument");
   *out = nullptr;
   const mlm_llama_config &c = *cfg;
+  MLM_REQUIRE(ctx, batch >= 1 && batch <= 64 && batch <= std::min(c.max_seq, 1024), MLM_ERR_SHAPE,
+              "mlm_llama_create_batch: batch %d (1 .. min(64, max_seq))", batch);
   MLM_REQUIRE(ctx, c.n_layers > 0 && c.vocab > 0 && c.max_seq > 0 && c.max_seq <= 8192,
               MLM_ERR_SHAPE, "mlm_llama_create: layers=%d vocab=%d max_seq=%d (max 8192)",
               c.n_layers, c.vocab, c.max_seq);
@@ -302,6 +394,8 @@ extern "C" int mlm_llama_create(mlm_ctx *ctx, const mlm_llama_config *cfg, mlm_l
   m->tp_on = ctx->tp_comm != nullptr;
   m->tp = tp;
   m->rank = ctx->tp_comm ? ctx->tp_rank : 0;
+  m->batch = batch;
+  m->seq_pos.assign(batch, 0);
   auto fail = [&](int code) {
     m->destroy();
     delete m;
@@ -309,7 +403,7 @@ extern "C" int mlm_llama_create(mlm_ctx *ctx, const mlm_llama_config *cfg, mlm_l
   };
   const size_t rb_dim = q4k_row_bytes(c.dim), rb_ffn = q4k_row_bytes(m->ffn()),
                rb_q = q4k_row_bytes(m->qdim());
-  const size_t cache_bytes = (size_t)c.max_seq * m->kvdim() * sizeof(__half);
+  const size_t cache_bytes = (size_t)batch * c.max_seq * m->kvdim() * sizeof(__half);
   m->layers.resize(c.n_layers);
   for (int l = 0; l < c.n_layers; ++l) {
     LayerBuf &L = m->layers[l];
@@ -342,6 +436,14 @@ extern "C" int mlm_llama_create(mlm_ctx *ctx, const mlm_llama_config *cfg, mlm_l
         m->alloc(&m->pf_x, 2 * T * xw) || m->alloc(&m->pf_q16, 2 * T * m->qdim()) ||
         m->alloc(&m->pf_attn, 2 * T * m->qdim()) || m->alloc(&m->pf_tokens, sizeof(int32_t) * T))
       return fail(MLM_ERR_ALLOC);
+    m->b_partial_floats = (size_t)batch * attn_decode_partial_floats(m->nh(), c.max_seq);
+    if (m->alloc(&m->pos_b, sizeof(int) * batch) || m->alloc(&m->tok_b, sizeof(int32_t) * batch) ||
+        m->alloc(&m->gen_b, sizeof(int32_t) * c.max_seq * batch) ||
+        m->alloc(&m->b_logits, sizeof(float) * batch * m->vocab_l()) ||
+        m->alloc(&m->b_partials, sizeof(float) * m->b_partial_floats) ||
+        m->alloc(&m->b_keys_l, sizeof(unsigned long long) * batch) ||
+        m->alloc(&m->b_keys, sizeof(unsigned long long) * batch * tp))
+      return fail(MLM_ERR_ALLOC);
     if (m->tp_on &&
         (m->alloc(&m->part, sizeof(float) * c.dim) ||
          m->alloc(&m->pf_part, sizeof(float) * T * c.dim) ||
@@ -354,6 +456,15 @@ extern "C" int mlm_llama_create(mlm_ctx *ctx, const mlm_llama_config *cfg, mlm_l
     return fail(set_error(ctx, MLM_ERR_CUDA, "mlm_llama_create: memset failed"));
   *out = m;
   return MLM_OK;
+}
+
+extern "C" int mlm_llama_create(mlm_ctx *ctx, const mlm_llama_config *cfg, mlm_llama **out) {
+  return llama_create(ctx, cfg, 1, out);
+}
+
+extern "C" int mlm_llama_create_batch(mlm_ctx *ctx, const mlm_llama_config *cfg, int batch,
+                                      mlm_llama **out) {
+  return llama_create(ctx, cfg, batch, out);
 }
 
 extern "C" void mlm_llama_destroy(mlm_llama *m) {
@@ -396,7 +507,13 @@ extern "C" int mlm_llama_global_tensors(mlm_llama *m, mlm_llama_globals *out) {
 extern "C" int mlm_llama_reset(mlm_llama *m) {
   if (!m) return MLM_ERR_ARG;
   m->pos = 0;
+  std::fill(m->seq_pos.begin(), m->seq_pos.end(), 0);
   return MLM_OK;
+}
+
+extern "C" int mlm_llama_seq_position(const mlm_llama *m, int seq) {
+  if (!m || seq < 0 || seq >= m->batch) return -1;
+  return m->position(seq);
 }
 
 extern "C" int mlm_llama_set_position(mlm_llama *m, int pos) {
@@ -497,5 +614,92 @@ extern "C" int mlm_llama_decode_greedy(mlm_llama *m, int token, int steps, int32
   MLM_CUDA_TRY(ctx, cudaMemcpyAsync(tokens_out, m->gen_tokens, sizeof(int32_t) * steps,
                                     cudaMemcpyDeviceToDevice, ctx->stream));
   m->pos += steps;
+  return MLM_OK;
+}
+
+extern "C" int mlm_llama_prefill_seq(mlm_llama *m, int seq, const int32_t *tokens, int n,
+                                     float *logits, int32_t *next) {
+  if (!m) return MLM_ERR_ARG;
+  MLM_REQUIRE(m->ctx, seq >= 0 && seq < m->batch, MLM_ERR_ARG,
+              "mlm_llama_prefill_seq: sequence %d of %d", seq, m->batch);
+  if (seq == 0) return mlm_llama_prefill(m, tokens, n, logits, next);
+  const int saved = m->pos;
+  m->pos = m->seq_pos[seq];
+  m->cur = seq;
+  const int st = mlm_llama_prefill(m, tokens, n, logits, next);
+  m->seq_pos[seq] = m->pos;
+  m->pos = saved;
+  m->cur = 0;
+  return st;
+}
+
+// device tokens and positions of the batch from the host
+static int batch_begin(mlm_llama *m, const int32_t *tokens, int steps, const char *what) {
+  mlm_ctx *ctx = m->ctx;
+  MLM_REQUIRE(ctx, tokens, MLM_ERR_ARG, "%s: no tokens", what);
+  std::vector<int> pos(m->batch);
+  for (int b = 0; b < m->batch; ++b) {
+    MLM_REQUIRE(ctx, tokens[b] >= 0 && tokens[b] < m->cfg.vocab, MLM_ERR_ARG,
+                "%s: invalid token id %d for sequence %d", what, tokens[b], b);
+    pos[b] = m->position(b);
+    MLM_REQUIRE(ctx, pos[b] + steps <= m->cfg.max_seq, MLM_ERR_STATE,
+                "%s: %d steps at position %d of sequence %d exceed the cache (%d)", what, steps,
+                pos[b], b, m->cfg.max_seq);
+  }
+  MLM_CUDA_TRY(ctx, cudaMemcpyAsync(m->tok_b, tokens, sizeof(int32_t) * m->batch,
+                                    cudaMemcpyHostToDevice, ctx->stream));
+  MLM_CUDA_TRY(ctx, cudaMemcpyAsync(m->pos_b, pos.data(), sizeof(int) * m->batch,
+                                    cudaMemcpyHostToDevice, ctx->stream));
+  // the copies read pageable host memory: let them finish before `pos` goes
+  MLM_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+  return MLM_OK;
+}
+
+static void batch_advance(mlm_llama *m, int steps) {
+  m->pos += steps;
+  for (int b = 1; b < m->batch; ++b) m->seq_pos[b] += steps;
+}
+
+extern "C" int mlm_llama_forward_batch(mlm_llama *m, const int32_t *tokens, float *logits) {
+  if (!m) return MLM_ERR_ARG;
+  int st = batch_begin(m, tokens, 1, "mlm_llama_forward_batch");
+  if (st == MLM_OK) st = m->step_batch(logits);
+  if (st == MLM_OK) batch_advance(m, 1);
+  return st;
+}
+
+extern "C" int mlm_llama_decode_greedy_batch(mlm_llama *m, const int32_t *tokens, int steps,
+                                             int32_t *tokens_out) {
+  if (!m) return MLM_ERR_ARG;
+  mlm_ctx *ctx = m->ctx;
+  MLM_REQUIRE(ctx, tokens_out && steps > 0, MLM_ERR_ARG, "mlm_llama_decode_greedy_batch: no output");
+  int st = batch_begin(m, tokens, steps, "mlm_llama_decode_greedy_batch");
+  if (st != MLM_OK) return st;
+  if (!m->bstep_exec) {
+    // capture one batched step: embedding .. argmax, then record the tokens
+    MLM_CUDA_TRY(ctx, cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+    st = m->step_batch(nullptr);
+    if (st == MLM_OK) {
+      advance_batch_kernel<<<1, 64, 0, ctx->stream>>>(m->state, m->pos_b, m->tok_b, m->gen_b,
+                                                     m->batch);
+      st = check_launch(ctx, "mlm_llama_decode_greedy_batch (advance)");
+    }
+    cudaGraph_t g = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(ctx->stream, &g);
+    if (st != MLM_OK || e != cudaSuccess) {
+      if (g) cudaGraphDestroy(g);
+      cudaGetLastError();
+      return st != MLM_OK ? st
+                          : set_error(ctx, MLM_ERR_CUDA, "mlm_llama_decode_greedy_batch: capture: %s",
+                                      cudaGetErrorString(e));
+    }
+    m->bstep_graph = g;
+    MLM_CUDA_TRY(ctx, cudaGraphInstantiate(&m->bstep_exec, g, 0));
+  }
+  if ((st = m->set_state(0, 0, 0)) != MLM_OK) return st;
+  for (int i = 0; i < steps; ++i) MLM_CUDA_TRY(ctx, cudaGraphLaunch(m->bstep_exec, ctx->stream));
+  MLM_CUDA_TRY(ctx, cudaMemcpyAsync(tokens_out, m->gen_b, sizeof(int32_t) * steps * m->batch,
+                                    cudaMemcpyDeviceToDevice, ctx->stream));
+  batch_advance(m, steps);
   return MLM_OK;
 }

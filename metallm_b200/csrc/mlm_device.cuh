@@ -97,6 +97,18 @@ __device__ __forceinline__ float safe_weight(float w) {
 }
 // SiLU-gated product of the decode FFN (kernel_silu_f16 then kernel_mul_f16,
 // ActivationKernels.metal:6-27, in fp32)
+// round an fp32 value to the storage type of an output (round to nearest even)
+template <class T>
+__device__ __forceinline__ T from_float(float v);
+template <>
+__device__ __forceinline__ __half from_float<__half>(float v) {
+  return __float2half_rn(v);
+}
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_float<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
 __device__ __forceinline__ float swiglu(float g, float u) {
   return g * (1.0f / (1.0f + expf(-g))) * u;
 }

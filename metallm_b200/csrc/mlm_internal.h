@@ -55,7 +55,7 @@ struct mlm_ctx {
   // receive area (its own, then the other ranks' IPC mappings), each CTA's
   // epoch counter
   bool ar_ready = false;
-  float *ar_peer[8] = {};
+  void *ar_peer[8] = {};
   void *ar_own = nullptr;
   int *ar_epoch = nullptr;
 };
@@ -105,6 +105,15 @@ int rope_qk_kv_launch(mlm_ctx *ctx, const float *q, const float *k, const float 
 int attn_decode_launch(mlm_ctx *ctx, const void *q, const void *kc, const void *vc, int n_heads,
                        int n_kv, int head_dim, int seq_len, void *out, float *partials,
                        size_t partial_floats, cudaStream_t stream, const int *pos_dev);
+// decode attention of `batch` sequences at once (one new token each, at
+// position pos_dev[b]): q fp16 [batch][n_heads][128], caches of sequence b at
+// kc/vc + b * kv_bs elements (capacity positions each), out bf16
+// [batch][n_heads][128]; partials hold batch * attn_decode_partial_floats
+int attn_decode_batch_launch(mlm_ctx *ctx, const void *q, const void *kc, const void *vc,
+                             int n_heads, int n_kv, int head_dim, int capacity, int batch,
+                             size_t kv_bs, void *out_bf16, float *partials,
+                             size_t partial_floats, cudaStream_t stream, const int *pos_dev);
+size_t attn_decode_partial_floats(int n_heads, int capacity);
 int silu_mul_launch(mlm_ctx *ctx, const float *g, const float *u, void *out, int n,
                     cudaStream_t stream);
 // batched prompt pass (prefill.cu, q4k_gemm.cu)
@@ -117,6 +126,10 @@ int rmsnorm_rows_bf16_launch(mlm_ctx *ctx, const float *x, const float *w, void 
 int rope_kv_rows_launch(mlm_ctx *ctx, const float *qkv, const float *freqs, const mlm_rope_args &a,
                         int nq, int nkv, int d, int pos0, int T, void *q_out, void *kc, void *vc,
                         cudaStream_t stream);
+int rope_kv_batch_launch(mlm_ctx *ctx, const float *qkv, const float *freqs,
+                         const mlm_rope_args &a, int nq, int nkv, int d, int batch,
+                         const int *pos_dev, size_t kv_bs, void *q_out, void *kc, void *vc,
+                         cudaStream_t stream);
 int attn_prefill_launch(mlm_ctx *ctx, const void *q16, const void *kc, const void *vc, int pos0,
                         int T, int n_heads, int n_kv, int head_dim, void *out, cudaStream_t stream);
 int swiglu_rows_bf16_launch(mlm_ctx *ctx, const float *gu, int ffn, int T, void *out,
@@ -131,6 +144,8 @@ int argmax_key_launch(mlm_ctx *ctx, const float *x, int n, int offset, unsigned 
                       cudaStream_t stream);
 int argmax_keys_launch(mlm_ctx *ctx, const unsigned long long *keys, int nkeys, int32_t *out,
                        cudaStream_t stream);
+int argmax_keys_rows_launch(mlm_ctx *ctx, const unsigned long long *keys, int nkeys, int rows,
+                            int32_t *out, cudaStream_t stream);
 // NCCL collectives on ctx->tp_comm (tp.cu)
 int tp_allreduce_sum(mlm_ctx *ctx, const float *send, float *recv, size_t count,
                      cudaStream_t stream);

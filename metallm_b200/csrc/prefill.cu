@@ -45,13 +45,20 @@ __global__ void __launch_bounds__(512) rmsnorm_rows_bf16_kernel(const float *__r
 
 // RoPE of q and k of token t at position pos0 + t; q -> fp16 q_out, rotated
 // k and v -> fp16 cache rows (rope_qk_kv_kernel for many tokens).
-// qkv: fp32 [T][nq*d | nkv*d | nkv*d].
+// qkv: fp32 [T][nq*d | nkv*d | nkv*d].  With pos_dev (a batch of sequences,
+// one token each): token t is at position pos_dev[t] of sequence t, whose
+// caches start kv_bs elements after sequence t-1's.
 __global__ void rope_kv_rows_kernel(mlm_rope_args a, RopeConsts k, const float *__restrict__ freqs,
                                     const float *__restrict__ qkv, int nq, int nkv, int d,
                                     int pos0, __half *__restrict__ q_out, __half *__restrict__ kc,
-                                    __half *__restrict__ vc) {
+                                    __half *__restrict__ vc, const int *__restrict__ pos_dev,
+                                    size_t kv_bs) {
   const int t = blockIdx.y;
-  const int pos = pos0 + t;
+  const int pos = pos_dev ? pos_dev[t] : pos0 + t;
+  if (pos_dev) {
+    kc += t * kv_bs;
+    vc += t * kv_bs;
+  }
   const int pairs = d / 2;
   const int nqp = nq * pairs, nkp = nkv * pairs;
   const float *row = qkv + (size_t)t * (nq + 2 * nkv) * d;
@@ -293,8 +300,20 @@ int rope_kv_rows_launch(mlm_ctx *ctx, const float *qkv, const float *freqs, cons
   const int total = nq * (d / 2) + 2 * nkv * (d / 2);
   rope_kv_rows_kernel<<<dim3((total + 255) / 256, T), 256, 0, stream>>>(
       a, k, freqs, qkv, nq, nkv, d, pos0, reinterpret_cast<__half *>(q_out),
-      reinterpret_cast<__half *>(kc), reinterpret_cast<__half *>(vc));
+      reinterpret_cast<__half *>(kc), reinterpret_cast<__half *>(vc), nullptr, 0);
   return check_launch(ctx, "prefill (rope)");
+}
+
+int rope_kv_batch_launch(mlm_ctx *ctx, const float *qkv, const float *freqs,
+                         const mlm_rope_args &a, int nq, int nkv, int d, int batch,
+                         const int *pos_dev, size_t kv_bs, void *q_out, void *kc, void *vc,
+                         cudaStream_t stream) {
+  const RopeConsts k = rope_consts(a);
+  const int total = nq * (d / 2) + 2 * nkv * (d / 2);
+  rope_kv_rows_kernel<<<dim3((total + 255) / 256, batch), 256, 0, stream>>>(
+      a, k, freqs, qkv, nq, nkv, d, 0, reinterpret_cast<__half *>(q_out),
+      reinterpret_cast<__half *>(kc), reinterpret_cast<__half *>(vc), pos_dev, kv_bs);
+  return check_launch(ctx, "batched decode (rope)");
 }
 
 int attn_prefill_launch(mlm_ctx *ctx, const void *q16, const void *kc, const void *vc, int pos0,

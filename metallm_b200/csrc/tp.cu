@@ -15,14 +15,14 @@
 // as one kernel over NVLink peer memory ("one-shot"): every rank has a
 // receive area with one slot per source rank, mapped into the other ranks'
 // address spaces through CUDA IPC when the group forms.  CTA c of each rank
-// stores its slice of the partial into slot [rank] of every rank's area,
-// then raises its flag there (the value is CTA c's epoch, a device counter
-// that advances with every call, so a captured graph replays correctly);
-// it waits (bounded) for the flags of CTA c of every rank in its own area
-// and adds the slots in rank order, so every rank computes the same sum
-// bit for bit.  Two areas alternate by epoch parity: a rank can only start
-// call e+2 after every rank's part of call e+1 arrived, which each rank
-// sends only after it finished reading call e.  Larger reductions (the
+// stores its slice of the partial into slot [rank] of every rank's area as
+// 8-byte words (value, epoch) -- the epoch is CTA c's device counter, which
+// advances with every call, so a captured graph replays correctly -- then
+// polls (bounded) its own area until every rank's words of its slice carry
+// the epoch, and adds them in rank order, so every rank computes the same
+// sum bit for bit.  Two areas alternate by epoch parity: a rank can only
+// start call e+2 after every rank's part of call e+1 arrived, which each
+// rank sends only after it finished reading call e.  Larger reductions (the
 // prompt pass) go to NCCL.
 #include <dlfcn.h>
 #include <nccl.h>
@@ -88,81 +88,73 @@ constexpr int kArMaxRanks = 8;
 constexpr int kArMaxFloats = 64 * 1024;  // per call: 256 KB of fp32
 constexpr int kArCtas = 16;
 constexpr int kArThreads = 256;
-// receive area: data [2][ranks][kArMaxFloats] floats, then flags
-// [2][ranks][kArCtas] ints
-constexpr size_t kArDataFloats = (size_t)2 * kArMaxRanks * kArMaxFloats;
-constexpr size_t kArBytes = kArDataFloats * sizeof(float) + 2 * kArMaxRanks * kArCtas * sizeof(int);
+// receive area: [2 parities][ranks][kArMaxFloats] 8-byte words, each the
+// value's bits and the epoch that wrote it
+constexpr size_t kArWords = (size_t)2 * kArMaxRanks * kArMaxFloats;
+constexpr size_t kArBytes = kArWords * sizeof(uint2);
 
 struct ArPeers {
-  float *area[kArMaxRanks];
+  uint2 *area[kArMaxRanks];
 };
 
-__device__ __forceinline__ int *ar_flags(float *area) {
-  return reinterpret_cast<int *>(area + kArDataFloats);
-}
-
+// Each word carries its own epoch: an aligned 8-byte store is single-copy
+// atomic, so a receiver that sees epoch e in a word sees the value stored
+// with it, and no fence or separate flag is needed.
 __global__ void __launch_bounds__(kArThreads) ar_oneshot_kernel(const float *__restrict__ send,
                                                                float *__restrict__ recv, int count,
                                                                ArPeers peers, int rank, int nranks,
                                                                int *epoch, int *status) {
-  __shared__ int s_e, s_ok;
+  __shared__ int s_e;
   const int c = blockIdx.x;
-  if (threadIdx.x == 0) {
-    s_e = epoch[c] + 1;
-    s_ok = 1;
-  }
+  // launched as a programmatic dependent of the kernel that wrote `send`: the
+  // epoch was last written two launches back, which that kernel waited for
+  // before it let this one start; `send` is read only after the wait.  The
+  // kernel after this one (the next GEMV) may start streaming its weights
+  // while this one exchanges; it waits for this grid before reading `recv`.
+  if (threadIdx.x == 0) s_e = epoch[c] + 1;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;");
   __syncthreads();
-  const int e = s_e, par = e & 1;
-  // this CTA's slice, in float4s
-  const int n4 = count >> 2, per = (n4 + kArCtas - 1) / kArCtas;
-  const int lo = c * per, hi = min(n4, lo + per);
-  const float4 *src = reinterpret_cast<const float4 *>(send);
-  for (int p = 0; p < nranks; ++p) {
-    float4 *dst = reinterpret_cast<float4 *>(peers.area[p] +
-                                             ((size_t)par * kArMaxRanks + rank) * kArMaxFloats);
-    for (int i = lo + threadIdx.x; i < hi; i += kArThreads) dst[i] = src[i];
+  const uint32_t e = (uint32_t)s_e;
+  const size_t par = e & 1;
+  const int per = (count + kArCtas - 1) / kArCtas;
+  const int lo = c * per, hi = min(count, lo + per);
+  for (int i = lo + threadIdx.x; i < hi; i += kArThreads) {
+    const uint2 w = make_uint2(__float_as_uint(send[i]), e);
+    for (int p = 0; p < nranks; ++p) {
+      uint2 *dst = peers.area[p] + (par * kArMaxRanks + rank) * kArMaxFloats + i;
+      asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(dst), "r"(w.x), "r"(w.y)
+                   : "memory");
+    }
   }
-  // the barrier orders the CTA's stores before the flag's release store, and a
-  // release is cumulative over what the releasing thread has observed
-  __syncthreads();
-  if (threadIdx.x < nranks) {  // raise this CTA's flag in rank threadIdx.x's area
-    int *f = ar_flags(peers.area[threadIdx.x]) + ((size_t)par * kArMaxRanks + rank) * kArCtas + c;
-    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(f), "r"(e) : "memory");
-  }
-  if (threadIdx.x < nranks) {  // wait for source rank threadIdx.x in this rank's area
-    const int *f = ar_flags(peers.area[rank]) +
-                   ((size_t)par * kArMaxRanks + threadIdx.x) * kArCtas + c;
-    const unsigned long long t0 = global_ns();
-    for (int spin = 0;; ++spin) {
-      int v;
-      asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-      if (v == e) break;
-      if ((spin & 255) == 255) {  // check the budget now and then; sleep once spinning is long
-        if (global_ns() - t0 > kWaitBudgetNs) {
-          atomicExch(status, MLM_ERR_TIMEOUT);
-          s_ok = 0;
-          break;
+  const uint2 *mine = peers.area[rank] + par * kArMaxRanks * kArMaxFloats;
+  bool ok = true;
+  for (int i = lo + threadIdx.x; i < hi; i += kArThreads) {
+    float acc = 0.f;
+    for (int r = 0; r < nranks && ok; ++r) {  // rank order: every rank sums alike
+      const uint2 *src = mine + (size_t)r * kArMaxFloats + i;
+      uint32_t v, f;
+      asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v), "=r"(f) : "l"(src)
+                   : "memory");
+      if (f != e) {
+        const unsigned long long t0 = global_ns();
+        for (int spin = 0; f != e; ++spin) {
+          asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v), "=r"(f) : "l"(src)
+                       : "memory");
+          if ((spin & 255) == 255 && global_ns() - t0 > kWaitBudgetNs) {
+            atomicExch(status, MLM_ERR_TIMEOUT);
+            ok = false;
+            break;
+          }
         }
-        if (spin > 4096) __nanosleep(64);
       }
+      acc += __uint_as_float(v);
     }
+    if (!ok) break;
+    recv[i] = acc;
   }
   __syncthreads();
-  if (s_ok) {
-    const float *mine = peers.area[rank] + (size_t)par * kArMaxRanks * kArMaxFloats;
-    for (int i = lo + threadIdx.x; i < hi; i += kArThreads) {
-      float4 a = __ldcg(reinterpret_cast<const float4 *>(mine) + i);
-      for (int r = 1; r < nranks; ++r) {
-        const float4 b = __ldcg(reinterpret_cast<const float4 *>(mine + (size_t)r * kArMaxFloats) + i);
-        a.x += b.x;
-        a.y += b.y;
-        a.z += b.z;
-        a.w += b.w;
-      }
-      reinterpret_cast<float4 *>(recv)[i] = a;
-    }
-  }
-  if (threadIdx.x == 0) epoch[c] = e;
+  if (threadIdx.x == 0) epoch[c] = (int)e;
 }
 
 // maps every rank's receive area: IPC handles travel by an NCCL all-gather
@@ -194,7 +186,7 @@ int ar_setup(mlm_ctx *ctx) {
   if (st != MLM_OK) return st;
   for (int p = 0; p < n; ++p) {
     if (p == ctx->tp_rank) {
-      ctx->ar_peer[p] = static_cast<float *>(ctx->ar_own);
+      ctx->ar_peer[p] = ctx->ar_own;
       continue;
     }
     void *ptr = nullptr;
@@ -202,7 +194,7 @@ int ar_setup(mlm_ctx *ctx) {
       cudaGetLastError();
       return set_error(ctx, MLM_ERR_CUDA, "mlm_tp_init: opening rank %d's receive area", p);
     }
-    ctx->ar_peer[p] = static_cast<float *>(ptr);
+    ctx->ar_peer[p] = ptr;
   }
   ctx->ar_ready = true;
   return MLM_OK;
@@ -212,14 +204,27 @@ int ar_setup(mlm_ctx *ctx) {
 
 int tp_allreduce_sum(mlm_ctx *ctx, const float *send, float *recv, size_t count,
                      cudaStream_t stream) {
-  if (ctx->ar_ready && count <= (size_t)kArMaxFloats && count % 4 == 0 && aligned16(send) &&
-      aligned16(recv)) {
+  if (ctx->ar_ready && count <= (size_t)kArMaxFloats) {
     ArPeers peers{};
-    for (int p = 0; p < ctx->tp_size; ++p) peers.area[p] = ctx->ar_peer[p];
-    ar_oneshot_kernel<<<kArCtas, kArThreads, 0, stream>>>(send, recv, (int)count, peers,
-                                                          ctx->tp_rank, ctx->tp_size,
-                                                          ctx->ar_epoch, ctx->dev_status);
-    return check_launch(ctx, "one-shot all-reduce");
+    for (int p = 0; p < ctx->tp_size; ++p) peers.area[p] = static_cast<uint2 *>(ctx->ar_peer[p]);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kArCtas);
+    cfg.blockDim = dim3(kArThreads);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, ar_oneshot_kernel, send, recv, (int)count,
+                                             peers, ctx->tp_rank, ctx->tp_size, ctx->ar_epoch,
+                                             ctx->dev_status);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return set_error(ctx, MLM_ERR_CUDA, "one-shot all-reduce: launch failed: %s",
+                       cudaGetErrorString(e));
+    }
+    return MLM_OK;
   }
   return nccl_check(ctx,
                     g_nccl.AllReduce(send, recv, count, ncclFloat32, ncclSum,

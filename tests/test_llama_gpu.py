@@ -234,6 +234,66 @@ def test_prefill_then_decode_matches_forward(ctx):
     m.close()
 
 
+def _greedy_with_gaps(cfg, layers, glob, caches, tok, pos, steps):
+    """The oracle's greedy continuation and, per step, the relative gap
+    between its two largest logits."""
+    out, gaps = [], []
+    for _ in range(steps):
+        lg = LO.model_forward(layers, glob, caches, tok, pos, cfg_dict(cfg))
+        top = np.sort(lg)[::-1]
+        gaps.append(float((top[0] - top[1]) / max(abs(top[0]), 1e-30)))
+        tok = int(np.argmax(lg))
+        out.append(tok)
+        pos += 1
+    return out, gaps
+
+
+def test_batch_of_sequences_matches_oracle(ctx):
+    """Three sequences with prompts of 5, 9 and 3 tokens, each through its own
+    caches; one batched step (logits of every sequence) and a greedy batch
+    continuation against the oracle's per-sequence runs.  The batched step
+    feeds bf16 activations to the tensor-core GEMM, so greedy tokens must
+    agree up to the first step whose oracle top-2 logits are within a
+    relative 1e-3 of each other (beyond it either choice is a rounding away)."""
+    from metallm_b200.synthetic import fill_llama
+    cfg = _small_cfg()
+    B, steps = 3, 6
+    m = Llama(ctx, cfg, batch=B)
+    fill_llama(m, SEED)
+    rng = np.random.default_rng(3)
+    prompts = [rng.integers(0, cfg.vocab, size=n).tolist() for n in (5, 9, 3)]
+    nxt = ctx.alloc(16)
+    firsts = []
+    for b, pr in enumerate(prompts):
+        m.prefill(pr, nxt, None, seq=b)
+        firsts.append(int(nxt.download(np.int32)[0]))
+        assert m.seq_position(b) == len(pr)
+    logits = ctx.alloc(4 * B * cfg.vocab)
+    m.forward_batch(firsts, logits)
+    got = logits.download(np.float32).reshape(B, cfg.vocab)
+    want_next, oracle_state = [], []
+    for b, pr in enumerate(prompts):
+        layers, glob, caches = _oracle_model(cfg)
+        for pos, tok in enumerate(pr):
+            LO.model_forward(layers, glob, caches, tok, pos, cfg_dict(cfg))
+        w = LO.model_forward(layers, glob, caches, firsts[b], len(pr), cfg_dict(cfg))
+        assert rel_l2(got[b], w) < TOL, (b, rel_l2(got[b], w))
+        want_next.append(int(np.argmax(w)))
+        oracle_state.append((layers, glob, caches))
+    assert all(m.seq_position(b) == len(pr) + 1 for b, pr in enumerate(prompts))
+    out = ctx.alloc(4 * steps * B)
+    m.decode_greedy_batch(want_next, steps, out)
+    toks = out.download(np.int32).reshape(steps, B)
+    for b, pr in enumerate(prompts):
+        layers, glob, caches = oracle_state[b]
+        ref, gaps = _greedy_with_gaps(cfg, layers, glob, caches, want_next[b], len(pr) + 1, steps)
+        for i in range(steps):
+            assert int(toks[i, b]) == ref[i], (b, i, toks[:, b].tolist(), ref, gaps)
+            if gaps[i] < 1e-3:
+                break
+    m.close()
+
+
 def test_llama_errors(ctx):
     from metallm_b200.synthetic import llama_config as lc
     with pytest.raises(MLMError) as e:

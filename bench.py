@@ -59,24 +59,24 @@ LLAMA_WORKLOADS = {
     "prefill": "Llama-3-8B-shape Q4_K model, batch 1: the 512-token prompt pass (tcgen05 Q4_K "
                "GEMM, bf16 activations) up to the first generated token (BASELINE config 3)",
     "tp70b": "Llama-3-70B-shape Q4_K model (80 layers, hidden 8192, 64/8 heads of 128, FFN 28672, "
-             "vocab 128256), one sequence: 2048-token prompt then greedy decode, tensor-parallel "
-             "over the N GPUs (BASELINE config 4 shape, batch 1)",
+             "vocab 128256), a batch of 8 sequences: each a 2048-token prompt, then greedy "
+             "decode of all 8 together, tensor-parallel over the N GPUs (BASELINE config 4)",
 }
 
 L70 = dict(n_layers=80, dim=8192, n_heads=64, n_kv_heads=8, ffn_dim=28672, vocab=128256)
 
 
-def llama70_rank_bytes(tp: int, pos: int) -> int:
+def llama70_rank_bytes(tp: int, pos: int, batch: int = 1) -> int:
     """Algorithmic HBM bytes one rank reads and writes in a decode step of the
-    70B shape at position pos: its shard of every weight once, its KV heads
-    up to pos, the appended K/V row."""
+    70B shape at position pos: its shard of every weight once (for the whole
+    batch), every sequence's KV heads up to pos, the appended K/V rows."""
     d, hd, ffn, vocab = 8192, 128, 28672, 128256
     nh, nkv = 64 // tp, 8 // tp
     blk = lambda rows, cols: rows * (cols // 256) * 144
     layer = (blk((nh + 2 * nkv) * hd, d) + blk(d, nh * hd) + blk(2 * ffn // tp, d)
              + blk(d, ffn // tp))
-    kv = 2 * (pos + 1) * nkv * hd * 2
-    return 80 * (layer + kv) + blk(vocab // tp, d) + 2 * d
+    kv = 2 * (pos + 1) * nkv * hd * 2 * batch
+    return 80 * (layer + kv) + blk(vocab // tp, d) + 2 * d * batch
 
 
 def llama_prefill_flops(n_layers: int, T: int) -> int:
@@ -813,7 +813,8 @@ def run_llama(args, world, rank, local, pg) -> dict:
 
 def run_tp70b(args, world, rank, local, pg) -> dict:
     """The 70B shape tensor-parallel over the launch's ranks (one process and
-    one NCCL rank per GPU): prompt pass, then timed greedy decode."""
+    one NCCL rank per GPU): every sequence's prompt pass, then timed batched
+    greedy decode."""
     import torch
 
     from metallm_b200 import Context, Llama
@@ -825,12 +826,13 @@ def run_tp70b(args, world, rank, local, pg) -> dict:
     peaks = measured_peaks()
     if world > 1:
         bootstrap(ctx)
-    prompt_len, gen_len = 2048, 128
-    steps = min(args.steps, gen_len - args.warmup)
+    B, prompt_len, gen_len = args.batch, 2048, 128
+    steps = min(args.steps, gen_len - args.warmup - 2)
     cfg = llama_config(max_seq=prompt_len + gen_len, **L70)
-    m = Llama(ctx, cfg)
+    m = Llama(ctx, cfg, batch=B)
     fill_llama(m, 1)
-    prompt = np.random.default_rng(2048).integers(0, 128000, size=prompt_len).tolist()
+    prompts = [np.random.default_rng(2048 + b).integers(0, 128000, size=prompt_len).tolist()
+               for b in range(B)]
     nxt = ctx.alloc(16)
 
     def timed(fn):
@@ -842,71 +844,72 @@ def run_tp70b(args, world, rank, local, pg) -> dict:
         ev1.synchronize()
         return ev0.elapsed_time(ev1)
 
-    m.prefill(prompt[:256], nxt)  # loads the kernels
+    m.prefill(prompts[0][:256], nxt)  # loads the kernels
     m.reset()
     ctx.wait()
     barrier(pg, local)
-    prefill_ms = max_over_ranks(timed(lambda: m.prefill(prompt, nxt)), pg, local)
-    first = int(nxt.download(np.int32)[0])
-    out = ctx.alloc(4 * gen_len)
-    m.decode_greedy(first, args.warmup, out)  # captures the step graph
-    last = int(out.download(np.int32, args.warmup)[-1])
+    firsts = []
+
+    def prompt_pass():
+        for b in range(B):
+            m.prefill(prompts[b], nxt, None, seq=b)
+            firsts.append(int(nxt.download(np.int32)[0]))
+    prefill_ms = max_over_ranks(timed(prompt_pass), pg, local)
+    out = ctx.alloc(4 * gen_len * B)
+    m.decode_greedy_batch(firsts, args.warmup, out)  # captures the batched step
+    last = out.download(np.int32, args.warmup * B).reshape(args.warmup, B)[-1].tolist()
     ctx.wait()
     barrier(pg, local)
     sampler = ClockSampler(local)
     sampler.start()
     time.sleep(0.3)
-    pos0 = m.position
-    dev_ms = timed(lambda: m.decode_greedy(last, steps, out))
+    pos0 = m.seq_position(0)
+    dev_ms = timed(lambda: m.decode_greedy_batch(last, steps, out))
     clocks = sampler.stop()
-    toks = out.download(np.int32, steps)
+    toks = out.download(np.int32, steps * B).reshape(steps, B)
     ms_max = max_over_ranks(dev_ms, pg, local)
     per_step_ms = ms_max / steps
-    alg = llama70_rank_bytes(world, pos0 + steps // 2)
+    alg = llama70_rank_bytes(world, pos0 + steps // 2, B)
     kernel_gbs = alg / (per_step_ms * 1e-3) / 1e9
-    # e2e: forward(tokenID:) per token through the C ABI, the token read back
-    lib, h = ctx.lib, ctx.handle
-    htok = ctypes.c_void_p()
-    lib.mlm_host_alloc(h, 16, ctypes.byref(htok))
-    logits = ctx.alloc(4 * cfg.vocab)
-    tok_dev = ctx.alloc(16)
-    m.set_position(prompt_len)
-    tok, e2e_steps = first, min(steps, 16)
+    # e2e: one greedy batched step per call through the C ABI, the batch's
+    # tokens in from host memory and out again
+    tok = toks[-1].tolist()
+    e2e_steps = 2
     barrier(pg, local)
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
-        m.forward(tok, logits)
-        ctx.call("mlm_argmax_f32", logits, cfg.vocab, tok_dev)
-        ctx._check(lib.mlm_download_async(h, htok, ctypes.c_void_p(tok_dev.ptr), 4), "dn")
-        ctx.wait()
-        tok = ctypes.c_int32.from_address(htok.value).value
+        m.decode_greedy_batch(tok, 1, out)
+        tok = out.download(np.int32, B).tolist()
     e2e_s = max_over_ranks(time.perf_counter() - t0, pg, local)
-    lib.mlm_host_free(h, htok)
     line = {
-        "metric": METRIC, "value": round(steps / (ms_max * 1e-3), 2), "unit": "tokens/s",
+        "metric": METRIC, "value": round(B * steps / (ms_max * 1e-3), 2), "unit": "tokens/s",
         "n_gpus": world, "steps": steps, "warmup": args.warmup,
         "ms_per_step": round(per_step_ms, 5), "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "q4k x f16 -> f32 (fp16 KV cache)",
+        "vs_baseline": None,
+        "dtype": "q4k -> bf16 x bf16 -> f32 (tcgen05 GEMM over the batch), fp16 KV cache",
         "data": "synthetic (seeded Q4_K weights, fp16 embedding, fp32 norms generated on device; "
-                "every rank its shard of one model)",
-        "config": {"workload": LLAMA_WORKLOADS["tp70b"], "batch": 1, "prompt_tokens": prompt_len,
+                "every rank its shard of one model; uniform random prompt ids)",
+        "config": {"workload": LLAMA_WORKLOADS["tp70b"], "batch": B, "prompt_tokens": prompt_len,
                    "decode_steps_timed": steps, "parallelism": f"tp{world}",
-                   "l2": "inputs larger than L2: Q4_K weights of 39.1 GB / N per token",
+                   "l2": "inputs larger than L2: Q4_K weights of 39.1 GB / N per step",
                    "algorithmic_bytes_per_step_per_rank": alg},
-        "e2e": {"value": round(e2e_steps / e2e_s, 2), "unit": "tokens/s",
-                "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 4},
-        # embed; per layer 7 kernels (+ 2 one-shot all-reduces with TP); head
-        # GEMV, argmax (key + key reduce with TP), advance
-        "gpu_launches": steps * (1 + 80 * (9 if world > 1 else 7) + (4 if world > 1 else 3)),
-        "launch": "CUDA graph (one decode step, NCCL all-reduces included, replayed per token)",
+        "e2e": {"value": round(B * e2e_steps / e2e_s, 2), "unit": "tokens/s",
+                "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B},
+        # per step: embedding; per layer 2 RMSNorm rows, 3 GEMMs + 2 more, RoPE,
+        # 2 attention, SwiGLU (+ 2 one-shot all-reduces with TP); head: RMSNorm,
+        # GEMM, B argmaxes (+ key reduce with TP); advance
+        "gpu_launches": steps * (1 + 80 * (10 + (2 if world > 1 else 0)) + 2 + B
+                                 + (1 if world > 1 else 0) + 1),
+        "launch": "CUDA graph (one batched decode step, all-reduces included, replayed per step)",
         "roofline": {"bound": "hbm", "achieved": round(kernel_gbs, 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(kernel_gbs / peaks["hbm_gbs"], 4),
                      "peak_source": peaks["source"], "traffic": None,
-                     "note": "per rank: its weight shard and KV heads per step"},
-        "prefill": {"value": round(prompt_len / (prefill_ms * 1e-3), 2), "unit": "tokens/s",
-                    "path": "batched prompt pass: tcgen05 Q4_K GEMM, NCCL all-reduce per "
+                     "note": "per rank: its weight shard once per step and its KV heads of "
+                             "every sequence"},
+        "prefill": {"value": round(B * prompt_len / (prefill_ms * 1e-3), 2), "unit": "tokens/s",
+                    "path": "batched prompt pass per sequence: tcgen05 Q4_K GEMM, all-reduce per "
                             "projection"},
-        "first_tokens": [int(t) for t in toks[:8]],
+        "first_tokens": [int(t) for t in toks[:4, 0]],
         "clocks": clocks,
     }
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -997,6 +1000,7 @@ def main() -> None:
     ap.add_argument("--copies", type=int, default=6, help="rotating weight copies (> L2)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--batch", type=int, default=8, help="sequences of the tp70b workload")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

@@ -90,9 +90,10 @@ constexpr int kMinUnitsPerCta = 16;  // K stages: keeps each CTA's share above t
 constexpr int kTmemCols = 512;  // two fp32 accumulators of 256 columns
 
 // tcgen05 instruction descriptor: fp32 accumulate, bf16 A and B, both
-// K-major, N = 256, M = 128
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((256u >> 3) << 17) |
-                            ((128u >> 4) << 24);
+// K-major, M = 128, N = n (16 .. 256 in steps of 16)
+constexpr uint32_t idesc_for(int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((128u >> 4) << 24);
+}
 
 // shared-memory matrix descriptor of a K-major bf16 tile in the 64-byte
 // swizzle layout: rows of 64 bytes, 8-row atoms of 512 bytes (stride 512),
@@ -112,6 +113,8 @@ struct GemmArgs {
   int tiles_n;            // row tiles (the fast index of a tile number)
   int ks;                 // K stages per tile
   int dp_waves;           // whole-tile waves before the stream-K tiles
+  int mma_n;              // tokens per MMA: 256, or the tokens rounded up to 16
+                          // when they fit one tile (a decode batch)
   long long units;        // stream-K stages: (tiles - dp_waves * grid) * ks
 };
 
@@ -266,7 +269,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             ok = false;
             break;
           }
-          mbar_expect_tx(bfull + 8 * s, kBStage);
+          mbar_expect_tx(bfull + 8 * s, p.mma_n * kGemmKStep * 2);
           tma2d(sbase + kOffB + s * kBStage, &tmap_x, k * kGemmKStep, t0, bfull + 8 * s);
           ++it;
         }
@@ -310,7 +313,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                   "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
                   " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(
                       tmem + h * kGemmTok),
-                  "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(acc)
+                  "l"(adesc), "l"(bdesc), "r"(idesc_for(p.mma_n)), "r"(acc)
                   : "memory");
             }
           }
@@ -416,11 +419,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (go) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         constexpr int kCols = kGemmTok / kDqGroups;
+        const int col_end = min((group + 1) * kCols, p.mma_n);
 #pragma unroll 1
         for (int rp = 0; rp < kRowsPerThread; ++rp) {
           const int h = kRowsPerThread == 2 ? rp : h_one;
           const int n = n0 + h * kMmaM + r;
-          for (int col = group * kCols; col < (group + 1) * kCols; col += 8) {
+          for (int col = group * kCols; col < col_end; col += 8) {
             uint32_t v[8];
             asm volatile(
                 "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
@@ -538,6 +542,9 @@ int gemm_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_b
               "mlm_q4k_gemm: needs %d bytes of shared memory", kGemmSmem);
   EncodeFn encode = tensor_map_encoder(ctx);
   if (!encode) return MLM_ERR_CUDA;
+  // a single token tile (a decode batch, a short prompt) multiplies only its
+  // tokens, rounded up to the MMA's N granularity of 16
+  const int mma_n = tokens <= kGemmTok ? (tokens + 15) / 16 * 16 : kGemmTok;
   const int nb = cols / kQK;
   CUtensorMap mw, mx;
   {
@@ -554,7 +561,7 @@ int gemm_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_b
   {
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)tokens};
     const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-    const cuuint32_t box[2] = {(cuuint32_t)kGemmKStep, (cuuint32_t)kGemmTok};
+    const cuuint32_t box[2] = {(cuuint32_t)kGemmKStep, (cuuint32_t)mma_n};
     const cuuint32_t estr[2] = {1, 1};
     CUresult r = encode(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(x_bf16),
                         dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -576,6 +583,7 @@ int gemm_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_b
   a.K = cols;
   a.T = tokens;
   a.tiles_n = tiles_n;
+  a.mma_n = mma_n;
   a.ks = nb * kStagesPerBlock;
   const long long tiles = (long long)tiles_n * tiles_t;
   // one persistent CTA per SM, each with at least kMinUnitsPerCta stages

@@ -42,7 +42,10 @@ def _run(ctx, rows, cols, tokens, seed=5):
 
 @pytest.mark.parametrize("rows,cols,tokens", [(128, 256, 512), (256, 1024, 512), (200, 768, 100),
                                               (4096, 4096, 512), (1000, 2048, 1300),
-                                              (6144, 4096, 64)])
+                                              (6144, 4096, 64),
+                                              # one token tile: the MMA shrinks to 16 .. 256
+                                              (4096, 4096, 1), (2048, 1024, 8), (1000, 2048, 17),
+                                              (512, 512, 250)])
 def test_gemm_shapes(ctx, rows, cols, tokens):
     got, ref = _run(ctx, rows, cols, tokens)
     assert np.all(np.isfinite(got))
@@ -50,7 +53,8 @@ def test_gemm_shapes(ctx, rows, cols, tokens):
     assert err < TOL, (rows, cols, tokens, err)
 
 
-@pytest.mark.parametrize("rows,cols,tokens", [(4096, 4096, 512), (1000, 2048, 1300)])
+@pytest.mark.parametrize("rows,cols,tokens", [(4096, 4096, 512), (1000, 2048, 1300),
+                                              (8192, 1024, 8)])
 def test_gemm_residual_in_place(ctx, rows, cols, tokens):
     """y = x W^T + y (the residual stream updated in place), split and unsplit."""
     nb = rows * cols // 256

@@ -184,6 +184,17 @@ int mlm_q4k_gemv_swiglu(mlm_ctx *ctx, const void *W, int rows, int cols, const f
  * added into y with fp32 atomics (summation order may then differ from run
  * to run in the last bits).  residual (fp32 [tokens][rows], may be y
  * itself) is added when not NULL. */
+/* The decode linears for a batch of 1..8 tokens (independent sequences):
+ * y[t][n] = sum_k x[t][k] * W[n][k] (+ residual), x bf16 [tokens][cols], y
+ * fp32 [tokens][rows].  The reference multiplies one token at a time
+ * (encodeMPSMatrixMultiply, MetalService.swift:797-925); here the packed
+ * weights are read once for the whole batch and go to the tensor cores as in
+ * mlm_q4k_gemv, the tokens as the MMA's columns.  cols % 256 == 0; W and x
+ * 16-byte aligned; residual may be y itself (fp32 atomics add the partial
+ * sums of K chunks into y, so the last bits may differ from run to run). */
+int mlm_q4k_gemv_batch(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_bf16,
+                       int tokens, float *y, const float *residual);
+
 int mlm_q4k_gemm(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_bf16,
                  int tokens, float *y, const float *residual);
 

@@ -96,6 +96,7 @@ SIGNATURES = [
     ("mlm_q4k_gemv_rmsnorm", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_float, c_vp, c_vp]),
     ("mlm_q4k_gemv_swiglu", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_vp]),
     ("mlm_q4k_gemm", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_int, c_vp, c_vp]),
+    ("mlm_q4k_gemv_batch", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_int, c_vp, c_vp]),
     ("mlm_q4k_gemv_static", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_vp]),
     ("mlm_q4k_tiled_bytes", ctypes.c_size_t, [c_int, c_int]),
     ("mlm_q4k_tile", c_int, [c_vp, c_vp, c_int, c_int, c_vp]),

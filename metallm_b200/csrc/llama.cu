@@ -250,7 +250,7 @@ struct mlm_llama {
       const LayerBuf &L = layers[l];
       if ((st = rmsnorm_rows_bf16_launch(ctx, pf_hidden, L.attn_norm, pf_x, T, c.dim, c.rms_eps, s)))
         return st;
-      if ((st = gemm_launch(ctx, L.qkv, qkv_rows(), c.dim, pf_x, T, pf_qkv, nullptr, s))) return st;
+      if ((st = linear(L.qkv, qkv_rows(), c.dim, pf_x, T, pf_qkv, nullptr))) return st;
       __half *kc = L.kc + cur * seq_elems(), *vc = L.vc + cur * seq_elems();
       if ((st = rope_kv_rows_launch(ctx, pf_qkv, rope_freqs, c.rope, nh(), nkv(), c.head_dim, pos,
                                     T, pf_q16, kc, vc, s)))
@@ -261,7 +261,7 @@ struct mlm_llama {
       if ((st = row_parallel_rows(L.wo, qdim(), pf_attn, T))) return st;
       if ((st = rmsnorm_rows_bf16_launch(ctx, pf_hidden, L.ffn_norm, pf_x, T, c.dim, c.rms_eps, s)))
         return st;
-      if ((st = gemm_launch(ctx, L.gu, 2 * ffn(), c.dim, pf_x, T, pf_gu, nullptr, s))) return st;
+      if ((st = linear(L.gu, 2 * ffn(), c.dim, pf_x, T, pf_gu, nullptr))) return st;
       if ((st = swiglu_rows_bf16_launch(ctx, pf_gu, ffn(), T, pf_x, s))) return st;
       if ((st = row_parallel_rows(L.down, ffn(), pf_x, T))) return st;
     }
@@ -283,7 +283,7 @@ struct mlm_llama {
       const LayerBuf &L = layers[l];
       if ((st = rmsnorm_rows_bf16_launch(ctx, pf_hidden, L.attn_norm, pf_x, B, c.dim, c.rms_eps, s)))
         return st;
-      if ((st = gemm_launch(ctx, L.qkv, qkv_rows(), c.dim, pf_x, B, pf_qkv, nullptr, s))) return st;
+      if ((st = linear(L.qkv, qkv_rows(), c.dim, pf_x, B, pf_qkv, nullptr))) return st;
       if ((st = rope_kv_batch_launch(ctx, pf_qkv, rope_freqs, c.rope, nh(), nkv(), c.head_dim, B,
                                      pos_b, seq_elems(), pf_q16, L.kc, L.vc, s)))
         return st;
@@ -294,13 +294,13 @@ struct mlm_llama {
       if ((st = row_parallel_rows(L.wo, qdim(), pf_attn, B))) return st;
       if ((st = rmsnorm_rows_bf16_launch(ctx, pf_hidden, L.ffn_norm, pf_x, B, c.dim, c.rms_eps, s)))
         return st;
-      if ((st = gemm_launch(ctx, L.gu, 2 * ffn(), c.dim, pf_x, B, pf_gu, nullptr, s))) return st;
+      if ((st = linear(L.gu, 2 * ffn(), c.dim, pf_x, B, pf_gu, nullptr))) return st;
       if ((st = swiglu_rows_bf16_launch(ctx, pf_gu, ffn(), B, pf_x, s))) return st;
       if ((st = row_parallel_rows(L.down, ffn(), pf_x, B))) return st;
     }
     if ((st = rmsnorm_rows_bf16_launch(ctx, pf_hidden, out_norm, pf_x, B, c.dim, c.rms_eps, s)))
       return st;
-    if ((st = gemm_launch(ctx, output, vocab_l(), c.dim, pf_x, B, b_logits, nullptr, s))) return st;
+    if ((st = linear(output, vocab_l(), c.dim, pf_x, B, b_logits, nullptr))) return st;
     for (int b = 0; b < B; ++b) {
       st = tp_on ? argmax_key_launch(ctx, b_logits + (size_t)b * vocab_l(), vocab_l(),
                                      rank * vocab_l(), b_keys_l + b, s)
@@ -326,12 +326,20 @@ struct mlm_llama {
     return MLM_OK;
   }
 
+  // Y = X W^T (+ residual) over T token rows of bf16 X: up to 8 rows (a
+  // decode batch) stream the weights through the batched GEMV, more through
+  // the tensor-core GEMM
+  int linear(const uint8_t *W, int rows, int cols, const void *x, int T, float *y,
+             const float *res) {
+    if (T <= 8) return gemv_batch_launch(ctx, W, rows, cols, x, T, y, res, ctx->stream);
+    return gemm_launch(ctx, W, rows, cols, x, T, y, res, ctx->stream);
+  }
+
   // pf_hidden += X W^T over T rows for a projection with split input
   // columns (see row_parallel)
   int row_parallel_rows(const uint8_t *W, int cols, const void *x, int T) {
-    if (!tp_on) return gemm_launch(ctx, W, cfg.dim, cols, x, T, pf_hidden, pf_hidden, ctx->stream);
-    int st = gemm_launch(ctx, W, cfg.dim, cols, x, T, pf_part, rank == 0 ? pf_hidden : nullptr,
-                         ctx->stream);
+    if (!tp_on) return linear(W, cfg.dim, cols, x, T, pf_hidden, pf_hidden);
+    int st = linear(W, cfg.dim, cols, x, T, pf_part, rank == 0 ? pf_hidden : nullptr);
     if (st != MLM_OK) return st;
     return tp_allreduce_sum(ctx, pf_part, pf_hidden, (size_t)T * cfg.dim, ctx->stream);
   }

@@ -116,6 +116,10 @@ int attn_decode_batch_launch(mlm_ctx *ctx, const void *q, const void *kc, const 
 size_t attn_decode_partial_floats(int n_heads, int capacity);
 int silu_mul_launch(mlm_ctx *ctx, const float *g, const float *u, void *out, int n,
                     cudaStream_t stream);
+// decode linears of a batch of up to 8 tokens (q4k_gemv_batch.cu): Y[t] =
+// W X[t] (+ residual, which may be Y itself), X bf16 [tokens][cols]
+int gemv_batch_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_bf16,
+                      int tokens, float *y, const float *residual, cudaStream_t stream);
 // batched prompt pass (prefill.cu, q4k_gemm.cu)
 int gemm_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_bf16, int tokens,
                 float *y, const float *residual, cudaStream_t stream);

@@ -56,8 +56,14 @@
 
 namespace mlm {
 
-constexpr int kGemvMaxWarps = 12;                     // warps per CTA (upper bound)
-constexpr int kGemvStages = 3;                        // smem stages per warp
+#ifndef MLM_GEMV_WARPS
+#define MLM_GEMV_WARPS 12
+#endif
+#ifndef MLM_GEMV_STAGES
+#define MLM_GEMV_STAGES 3
+#endif
+constexpr int kGemvMaxWarps = MLM_GEMV_WARPS;          // warps per CTA (upper bound)
+constexpr int kGemvStages = MLM_GEMV_STAGES;           // smem stages per warp
 constexpr int kStageBytes = kTileRows * kBlockBytes;  // 4608
 
 struct GemvArgs {

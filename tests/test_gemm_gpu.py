@@ -79,3 +79,47 @@ def test_gemm_bad_args(ctx):
     with pytest.raises(MLMError) as e:
         ctx.call("mlm_q4k_gemm", buf.ptr + 8, 128, 256, buf, 16, buf, None)
     assert e.value.status == -3
+
+
+# -- the decode linears of a batch of 1..8 tokens (mlm_q4k_gemv_batch) ---------
+# Bar: relative L2 <= 1e-5 against a float64 product of the exact fp32
+# dequantized weights and the bf16 tokens (the weights are not rounded here;
+# x goes to fp16 with a power-of-two scale per sub-block, which is exact for
+# bf16 values in range).
+
+GEMV_TOL = 1e-5
+
+
+@pytest.mark.parametrize("rows,cols,tokens,scale", [(4096, 4096, 8, 1.0), (1000, 2048, 3, 1.0),
+                                                    (6144, 4096, 5, 1.0), (300, 512, 1, 1.0),
+                                                    (4096, 14336, 8, 1.0),
+                                                    # beyond the fp16 range: the scales hold it
+                                                    (2048, 1024, 4, 3.0e5)])
+def test_gemv_batch(ctx, rows, cols, tokens, scale):
+    nb = rows * cols // 256
+    blocks = O.gen_q4k(9, 1, nb)
+    xb = bf16_bits(O.gen_f32(9, 2, tokens * cols) * np.float32(scale))
+    r = O.gen_f32(9, 3, tokens * rows, 0.0, 10.0)
+    y = ctx.to_device(r)
+    ctx.call("mlm_q4k_gemv_batch", ctx.to_device(blocks), rows, cols, ctx.to_device(xb), tokens,
+             y, y)
+    got = y.download(np.float32, rows * tokens).reshape(tokens, rows)
+    w = O.q4k_dequant_f32(blocks, rows * cols).reshape(rows, cols).astype(np.float64)
+    ref = bf16_value(xb).reshape(tokens, cols).astype(np.float64) @ w.T
+    ref += r.reshape(tokens, rows)
+    assert rel_l2(got, ref) < GEMV_TOL, rel_l2(got, ref)
+    # and without a residual: y is written from zero
+    y2 = ctx.alloc(4 * rows * tokens)
+    ctx.call("mlm_q4k_gemv_batch", ctx.to_device(blocks), rows, cols, ctx.to_device(xb), tokens,
+             y2, None)
+    got2 = y2.download(np.float32, rows * tokens).reshape(tokens, rows)
+    assert rel_l2(got2, ref - r.reshape(tokens, rows)) < GEMV_TOL
+
+
+def test_gemv_batch_bad_args(ctx):
+    from metallm_b200 import MLMError
+    buf = ctx.alloc(1 << 16)
+    with pytest.raises(MLMError):
+        ctx.call("mlm_q4k_gemv_batch", buf, 128, 256, buf, 9, buf, None)  # > 8 tokens
+    with pytest.raises(MLMError):
+        ctx.call("mlm_q4k_gemv_batch", buf, 128, 300, buf, 2, buf, None)  # cols % 256

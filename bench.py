@@ -128,6 +128,7 @@ PROFILES = {
     "dequant": "q4k_dequant_f32_4096x4096.md",
     "prefill": "q4k_gemm_28672x4096x512.md",
     "gemm": "q4k_gemm_28672x4096x512.md",
+    "gemv_batch": "q4k_gemv_batch_57344x8192x8.md",
 }
 
 
@@ -484,6 +485,93 @@ def cpu_gemm_rate(budget_s: float, threads: int) -> dict:
     tflops = r["value"] * 1e9 / gemv_bytes(rows, cols) * 2 * rows * cols / 1e12
     return {"value": round(tflops, 6), "unit": "TFLOP/s", "cores": threads, "kind": r["kind"],
             "sample": r["sample"] + "; TFLOP/s = 2 x rows x cols per matvec"}
+
+
+GEMV_BATCH_SHAPE = (57344, 8192, 8)
+GEMV_BATCH_DESC = ("Q4_K batched decode GEMV: the fused gate/up weights of a Llama-3-70B layer "
+                   "(57344 x 8192 Q4_K) on the 8 tokens of a decode batch (BASELINE config 4)")
+
+
+def run_gemv_batch(args, world, rank, local, pg) -> dict:
+    """The batched decode linear alone: each step is one 57344 x 8192 launch
+    over 8 bf16 tokens, rotating over two weight copies (528 MB > L2)."""
+    import torch
+
+    from metallm_b200 import Context
+    rows, cols, T = GEMV_BATCH_SHAPE
+    ctx = Context(local)
+    torch.cuda.set_device(local)
+    tstream = torch.cuda.ExternalStream(ctx.stream(), device=f"cuda:{local}")
+    peaks = measured_peaks()
+    nb = rows * cols // 256
+    Ws = []
+    for c in range(2):
+        W = ctx.alloc(nb * 144)
+        ctx.gen_q4k(1000 + c, 1, nb, W)
+        Ws.append(W)
+    x = ctx.alloc(2 * T * cols)
+    ctx.gen_f16(7, 2, T * cols, x)  # fp16 normals read as bf16: finite, small
+    y = ctx.alloc(4 * T * rows)
+    step = lambda i: ctx.call("mlm_q4k_gemv_batch", Ws[i % 2], rows, cols, x, T, y, None)
+    for i in range(args.warmup):
+        step(i)
+    ctx.wait()
+    barrier(pg, local)
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(tstream)
+    for i in range(args.steps):
+        step(i)
+    ev1.record(tstream)
+    ev1.synchronize()
+    dev_ms = ev0.elapsed_time(ev1)
+    clocks = sampler.stop()
+    ms_max = max_over_ranks(dev_ms, pg, local)
+    per_ms = ms_max / args.steps
+    alg = nb * 144 + 2 * T * cols + 4 * T * rows
+    gbs = alg / (per_ms * 1e-3) / 1e9
+    # e2e: the tokens from pinned host memory, the product back to it
+    lib, h = ctx.lib, ctx.handle
+    hx, hy = ctypes.c_void_p(), ctypes.c_void_p()
+    lib.mlm_host_alloc(h, 2 * T * cols, ctypes.byref(hx))
+    lib.mlm_host_alloc(h, 4 * T * rows, ctypes.byref(hy))
+    e2e_steps = min(args.steps, 20)
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        ctx._check(lib.mlm_upload_async(h, ctypes.c_void_p(x.ptr), hx, 2 * T * cols), "up")
+        step(i)
+        ctx._check(lib.mlm_download_async(h, hy, ctypes.c_void_p(y.ptr), 4 * T * rows), "dn")
+        ctx.wait()
+    e2e_s = max_over_ranks(time.perf_counter() - t0, pg, local)
+    lib.mlm_host_free(h, hx)
+    lib.mlm_host_free(h, hy)
+    line = {
+        "metric": METRIC, "value": round(gbs * world, 2), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_ms, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "q4k x bf16 (as fp16 with per-sub-block scales) -> f32",
+        "data": "synthetic (seeded Q4_K blocks, fp16 normals read as bf16, generated on device)",
+        "config": {"workload": GEMV_BATCH_DESC, "rows": rows, "cols": cols, "tokens": T,
+                   "parallelism": "replicas" if world > 1 else "single GPU",
+                   "l2": f"2 rotating weight copies ({2 * nb * 144 / 1e6:.0f} MB > L2)",
+                   "algorithmic_bytes_per_step": alg},
+        "e2e": {"value": round(alg * e2e_steps * world / e2e_s / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": 2 * T * cols, "d2h_bytes_per_step": 4 * T * rows},
+        "gpu_launches": args.steps,
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
+                     "peak_source": peaks["source"], "traffic": ncu_traffic("gemv_batch")},
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        r = cpu_gemv_rate(rows, cols, args.cpu_seconds, host_threads(), "reference")
+        line["cpu_baseline"] = dict(r, sample=r["sample"] + "; one token per matvec, GB/s of "
+                                    "the weights streamed per token")
+    ctx.close()
+    return line
 
 
 def run_gemm(args, world, rank, local, pg) -> dict:
@@ -922,6 +1010,19 @@ def run_tp70b(args, world, rank, local, pg) -> dict:
 def run_reference(args, world, rank) -> dict | None:
     if rank != 0:
         return None
+    if args.workload == "gemv_batch":
+        rows, cols, T = GEMV_BATCH_SHAPE
+        r = cpu_gemv_rate(rows, cols, args.cpu_seconds, host_threads(), "reference")
+        v = r["value"]
+        return {"impl": "reference", "metric": METRIC, "value": v, "unit": "GB/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(gemv_bytes(rows, cols) / (v * 1e9) * 1e3 * T, 3),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "q4k x f16 -> f32", "data": "synthetic (seeded Q4_K blocks)",
+                "config": {"workload": GEMV_BATCH_DESC, "rows": rows, "cols": cols, "tokens": T},
+                "cpu_baseline": dict(r, sample=r["sample"] + "; one token per matvec"),
+                "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
     if args.workload == "gemm":
         r = cpu_gemm_rate(args.cpu_seconds, host_threads())
         rows, cols, T = GEMM_SHAPE
@@ -995,7 +1096,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--workload", default="gemv_up",
-                    choices=sorted(WORKLOADS) + sorted(LLAMA_WORKLOADS) + ["gemm"])
+                    choices=sorted(WORKLOADS) + sorted(LLAMA_WORKLOADS) + ["gemm", "gemv_batch"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--copies", type=int, default=6, help="rotating weight copies (> L2)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -1014,8 +1115,8 @@ def main() -> None:
 
     world, rank, local, pg = dist_setup(args)
     try:
-        run = run_gemm if args.workload == "gemm" else run_tp70b if args.workload == "tp70b" \
-            else run_llama if args.workload in LLAMA_WORKLOADS else run_gpu
+        run = {"gemm": run_gemm, "gemv_batch": run_gemv_batch, "tp70b": run_tp70b}.get(
+            args.workload, run_llama if args.workload in LLAMA_WORKLOADS else run_gpu)
         line = run(args, world, rank, local, pg)
         if rank == 0:
             print(json.dumps(line), flush=True)

@@ -23,6 +23,7 @@ int gemv_tiled_init(mlm_ctx *ctx);
 int attn_init(mlm_ctx *ctx);
 int gemm_init(mlm_ctx *ctx);
 int prefill_init(mlm_ctx *ctx);
+int gemv_batch_init(mlm_ctx *ctx);
 int gemv_max_ctas(int sm_count);
 size_t attn_partial_floats_max(int max_heads);
 
@@ -133,7 +134,8 @@ extern "C" int mlm_create(int device, mlm_ctx **out) {
       return fail(MLM_ERR_CUDA);
   }
   if (gemv_init(ctx) != MLM_OK || gemv_tiled_init(ctx) != MLM_OK || attn_init(ctx) != MLM_OK ||
-      gemm_init(ctx) != MLM_OK || prefill_init(ctx) != MLM_OK)
+      gemm_init(ctx) != MLM_OK || prefill_init(ctx) != MLM_OK ||
+      gemv_batch_init(ctx) != MLM_OK)
     return fail(MLM_ERR_CUDA);
   if (cudaDeviceSynchronize() != cudaSuccess) return fail(MLM_ERR_CUDA);
   *out = ctx;

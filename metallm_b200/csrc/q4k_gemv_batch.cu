@@ -16,10 +16,16 @@
 //
 // Work: 16-row tiles x chunks of 8 block columns (2048 elements).  A CTA
 // owns one chunk: it stages the chunk's x of every token once in shared
-// memory (fp16 with a power-of-two scale per token and sub-block, which
-// keeps large activations in range; the scale is undone in fp32) and its
-// warps take the chunk's tiles.  Each (tile, chunk) adds its partial into Y
-// with fp32 atomics; Y starts from the residual (or zero).
+// memory (fp16 with a power-of-two scale per token, which keeps large
+// activations in range and is undone in fp32 after the chunk; the x of the
+// high-nibble positions is also divided by 16, an exact exponent shift, so
+// both nibble MMAs of a sub-block add into one accumulator) and its warps
+// take the chunk's tiles.  A warp copies its tile's 16 blocks of each
+// block column into a two-deep shared-memory stage with coalesced 16-byte
+// cp.async (the next column's copy overlaps the current column's MMAs); with
+// the 144-byte row stride every fragment load is conflict-free.  Each
+// (tile, chunk) adds its partial into Y with fp32 atomics; Y starts from the
+// residual (or zero).
 #include <algorithm>
 
 #include "mlm_device.cuh"
@@ -34,6 +40,9 @@ constexpr int kBgSub = kBgChunk * 8;  // sub-blocks per chunk
 constexpr int kBgWarps = 16;
 constexpr int kBgThreads = kBgWarps * 32;
 constexpr int kBgMaxT = 8;
+constexpr int kBgXStride = kBgSub * 4 + 1;  // uint4 per token, padded against bank conflicts
+constexpr int kBgStage = kBgRows * kBlockBytes;  // one block column of a tile: 2304 bytes
+constexpr int kBgSmem = kBgWarps * 2 * kBgStage;  // dynamic: the warps' weight stages
 
 struct BgArgs {
   const uint8_t *W;
@@ -56,11 +65,33 @@ __device__ __forceinline__ uint32_t h2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t *>(&h);
 }
 
-__global__ void __launch_bounds__(kBgThreads) q4k_gemv_batch_kernel(BgArgs p) {
+// The 8 (scale, min) pairs of a block (get_scale_min_k4, DequantKernels.metal:
+// 43-56) as bytes of four words: scales of sub-blocks 0-3 / 4-7, mins 0-3 / 4-7
+__device__ __forceinline__ void q4k_scales_packed(const uint4 &h, uint32_t &sc_lo, uint32_t &sc_hi,
+                                                  uint32_t &m_lo, uint32_t &m_hi) {
+  sc_lo = h.y & 0x3F3F3F3Fu;
+  m_lo = h.z & 0x3F3F3F3Fu;
+  sc_hi = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+  m_hi = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+}
+
+// byte b of w as the fp32 value 2^23 + byte (a byte permute)
+__device__ __forceinline__ float byte_plus_2p23(uint32_t w, int b) {
+  return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u + b));
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(kBgThreads, 2) q4k_gemv_batch_kernel(BgArgs p) {
   // x of the chunk: [token][sub-block][lane t] -> 8 fp16 in mask order
-  __shared__ uint4 xperm[kBgMaxT * kBgSub * 4];
-  __shared__ float xscale[kBgSub][kBgMaxT];  // power of two per (sub-block, token)
-  __shared__ float xsum[kBgSub][kBgMaxT];    // sum of the unscaled x
+  __shared__ uint4 xperm[kBgMaxT * kBgXStride];
+  extern __shared__ __align__(16) uint8_t wstage[];
+  __shared__ float xsum[kBgSub][kBgMaxT];    // per (sub-block, token): sum of the x
+  __shared__ uint32_t tokmax[kBgMaxT];       // per token: bits of the chunk's max |x|
+  __shared__ float tokscale[kBgMaxT];        // per token: the power of two x was divided by
 
   const int chunk = blockIdx.x / p.ctas_per_chunk, cj = blockIdx.x % p.ctas_per_chunk;
   const int kb0 = chunk * kBgChunk, nkb = min(kBgChunk, p.nb - kb0);
@@ -68,11 +99,10 @@ __global__ void __launch_bounds__(kBgThreads) q4k_gemv_batch_kernel(BgArgs p) {
   const int g = lane >> 2, t = lane & 3;
 
   // ---- stage x: one thread per (token, sub-block, t): elements 8t .. 8t+7 --
-  for (int i = threadIdx.x; i < kBgMaxT * kBgSub * 4; i += kBgThreads) {
-    const int tq = i & 3, s = (i >> 2) % kBgSub, n = i / (kBgSub * 4);
-    float v[8];
-    const bool live = n < p.T && s < nkb * 8;
-    if (live) {
+  if (threadIdx.x < kBgMaxT) tokmax[threadIdx.x] = 0;
+  __syncthreads();
+  auto load8 = [&](int n, int s, int tq, float (&v)[8]) {
+    if (n < p.T && s < nkb * 8) {
       const __nv_bfloat16 *src = p.x + (size_t)n * p.cols + (size_t)kb0 * 256 + 32 * s + 8 * tq;
       const uint4 raw = *reinterpret_cast<const uint4 *>(src);
       const __nv_bfloat162 *b2 = reinterpret_cast<const __nv_bfloat162 *>(&raw);
@@ -86,6 +116,12 @@ __global__ void __launch_bounds__(kBgThreads) q4k_gemv_batch_kernel(BgArgs p) {
 #pragma unroll
       for (int e = 0; e < 8; ++e) v[e] = 0.f;
     }
+  };
+  // pass 1: the sub-blocks' sums and each token's largest magnitude
+  for (int i = threadIdx.x; i < kBgMaxT * kBgSub * 4; i += kBgThreads) {
+    const int tq = i & 3, s = (i >> 2) % kBgSub, n = i / (kBgSub * 4);
+    float v[8];
+    load8(n, s, tq, v);
     float mx = 0.f, sm = 0.f;
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
@@ -97,61 +133,109 @@ __global__ void __launch_bounds__(kBgThreads) q4k_gemv_batch_kernel(BgArgs p) {
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
     sm += __shfl_xor_sync(0xffffffffu, sm, 1);
     sm += __shfl_xor_sync(0xffffffffu, sm, 2);
-    // scale 2^-ex keeps the sub-block's largest magnitude below 2^15
-    const int ex = max(0, (int)((__float_as_uint(mx) >> 23) & 0xFF) - 127 - 14);
-    const float inv = __uint_as_float((uint32_t)(127 - ex) << 23);
-    xperm[i] = make_uint4(h2(v[0] * inv, v[4] * inv), h2(v[2] * inv, v[6] * inv),
-                          h2(v[1] * inv, v[5] * inv), h2(v[3] * inv, v[7] * inv));
     if (tq == 0) {
-      xscale[s][n] = __uint_as_float((uint32_t)(127 + ex) << 23);
       xsum[s][n] = sm;
+      atomicMax(tokmax + n, __float_as_uint(mx));  // non-negative: bit order = value order
     }
+  }
+  __syncthreads();
+  if (threadIdx.x < kBgMaxT) {
+    // 2^-ex keeps the token's largest magnitude below 2^15
+    const int ex = max(0, (int)((tokmax[threadIdx.x] >> 23) & 0xFF) - 127 - 14);
+    tokscale[threadIdx.x] = __uint_as_float((uint32_t)(127 + ex) << 23);
+  }
+  __syncthreads();
+  // pass 2: scaled fp16 in the order of the nibble masks
+  for (int i = threadIdx.x; i < kBgMaxT * kBgSub * 4; i += kBgThreads) {
+    const int tq = i & 3, s = (i >> 2) % kBgSub, n = i / (kBgSub * 4);
+    float v[8];
+    load8(n, s, tq, v);
+    const float inv = 1.0f / tokscale[n], inv16 = inv * 0.0625f;  // powers of two: exact
+    xperm[n * kBgXStride + s * 4 + tq] =
+        make_uint4(h2(v[0] * inv, v[4] * inv), h2(v[2] * inv, v[6] * inv),
+                   h2(v[1] * inv16, v[5] * inv16), h2(v[3] * inv16, v[7] * inv16));
   }
   __syncthreads();
 
   // ---- tiles of this chunk, round-robin over the CTA's warps ---------------
   const uint32_t M = 0x000F000Fu, MH = 0x00F000F0u;
+  uint8_t *mystage = wstage + warp * 2 * kBgStage;
+  const uint32_t stage_addr = (uint32_t)__cvta_generic_to_shared(mystage);
   for (int tile = cj + p.ctas_per_chunk * warp; tile < p.tiles;
        tile += p.ctas_per_chunk * kBgWarps) {
     const int r0 = tile * kBgRows + g, r1 = r0 + 8;
     const bool ok0 = r0 < p.rows, ok1 = r1 < p.rows;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};  // (r0, 2t) (r0, 2t+1) (r1, 2t) (r1, 2t+1)
-    for (int kb = 0; kb < nkb; ++kb) {
-      const uint8_t *b0 = p.W + ((size_t)(ok0 ? r0 : 0) * p.nb + kb0 + kb) * kBlockBytes;
-      const uint8_t *b1 = p.W + ((size_t)(ok1 ? r1 : 0) * p.nb + kb0 + kb) * kBlockBytes;
-      uint4 h0 = make_uint4(0, 0, 0, 0), h1 = make_uint4(0, 0, 0, 0);
-      uint32_t q0[8], q1[8];
-      if (ok0) h0 = __ldg(reinterpret_cast<const uint4 *>(b0));
-      if (ok1) h1 = __ldg(reinterpret_cast<const uint4 *>(b1));
-#pragma unroll
-      for (int sb = 0; sb < 8; ++sb) {
-        q0[sb] = ok0 ? __ldg(reinterpret_cast<const uint32_t *>(b0 + 16 + 16 * sb + 4 * t)) : 0u;
-        q1[sb] = ok1 ? __ldg(reinterpret_cast<const uint32_t *>(b1 + 16 + 16 * sb + 4 * t)) : 0u;
+    // block column kb of the tile's 16 rows -> stage buf (rows past the end
+    // are zero-filled)
+    auto issue = [&](int kb, int buf) {
+      for (int c = lane; c < kBgRows * 9; c += 32) {
+        const int row = c / 9, part = c - row * 9;
+        const int gr = tile * kBgRows + row;
+        const bool live = gr < p.rows;
+        const uint8_t *src =
+            p.W + ((size_t)(live ? gr : 0) * p.nb + kb0 + kb) * kBlockBytes + part * 16;
+        cp_async16(stage_addr + buf * kBgStage + row * kBlockBytes + part * 16, src,
+                   live ? 16u : 0u);
       }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    // (r0, 2t) (r0, 2t+1) (r1, 2t) (r1, 2t+1): the scaled-x products and the
+    // min terms
+    float aq[4] = {0.f, 0.f, 0.f, 0.f}, am[4] = {0.f, 0.f, 0.f, 0.f};
+    issue(0, 0);
+    for (int kb = 0; kb < nkb; ++kb) {
+      if (kb + 1 < nkb) {
+        issue(kb + 1, (kb + 1) & 1);
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+      } else {
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+      }
+      __syncwarp();
+      const uint8_t *s0 = mystage + (kb & 1) * kBgStage + g * kBlockBytes;
+      const uint8_t *s1 = s0 + 8 * kBlockBytes;
+      const uint4 h0 = *reinterpret_cast<const uint4 *>(s0);
+      const uint4 h1 = *reinterpret_cast<const uint4 *>(s1);
+      // d 2^24 (undoes the subnormal scale of the nibbles) and dmin; with
+      // f = 2^23 + sc, fma(D, f, -D 2^23) is D sc exactly (at most 17
+      // significant bits), so the 6-bit values need no conversion
       const float D0 = half_bits_to_float(h0.x) * 16777216.0f, Dm0 = half_bits_to_float(h0.x >> 16);
       const float D1 = half_bits_to_float(h1.x) * 16777216.0f, Dm1 = half_bits_to_float(h1.x >> 16);
+      const float nD0 = -D0 * 8388608.0f, nDm0 = -Dm0 * 8388608.0f;
+      const float nD1 = -D1 * 8388608.0f, nDm1 = -Dm1 * 8388608.0f;
+      uint32_t scl0, sch0, ml0, mh0, scl1, sch1, ml1, mh1;
+      q4k_scales_packed(h0, scl0, sch0, ml0, mh0);
+      q4k_scales_packed(h1, scl1, sch1, ml1, mh1);
 #pragma unroll
       for (int sb = 0; sb < 8; ++sb) {
         const int s = kb * 8 + sb;
-        const uint4 xv = xperm[(g * kBgSub + s) * 4 + t];
-        const uint32_t w0 = q0[sb], w1 = q1[sb], u0 = w0 >> 8, u1 = w1 >> 8;
-        float clo[4] = {0.f, 0.f, 0.f, 0.f}, chi[4] = {0.f, 0.f, 0.f, 0.f};
-        mma16816(clo, w0 & M, w1 & M, u0 & M, u1 & M, xv.x, xv.y);
-        mma16816(chi, w0 & MH, w1 & MH, u0 & MH, u1 & MH, xv.z, xv.w);
-        int sc0, m0, sc1, m1;
-        q4k_scale_min_regs(sb, h0.y, h0.z, h0.w, sc0, m0);
-        q4k_scale_min_regs(sb, h1.y, h1.z, h1.w, sc1, m1);
-        const float ds0 = D0 * (float)sc0, dm0 = Dm0 * (float)m0;
-        const float ds1 = D1 * (float)sc1, dm1 = Dm1 * (float)m1;
-        const float2 xs = *reinterpret_cast<const float2 *>(&xscale[s][2 * t]);
+        const uint4 xv = xperm[g * kBgXStride + s * 4 + t];
+        const uint32_t w0 = *reinterpret_cast<const uint32_t *>(s0 + 16 + 16 * sb + 4 * t);
+        const uint32_t w1 = *reinterpret_cast<const uint32_t *>(s1 + 16 + 16 * sb + 4 * t);
+        const uint32_t u0 = w0 >> 8, u1 = w1 >> 8;
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
+        mma16816(c, w0 & M, w1 & M, u0 & M, u1 & M, xv.x, xv.y);
+        mma16816(c, w0 & MH, w1 & MH, u0 & MH, u1 & MH, xv.z, xv.w);
+        const int bsel = sb & 3;
+        const float ds0 = fmaf(D0, byte_plus_2p23(sb < 4 ? scl0 : sch0, bsel), nD0);
+        const float dm0 = fmaf(Dm0, byte_plus_2p23(sb < 4 ? ml0 : mh0, bsel), nDm0);
+        const float ds1 = fmaf(D1, byte_plus_2p23(sb < 4 ? scl1 : sch1, bsel), nD1);
+        const float dm1 = fmaf(Dm1, byte_plus_2p23(sb < 4 ? ml1 : mh1, bsel), nDm1);
         const float2 xm = *reinterpret_cast<const float2 *>(&xsum[s][2 * t]);
-        acc[0] += ds0 * (fmaf(0.0625f, chi[0], clo[0]) * xs.x) - dm0 * xm.x;
-        acc[1] += ds0 * (fmaf(0.0625f, chi[1], clo[1]) * xs.y) - dm0 * xm.y;
-        acc[2] += ds1 * (fmaf(0.0625f, chi[2], clo[2]) * xs.x) - dm1 * xm.x;
-        acc[3] += ds1 * (fmaf(0.0625f, chi[3], clo[3]) * xs.y) - dm1 * xm.y;
+        aq[0] = fmaf(ds0, c[0], aq[0]);
+        aq[1] = fmaf(ds0, c[1], aq[1]);
+        aq[2] = fmaf(ds1, c[2], aq[2]);
+        aq[3] = fmaf(ds1, c[3], aq[3]);
+        am[0] = fmaf(dm0, xm.x, am[0]);
+        am[1] = fmaf(dm0, xm.y, am[1]);
+        am[2] = fmaf(dm1, xm.x, am[2]);
+        am[3] = fmaf(dm1, xm.y, am[3]);
       }
+      __syncwarp();  // the stage is read before the next copy overwrites it
     }
     const int n0 = 2 * t, n1 = 2 * t + 1;
+    const float xs0 = tokscale[n0], xs1 = tokscale[n1];
+    const float acc[4] = {aq[0] * xs0 - am[0], aq[1] * xs1 - am[1], aq[2] * xs0 - am[2],
+                          aq[3] * xs1 - am[3]};
     if (ok0 && n0 < p.T) atomicAdd(p.y + (size_t)n0 * p.rows + r0, acc[0]);
     if (ok0 && n1 < p.T) atomicAdd(p.y + (size_t)n1 * p.rows + r0, acc[1]);
     if (ok1 && n0 < p.T) atomicAdd(p.y + (size_t)n0 * p.rows + r1, acc[2]);
@@ -160,6 +244,12 @@ __global__ void __launch_bounds__(kBgThreads) q4k_gemv_batch_kernel(BgArgs p) {
 }
 
 }  // namespace
+
+int gemv_batch_init(mlm_ctx *ctx) {
+  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(q4k_gemv_batch_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kBgSmem));
+  return MLM_OK;
+}
 
 int gemv_batch_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_bf16,
                       int tokens, float *y, const float *residual, cudaStream_t stream) {
@@ -190,7 +280,7 @@ int gemv_batch_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const voi
   // about two CTAs per SM over all chunks; never more CTAs than tiles
   a.ctas_per_chunk =
       std::max(1, std::min(a.tiles / kBgWarps + 1, (2 * ctx->sm_count + nchunks - 1) / nchunks));
-  q4k_gemv_batch_kernel<<<nchunks * a.ctas_per_chunk, kBgThreads, 0, stream>>>(a);
+  q4k_gemv_batch_kernel<<<nchunks * a.ctas_per_chunk, kBgThreads, kBgSmem, stream>>>(a);
   return check_launch(ctx, "mlm_q4k_gemv_batch");
 }
 

@@ -28,6 +28,8 @@ pytestmark = pytest.mark.gpu
 
 PROMPT = [17, 4000, 3, 999, 2048]
 STEPS = 6
+BATCH_PROMPTS = [[11, 22, 33, 44], [3000, 7]]
+BATCH_NEXT = [5, 4095]
 
 
 def _tp_cfg():
@@ -70,11 +72,29 @@ def _device_run(ctx, cfg):
     m.prefill(PROMPT, nxt, pl)
     pre = (pl.download(np.float32), int(nxt.download(np.int32)[0]))
     m.close()
-    return lgs, first, toks, pre
+    # a batch of two sequences: both prompts, then one batched step
+    mb = Llama(ctx, cfg, batch=2)
+    fill_llama(mb, SEED)
+    for b, pr in enumerate(BATCH_PROMPTS):
+        mb.prefill(pr, nxt, None, seq=b)
+    bl = ctx.alloc(4 * 2 * cfg.vocab)
+    mb.forward_batch(BATCH_NEXT, bl)
+    btoks = ctx.alloc(4 * 2 * 3)
+    mb.decode_greedy_batch(BATCH_NEXT, 3, btoks)
+    batch = (bl.download(np.float32).reshape(2, cfg.vocab), btoks.download(np.int32).reshape(3, 2))
+    mb.close()
+    return lgs, first, toks, pre, batch
 
 
 def _check(cfg, got):
-    lgs, first, toks, (pre_lg, pre_next) = got
+    lgs, first, toks, (pre_lg, pre_next), (blg, _) = got
+    for b, pr in enumerate(BATCH_PROMPTS):  # the batched step, per sequence
+        layers, glob, caches = _oracle_model(cfg)
+        for pos, tok in enumerate(pr):
+            LO.model_forward(layers, glob, caches, tok, pos, cfg_dict(cfg))
+        w = LO.model_forward(layers, glob, caches, BATCH_NEXT[b], len(pr), cfg_dict(cfg))
+        assert rel_l2(blg[b], w) < TOL, (b, rel_l2(blg[b], w))
+        assert int(np.argmax(blg[b])) == int(np.argmax(w)), b
     want_lgs, want_first, want_toks = _oracle_run(cfg)
     for p, (g, w) in enumerate(zip(lgs, want_lgs)):
         assert rel_l2(g, w) < TOL, (p, rel_l2(g, w))
@@ -144,3 +164,5 @@ def test_two_ranks_match_oracle():
     cfg = _tp_cfg()
     for rank in (0, 1):
         _check(cfg, res[rank])
+    # both ranks drew the same greedy tokens for the batch
+    assert np.array_equal(res[0][4][1], res[1][4][1])

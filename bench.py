@@ -729,7 +729,7 @@ def run_llama(args, world, rank, local, pg) -> dict:
         alg = llama_token_bytes(1, pos, with_head=False) - 2 * 4096
         value = alg * args.steps * world / (ms_max * 1e-3) / 1e9
         unit, metric_value_desc = "GB/s", "one decoder layer per step"
-        launches = args.steps * 8  # state + QKV GEMV, RoPE, 2 attention, 3 GEMVs
+        launches = args.steps * 7  # state, QKV GEMV, RoPE, attention, 3 GEMVs
         # e2e: hidden state in from pinned host memory, the layer, out again
         lib, h = ctx.lib, ctx.handle
         hbuf = ctypes.c_void_p()
@@ -842,7 +842,7 @@ def run_llama(args, world, rank, local, pg) -> dict:
         value = steps * world / (ms_max * 1e-3)
         unit = "tokens/s"
         alg = llama_token_bytes(32, pos0 + steps // 2)
-        launches = steps * (1 + 32 * 7 + 3)  # embed, 7 per layer, head, argmax, advance
+        launches = steps * (1 + 32 * 6 + 3)  # embed, 6 per layer, head, argmax, advance
         # e2e: forward(tokenID:) per token through the C ABI, the argmax read back
         m.set_position(prompt_len)
         lib, h = ctx.lib, ctx.handle
@@ -984,9 +984,9 @@ def run_tp70b(args, world, rank, local, pg) -> dict:
         "e2e": {"value": round(B * e2e_steps / e2e_s, 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B},
         # per step: embedding; per layer 2 RMSNorm rows, 3 GEMMs + 2 more, RoPE,
-        # 2 attention, SwiGLU (+ 2 one-shot all-reduces with TP); head: RMSNorm,
+        # attention, SwiGLU (+ 2 one-shot all-reduces with TP); head: RMSNorm,
         # GEMM, B argmaxes (+ key reduce with TP); advance
-        "gpu_launches": steps * (1 + 80 * (10 + (2 if world > 1 else 0)) + 2 + B
+        "gpu_launches": steps * (1 + 80 * (9 + (2 if world > 1 else 0)) + 2 + B
                                  + (1 if world > 1 else 0) + 1),
         "launch": "CUDA graph (one batched decode step, all-reduces included, replayed per step)",
         "roofline": {"bound": "hbm", "achieved": round(kernel_gbs, 1), "peak": peaks["hbm_gbs"],

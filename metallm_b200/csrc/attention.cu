@@ -8,7 +8,7 @@
 // of positions and serves all n_heads/n_kv_heads query heads of that KV head,
 // so each K and V row is read from HBM exactly once.  Softmax is fp32 with a
 // running max; each CTA writes (max, sum, unnormalised output) for its chunk
-// and a second kernel merges the chunks.
+// and the last CTA of a KV head to finish merges the chunks.
 #include "mlm_device.cuh"
 #include "mlm_internal.h"
 
@@ -17,6 +17,7 @@ namespace mlm {
 constexpr int kAttnD = 128;       // head_dim handled by this kernel
 constexpr int kAttnChunk = 64;    // positions per CTA (upper bound)
 constexpr int kAttnMaxChunks = 64;
+constexpr int kAttnMaxArrivals = 8192;  // (sequence, KV head) pairs of one launch
 constexpr int kAttnThreads = 128;
 
 // partial layout per (chunk, head): [m, l, o[128]]
@@ -28,14 +29,15 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
 
-template <int G>
+template <int G, class OutT>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_partial_kernel(
     const __half *__restrict__ q, const __half *__restrict__ kc, const __half *__restrict__ vc,
     int n_heads, int n_kv, int seq_len, int chunk_len, float scale,
     float *__restrict__ partials, const int *__restrict__ pos_dev, size_t q_bs, size_t kv_bs,
-    size_t part_bs) {
+    size_t part_bs, OutT *__restrict__ out, size_t out_bs, int *__restrict__ arrivals) {
   __shared__ float s_scores[G][kAttnChunk * 2];
   __shared__ float s_out[kAttnThreads / 32][G][kAttnD];
+  pdl_wait_then_release();
   const int kvh = blockIdx.x;
   const int chunk = blockIdx.y;
   const int p0 = chunk * chunk_len;
@@ -165,29 +167,65 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_partial_kernel(
       pp[1] = s_l[gh];
     }
   }
-}
 
-template <class OutT>
-__global__ void attn_decode_merge_kernel(const float *__restrict__ partials, int n_heads,
-                                         int nchunks, OutT *__restrict__ out,
-                                         const int *__restrict__ pos_dev, int chunk_len,
-                                         size_t part_bs, size_t out_bs) {
-  const int h = blockIdx.x;
-  const int dd = threadIdx.x;  // 128 threads
-  const int bz = blockIdx.y;   // sequence of a batch
-  partials += bz * part_bs;
-  out += bz * out_bs;
-  if (pos_dev) nchunks = (pos_dev[bz] + chunk_len) / chunk_len;
-  float M = -INFINITY;
-  for (int c = 0; c < nchunks; ++c) M = fmaxf(M, partials[((size_t)c * n_heads + h) * kAttnPartial]);
-  float L = 0.f, O = 0.f;
-  for (int c = 0; c < nchunks; ++c) {
-    const float *pp = partials + ((size_t)c * n_heads + h) * kAttnPartial;
-    const float w = __expf(pp[0] - M);
-    L += pp[1] * w;
-    O += pp[2 + dd] * w;
+  // The last chunk of this (sequence, KV head) to finish merges the chunks
+  // of its G query heads, in chunk order; it re-zeroes the arrival counter
+  // for the next launch.
+  __threadfence();
+  __syncthreads();
+  __shared__ bool s_last;
+  const int nlive = (seq_len + chunk_len - 1) / chunk_len;  // chunks with positions
+  if (threadIdx.x == 0) {
+    int *arr = arrivals + (size_t)bz * n_kv + kvh;
+    s_last = atomicAdd(arr, 1) == nlive - 1;
+    if (s_last) *arr = 0;
   }
-  out[(size_t)h * kAttnD + dd] = from_float<OutT>(O / L);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  out += bz * out_bs;
+  // (max, sum) of every (chunk, head) into shared memory (s_out is free now)
+  static_assert(kAttnThreads == kAttnD, "one thread per output dimension");
+  static_assert(3 * kAttnMaxChunks <= (kAttnThreads / 32) * kAttnD, "merge scratch");
+  float *s_cm = &s_out[0][0][0];           // [chunk][G] chunk maxima
+  float *s_cl = s_cm + kAttnMaxChunks * G;  // [chunk][G] chunk sums
+  float *s_cw = s_cl + kAttnMaxChunks * G;  // [chunk][G] chunk weights exp(m - M)
+  __shared__ float s_L[G];
+  for (int i = threadIdx.x; i < nlive * G; i += kAttnThreads) {
+    const float *pp = partials + ((size_t)(i / G) * n_heads + kvh * G) * kAttnPartial +
+                      (i % G) * kAttnPartial;
+    s_cm[i] = __ldcg(pp);
+    s_cl[i] = __ldcg(pp + 1);
+  }
+  __syncthreads();
+  for (int gh = warp; gh < G; gh += nwarp) {
+    float m = -INFINITY;
+    for (int c = lane; c < nlive; c += 32) m = fmaxf(m, s_cm[c * G + gh]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (int c = lane; c < nlive; c += 32) {
+      const float w = __expf(s_cm[c * G + gh] - m);
+      s_cw[c * G + gh] = w;
+      l += s_cl[c * G + gh] * w;
+    }
+    l = warp_sum(l);
+    if (lane == 0) s_L[gh] = l;
+  }
+  __syncthreads();
+  // thread dd: dimension dd of the G heads, chunks in order
+  const int dd = threadIdx.x;
+  float O[G];
+#pragma unroll
+  for (int gh = 0; gh < G; ++gh) O[gh] = 0.f;
+#pragma unroll 4
+  for (int c = 0; c < nlive; ++c) {
+    const float *pc = partials + ((size_t)c * n_heads + kvh * G) * kAttnPartial + 2 + dd;
+#pragma unroll
+    for (int gh = 0; gh < G; ++gh) O[gh] += __ldcg(pc + gh * kAttnPartial) * s_cw[c * G + gh];
+  }
+#pragma unroll
+  for (int gh = 0; gh < G; ++gh)
+    out[(size_t)(kvh * G + gh) * kAttnD + dd] = from_float<OutT>(O[gh] / s_L[gh]);
 }
 
 // seq_len positions, or, when pos_dev is set, pos_dev[b] + 1 positions read
@@ -234,33 +272,19 @@ static int attn_decode_impl(mlm_ctx *ctx, const void *q, const void *kc, const v
   const __half *qh = reinterpret_cast<const __half *>(q);
   const __half *kh = reinterpret_cast<const __half *>(kc);
   const __half *vh = reinterpret_cast<const __half *>(vc);
-  switch (G) {
-    case 1:
-      attn_decode_partial_kernel<1><<<grid, kAttnThreads, kAttnStageBytes, stream>>>(
-          qh, kh, vh, n_heads, n_kv, seq_len, chunk_len, scale, partials, pos_dev, q_bs, kv_bs,
-          part_bs);
-      break;
-    case 2:
-      attn_decode_partial_kernel<2><<<grid, kAttnThreads, kAttnStageBytes, stream>>>(
-          qh, kh, vh, n_heads, n_kv, seq_len, chunk_len, scale, partials, pos_dev, q_bs, kv_bs,
-          part_bs);
-      break;
-    case 4:
-      attn_decode_partial_kernel<4><<<grid, kAttnThreads, kAttnStageBytes, stream>>>(
-          qh, kh, vh, n_heads, n_kv, seq_len, chunk_len, scale, partials, pos_dev, q_bs, kv_bs,
-          part_bs);
-      break;
-    default:
-      attn_decode_partial_kernel<8><<<grid, kAttnThreads, kAttnStageBytes, stream>>>(
-          qh, kh, vh, n_heads, n_kv, seq_len, chunk_len, scale, partials, pos_dev, q_bs, kv_bs,
-          part_bs);
-      break;
-  }
-  int st = check_launch(ctx, "mlm_attn_decode (partial)");
-  if (st != MLM_OK) return st;
-  attn_decode_merge_kernel<OutT><<<dim3(n_heads, batch), kAttnD, 0, stream>>>(
-      partials, n_heads, nchunks, out, pos_dev, chunk_len, part_bs, out_bs);
-  return check_launch(ctx, "mlm_attn_decode (merge)");
+  MLM_REQUIRE(ctx, (size_t)batch * n_kv <= kAttnMaxArrivals, MLM_ERR_SHAPE,
+              "mlm_attn_decode: %d KV heads x %d sequences exceed %d", n_kv, batch,
+              kAttnMaxArrivals);
+  auto kern = G == 1   ? attn_decode_partial_kernel<1, OutT>
+              : G == 2 ? attn_decode_partial_kernel<2, OutT>
+              : G == 4 ? attn_decode_partial_kernel<4, OutT>
+                       : attn_decode_partial_kernel<8, OutT>;
+  return check_launch_pdl(
+      ctx,
+      launch_pdl(kern, grid, dim3(kAttnThreads), kAttnStageBytes, stream, qh, kh, vh, n_heads,
+                 n_kv, seq_len, chunk_len, scale, partials, pos_dev, q_bs, kv_bs, part_bs, out,
+                 out_bs, ctx->attn_arrivals),
+      "mlm_attn_decode");
 }
 
 int attn_decode_launch(mlm_ctx *ctx, const void *q, const void *kc, const void *vc, int n_heads,
@@ -286,15 +310,28 @@ size_t attn_decode_partial_floats(int n_heads, int capacity) {
 }
 
 // called once per context, with its device current
+template <class OutT>
+static int attn_init_out(mlm_ctx *ctx) {
+  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_partial_kernel<1, OutT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnStageBytes));
+  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_partial_kernel<2, OutT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnStageBytes));
+  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_partial_kernel<4, OutT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnStageBytes));
+  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_partial_kernel<8, OutT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnStageBytes));
+  return MLM_OK;
+}
+
 int attn_init(mlm_ctx *ctx) {
-  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_partial_kernel<1>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnStageBytes));
-  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_partial_kernel<2>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnStageBytes));
-  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_partial_kernel<4>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnStageBytes));
-  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_partial_kernel<8>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnStageBytes));
+  int st = attn_init_out<__half>(ctx);
+  if (st != MLM_OK) return st;
+  st = attn_init_out<__nv_bfloat16>(ctx);
+  if (st != MLM_OK) return st;
+  // arrival counters of the chunk merge, zero between launches
+  if (cudaMalloc(&ctx->attn_arrivals, sizeof(int) * kAttnMaxArrivals) != cudaSuccess)
+    return set_error(ctx, MLM_ERR_ALLOC, "attention: arrival counters");
+  MLM_CUDA_TRY(ctx, cudaMemset(ctx->attn_arrivals, 0, sizeof(int) * kAttnMaxArrivals));
   return MLM_OK;
 }
 
@@ -306,6 +343,7 @@ size_t attn_partial_floats_max(int max_heads) {
 
 __global__ void embed_f16_kernel(const __half *__restrict__ table, int vocab, int dim,
                                  const int32_t *__restrict__ token, float *__restrict__ out) {
+  pdl_wait_then_release();
   int t = *token;
   t = t < 0 ? 0 : (t >= vocab ? vocab - 1 : t);
   const __half *row = table + (size_t)t * dim;
@@ -332,6 +370,7 @@ constexpr int kArgmaxThreads = 256;
 __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(
     const float *__restrict__ x, int n, int offset, unsigned long long *scratch,
     int32_t *__restrict__ out, unsigned long long *key_out) {
+  pdl_wait_then_release();
   unsigned long long best = 0;
   const int stride = gridDim.x * blockDim.x;
 #pragma unroll 8
@@ -368,6 +407,7 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(
 // keys): out[b] = the index of the largest key of row b
 __global__ void argmax_keys_rows_kernel(const unsigned long long *keys, int nkeys, int rows,
                                         int32_t *out) {
+  pdl_wait_then_release();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= rows) return;
   unsigned long long k = 0;
@@ -376,6 +416,7 @@ __global__ void argmax_keys_rows_kernel(const unsigned long long *keys, int nkey
 }
 
 __global__ void argmax_keys_kernel(const unsigned long long *keys, int nkeys, int32_t *out) {
+  pdl_wait_then_release();
   unsigned long long k = 0;
   for (int i = 0; i < nkeys; ++i) k = max(k, keys[i]);
   *out = k ? (int32_t)~(uint32_t)(k & 0xFFFFFFFFull) : 0;
@@ -384,36 +425,44 @@ __global__ void argmax_keys_kernel(const unsigned long long *keys, int nkeys, in
 int argmax_launch(mlm_ctx *ctx, const float *x, int n, int32_t *out, cudaStream_t stream) {
   const int ctas = std::max(1, std::min(ctx->sm_count, (n + 8 * kArgmaxThreads - 1) /
                                                            (8 * kArgmaxThreads)));
-  argmax_kernel<<<ctas, kArgmaxThreads, 0, stream>>>(x, n, 0, ctx->argmax_scratch, out, nullptr);
-  return check_launch(ctx, "mlm_argmax_f32");
+  return check_launch_pdl(ctx,
+                          launch_pdl(argmax_kernel, dim3(ctas), dim3(kArgmaxThreads), 0, stream,
+                                     x, n, 0, ctx->argmax_scratch, out, nullptr),
+                          "mlm_argmax_f32");
 }
 
 int argmax_keys_rows_launch(mlm_ctx *ctx, const unsigned long long *keys, int nkeys, int rows,
                             int32_t *out, cudaStream_t stream) {
-  argmax_keys_rows_kernel<<<(rows + 127) / 128, 128, 0, stream>>>(keys, nkeys, rows, out);
-  return check_launch(ctx, "argmax (row keys)");
+  return check_launch_pdl(ctx,
+                          launch_pdl(argmax_keys_rows_kernel, dim3((rows + 127) / 128), dim3(128),
+                                     0, stream, keys, nkeys, rows, out),
+                          "argmax (row keys)");
 }
 
 int argmax_key_launch(mlm_ctx *ctx, const float *x, int n, int offset, unsigned long long *key,
                       cudaStream_t stream) {
   const int ctas = std::max(1, std::min(ctx->sm_count, (n + 8 * kArgmaxThreads - 1) /
                                                            (8 * kArgmaxThreads)));
-  argmax_kernel<<<ctas, kArgmaxThreads, 0, stream>>>(x, n, offset, ctx->argmax_scratch, nullptr,
-                                                      key);
-  return check_launch(ctx, "argmax (key)");
+  return check_launch_pdl(ctx,
+                          launch_pdl(argmax_kernel, dim3(ctas), dim3(kArgmaxThreads), 0, stream,
+                                     x, n, offset, ctx->argmax_scratch, nullptr, key),
+                          "argmax (key)");
 }
 
 int argmax_keys_launch(mlm_ctx *ctx, const unsigned long long *keys, int nkeys, int32_t *out,
                        cudaStream_t stream) {
-  argmax_keys_kernel<<<1, 1, 0, stream>>>(keys, nkeys, out);
-  return check_launch(ctx, "argmax (keys)");
+  return check_launch_pdl(
+      ctx, launch_pdl(argmax_keys_kernel, dim3(1), dim3(1), 0, stream, keys, nkeys, out),
+      "argmax (keys)");
 }
 
 int embed_launch(mlm_ctx *ctx, const void *table, int vocab, int dim, const int32_t *tok,
                  float *out, cudaStream_t stream) {
-  embed_f16_kernel<<<(dim + 255) / 256, 256, 0, stream>>>(reinterpret_cast<const __half *>(table),
-                                                          vocab, dim, tok, out);
-  return check_launch(ctx, "mlm_embed_f16");
+  return check_launch_pdl(
+      ctx,
+      launch_pdl(embed_f16_kernel, dim3((dim + 255) / 256), dim3(256), 0, stream,
+                 reinterpret_cast<const __half *>(table), vocab, dim, tok, out),
+      "mlm_embed_f16");
 }
 
 }  // namespace mlm

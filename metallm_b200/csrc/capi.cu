@@ -150,6 +150,7 @@ extern "C" void mlm_destroy(mlm_ctx *ctx) {
   if (ctx->gemv_counters) cudaFree(ctx->gemv_counters);
   if (ctx->gemv_partials) cudaFree(ctx->gemv_partials);
   if (ctx->attn_partials) cudaFree(ctx->attn_partials);
+  if (ctx->attn_arrivals) cudaFree(ctx->attn_arrivals);
   if (ctx->gemm_flags) cudaFree(ctx->gemm_flags);
   if (ctx->argmax_scratch) cudaFree(ctx->argmax_scratch);
   if (ctx->host_status) cudaFreeHost(const_cast<int *>(ctx->host_status));

@@ -64,6 +64,7 @@ __global__ void set_state_kernel(int *st, int token, int pos, int step) {
 
 // after the argmax of a step: record its token, move to the next position
 __global__ void advance_kernel(int *st, int32_t *tokens) {
+  pdl_wait_then_release();
   tokens[st[kStep]] = st[kToken];
   st[kStep] += 1;
   st[kPos] += 1;
@@ -72,6 +73,7 @@ __global__ void advance_kernel(int *st, int32_t *tokens) {
 // the same for a batch of sequences: gen[step][b] = tok[b], positions + 1
 __global__ void advance_batch_kernel(int *st, int *pos, const int32_t *tok, int32_t *gen,
                                      int batch) {
+  pdl_wait_then_release();
   const int step = st[kStep];
   for (int b = threadIdx.x; b < batch; b += blockDim.x) {
     gen[(size_t)step * batch + b] = tok[b];
@@ -601,8 +603,10 @@ extern "C" int mlm_llama_decode_greedy(mlm_llama *m, int token, int steps, int32
     MLM_CUDA_TRY(ctx, cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
     int st = m->step(true, nullptr);
     if (st == MLM_OK) {
-      advance_kernel<<<1, 1, 0, ctx->stream>>>(m->state, m->gen_tokens);
-      st = check_launch(ctx, "mlm_llama_decode_greedy (advance)");
+      st = check_launch_pdl(ctx,
+                            launch_pdl(advance_kernel, dim3(1), dim3(1), 0, ctx->stream,
+                                       m->state, m->gen_tokens),
+                            "mlm_llama_decode_greedy (advance)");
     }
     cudaGraph_t g = nullptr;
     const cudaError_t e = cudaStreamEndCapture(ctx->stream, &g);
@@ -688,9 +692,10 @@ extern "C" int mlm_llama_decode_greedy_batch(mlm_llama *m, const int32_t *tokens
     MLM_CUDA_TRY(ctx, cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
     st = m->step_batch(nullptr);
     if (st == MLM_OK) {
-      advance_batch_kernel<<<1, 64, 0, ctx->stream>>>(m->state, m->pos_b, m->tok_b, m->gen_b,
-                                                     m->batch);
-      st = check_launch(ctx, "mlm_llama_decode_greedy_batch (advance)");
+      st = check_launch_pdl(ctx,
+                            launch_pdl(advance_batch_kernel, dim3(1), dim3(64), 0, ctx->stream,
+                                       m->state, m->pos_b, m->tok_b, m->gen_b, m->batch),
+                            "mlm_llama_decode_greedy_batch (advance)");
     }
     cudaGraph_t g = nullptr;
     const cudaError_t e = cudaStreamEndCapture(ctx->stream, &g);

@@ -71,6 +71,14 @@ __device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
   return __half2float(__ushort_as_half((unsigned short)(bits16 & 0xFFFF)));
 }
 
+// Programmatic dependent launch (see launch_pdl): wait for the preceding
+// kernel's completion and memory, then let the next kernel be scheduled.
+// Both are no-ops in a grid that was not launched as a dependent.
+__device__ __forceinline__ void pdl_wait_then_release() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

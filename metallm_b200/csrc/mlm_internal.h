@@ -38,6 +38,7 @@ struct mlm_ctx {
   // split-K scratch of decode attention
   float *attn_partials = nullptr;
   size_t attn_partials_floats = 0;
+  int *attn_arrivals = nullptr;  // per (sequence, KV head); zero between launches
 
   // stream-K hand-off flags of the prefill GEMM, one per output tile; zero
   // between launches (each launch's waiters count them back down)
@@ -65,6 +66,37 @@ namespace mlm {
 int set_error(mlm_ctx *ctx, int code, const char *fmt, ...)
     __attribute__((format(printf, 3, 4)));
 int check_launch(mlm_ctx *ctx, const char *what);
+
+// Launch as a programmatic dependent of the previous kernel on the stream:
+// the grid may be scheduled once every CTA of that kernel has executed
+// griddepcontrol.launch_dependents (or exited), and must execute
+// griddepcontrol.wait before it reads anything that kernel writes.  Every
+// kernel of the decode step does both, so the launch latency of each kernel
+// and the weight prefetch of each GEMV overlap the kernel before it.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// status of a launch_pdl call (clears the error it may have left)
+inline int check_launch_pdl(mlm_ctx *ctx, cudaError_t e, const char *what) {
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(ctx, MLM_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
+  }
+  return check_launch(ctx, what);
+}
 
 // Kernel launchers shared between translation units (stream-ordered; each
 // returns an MLM_* status and records the reason in ctx on failure).

@@ -97,6 +97,7 @@ __global__ void rope_qk_kv_kernel(mlm_rope_args a, RopeConsts k, const float *__
                                   __half *__restrict__ q_out, __half *__restrict__ kc,
                                   __half *__restrict__ vc, int pos,
                                   const int *__restrict__ pos_dev) {
+  pdl_wait_then_release();
   // graph-replayed decode reads the position from device memory: it is both
   // the rotation angle's position and the cache row
   const int apos = pos_dev ? *pos_dev : a.pos_offset;
@@ -171,10 +172,11 @@ int rope_qk_kv_launch(mlm_ctx *ctx, const float *q, const float *k, const float 
                       const int *pos_dev) {
   const RopeConsts kc_ = rope_consts(a);
   const int total = nq * (d / 2) + 2 * nkv * (d / 2);
-  rope_qk_kv_kernel<<<(total + 255) / 256, 256, 0, stream>>>(
-      a, kc_, freqs, q, k, v, nq, nkv, d, reinterpret_cast<__half *>(q_out),
-      reinterpret_cast<__half *>(kc), reinterpret_cast<__half *>(vc), pos, pos_dev);
-  return check_launch(ctx, "mlm_rope_qk_kv_append");
+  const cudaError_t e = launch_pdl(
+      rope_qk_kv_kernel, dim3((total + 255) / 256), dim3(256), 0, stream, a, kc_, freqs, q, k, v,
+      nq, nkv, d, reinterpret_cast<__half *>(q_out), reinterpret_cast<__half *>(kc),
+      reinterpret_cast<__half *>(vc), pos, pos_dev);
+  return check_launch_pdl(ctx, e, "mlm_rope_qk_kv_append");
 }
 
 int silu_mul_launch(mlm_ctx *ctx, const float *g, const float *u, void *out, int n,

@@ -53,6 +53,7 @@ __global__ void rope_kv_rows_kernel(mlm_rope_args a, RopeConsts k, const float *
                                     int pos0, __half *__restrict__ q_out, __half *__restrict__ kc,
                                     __half *__restrict__ vc, const int *__restrict__ pos_dev,
                                     size_t kv_bs) {
+  pdl_wait_then_release();
   const int t = blockIdx.y;
   const int pos = pos_dev ? pos_dev[t] : pos0 + t;
   if (pos_dev) {
@@ -310,10 +311,12 @@ int rope_kv_batch_launch(mlm_ctx *ctx, const float *qkv, const float *freqs,
                          cudaStream_t stream) {
   const RopeConsts k = rope_consts(a);
   const int total = nq * (d / 2) + 2 * nkv * (d / 2);
-  rope_kv_rows_kernel<<<dim3((total + 255) / 256, batch), 256, 0, stream>>>(
-      a, k, freqs, qkv, nq, nkv, d, 0, reinterpret_cast<__half *>(q_out),
-      reinterpret_cast<__half *>(kc), reinterpret_cast<__half *>(vc), pos_dev, kv_bs);
-  return check_launch(ctx, "batched decode (rope)");
+  return check_launch_pdl(
+      ctx,
+      launch_pdl(rope_kv_rows_kernel, dim3((total + 255) / 256, batch), dim3(256), 0, stream, a,
+                 k, freqs, qkv, nq, nkv, d, 0, reinterpret_cast<__half *>(q_out),
+                 reinterpret_cast<__half *>(kc), reinterpret_cast<__half *>(vc), pos_dev, kv_bs),
+      "batched decode (rope)");
 }
 
 int attn_prefill_launch(mlm_ctx *ctx, const void *q16, const void *kc, const void *vc, int pos0,

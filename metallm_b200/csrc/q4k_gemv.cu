@@ -57,10 +57,13 @@
 namespace mlm {
 
 #ifndef MLM_GEMV_WARPS
-#define MLM_GEMV_WARPS 12
+#define MLM_GEMV_WARPS 8
 #endif
 #ifndef MLM_GEMV_STAGES
-#define MLM_GEMV_STAGES 3
+#define MLM_GEMV_STAGES 4
+#endif
+#ifndef MLM_GEMV_MIN_BLOCKS
+#define MLM_GEMV_MIN_BLOCKS 1  // resident CTAs per SM the register budget allows
 #endif
 constexpr int kGemvMaxWarps = MLM_GEMV_WARPS;          // warps per CTA (upper bound)
 constexpr int kGemvStages = MLM_GEMV_STAGES;           // smem stages per warp
@@ -99,7 +102,7 @@ __device__ __forceinline__ void tma_unit(uint32_t dst, const CUtensorMap *tmap, 
       : "memory");
 }
 
-__global__ void __launch_bounds__(kGemvMaxWarps * 32, 1)
+__global__ void __launch_bounds__(kGemvMaxWarps * 32, MLM_GEMV_MIN_BLOCKS)
     q4k_gemv_kernel(const __grid_constant__ CUtensorMap tmap, GemvArgs p) {
   // TMA tensor destinations need 128-byte alignment: stages sit at multiples
   // of 4608 = 36 * 128 bytes from this base
@@ -586,8 +589,10 @@ int gemv_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const GemvInput
               "mlm_q4k_gemv: %d rows exceed the %d-row scratch limit", rows,
               max_tiles * kTileRows);
   GemvPlan pl;
-  const bool ok = plan_gemv(rows, nb, std::min(ctx->sm_count, max_ctas),
-                            (size_t)ctx->max_smem_optin, pl);
+  // 228 KB of shared memory per SM, 1 KB of it reserved per resident CTA
+  const size_t smem_cap = std::min((size_t)ctx->max_smem_optin,
+                                   (size_t)233472 / MLM_GEMV_MIN_BLOCKS - 1024);
+  const bool ok = plan_gemv(rows, nb, std::min(ctx->sm_count, max_ctas), smem_cap, pl);
   MLM_REQUIRE(ctx, ok, MLM_ERR_UNSUPPORTED,
               "mlm_q4k_gemv: rows=%d cols=%d does not fit the shared-memory plan", rows, cols);
   CUtensorMap tmap;

@@ -129,6 +129,8 @@ PROFILES = {
     "prefill": "q4k_gemm_28672x4096x512.md",
     "gemm": "q4k_gemm_28672x4096x512.md",
     "gemv_batch": "q4k_gemv_batch_57344x8192x8.md",
+    "gemv_q6k": "q6k_gemv_128256x4096.md",
+    "repack": "q4k_repack_4096x4096.md",
 }
 
 
@@ -1007,9 +1009,183 @@ def run_tp70b(args, world, rank, local, pg) -> dict:
     return line
 
 
+
+FORMAT_WORKLOADS = {
+    # name: (rows, cols, description)
+    "gemv_q6k": (128256, 4096, "Q6_K x fp16 GEMV 128256x4096 (the Llama-3-8B output head as "
+                               "Q4_K_M files store it), batch 1"),
+    "repack": (4096, 4096, "GGUF-order Q4_K -> kernel-order repack of one 4096x4096 tensor "
+                           "(65,536 super-blocks, in place)"),
+}
+
+
+def q6k_gemv_bytes(rows: int, cols: int) -> int:
+    return rows * (cols // 256) * 210 + 2 * cols + 4 * rows
+
+
+def cpu_q6k_gemv_rate(rows: int, cols: int, budget_s: float, threads: int) -> dict:
+    """The reference's path for a Q6_K linear on the host: its own
+    kernel_dequantize_q6_K_f32 (oracle/_ref) over the matrix, then the fp32
+    product with x (the reference hands the dequantized matrix to MPS), on a
+    bounded row sample; GB/s of packed weights."""
+    import numpy as np
+
+    from oracle import oracle as O
+    sample = min(rows, 8192)
+    W = O.gen_q6k(11, 1, sample * cols // 256)
+    x = O.gen_f16(11, 2, cols).astype(np.float32)
+    use_ref = O.ref_lib() is not None
+    deq = (lambda: O.ref_q6k_dequant_f32(W, sample * cols, threads)) if use_ref else \
+        (lambda: O.q6k_dequant_f32(W, sample * cols, threads))
+    fn = lambda: deq().reshape(sample, cols) @ x  # noqa: E731
+    fn()
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        fn()
+        reps += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": round(q6k_gemv_bytes(sample, cols) / dt / 1e9, 4), "unit": "GB/s",
+            "cores": threads, "kind": "reference" if use_ref else "port",
+            "sample": f"{reps} x ({sample} rows x {cols} Q6_K dequantized by the reference kernel "
+                      f"+ fp32 product) in {time.perf_counter() - t0:.1f} s, {threads} threads"}
+
+
+def cpu_repack_rate(nblocks: int, budget_s: float) -> dict:
+    """The oracle's repack (a plain C loop, one thread): the reference has no
+    repack at all (it reads GGUF blocks in its own order)."""
+    from oracle import oracle as O
+    b = O.gen_q4k(5, 1, nblocks)
+    O.q4k_canonical_to_interleaved(b)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        O.q4k_canonical_to_interleaved(b)
+        reps += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": round(2 * 144 * nblocks / dt / 1e9, 4), "unit": "GB/s", "cores": 1,
+            "kind": "port",
+            "sample": f"{reps} x {nblocks} blocks in {time.perf_counter() - t0:.1f} s, 1 thread"}
+
+
+def run_formats(args, world, rank, local, pg) -> dict:
+    """The Q6_K GEMV (the output head of a Q4_K_M file) and the GGUF-order
+    Q4_K repack, each step one launch over rotating inputs larger than L2."""
+    import torch
+
+    from metallm_b200 import Context
+    rows, cols, desc = FORMAT_WORKLOADS[args.workload]
+    ctx = Context(local)
+    torch.cuda.set_device(local)
+    tstream = torch.cuda.ExternalStream(ctx.stream(), device=f"cuda:{local}")
+    peaks = measured_peaks()
+    nb = rows * cols // 256
+    q6 = args.workload == "gemv_q6k"
+    bb = 210 if q6 else 144
+    copies = max(2, -(-400_000_000 // (nb * bb)))  # > 3x the 126 MB L2
+    Ws = []
+    for c in range(copies):
+        W = ctx.alloc(nb * bb)
+        (ctx.gen_q6k if q6 else ctx.gen_q4k)(1000 + c, 1, nb, W)
+        Ws.append(W)
+    x = ctx.alloc(2 * cols)
+    ctx.gen_f16(7, 2, cols, x)
+    y = ctx.alloc(4 * rows)
+    if q6:
+        step = lambda i: ctx.q6k_gemv(Ws[i % copies], rows, cols, x, y)  # noqa: E731
+        alg = q6k_gemv_bytes(rows, cols)
+    else:  # in place: each pass shuffles a copy again (a bijection, same traffic)
+        step = lambda i: ctx.q4k_repack_canonical(Ws[i % copies], Ws[i % copies], nb)  # noqa: E731
+        alg = 2 * 144 * nb
+    ctx.graph_begin()
+    for i in range(args.steps):
+        step(i)
+    graph = ctx.graph_end()
+    for i in range(args.warmup):
+        step(i)
+    ctx.wait()
+    barrier(pg, local)
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(tstream)
+    graph.launch()
+    ev1.record(tstream)
+    ev1.synchronize()
+    dev_ms = ev0.elapsed_time(ev1)
+    clocks = sampler.stop()
+    graph.destroy()
+    ms_max = max_over_ranks(dev_ms, pg, local)
+    per_ms = ms_max / args.steps
+    gbs = alg / (per_ms * 1e-3) / 1e9
+    # e2e through the C ABI with host buffers: x in (GEMV) or the GGUF blocks
+    # in and the repacked blocks out (repack), from/to pinned host memory
+    lib, h = ctx.lib, ctx.handle
+    in_bytes = 2 * cols if q6 else nb * 144
+    out_bytes = 4 * rows if q6 else nb * 144
+    hin, hout = ctypes.c_void_p(), ctypes.c_void_p()
+    lib.mlm_host_alloc(h, in_bytes, ctypes.byref(hin))
+    lib.mlm_host_alloc(h, out_bytes, ctypes.byref(hout))
+    dst_in = x if q6 else Ws[0]
+    dst_out = y if q6 else Ws[0]
+    e2e_steps = min(args.steps, 20)
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        ctx._check(lib.mlm_upload_async(h, ctypes.c_void_p(dst_in.ptr), hin, in_bytes), "up")
+        step(i if q6 else 0)
+        ctx._check(lib.mlm_download_async(h, hout, ctypes.c_void_p(dst_out.ptr), out_bytes), "dn")
+        ctx.wait()
+    e2e_s = max_over_ranks(time.perf_counter() - t0, pg, local)
+    lib.mlm_host_free(h, hin)
+    lib.mlm_host_free(h, hout)
+    line = {
+        "metric": METRIC, "value": round(gbs * world, 2), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_ms, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "q6k x f16 -> f32" if q6 else "u8 (nibble shuffle)",
+        "data": "synthetic (seeded blocks generated on device)",
+        "config": {"workload": desc, "rows": rows, "cols": cols,
+                   "parallelism": "replicas" if world > 1 else "single GPU",
+                   "l2": f"{copies} rotating copies ({copies * nb * bb / 1e6:.0f} MB > L2)",
+                   "algorithmic_bytes_per_step": alg},
+        "e2e": {"value": round(alg * e2e_steps * world / e2e_s / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": out_bytes},
+        "gpu_launches": args.steps,
+        "launch": "CUDA graph of K steps",
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
+                     "peak_source": peaks["source"], "traffic": ncu_traffic(args.workload)},
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = (cpu_q6k_gemv_rate(rows, cols, args.cpu_seconds, host_threads())
+                                if q6 else cpu_repack_rate(nb, args.cpu_seconds))
+    ctx.close()
+    return line
+
 def run_reference(args, world, rank) -> dict | None:
     if rank != 0:
         return None
+    if args.workload in FORMAT_WORKLOADS:
+        rows, cols, desc = FORMAT_WORKLOADS[args.workload]
+        q6 = args.workload == "gemv_q6k"
+        r = (cpu_q6k_gemv_rate(rows, cols, args.cpu_seconds, host_threads()) if q6
+             else cpu_repack_rate(rows * cols // 256, args.cpu_seconds))
+        v = r["value"]
+        alg = q6k_gemv_bytes(rows, cols) if q6 else 2 * 144 * (rows * cols // 256)
+        return {"impl": "reference", "metric": METRIC, "value": v, "unit": "GB/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(alg / (v * 1e9) * 1e3, 4), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None,
+                "dtype": "q6k x f16 -> f32" if q6 else "u8 (nibble shuffle)",
+                "data": "synthetic (seeded blocks)",
+                "config": {"workload": desc, "rows": rows, "cols": cols}, "cpu_baseline": r,
+                "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
     if args.workload == "gemv_batch":
         rows, cols, T = GEMV_BATCH_SHAPE
         r = cpu_gemv_rate(rows, cols, args.cpu_seconds, host_threads(), "reference")
@@ -1096,7 +1272,8 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--workload", default="gemv_up",
-                    choices=sorted(WORKLOADS) + sorted(LLAMA_WORKLOADS) + ["gemm", "gemv_batch"])
+                    choices=sorted(WORKLOADS) + sorted(LLAMA_WORKLOADS) + sorted(FORMAT_WORKLOADS)
+                    + ["gemm", "gemv_batch"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--copies", type=int, default=6, help="rotating weight copies (> L2)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -1115,7 +1292,8 @@ def main() -> None:
 
     world, rank, local, pg = dist_setup(args)
     try:
-        run = {"gemm": run_gemm, "gemv_batch": run_gemv_batch, "tp70b": run_tp70b}.get(
+        run = {"gemm": run_gemm, "gemv_batch": run_gemv_batch, "tp70b": run_tp70b,
+               "gemv_q6k": run_formats, "repack": run_formats}.get(
             args.workload, run_llama if args.workload in LLAMA_WORKLOADS else run_gpu)
         line = run(args, world, rank, local, pg)
         if rank == 0:

@@ -108,6 +108,11 @@ int mlm_gen_q4k(mlm_ctx *ctx, uint64_t seed, uint64_t stream, uint64_t first_blo
  * shard of a tensor whose input columns are split over ranks */
 int mlm_gen_q4k_sub(mlm_ctx *ctx, uint64_t seed, uint64_t stream, uint64_t nb_full, uint64_t row0,
                     uint64_t rows, uint64_t kb0, uint64_t nkb, void *out);
+/* Q6_K blocks [first_block, first_block + nblocks) of tensor `stream`: the
+ * 208 bytes of ql, qh and scales uniform, d = fp16(|N(0,1)| * 0.01); out
+ * 2-byte aligned */
+int mlm_gen_q6k(mlm_ctx *ctx, uint64_t seed, uint64_t stream, uint64_t first_block,
+                uint64_t nblocks, void *out);
 int mlm_gen_f16(mlm_ctx *ctx, uint64_t seed, uint64_t stream, uint64_t first,
                 uint64_t n, float mean, float std, void *out_f16);
 int mlm_gen_f32(mlm_ctx *ctx, uint64_t seed, uint64_t stream, uint64_t first,
@@ -132,6 +137,36 @@ int mlm_q4k_dequant_f16(mlm_ctx *ctx, const void *blocks, void *out_f16, uint64_
 /* bf16 rounding of the exact fp32 dequant (no reference counterpart; feeds
  * the tensor-core prefill path) */
 int mlm_q4k_dequant_bf16(mlm_ctx *ctx, const void *blocks, void *out_bf16, uint64_t n);
+
+/* GGUF (ggml) Q4_K blocks -> the element order the reference's kernels and
+ * every kernel here read.  A GGUF file (GGUF.swift:271-297 hands its tensor
+ * bytes over unchanged) stores element 64j + l of a super-block in the low
+ * nibble of qs[32j + l] for l < 32 and in the high nibble of qs[32j + l - 32]
+ * otherwise; DequantKernels.metal:86-88 reads element i from qs[i / 2], low
+ * nibble for even i, which garbles real files.  This byte shuffle (d, dmin
+ * and scales unchanged) makes a GGUF tensor usable by every op of this
+ * library; dequantizing the result equals the GGUF dequant bit for bit.
+ * Stream-ordered; src == dst allowed (other overlaps are rejected); both
+ * 16-byte aligned. */
+int mlm_q4k_repack_canonical(mlm_ctx *ctx, const void *src, void *dst, uint64_t nblocks);
+
+/* Q6_K (210-byte blocks: ql[128], qh[64], int8 scales[16], fp16 d;
+ * block_q6_K, DequantKernels.metal:29-34).  kernel_dequantize_q6_K_f32
+ * (DequantKernels.metal:131-172) as MetalService.dequantizeQ6K_to_f32
+ * (MetalService.swift:318-388) calls it, without its allocation and wait:
+ * out = (d * scale) * (q - 32) in fp32, bit-exact.  The fp16 and bf16 forms
+ * round that fp32 value (the reference's Q6_K -> fp16 kernel,
+ * DequantKernels.metal:176-215, reads another element order and is not
+ * followed).  n a multiple of 256; blocks 2-byte aligned. */
+int mlm_q6k_dequant_f32(mlm_ctx *ctx, const void *blocks, float *out, uint64_t n);
+int mlm_q6k_dequant_f16(mlm_ctx *ctx, const void *blocks, void *out_f16, uint64_t n);
+int mlm_q6k_dequant_bf16(mlm_ctx *ctx, const void *blocks, void *out_bf16, uint64_t n);
+/* y = W x (+ residual) on packed Q6_K weights W[rows][cols] (the Q6_K
+ * tensors ModelLoader.swift:282-287 dequantizes for an MPS linear), x fp16,
+ * fp32 accumulation; cols a multiple of 2048 and at most 32768; W and x
+ * 16-byte aligned.  Stream-ordered. */
+int mlm_q6k_gemv(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_f16, float *y,
+                 const float *residual);
 
 /* MetalService.dequantizeQ4KM_to_f32 / _f16 (MetalService.swift:170, 243):
  * allocate the output, run, wait.  *out receives a device pointer to free

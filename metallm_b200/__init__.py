@@ -207,6 +207,27 @@ class Context:
     def q4k_gemv(self, W, rows: int, cols: int, x, y, residual=None) -> None:
         self.call("mlm_q4k_gemv", W, rows, cols, x, y, residual)
 
+    def q4k_repack_canonical(self, src, dst, nblocks: int) -> None:
+        """GGUF-order Q4_K blocks into the order every op here reads."""
+        self.call("mlm_q4k_repack_canonical", src, dst, nblocks)
+
+    def gen_q6k(self, seed: int, stream: int, nblocks: int, out: DeviceBuffer,
+                first_block: int = 0) -> DeviceBuffer:
+        self.call("mlm_gen_q6k", seed, stream, first_block, nblocks, out)
+        return out
+
+    def q6k_dequant_f32(self, blocks, out, n: int) -> None:
+        self.call("mlm_q6k_dequant_f32", blocks, out, n)
+
+    def q6k_dequant_f16(self, blocks, out, n: int) -> None:
+        self.call("mlm_q6k_dequant_f16", blocks, out, n)
+
+    def q6k_dequant_bf16(self, blocks, out, n: int) -> None:
+        self.call("mlm_q6k_dequant_bf16", blocks, out, n)
+
+    def q6k_gemv(self, W, rows: int, cols: int, x, y, residual=None) -> None:
+        self.call("mlm_q6k_gemv", W, rows, cols, x, y, residual)
+
     def q4k_tiled_bytes(self, rows: int, cols: int) -> int:
         return int(self.lib.mlm_q4k_tiled_bytes(rows, cols))
 

@@ -89,6 +89,12 @@ SIGNATURES = [
     ("mlm_q4k_dequant_f32", c_int, [c_vp, c_vp, c_vp, c_u64]),
     ("mlm_q4k_dequant_f16", c_int, [c_vp, c_vp, c_vp, c_u64]),
     ("mlm_q4k_dequant_bf16", c_int, [c_vp, c_vp, c_vp, c_u64]),
+    ("mlm_q4k_repack_canonical", c_int, [c_vp, c_vp, c_vp, c_u64]),
+    ("mlm_gen_q6k", c_int, [c_vp, c_u64, c_u64, c_u64, c_u64, c_vp]),
+    ("mlm_q6k_dequant_f32", c_int, [c_vp, c_vp, c_vp, c_u64]),
+    ("mlm_q6k_dequant_f16", c_int, [c_vp, c_vp, c_vp, c_u64]),
+    ("mlm_q6k_dequant_bf16", c_int, [c_vp, c_vp, c_vp, c_u64]),
+    ("mlm_q6k_gemv", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_vp]),
     ("mlm_dequantize_q4k_to_f32", c_int, [c_vp, c_vp, c_u64, ctypes.POINTER(c_vp)]),
     ("mlm_dequantize_q4k_to_f16", c_int, [c_vp, c_vp, c_u64, ctypes.POINTER(c_vp)]),
     ("mlm_q4k_gemv", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_vp]),

@@ -135,7 +135,7 @@ extern "C" int mlm_create(int device, mlm_ctx **out) {
   }
   if (gemv_init(ctx) != MLM_OK || gemv_tiled_init(ctx) != MLM_OK || attn_init(ctx) != MLM_OK ||
       gemm_init(ctx) != MLM_OK || prefill_init(ctx) != MLM_OK ||
-      gemv_batch_init(ctx) != MLM_OK)
+      gemv_batch_init(ctx) != MLM_OK || q6k_init(ctx) != MLM_OK)
     return fail(MLM_ERR_CUDA);
   if (cudaDeviceSynchronize() != cudaSuccess) return fail(MLM_ERR_CUDA);
   *out = ctx;

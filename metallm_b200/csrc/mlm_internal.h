@@ -66,6 +66,7 @@ namespace mlm {
 int set_error(mlm_ctx *ctx, int code, const char *fmt, ...)
     __attribute__((format(printf, 3, 4)));
 int check_launch(mlm_ctx *ctx, const char *what);
+int q6k_init(mlm_ctx *ctx);  // q6k.cu: the GEMV's shared-memory limit
 
 // Launch as a programmatic dependent of the previous kernel on the stream:
 // the grid may be scheduled once every CTA of that kernel has executed

@@ -14,6 +14,8 @@
 // contiguously.  The kernel is HBM-bound (read 144 B, write 1024 B / 512 B
 // per block); a grid-stride loop with four blocks in flight per warp keeps
 // enough loads outstanding.
+#include <algorithm>
+
 #include "mlm_device.cuh"
 #include "mlm_internal.h"
 
@@ -176,6 +178,62 @@ __global__ void __launch_bounds__(256) q4k_dequant_f32_kernel(const uint8_t *__r
   }
 }
 
+// ---- GGUF element order -> the order the kernels read ----------------------------
+//
+// GGUF (ggml) Q4_K blocks hold element 64j + l (l < 32) in the low nibble of
+// qs[32j + l] and element 64j + 32 + l in its high nibble; the reference's
+// kernels, and every kernel of this library, read element i from qs[i / 2],
+// low nibble for even i (DequantKernels.metal:86-88).  The repack is a byte
+// shuffle of the 128 quant bytes (d, dmin and the scales are the same in
+// both), so dequantizing the repacked block is bit-identical to
+// dequantizing the GGUF block in its own order.  A CTA stages 128 blocks
+// (18,432 bytes) with coalesced 16-byte loads, one thread shuffles each
+// block in shared memory, and the CTA stores them back coalesced; in place
+// (src == dst) is allowed.
+constexpr int kRepackBlocks = 128;
+
+// interleaved quant word w (bytes 4w .. 4w+3 of a 64-element group) from the
+// group's 8 GGUF words c: w < 4 takes the low nibbles of bytes 8w .. 8w+7,
+// w >= 4 the high nibbles of bytes 8(w-4) .. 8(w-4)+7
+__device__ __forceinline__ uint32_t repack_word(const uint32_t *c, int w) {
+  const int sh = w < 4 ? 0 : 4;
+  const int s = w & 3;
+  const uint32_t a = (c[2 * s] >> sh) & 0x0F0F0F0Fu, b = (c[2 * s + 1] >> sh) & 0x0F0F0F0Fu;
+  // bytes 0 and 2 of x | (x >> 4) are (n0 | n1 << 4) and (n2 | n3 << 4)
+  return __byte_perm(a | (a >> 4), b | (b >> 4), 0x6420);
+}
+
+__global__ void __launch_bounds__(kRepackBlocks) q4k_repack_kernel(const uint8_t *src,
+                                                                   uint8_t *dst,
+                                                                   uint64_t nblocks) {
+  __shared__ __align__(16) uint8_t s[kRepackBlocks * kBlockBytes];
+  uint4 *sv = reinterpret_cast<uint4 *>(s);
+  for (uint64_t b0 = blockIdx.x * (uint64_t)kRepackBlocks; b0 < nblocks;
+       b0 += gridDim.x * (uint64_t)kRepackBlocks) {
+    const int nbk = (int)min((uint64_t)kRepackBlocks, nblocks - b0);
+    const uint4 *g = reinterpret_cast<const uint4 *>(src + b0 * kBlockBytes);
+    for (int i = threadIdx.x; i < nbk * 9; i += kRepackBlocks) sv[i] = g[i];
+    __syncthreads();
+    if (threadIdx.x < nbk) {
+      uint32_t *qs = reinterpret_cast<uint32_t *>(s + threadIdx.x * kBlockBytes + 16);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t c[8], o[8];
+#pragma unroll
+        for (int w = 0; w < 8; ++w) c[w] = qs[8 * j + w];
+#pragma unroll
+        for (int w = 0; w < 8; ++w) o[w] = repack_word(c, w);
+#pragma unroll
+        for (int w = 0; w < 8; ++w) qs[8 * j + w] = o[w];
+      }
+    }
+    __syncthreads();
+    uint4 *gd = reinterpret_cast<uint4 *>(dst + b0 * kBlockBytes);
+    for (int i = threadIdx.x; i < nbk * 9; i += kRepackBlocks) gd[i] = sv[i];
+    __syncthreads();
+  }
+}
+
 // ---- generators -------------------------------------------------------------
 
 // block b of a generated tensor, written to o (144 bytes, 16-byte aligned)
@@ -269,6 +327,24 @@ extern "C" int mlm_q4k_dequant_f16(mlm_ctx *ctx, const void *blocks, void *out, 
 
 extern "C" int mlm_q4k_dequant_bf16(mlm_ctx *ctx, const void *blocks, void *out, uint64_t n) {
   return launch_dequant<kOutBF16>(ctx, blocks, out, n, "mlm_q4k_dequant_bf16");
+}
+
+extern "C" int mlm_q4k_repack_canonical(mlm_ctx *ctx, const void *src, void *dst,
+                                        uint64_t nblocks) {
+  MLM_CHECK_CTX(ctx);
+  if (nblocks == 0) return MLM_OK;
+  MLM_REQUIRE(ctx, src && dst, MLM_ERR_ARG, "mlm_q4k_repack_canonical: null buffer");
+  MLM_REQUIRE(ctx, aligned16(src) && aligned16(dst), MLM_ERR_ALIGN,
+              "mlm_q4k_repack_canonical: buffers must be 16-byte aligned");
+  const char *s0 = reinterpret_cast<const char *>(src), *d0 = reinterpret_cast<const char *>(dst);
+  const size_t bytes = (size_t)nblocks * kBlockBytes;
+  MLM_REQUIRE(ctx, s0 == d0 || s0 + bytes <= d0 || d0 + bytes <= s0, MLM_ERR_ARG,
+              "mlm_q4k_repack_canonical: src and dst overlap without being equal");
+  const uint64_t groups = (nblocks + kRepackBlocks - 1) / kRepackBlocks;
+  const unsigned grid = (unsigned)std::min<uint64_t>(groups, (uint64_t)ctx->sm_count * 8);
+  q4k_repack_kernel<<<grid, kRepackBlocks, 0, ctx->stream>>>(
+      reinterpret_cast<const uint8_t *>(src), reinterpret_cast<uint8_t *>(dst), nblocks);
+  return check_launch(ctx, "mlm_q4k_repack_canonical");
 }
 
 extern "C" int mlm_gen_q4k(mlm_ctx *ctx, uint64_t seed, uint64_t stream, uint64_t first_block,

@@ -27,6 +27,7 @@ _ref: Optional[ctypes.CDLL] = None
 
 QK_K = 256
 BLOCK_BYTES = 144
+Q6K_BLOCK_BYTES = 210
 
 c_u64 = ctypes.c_uint64
 c_vp = ctypes.c_void_p
@@ -62,6 +63,11 @@ def lib() -> ctypes.CDLL:
         L.orc_attn_decode.argtypes = [c_vp, c_vp, c_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                       ctypes.c_int, c_vp, ctypes.c_int]
         L.orc_silu_mul.argtypes = [c_vp, c_vp, c_vp, ctypes.c_int]
+        L.orc_q4k_dequant_canonical_f32.argtypes = [c_vp, c_u64, c_vp]
+        L.orc_q4k_canonical_to_interleaved.argtypes = [c_vp, c_vp, c_u64]
+        L.orc_gen_q6k.argtypes = [c_u64, c_u64, c_u64, c_u64, c_vp]
+        L.orc_q6k_dequant_f32.argtypes = [c_vp, c_u64, c_vp, ctypes.c_int]
+        L.orc_q6k_matvec.argtypes = [c_vp, ctypes.c_int, ctypes.c_int, c_vp, c_vp, ctypes.c_int]
         _lib = L
     return _lib
 
@@ -87,6 +93,7 @@ def ref_lib() -> Optional[ctypes.CDLL]:
         R.ref_repeat_kv_f16.argtypes = [c_vp, c_vp, ctypes.c_uint32, ctypes.c_uint32,
                                         ctypes.c_uint32, ctypes.c_uint32]
         R.ref_threads_available.restype = ctypes.c_int
+        R.ref_q6k_dequant_f32.argtypes = [c_vp, c_vp, c_u64, ctypes.c_int]
         _ref = R
     return _ref
 
@@ -98,6 +105,12 @@ def ref_lib() -> Optional[ctypes.CDLL]:
 def gen_q4k(seed: int, stream: int, nblocks: int, first_block: int = 0) -> np.ndarray:
     out = np.empty(nblocks * BLOCK_BYTES, dtype=np.uint8)
     lib().orc_gen_q4k(seed, stream, first_block, nblocks, _p(out))
+    return out
+
+
+def gen_q6k(seed: int, stream: int, nblocks: int, first_block: int = 0) -> np.ndarray:
+    out = np.empty(nblocks * Q6K_BLOCK_BYTES, dtype=np.uint8)
+    lib().orc_gen_q6k(seed, stream, first_block, nblocks, _p(out))
     return out
 
 
@@ -123,6 +136,33 @@ def q4k_dequant_f32(blocks: np.ndarray, n: int, nthreads: int = 0) -> np.ndarray
     out = np.empty(n, dtype=np.float32)
     lib().orc_q4k_dequant_f32(_p(blocks), n, _p(out), nthreads)
     return out
+
+
+def q4k_dequant_canonical_f32(blocks: np.ndarray, n: int) -> np.ndarray:
+    """Dequant of Q4_K blocks in the GGUF element order (q4k_oracle.h)."""
+    out = np.empty(n, dtype=np.float32)
+    lib().orc_q4k_dequant_canonical_f32(_p(blocks), n, _p(out))
+    return out
+
+
+def q4k_canonical_to_interleaved(blocks: np.ndarray) -> np.ndarray:
+    out = np.empty_like(blocks)
+    lib().orc_q4k_canonical_to_interleaved(_p(blocks), _p(out), blocks.size // BLOCK_BYTES)
+    return out
+
+
+def q6k_dequant_f32(blocks: np.ndarray, n: int, nthreads: int = 0) -> np.ndarray:
+    out = np.empty(n, dtype=np.float32)
+    lib().orc_q6k_dequant_f32(_p(blocks), n, _p(out), nthreads)
+    return out
+
+
+def q6k_matvec(W: np.ndarray, rows: int, cols: int, x_f16: np.ndarray,
+               nthreads: int = 0) -> np.ndarray:
+    y = np.empty(rows, dtype=np.float32)
+    x = np.ascontiguousarray(x_f16, dtype=np.float16)
+    lib().orc_q6k_matvec(_p(W), rows, cols, _p(x), _p(y), nthreads)
+    return y
 
 
 def q4k_dequant_f16(blocks: np.ndarray, n: int, nthreads: int = 0) -> np.ndarray:
@@ -222,6 +262,13 @@ def ref_q4k_dequant_f32(blocks: np.ndarray, n: int, nthreads: int = 1) -> np.nda
     R = ref_lib()
     out = np.empty(n, dtype=np.float32)
     R.ref_q4k_dequant_f32(_p(blocks), _p(out), n, nthreads)
+    return out
+
+
+def ref_q6k_dequant_f32(blocks: np.ndarray, n: int, nthreads: int = 1) -> np.ndarray:
+    R = ref_lib()
+    out = np.empty(n, dtype=np.float32)
+    R.ref_q6k_dequant_f32(_p(blocks), _p(out), n, nthreads)
     return out
 
 

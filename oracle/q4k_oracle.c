@@ -418,3 +418,122 @@ void orc_silu_mul(const float *g, const float *u, float *out, int n) {
     out[i] = (float)(x / (1.0 + exp(-x)) * (double)u[i]);
   }
 }
+
+/* ------------------------------------------------------------------------ */
+/* Q4_K in the GGUF element order                                           */
+/* ------------------------------------------------------------------------ */
+
+/* the quant of element i (0..255) of a block in the GGUF order: 64-element
+ * group j = i/64 owns qs[32j .. 32j+31]; its first 32 elements are the low
+ * nibbles, the last 32 the high nibbles */
+static inline uint8_t canon_q(const uint8_t *qs, unsigned i) {
+  unsigned j = i / 64, l = i % 64;
+  return l < 32 ? (uint8_t)(qs[32 * j + l] & 0xF) : (uint8_t)(qs[32 * j + l - 32] >> 4);
+}
+
+void orc_q4k_dequant_canonical_f32(const void *blocks, uint64_t n, float *out) {
+  const uint8_t *src = (const uint8_t *)blocks;
+  for (uint64_t e = 0; e < n; ++e) {
+    const uint8_t *blk = src + (e / ORC_QK_K) * ORC_Q4K_BLOCK_BYTES;
+    unsigned i = (unsigned)(e % ORC_QK_K);
+    uint16_t hd, hm;
+    memcpy(&hd, blk, 2);
+    memcpy(&hm, blk + 2, 2);
+    uint8_t sc, m;
+    orc_q4k_scale_min((int)(i / 32), blk + 4, &sc, &m);
+    float final_scale = orc_half_to_float(hd) * (float)sc;
+    float final_min = orc_half_to_float(hm) * (float)m;
+    out[e] = final_scale * (float)canon_q(blk + 16, i) - final_min;
+  }
+}
+
+void orc_q4k_canonical_to_interleaved(const void *src, void *dst, uint64_t nblocks) {
+  const uint8_t *s = (const uint8_t *)src;
+  uint8_t *d = (uint8_t *)dst;
+  for (uint64_t b = 0; b < nblocks; ++b) {
+    uint8_t blk[ORC_Q4K_BLOCK_BYTES];
+    memcpy(blk, s + b * ORC_Q4K_BLOCK_BYTES, ORC_Q4K_BLOCK_BYTES);
+    uint8_t *o = d + b * ORC_Q4K_BLOCK_BYTES;
+    memcpy(o, blk, 16);
+    /* interleaved: element i in byte i/2, low nibble for even i */
+    for (unsigned k = 0; k < 128; ++k)
+      o[16 + k] = (uint8_t)(canon_q(blk + 16, 2 * k) | (canon_q(blk + 16, 2 * k + 1) << 4));
+  }
+}
+
+/* ------------------------------------------------------------------------ */
+/* Q6_K                                                                     */
+/* ------------------------------------------------------------------------ */
+
+#define ORC_TAG_Q6K 0x66ULL
+
+void orc_gen_q6k(uint64_t seed, uint64_t stream, uint64_t first_block,
+                 uint64_t nblocks, void *out) {
+  uint8_t *o = (uint8_t *)out;
+#pragma omp parallel for schedule(static)
+  for (int64_t bi = 0; bi < (int64_t)nblocks; ++bi) {
+    uint64_t b = first_block + (uint64_t)bi;
+    uint8_t *blk = o + (uint64_t)bi * ORC_Q6K_BLOCK_BYTES;
+    /* 26 words = 208 bytes of ql, qh and scales */
+    for (int k = 0; k < 26; ++k) {
+      uint64_t r = orc_rng_u64(seed, stream ^ (ORC_TAG_Q6K << 56), b * 26 + (uint64_t)k);
+      memcpy(blk + 8 * k, &r, 8);
+    }
+    float d = (float)fabs(orc_normal(seed, stream ^ (ORC_TAG_Q6K << 56), b));
+    uint16_t hd = orc_float_to_half(d * 0.01f);
+    memcpy(blk + 208, &hd, 2);
+  }
+}
+
+/* kernel_dequantize_q6_K_f32, DequantKernels.metal:131-172: element e of a
+ * block, half h = e/128, t = e%128, l = t%32, quarter k = t/32; the 6-bit
+ * quant is a nibble of ql (ql[64h + l] for k = 0, 2, ql[64h + l + 32] for
+ * k = 1, 3; low nibble for k < 2) with bits 2k..2k+1 of qh[32h + l] above
+ * it, minus 32; out = (d * scales[8h + l/16 + 2k]) * q in fp32. */
+static inline float q6k_elem(const uint8_t *blk, unsigned e) {
+  const uint8_t *ql = blk + 64 * (e / 128);
+  const uint8_t *qh = blk + 128 + 32 * (e / 128);
+  const int8_t *sc = (const int8_t *)(blk + 192) + 8 * (e / 128);
+  uint16_t hd;
+  memcpy(&hd, blk + 208, 2);
+  float d = orc_half_to_float(hd);
+  unsigned t = e % 128, l = t % 32, k = t / 32;
+  int is = (int)(l / 16);
+  uint8_t lo = (k == 0 || k == 2) ? ql[l] : ql[l + 32];
+  lo = (k < 2) ? (uint8_t)(lo & 0xF) : (uint8_t)(lo >> 4);
+  int q = (int)(int8_t)(uint8_t)(lo | (((qh[l] >> (2 * k)) & 3) << 4)) - 32;
+  return d * (float)sc[is + 2 * (int)k] * (float)q;
+}
+
+void orc_q6k_dequant_f32(const void *blocks, uint64_t n, float *out, int nthreads) {
+  const uint8_t *src = (const uint8_t *)blocks;
+#ifdef _OPENMP
+  if (nthreads <= 0) nthreads = omp_get_max_threads();
+#endif
+#pragma omp parallel for schedule(static) num_threads(nthreads > 0 ? nthreads : 1)
+  for (int64_t e = 0; e < (int64_t)n; ++e)
+    out[e] = q6k_elem(src + (uint64_t)(e / ORC_QK_K) * ORC_Q6K_BLOCK_BYTES,
+                      (unsigned)(e % ORC_QK_K));
+}
+
+void orc_q6k_matvec(const void *W, int rows, int cols, const uint16_t *x_f16,
+                    float *y, int nthreads) {
+  const uint8_t *src = (const uint8_t *)W;
+  int nb = cols / ORC_QK_K;
+  float *xf = (float *)malloc(sizeof(float) * (size_t)cols);
+  for (int k = 0; k < cols; ++k) xf[k] = orc_half_to_float(x_f16[k]);
+#ifdef _OPENMP
+  if (nthreads <= 0) nthreads = omp_get_max_threads();
+#endif
+#pragma omp parallel for schedule(static) num_threads(nthreads > 0 ? nthreads : 1)
+  for (int r = 0; r < rows; ++r) {
+    double a = 0.0;
+    for (int b = 0; b < nb; ++b) {
+      const uint8_t *blk = src + ((size_t)r * nb + b) * ORC_Q6K_BLOCK_BYTES;
+      for (unsigned i = 0; i < ORC_QK_K; ++i)
+        a += (double)q6k_elem(blk, i) * (double)xf[(size_t)b * ORC_QK_K + i];
+    }
+    y[r] = (float)a;
+  }
+  free(xf);
+}

@@ -20,6 +20,17 @@
  *                         of MetalLM/Backend/Metal/AttentionKernels.metal:43
  *   orc_silu_mul          MetalLM/Backend/Metal/ActivationKernels.metal:6-27 and
  *                         ElementwiseKernels.metal (kernel_mul_f16)
+ *   orc_q6k_dequant_f32   MetalLM/Backend/Metal/DequantKernels.metal:131-172
+ *                         (kernel_dequantize_q6_K_f32, block_q6_K :29-34)
+ *   orc_q6k_matvec        the Q6_K tensors of ModelLoader.swift:282-287 in a
+ *                         linear: fp32 dequant, then the dot product
+ *   orc_q4k_dequant_canonical_f32 / orc_q4k_canonical_to_interleaved
+ *                         the GGUF (ggml, llama.cpp) Q4_K element order, which
+ *                         the reference does not vendor: element 64j + l of a
+ *                         super-block is the low nibble of qs[32j + l] for
+ *                         l < 32 and the high nibble of qs[32j + l - 32]
+ *                         otherwise; scales, mins and the arithmetic are those
+ *                         of DequantKernels.metal:43-92
  *
  * The seeded generators (orc_gen_*) use integer-exact hashing plus IEEE
  * add/mul only, so the CUDA generators produce identical bytes.
@@ -65,6 +76,20 @@ void orc_q4k_matvec(const void *W, int rows, int cols, const uint16_t *x_f16,
 /* same with fp32 x (used by the layer composition) */
 void orc_q4k_matvec_f32x(const void *W, int rows, int cols, const float *x,
                          float *y, int nthreads);
+/* GGUF element order: dequant, and the byte shuffle to the interleaved order
+ * (scales and the two fp16 words are the same in both) */
+void orc_q4k_dequant_canonical_f32(const void *blocks, uint64_t n, float *out);
+void orc_q4k_canonical_to_interleaved(const void *src, void *dst, uint64_t nblocks);
+
+/* ---- Q6_K (210-byte blocks: ql[128], qh[64], int8 scales[16], fp16 d) --- */
+#define ORC_Q6K_BLOCK_BYTES 210
+/* d = fp16(|N(0,1)| * 0.01); the 208 bytes of ql, qh and scales uniform */
+void orc_gen_q6k(uint64_t seed, uint64_t stream, uint64_t first_block,
+                 uint64_t nblocks, void *out);
+void orc_q6k_dequant_f32(const void *blocks, uint64_t n, float *out, int nthreads);
+/* y[r] = sum_k deq(W[r][k]) * x[k], x fp16, fp64 accumulation */
+void orc_q6k_matvec(const void *W, int rows, int cols, const uint16_t *x_f16,
+                    float *y, int nthreads);
 
 /* ---- norms / rope / attention ------------------------------------------- */
 void orc_rmsnorm_f16(const uint16_t *x, const uint16_t *w, uint16_t *y,

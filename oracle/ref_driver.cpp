@@ -42,6 +42,17 @@ void ref_q4k_dequant_f16(const void *blocks, uint16_t *out, uint64_t n, int nthr
     kernel_dequantize_q4_K_f16(src, (half *)out, ne, (uint)gid);
 }
 
+/* Q6_K -> fp32 with the reference's kernel (dispatch: one thread per
+ * element, MetalService.swift:370-374) */
+void ref_q6k_dequant_f32(const void *blocks, float *out, uint64_t n, int nthreads) {
+  uint64_t ne = n;
+  const block_q6_K *src = (const block_q6_K *)blocks;
+  static_assert(sizeof(block_q6_K) == 210, "block_q6_K is 210 bytes");
+#pragma omp parallel for schedule(static) num_threads(nthreads > 0 ? nthreads : 1)
+  for (int64_t gid = 0; gid < (int64_t)n; ++gid)
+    kernel_dequantize_q6_K_f32(src, out, ne, (uint)gid);
+}
+
 /* y = W x: each row dequantized by the reference kernel, then an fp32 dot
  * product (the reference feeds the dequantized weights to MPS). */
 void ref_q4k_matvec(const void *W, int rows, int cols, const uint16_t *x_f16,

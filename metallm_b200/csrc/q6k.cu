@@ -20,6 +20,7 @@
 
 #include "mlm_device.cuh"
 #include "mlm_internal.h"
+#include "q4k_gemv_common.cuh"
 
 namespace mlm {
 
@@ -98,24 +99,38 @@ __global__ void __launch_bounds__(256) q6k_dequant_kernel(const uint8_t *__restr
 
 // ---- decode GEMV ------------------------------------------------------------------
 //
-// y[r] = sum_k deq(W[r][k]) x[k] (+ residual[r]), x fp16, fp32 accumulation.
-// Each warp owns rows r = gw, gw + nw, ...; its weights stream through a
-// per-warp ring of shared-memory stages, one stage per 8-block chunk of a
-// row (1,680 bytes = 105 x 16, 16-byte aligned when a row holds a multiple
-// of 8 blocks), copied with coalesced 16-byte cp.async and continuing across
-// row boundaries.  Lane (k = lane / 8, g = lane % 8) takes the four elements
-// 32k + 4g .. 32k + 4g + 3 of each half of every block: one 32-bit word of
-// ql and one of qh give the four 6-bit quants, a byte permute puts each under
-// the exponent of 2^23, and one subtraction of 2^23 + 32 gives q - 32
-// exactly; the four products with x are exact in fp32 and the block's
-// d * scale (exact, 19 bits) multiplies their sum.  x is staged once per CTA
-// in shared memory as fp32.
-constexpr int kQ6Warps = 8;
+// y[r] = sum_k deq(W[r][k]) x[k] (+ residual[r]), x fp16, fp32 accumulation,
+// on the tensor cores the way the Q4_K GEMV uses them: a 6-bit quant placed
+// under the fp16 exponent of 1024 (a byte permute) minus 1056 is q - 32
+// exactly, so the quants are exact fp16 operands of mma.sync.m16n8k16 and
+// their products with x are exact in the fp32 accumulators.
+//
+// MMA mapping: thread (g = lane / 4, t = lane % 4) holds, for rows g and g+8
+// of a 16-row tile, quarter k = t of each 128-element half of a block:
+// elements 32t + l (l = 0..31), i.e. the scale groups 2t (l < 16) and 2t + 1
+// (l >= 16) of the half.  One 32-bit word of ql and one of qh give four
+// consecutive quants; per word one MMA takes (l0, l1) and (l2, l3) as its
+// k-slots 2t, 2t+1 and 2t+8, 2t+9.  B column n carries x only for the
+// threads whose word belongs to scale group n (the others read zeros), so
+// after the 8 words of a half C[row][2t] and C[row][2t+1] hold the sums of
+// q * x of groups 2t and 2t+1 -- in the thread that holds their scales; the
+// epilogue multiplies them by d * scale and accumulates per row.
+//
+// Work: a CTA takes 16-row tiles; per tile it stages 8-block chunks of the
+// 16 rows (26,880 bytes, coalesced 16-byte cp.async, a 3-stage ring shared
+// by the CTA) and warp w takes block column w of each chunk.  Blocks sit at
+// 2-byte alignment (210 bytes each), so a thread loads the 9 aligned words
+// around its 8 and funnel-shifts them.  At the end of a tile the warps' row
+// sums are added in warp order (deterministic) and y is stored.
+constexpr int kQ6TileRows = 16;
+constexpr int kQ6Warps = 8;  // one block column of a chunk per warp
 constexpr int kQ6Threads = kQ6Warps * 32;
-constexpr int kQ6ChunkBlocks = 8;
-constexpr int kQ6ChunkBytes = kQ6ChunkBlocks * kQ6Bytes;  // 1680
-constexpr int kQ6Stages = 4;
-constexpr int kQ6StageSmem = kQ6Warps * kQ6Stages * kQ6ChunkBytes;  // 53,760
+constexpr int kQ6ChunkBlocks = kQ6Warps;
+constexpr int kQ6RowChunk = kQ6ChunkBlocks * kQ6Bytes;       // 1680 = 105 x 16
+constexpr int kQ6StageBytes = kQ6TileRows * kQ6RowChunk;     // 26,880
+constexpr int kQ6Stages = 3;
+constexpr int kQ6ZeroBytes = 512;  // zeros read by the inactive B columns
+constexpr int kQ6FixedSmem = kQ6ZeroBytes + kQ6Stages * kQ6StageBytes + kQ6Warps * kQ6TileRows * 4;
 constexpr int kQ6MaxCols = 32768;
 
 struct Q6GemvArgs {
@@ -123,38 +138,67 @@ struct Q6GemvArgs {
   const __half *x;
   float *y;
   const float *residual;
-  int rows, nb, nchunk;
+  int rows, nb, nchunk, tiles;
 };
 
 __device__ __forceinline__ void q6_cp_async16(uint32_t dst, const void *src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
 
-// a 32-bit word at a 2-byte-aligned shared-memory address
-__device__ __forceinline__ uint32_t ld_u32_a2(const uint8_t *p) {
-  const uint16_t *h = reinterpret_cast<const uint16_t *>(p);
-  return (uint32_t)h[0] | ((uint32_t)h[1] << 16);
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+
+// the 8 words at the 2-byte-aligned shared address a: 9 aligned loads,
+// funnel-shifted by 0 or 16 bits
+__device__ __forceinline__ void lds8_a2(uint32_t a, uint32_t (&w)[8]) {
+  const uint32_t base = a & ~3u, sh = (a & 2u) * 8u;
+  uint32_t r[9];
+#pragma unroll
+  for (int i = 0; i < 9; ++i) r[i] = lds32(base + 4 * i);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) w[i] = __funnelshift_r(r[i], r[i + 1], sh);
+}
+
+// four 6-bit quants (bytes of q4) -> two fp16x2 of q - 32
+__device__ __forceinline__ void q6_to_f16x2(uint32_t q4, uint32_t &lo, uint32_t &hi) {
+  const uint32_t kBias = 0xE420E420u;  // fp16 -1056 in both halves
+  uint32_t a = __byte_perm(q4, 0x64646464u, 0x4140), b = __byte_perm(q4, 0x64646464u, 0x4342);
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(lo) : "r"(a), "r"(kBias));
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(hi) : "r"(b), "r"(kBias));
 }
 
 __global__ void __launch_bounds__(kQ6Threads, 2) q6k_gemv_kernel(Q6GemvArgs p) {
   extern __shared__ __align__(16) uint8_t smem[];
-  float *xs = reinterpret_cast<float *>(smem);  // [nb * 256]
+  const int cols = p.nb * kQK;
+  uint8_t *xs = smem;                                   // fp16 x [cols]
+  uint8_t *zero = xs + (size_t)cols * 2;                // kQ6ZeroBytes
+  uint8_t *stages = zero + kQ6ZeroBytes;                // kQ6Stages x [16][1680]
+  float *red = reinterpret_cast<float *>(stages + kQ6Stages * kQ6StageBytes);  // [8][16]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  uint8_t *my = smem + (size_t)p.nb * kQK * 4 + (size_t)warp * kQ6Stages * kQ6ChunkBytes;
-  const uint32_t my_s = (uint32_t)__cvta_generic_to_shared(my);
+  const int g = lane >> 2, t = lane & 3;
+  const uint32_t stages_s = (uint32_t)__cvta_generic_to_shared(stages);
 
-  const int gw = blockIdx.x * kQ6Warps + warp, nw = gridDim.x * kQ6Warps;
-  const int my_rows = gw < p.rows ? (p.rows - 1 - gw) / nw + 1 : 0;
-  const int total = my_rows * p.nchunk;  // this warp's chunks, row-major
+  const int my_tiles = (int)blockIdx.x < p.tiles ? (p.tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int total = my_tiles * p.nchunk;
 
-  // chunk q of the sequence into stage q % kQ6Stages; always one commit group
+  // unit q (tile blockIdx.x + (q / nchunk) gridDim.x, chunk q % nchunk) into
+  // stage q % kQ6Stages; always one commit group
   auto issue = [&](int q) {
     if (q < total) {
-      const int ri = q / p.nchunk, c = q - ri * p.nchunk;
-      const size_t r = (size_t)gw + (size_t)ri * nw;
-      const uint8_t *src = p.W + (r * p.nb + (size_t)c * kQ6ChunkBlocks) * kQ6Bytes;
-      const uint32_t dst = my_s + (uint32_t)(q % kQ6Stages) * kQ6ChunkBytes;
-      for (int k = lane; k < kQ6ChunkBytes / 16; k += 32) q6_cp_async16(dst + 16 * k, src + 16 * k);
+      const int ti = q / p.nchunk, c = q - ti * p.nchunk;
+      const int r0 = ((int)blockIdx.x + ti * (int)gridDim.x) * kQ6TileRows;
+      const uint32_t dst0 = stages_s + (uint32_t)(q % kQ6Stages) * kQ6StageBytes;
+      for (int i = threadIdx.x; i < kQ6TileRows * (kQ6RowChunk / 16); i += kQ6Threads) {
+        const int rr = i / (kQ6RowChunk / 16), k = i - rr * (kQ6RowChunk / 16);
+        if (r0 + rr < p.rows) {
+          const uint8_t *src =
+              p.W + ((size_t)(r0 + rr) * p.nb + (size_t)c * kQ6ChunkBlocks) * kQ6Bytes + 16 * k;
+          q6_cp_async16(dst0 + rr * kQ6RowChunk + 16 * k, src);
+        }
+      }
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
@@ -162,75 +206,93 @@ __global__ void __launch_bounds__(kQ6Threads, 2) q6k_gemv_kernel(Q6GemvArgs p) {
 #pragma unroll
   for (int q = 0; q < kQ6Stages - 1; ++q) issue(q);
   pdl_wait_then_release();
-
   {
     const uint4 *xg = reinterpret_cast<const uint4 *>(p.x);
-    float4 *xo = reinterpret_cast<float4 *>(xs);
-    for (int i = threadIdx.x; i < p.nb * 32; i += kQ6Threads) {
-      const uint4 v = __ldg(xg + i);
-      const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&v.x));
-      const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&v.y));
-      const float2 c = __half22float2(*reinterpret_cast<const __half2 *>(&v.z));
-      const float2 e = __half22float2(*reinterpret_cast<const __half2 *>(&v.w));
-      xo[2 * i] = make_float4(a.x, a.y, b.x, b.y);
-      xo[2 * i + 1] = make_float4(c.x, c.y, e.x, e.y);
-    }
+    uint4 *xo = reinterpret_cast<uint4 *>(xs);
+    for (int i = threadIdx.x; i < cols / 8; i += kQ6Threads) xo[i] = __ldg(xg + i);
+    for (int i = threadIdx.x; i < kQ6ZeroBytes / 16; i += kQ6Threads)
+      reinterpret_cast<uint4 *>(zero)[i] = make_uint4(0, 0, 0, 0);
   }
-  __syncthreads();
 
-  const int k = lane >> 3, g = lane & 7;
-  const int ql_off = 32 * (k & 1) + 4 * g;  // + 64 h
-  const int qh_off = 128 + 4 * g;           // + 32 h
-  const int sc_off = 192 + 2 * k + (g >> 2);  // + 8 h
-  const int sh_lo = (k >= 2) ? 4 : 0;
-  const int x_off = 32 * k + 4 * g;  // + 128 h
-  const float kMagic = 8388640.0f;   // 2^23 + 32
-  float acc = 0.f;
+  // B operands: words 0..3 of a half belong to group 2t (column 2t), words
+  // 4..7 to group 2t + 1; thread (g, t) supplies x of its words when g is
+  // that column, zeros otherwise
+  const bool lo_on = g == 2 * t, hi_on = g == 2 * t + 1;
+  const uint32_t xs_s = (uint32_t)__cvta_generic_to_shared(xs) + 64 * t;  // element 32t
+  const uint32_t zero_s = (uint32_t)__cvta_generic_to_shared(zero);
+  const int sh_lo = t >= 2 ? 4 : 0;  // high nibbles for quarters 2, 3
+  const int ql_off = 32 * (t & 1);
+
+  float acc[2] = {0.f, 0.f};  // rows g, g + 8 of the tile
   for (int q = 0; q < total; ++q) {
+    asm volatile("cp.async.wait_group %0;" ::"n"(kQ6Stages - 2) : "memory");
+    __syncthreads();  // unit q landed for every thread; stage (q - 1) is free
     issue(q + kQ6Stages - 1);
-    asm volatile("cp.async.wait_group %0;" ::"n"(kQ6Stages - 1) : "memory");
-    __syncwarp();
-    const uint8_t *st = my + (q % kQ6Stages) * kQ6ChunkBytes;
-    const int ri = q / p.nchunk, c = q - ri * p.nchunk;
-    const float *xc = xs + (size_t)c * kQ6ChunkBlocks * kQK;
-#pragma unroll 2
-    for (int bi = 0; bi < kQ6ChunkBlocks; ++bi) {
-      const uint8_t *blk = st + bi * kQ6Bytes;
-      const float d =
-          __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t *>(blk + 208)));
+    const int ti = q / p.nchunk, c = q - ti * p.nchunk;
+    const uint32_t st = stages_s + (uint32_t)(q % kQ6Stages) * kQ6StageBytes;
+    const uint32_t blk_g = st + g * kQ6RowChunk + warp * kQ6Bytes;
+    const uint32_t blk_g8 = blk_g + 8 * kQ6RowChunk;
+    const uint32_t xblk = (uint32_t)(c * kQ6ChunkBlocks + warp) * (kQK * 2);  // byte offset of the block's x
+    const uint32_t xlo = lo_on ? xs_s + xblk : zero_s;
+    const uint32_t xhi = hi_on ? xs_s + xblk : zero_s;
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint32_t qlw = ld_u32_a2(blk + 64 * h + ql_off);
-        const uint32_t qhw = ld_u32_a2(blk + qh_off + 32 * h);
-        // bits 2k, 2k+1 of each qh byte to bits 4, 5; the nibble below
-        const uint32_t q4 = ((qlw >> sh_lo) & 0x0F0F0F0Fu) | (((qhw >> (2 * k)) << 4) & 0x30303030u);
-        const float4 xv = *reinterpret_cast<const float4 *>(xc + bi * kQK + 128 * h + x_off);
-        const float f0 = __int_as_float(__byte_perm(q4, 0x4B000000u, 0x7440)) - kMagic;
-        const float f1 = __int_as_float(__byte_perm(q4, 0x4B000000u, 0x7441)) - kMagic;
-        const float f2 = __int_as_float(__byte_perm(q4, 0x4B000000u, 0x7442)) - kMagic;
-        const float f3 = __int_as_float(__byte_perm(q4, 0x4B000000u, 0x7443)) - kMagic;
-        float s = f0 * xv.x;
-        s = fmaf(f1, xv.y, s);
-        s = fmaf(f2, xv.z, s);
-        s = fmaf(f3, xv.w, s);
-        const float ds = d * (float)(int8_t)blk[sc_off + 8 * h];
-        acc = fmaf(ds, s, acc);
+    for (int h = 0; h < 2; ++h) {
+      uint32_t qlg[8], qhg[8], ql8[8], qh8[8];
+      lds8_a2(blk_g + 64 * h + ql_off, qlg);
+      lds8_a2(blk_g + 128 + 32 * h, qhg);
+      lds8_a2(blk_g8 + 64 * h + ql_off, ql8);
+      lds8_a2(blk_g8 + 128 + 32 * h, qh8);
+      float cacc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        const uint32_t q4g = ((qlg[w] >> sh_lo) & 0x0F0F0F0Fu) | (((qhg[w] >> (2 * t)) << 4) & 0x30303030u);
+        const uint32_t q48 = ((ql8[w] >> sh_lo) & 0x0F0F0F0Fu) | (((qh8[w] >> (2 * t)) << 4) & 0x30303030u);
+        uint32_t a0, a2, a1, a3;
+        q6_to_f16x2(q4g, a0, a2);
+        q6_to_f16x2(q48, a1, a3);
+        // x of elements 128h + 32t + 4w .. +3 of this block (zeros when inactive)
+        const uint32_t xa = (w < 4 ? xlo : xhi) + 256 * h + 8 * w;
+        uint32_t b0, b1;
+        asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(b0), "=r"(b1) : "r"(xa));
+        mma_f16_16816(cacc, a0, a1, a2, a3, b0, b1);
       }
+      // scales of groups 8h + 2t, 8h + 2t + 1 and d of rows g and g + 8
+      const uint32_t scg = lds32((blk_g + 192 + 8 * h + 2 * t) & ~3u) >> (((blk_g + 2 * t) & 2u) * 8u);
+      const uint32_t sc8 = lds32((blk_g8 + 192 + 8 * h + 2 * t) & ~3u) >> (((blk_g8 + 2 * t) & 2u) * 8u);
+      const uint32_t dg = lds32((blk_g + 208) & ~3u) >> (((blk_g + 208) & 2u) * 8u);
+      const uint32_t d8 = lds32((blk_g8 + 208) & ~3u) >> (((blk_g8 + 208) & 2u) * 8u);
+      const float fdg = half_bits_to_float(dg & 0xFFFFu), fd8 = half_bits_to_float(d8 & 0xFFFFu);
+      acc[0] = fmaf(fdg * (float)(int8_t)(scg & 0xFF), cacc[0], acc[0]);
+      acc[0] = fmaf(fdg * (float)(int8_t)((scg >> 8) & 0xFF), cacc[1], acc[0]);
+      acc[1] = fmaf(fd8 * (float)(int8_t)(sc8 & 0xFF), cacc[2], acc[1]);
+      acc[1] = fmaf(fd8 * (float)(int8_t)((sc8 >> 8) & 0xFF), cacc[3], acc[1]);
     }
-    __syncwarp();  // the stage is read before the next issue overwrites it
-    if (c == p.nchunk - 1) {
-      acc = warp_sum(acc);
-      if (lane == 0) {
-        const size_t r = (size_t)gw + (size_t)ri * nw;
-        p.y[r] = acc + (p.residual ? p.residual[r] : 0.f);
+    if (c == p.nchunk - 1) {  // the tile's last chunk: add the warps' rows, store y
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], 1);
+        acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], 2);
       }
-      acc = 0.f;
+      if (t == 0) {
+        red[warp * kQ6TileRows + g] = acc[0];
+        red[warp * kQ6TileRows + g + 8] = acc[1];
+      }
+      acc[0] = acc[1] = 0.f;
+      __syncthreads();
+      const int r0 = ((int)blockIdx.x + ti * (int)gridDim.x) * kQ6TileRows;
+      if (threadIdx.x < kQ6TileRows && r0 + (int)threadIdx.x < p.rows) {
+        float s = red[threadIdx.x];
+#pragma unroll
+        for (int w = 1; w < kQ6Warps; ++w) s += red[w * kQ6TileRows + threadIdx.x];
+        const int r = r0 + threadIdx.x;
+        p.y[r] = s + (p.residual ? p.residual[r] : 0.f);
+      }
     }
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
-size_t q6k_gemv_smem(int cols) { return (size_t)cols * 4 + kQ6StageSmem; }
+size_t q6k_gemv_smem(int cols) { return (size_t)cols * 2 + kQ6FixedSmem; }
 
 int q6k_init(mlm_ctx *ctx) {
   MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(q6k_gemv_kernel,
@@ -308,7 +370,8 @@ extern "C" int mlm_q6k_gemv(mlm_ctx *ctx, const void *W, int rows, int cols, con
   a.rows = rows;
   a.nb = cols / kQK;
   a.nchunk = a.nb / kQ6ChunkBlocks;
-  const int ctas = std::max(1, std::min((rows + kQ6Warps - 1) / kQ6Warps, 2 * ctx->sm_count));
+  a.tiles = (rows + kQ6TileRows - 1) / kQ6TileRows;
+  const int ctas = std::max(1, std::min(a.tiles, 2 * ctx->sm_count));
   return check_launch_pdl(ctx,
                           launch_pdl(q6k_gemv_kernel, dim3(ctas), dim3(kQ6Threads),
                                      q6k_gemv_smem(cols), ctx->stream, a),

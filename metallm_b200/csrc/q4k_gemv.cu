@@ -272,32 +272,60 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, MLM_GEMV_MIN_BLOCKS)
       float tot = 0.f;
       for (int w = 0; w < nwarps; ++w) tot += red[w];
       const float scale = rms_scale(tot, ngroups * 8, p.eps);
-      for (int i = threadIdx.x; i < ngroups; i += blockDim.x) {
-        float a[8], w[8];
-        load8(p.xa, i, a);
-        load8(p.xb, i, w);
+      // XU groups' loads in flight per thread before any is used (each
+      // round trip to L2 is paid once per XU groups, not once per group)
+      constexpr int XU = 4;
+      for (int base = threadIdx.x; base < ngroups; base += XU * blockDim.x) {
+        float a[XU][8], w[XU][8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) a[e] = (a[e] * scale) * safe_weight(w[e]);
-        stage(i, pack(a), 1.0f);
+        for (int u = 0; u < XU; ++u) {
+          const int i = base + u * blockDim.x;
+          if (i < ngroups) {
+            load8(p.xa, i, a[u]);
+            load8(p.xb, i, w[u]);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < XU; ++u) {
+          const int i = base + u * blockDim.x;
+          if (i < ngroups) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) a[u][e] = (a[u][e] * scale) * safe_weight(w[u][e]);
+            stage(i, pack(a[u]), 1.0f);
+          }
+        }
       }
     } else {  // kSwiGLU, with a power-of-two scale per sub-block
-      for (int i = threadIdx.x; i < ngroups; i += blockDim.x) {
-        float g[8], u[8];
-        load8(p.xa, i, g);
-        load8(p.xb, i, u);
-        float m = 0.f;
+      constexpr int XU = 4;  // groups' loads in flight per thread, as above
+      for (int base = threadIdx.x; base < ngroups; base += XU * blockDim.x) {
+        float ga[XU][8], ua[XU][8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          g[e] = swiglu(g[e], u[e]);
-          m = fmaxf(m, fabsf(g[e]));
+        for (int v = 0; v < XU; ++v) {
+          const int i = base + v * blockDim.x;
+          if (i < ngroups) {
+            load8(p.xa, i, ga[v]);
+            load8(p.xb, i, ua[v]);
+          }
         }
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-        const int ex = max(0, (int)((__float_as_uint(m) >> 23) & 0xFF) - 127 - 14);
-        const float inv = __uint_as_float((uint32_t)(127 - ex) << 23);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) g[e] *= inv;
-        stage(i, pack(g), __uint_as_float((uint32_t)(127 + ex) << 23));
+        for (int v = 0; v < XU; ++v) {
+          const int i = base + v * blockDim.x;
+          if (i >= ngroups) continue;  // whole warps: ngroups is a multiple of 32
+          float *g = ga[v];
+          float m = 0.f;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            g[e] = swiglu(g[e], ua[v][e]);
+            m = fmaxf(m, fabsf(g[e]));
+          }
+          m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+          m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+          const int ex = max(0, (int)((__float_as_uint(m) >> 23) & 0xFF) - 127 - 14);
+          const float inv = __uint_as_float((uint32_t)(127 - ex) << 23);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) g[e] *= inv;
+          stage(i, pack(ga[v]), __uint_as_float((uint32_t)(127 + ex) << 23));
+        }
       }
     }
   }

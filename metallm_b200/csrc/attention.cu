@@ -7,8 +7,11 @@
 // (LlamaRunner.swift:669-952).  Here one CTA owns one KV head and one chunk
 // of positions and serves all n_heads/n_kv_heads query heads of that KV head,
 // so each K and V row is read from HBM exactly once.  Softmax is fp32 with a
-// running max; each CTA writes (max, sum, unnormalised output) for its chunk
-// and the last CTA of a KV head to finish merges the chunks.
+// running max; each CTA writes (max, sum, unnormalised output) for its chunk.
+// For one sequence the last CTA of a KV head to finish merges the chunks; for
+// a batch a second kernel merges them (one CTA per head and sequence), which
+// measured faster there (the merges of 8 sequences x 8 KV heads otherwise run
+// one per CTA at the kernel's tail).
 #include "mlm_device.cuh"
 #include "mlm_internal.h"
 
@@ -29,7 +32,7 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
 
-template <int G, class OutT>
+template <int G, class OutT, bool kMerge>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_partial_kernel(
     const __half *__restrict__ q, const __half *__restrict__ kc, const __half *__restrict__ vc,
     int n_heads, int n_kv, int seq_len, int chunk_len, float scale,
@@ -168,6 +171,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_partial_kernel(
     }
   }
 
+  if (!kMerge) return;  // attn_decode_merge_kernel combines the chunks
+
   // The last chunk of this (sequence, KV head) to finish merges the chunks
   // of its G query heads, in chunk order; it re-zeroes the arrival counter
   // for the next launch.
@@ -228,6 +233,32 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_partial_kernel(
     out[(size_t)(kvh * G + gh) * kAttnD + dd] = from_float<OutT>(O[gh] / s_L[gh]);
 }
 
+// chunk merge of a batch: one CTA per (head, sequence), thread dd = output
+// dimension dd; the chunks in order
+template <class OutT>
+__global__ void attn_decode_merge_kernel(const float *__restrict__ partials, int n_heads,
+                                         int nchunks, OutT *__restrict__ out,
+                                         const int *__restrict__ pos_dev, int chunk_len,
+                                         size_t part_bs, size_t out_bs) {
+  const int h = blockIdx.x;
+  const int dd = threadIdx.x;  // kAttnD threads
+  const int bz = blockIdx.y;
+  partials += bz * part_bs;
+  out += bz * out_bs;
+  if (pos_dev) nchunks = (pos_dev[bz] + chunk_len) / chunk_len;
+  float M = -INFINITY;
+  for (int c = 0; c < nchunks; ++c)
+    M = fmaxf(M, partials[((size_t)c * n_heads + h) * kAttnPartial]);
+  float L = 0.f, O = 0.f;
+  for (int c = 0; c < nchunks; ++c) {
+    const float *pp = partials + ((size_t)c * n_heads + h) * kAttnPartial;
+    const float w = __expf(pp[0] - M);
+    L += pp[1] * w;
+    O += pp[2 + dd] * w;
+  }
+  out[(size_t)h * kAttnD + dd] = from_float<OutT>(O / L);
+}
+
 // seq_len positions, or, when pos_dev is set, pos_dev[b] + 1 positions read
 // on the device out of a cache of capacity seq_len (a launch a captured graph
 // can replay at every step): fixed 128-position chunks covering the capacity.
@@ -272,19 +303,31 @@ static int attn_decode_impl(mlm_ctx *ctx, const void *q, const void *kc, const v
   const __half *qh = reinterpret_cast<const __half *>(q);
   const __half *kh = reinterpret_cast<const __half *>(kc);
   const __half *vh = reinterpret_cast<const __half *>(vc);
-  MLM_REQUIRE(ctx, (size_t)batch * n_kv <= kAttnMaxArrivals, MLM_ERR_SHAPE,
-              "mlm_attn_decode: %d KV heads x %d sequences exceed %d", n_kv, batch,
-              kAttnMaxArrivals);
-  auto kern = G == 1   ? attn_decode_partial_kernel<1, OutT>
-              : G == 2 ? attn_decode_partial_kernel<2, OutT>
-              : G == 4 ? attn_decode_partial_kernel<4, OutT>
-                       : attn_decode_partial_kernel<8, OutT>;
-  return check_launch_pdl(
-      ctx,
-      launch_pdl(kern, grid, dim3(kAttnThreads), kAttnStageBytes, stream, qh, kh, vh, n_heads,
-                 n_kv, seq_len, chunk_len, scale, partials, pos_dev, q_bs, kv_bs, part_bs, out,
-                 out_bs, ctx->attn_arrivals),
-      "mlm_attn_decode");
+  if (batch == 1) {  // one sequence: chunks merged in the kernel, dependent launch
+    auto kern = G == 1   ? attn_decode_partial_kernel<1, OutT, true>
+                : G == 2 ? attn_decode_partial_kernel<2, OutT, true>
+                : G == 4 ? attn_decode_partial_kernel<4, OutT, true>
+                         : attn_decode_partial_kernel<8, OutT, true>;
+    return check_launch_pdl(
+        ctx,
+        launch_pdl(kern, grid, dim3(kAttnThreads), kAttnStageBytes, stream, qh, kh, vh, n_heads,
+                   n_kv, seq_len, chunk_len, scale, partials, pos_dev, q_bs, kv_bs, part_bs, out,
+                   out_bs, ctx->attn_arrivals),
+        "mlm_attn_decode");
+  }
+  // a batch: the partials, then one merge CTA per (head, sequence)
+  auto kern = G == 1   ? attn_decode_partial_kernel<1, OutT, false>
+              : G == 2 ? attn_decode_partial_kernel<2, OutT, false>
+              : G == 4 ? attn_decode_partial_kernel<4, OutT, false>
+                       : attn_decode_partial_kernel<8, OutT, false>;
+  kern<<<grid, kAttnThreads, kAttnStageBytes, stream>>>(qh, kh, vh, n_heads, n_kv, seq_len,
+                                                        chunk_len, scale, partials, pos_dev, q_bs,
+                                                        kv_bs, part_bs, out, out_bs, nullptr);
+  int st = check_launch(ctx, "mlm_attn_decode (partial)");
+  if (st != MLM_OK) return st;
+  attn_decode_merge_kernel<OutT><<<dim3(n_heads, batch), kAttnD, 0, stream>>>(
+      partials, n_heads, nchunks, out, pos_dev, chunk_len, part_bs, out_bs);
+  return check_launch(ctx, "mlm_attn_decode (merge)");
 }
 
 int attn_decode_launch(mlm_ctx *ctx, const void *q, const void *kc, const void *vc, int n_heads,
@@ -310,23 +353,25 @@ size_t attn_decode_partial_floats(int n_heads, int capacity) {
 }
 
 // called once per context, with its device current
-template <class OutT>
+template <class OutT, bool kMerge>
 static int attn_init_out(mlm_ctx *ctx) {
-  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_partial_kernel<1, OutT>,
+  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_partial_kernel<1, OutT, kMerge>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnStageBytes));
-  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_partial_kernel<2, OutT>,
+  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_partial_kernel<2, OutT, kMerge>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnStageBytes));
-  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_partial_kernel<4, OutT>,
+  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_partial_kernel<4, OutT, kMerge>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnStageBytes));
-  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_partial_kernel<8, OutT>,
+  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_partial_kernel<8, OutT, kMerge>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnStageBytes));
   return MLM_OK;
 }
 
 int attn_init(mlm_ctx *ctx) {
-  int st = attn_init_out<__half>(ctx);
+  int st = attn_init_out<__half, true>(ctx);
+  if (st == MLM_OK) st = attn_init_out<__half, false>(ctx);
+  if (st == MLM_OK) st = attn_init_out<__nv_bfloat16, true>(ctx);
   if (st != MLM_OK) return st;
-  st = attn_init_out<__nv_bfloat16>(ctx);
+  st = attn_init_out<__nv_bfloat16, false>(ctx);
   if (st != MLM_OK) return st;
   // arrival counters of the chunk merge, zero between launches
   if (cudaMalloc(&ctx->attn_arrivals, sizeof(int) * kAttnMaxArrivals) != cudaSuccess)

@@ -57,10 +57,10 @@
 namespace mlm {
 
 #ifndef MLM_GEMV_WARPS
-#define MLM_GEMV_WARPS 8
+#define MLM_GEMV_WARPS 16
 #endif
 #ifndef MLM_GEMV_STAGES
-#define MLM_GEMV_STAGES 4
+#define MLM_GEMV_STAGES 2
 #endif
 #ifndef MLM_GEMV_MIN_BLOCKS
 #define MLM_GEMV_MIN_BLOCKS 1  // resident CTAs per SM the register budget allows

@@ -97,3 +97,38 @@ def test_linear_of_another_type_is_named(tmp_path):
     with G.GGUFFile(path) as f:
         with pytest.raises(G.GGUFError, match="blk.0.attn_v.weight is Q6_K"):
             G._check_tensor(f, "blk.0.attn_v.weight", (G.Q4_K,), 256, 1024)
+
+
+@pytest.mark.parametrize("size", [1, 2, 4])
+def test_loader_shards_tile_each_tensor(tmp_path, size):
+    """The blocks each rank's loader uploads (its tensor-parallel shard of a
+    GGUF tensor) put together give the whole tensor exactly once."""
+    from metallm_b200.synthetic import llama_config, q4k_shapes
+    from metallm_b200.tp import Shard, layer_shards, output_shard
+    cfg = llama_config(n_layers=1, dim=1024, n_heads=8, n_kv_heads=4, ffn_dim=2048, vocab=512)
+    shapes = q4k_shapes(cfg)
+    tensors = [(f"blk.0.{G.LAYER_TENSORS[n]}.weight", G.Q4_K, (c, r),
+                O.gen_q4k(9, i, r * c // 256)) for i, (n, (r, c)) in enumerate(shapes.items())]
+    tensors.append(("output.weight", G.Q4_K, (cfg.dim, cfg.vocab),
+                    O.gen_q4k(9, 99, cfg.vocab * cfg.dim // 256)))
+    path = str(tmp_path / "s.gguf")
+    G.write_gguf(path, _meta(), tensors)
+    with G.GGUFFile(path) as f:
+        for name, (rows, cols) in shapes.items():
+            full = f.tensor_data(f"blk.0.{G.LAYER_TENSORS[name]}.weight").reshape(rows, cols // 256, 144)
+            seen = np.zeros(full.shape[:2], dtype=np.int32)
+            for r in range(size):
+                sh = layer_shards(cfg, Shard(r, size))[name]
+                part = G._q4k_shard(f, f"blk.0.{G.LAYER_TENSORS[name]}.weight", rows, cols, sh)
+                sl = (slice(sh["row0"], sh["row0"] + sh["rows"]), slice(sh["kb0"], sh["kb0"] + sh["nkb"]))
+                assert np.array_equal(part, full[sl])
+                seen[sl] += 1
+            assert np.all(seen == 1), name
+        out = f.tensor_data("output.weight").reshape(cfg.vocab, cfg.dim // 256, 144)
+        parts = []
+        for r in range(size):
+            osh = output_shard(cfg, Shard(r, size))
+            parts.append(G._q4k_shard(f, "output.weight", cfg.vocab, cfg.dim,
+                                      dict(row0=osh["row0"], rows=osh["rows"], kb0=0,
+                                           nkb=cfg.dim // 256)))
+        assert np.array_equal(np.concatenate(parts), out)

@@ -66,3 +66,23 @@ def test_create_fails_cleanly_without_gpu():
     h = ctypes.c_void_p()
     st = lib.mlm_create(0, ctypes.byref(h))
     assert st in (-5, -1) and not h.value
+
+
+@pytest.mark.parametrize("lang", ["c", "c++"])
+def test_header_compiles_as_plain_c_and_cpp(tmp_path, lang):
+    """The header the Swift module map (include/module.modulemap) imports is
+    read by the C importer: it must compile as C11 alone, and as C++17."""
+    import shutil
+    import subprocess
+    cc = shutil.which("gcc" if lang == "c" else "g++")
+    if cc is None:
+        pytest.skip("no host compiler")
+    src = tmp_path / ("t.c" if lang == "c" else "t.cpp")
+    src.write_text('#include "metallm_cuda.h"\nint main(void) { return MLM_OK; }\n')
+    std = "-std=c11" if lang == "c" else "-std=c++17"
+    r = subprocess.run([cc, std, "-Wall", "-Werror", "-pedantic", "-fsyntax-only",
+                        "-I", os.path.join(ROOT, "include"), str(src)],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    mm = open(os.path.join(ROOT, "include", "module.modulemap")).read()
+    assert 'header "metallm_cuda.h"' in mm and 'link "metallm_cuda"' in mm

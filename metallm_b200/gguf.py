@@ -112,6 +112,15 @@ class GGUFFile:
     def __init__(self, path: str):
         self.path = path
         self._f = open(path, "rb")
+        self._mm = None
+        try:
+            self._parse()
+        except BaseException:
+            self.close()
+            raise
+
+    def _parse(self) -> None:
+        path = self.path
         size = os.fstat(self._f.fileno()).st_size
         if size < 24:
             raise GGUFError(f"{path}: {size} bytes is too short for a GGUF header")
@@ -149,10 +158,11 @@ class GGUFFile:
         return np.frombuffer(self._mm, dtype=np.uint8, count=t.n_bytes, offset=start)
 
     def close(self) -> None:
-        try:
-            self._mm.close()
-        except BufferError:  # tensor views still alive: the map goes with the last one
-            pass
+        if self._mm is not None:
+            try:
+                self._mm.close()
+            except BufferError:  # tensor views still alive: the map goes with the last one
+                pass
         self._f.close()
 
     def __enter__(self):

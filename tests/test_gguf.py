@@ -132,3 +132,19 @@ def test_loader_shards_tile_each_tensor(tmp_path, size):
                                       dict(row0=osh["row0"], rows=osh["rows"], kb0=0,
                                            nkb=cfg.dim // 256)))
         assert np.array_equal(np.concatenate(parts), out)
+
+
+def test_failed_parse_closes_the_file(tmp_path):
+    """A file rejected while parsing leaves no open handle behind."""
+    import gc
+    import os
+    bad = tmp_path / "short.gguf"
+    bad.write_bytes(b"GGUF" + (3).to_bytes(4, "little") + b"\xff" * 40)  # counts past the end
+    fd_dir = f"/proc/{os.getpid()}/fd"
+    before = len(os.listdir(fd_dir)) if os.path.isdir(fd_dir) else None
+    for _ in range(20):
+        with pytest.raises(G.GGUFError):
+            G.GGUFFile(str(bad))
+    gc.collect()
+    if before is not None:
+        assert len(os.listdir(fd_dir)) <= before + 1

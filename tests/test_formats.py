@@ -154,3 +154,18 @@ def test_q4k_repack_is_a_bijection():
         else:
             back[:, 32 * j + l - 32] |= nib[:, i] << 4
     assert np.array_equal(back, b.reshape(50, 144)[:, 16:])
+
+
+def test_q6k_matvec_matches_reference_dequant_dot():
+    """The Q6_K matvec oracle against rows dequantized by the reference's own
+    kernel_dequantize_q6_K_f32 (what the reference hands to MPS), fp64 dot."""
+    _ref_or_skip()
+    rows, cols = 24, 2048
+    W = O.gen_q6k(13, 2, rows * cols // 256)
+    x = O.gen_f16(13, 3, cols)
+    dense = O.ref_q6k_dequant_f32(W, rows * cols, 2).reshape(rows, cols).astype(np.float64)
+    want = dense @ x.astype(np.float64)
+    got = O.q6k_matvec(W, rows, cols, x)
+    # both fp64 sums of the same exact products, rounded once to fp32: only
+    # the summation order differs
+    assert np.allclose(got, want, rtol=1e-6, atol=1e-6)

@@ -1,11 +1,11 @@
-"""Tensor-parallel host logic on CPU: world-size-2 gloo process groups.
+"""Tensor-parallel host logic on CPU: gloo process groups of 2 (and 4) ranks.
 
 - bootstrap(): rank 0's NCCL unique id reaches every rank, each joins with
   its (size, rank);
 - the shard plan (metallm_b200.tp): every Q4_K tensor of a layer is covered
   exactly once by the ranks' shares, for 1/2/4/8 ranks on the Llama-3-70B
   shape;
-- the sharded decoder layer: each rank computes its heads' attention and its
+- the sharded decoder layer (2 and 4 ranks): each rank computes its heads' attention and its
   FFN rows from its shards of the whole-model tensors, the output and down
   projections' partial sums are summed by a gloo all-reduce, and the result
   equals the oracle's whole layer (LlamaRunner.swift:537-1085) -- the
@@ -109,6 +109,8 @@ def test_shards_reject_uneven_split():
 
 SEED, POS = 77, 5
 CFG = dict(n_layers=1, dim=512, n_heads=4, n_kv_heads=2, ffn_dim=1024, vocab=256, max_seq=8)
+# splits evenly over 4 ranks: 8 query heads, 4 KV heads, FFN 2048
+CFG4 = dict(n_layers=1, dim=1024, n_heads=8, n_kv_heads=4, ffn_dim=2048, vocab=256, max_seq=8)
 
 
 def _slice(blocks: np.ndarray, rows: int, nb: int, sh: dict) -> np.ndarray:
@@ -134,13 +136,13 @@ def _whole_layer(cfg):
     return w, caches, h
 
 
-def _sharded_layer_worker(rank: int, world: int, port: int, q) -> None:
+def _sharded_layer_worker(rank: int, world: int, port: int, q, cfg_kw=CFG) -> None:
     """One rank: its shard of the layer, partial sums all-reduced over gloo."""
     import torch
     import torch.distributed as dist
     from oracle import oracle as O
     _init(rank, world, port)
-    cfg = llama_config(**CFG)
+    cfg = llama_config(**cfg_kw)
     w, (kc, vc), h = _whole_layer(cfg)
     shard = Shard(rank, world)
     sh = layer_shards(cfg, shard)
@@ -180,10 +182,11 @@ def _sharded_layer_worker(rank: int, world: int, port: int, q) -> None:
     dist.destroy_process_group()
 
 
-def test_sharded_layer_equals_whole_layer_gloo_world2():
+@pytest.mark.parametrize("world,cfg_kw", [(2, CFG), (4, CFG4)])
+def test_sharded_layer_equals_whole_layer_gloo(world, cfg_kw):
     from oracle import llama_oracle as LO
-    res = _run(_sharded_layer_worker, 2)
-    cfg = llama_config(**CFG)
+    res = _run(_sharded_layer_worker, world, cfg_kw)
+    cfg = llama_config(**cfg_kw)
     w, (kc, vc), h = _whole_layer(cfg)
     cd = {"dim": cfg.dim, "head_dim": cfg.head_dim, "n_heads": cfg.n_heads,
           "n_kv_heads": cfg.n_kv_heads, "ffn_dim": cfg.ffn_dim, "rms_eps": cfg.rms_eps,

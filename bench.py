@@ -124,7 +124,6 @@ def measured_peaks() -> dict:
 # committed ncu summary of each workload's dominant kernel (named kernel + shape)
 PROFILES = {
     "gemv_up": "q4k_gemv_14336x4096.md",
-    "gemv_down": "q4k_gemv_4096x14336.md",
     "dequant": "q4k_dequant_f32_4096x4096.md",
     "prefill": "q4k_gemm_28672x4096x512.md",
     "gemm": "q4k_gemm_28672x4096x512.md",
@@ -136,6 +135,8 @@ PROFILES = {
 
 def ncu_traffic(workload: str):
     """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
+    if workload not in PROFILES:
+        return None
     p = os.path.join(ROOT, "profiles", PROFILES[workload])
     if not os.path.exists(p):
         return None

@@ -70,6 +70,68 @@ def test_gemm_residual_in_place(ctx, rows, cols, tokens):
     assert rel_l2(got, ref) < TOL
 
 
+def gemm_schedule(sm_count: int, rows: int, cols: int, tokens: int) -> dict:
+    """The launch plan of mlm_q4k_gemm (q4k_gemm.cu, gemm_launch): output
+    tiles of 256 rows x 256 tokens, one persistent CTA per SM with at least
+    16 K stages each, whole-tile waves first and one to two waves' worth of
+    tiles left to stream-K."""
+    tiles = -(-rows // 256) * -(-tokens // 256)
+    ks = cols // 256 * 8
+    ctas = min(sm_count, -(-tiles * ks // 16))
+    return {"tiles": tiles, "ctas": ctas, "dp_waves": max(0, tiles // ctas - 1)}
+
+
+def _sample_rows(rows: int, n: int, seed: int) -> np.ndarray:
+    return np.sort(np.random.default_rng(seed).choice(rows, size=min(rows, n), replace=False))
+
+
+@pytest.mark.parametrize("rows,cols,tokens,sample,in_place", [
+    # 320 tiles: one whole-tile wave, then stream-K
+    (20480, 256, 1024, 0, False),
+    (20480, 256, 1024, 0, True),
+    # the 8B gate/up on a 2048-token prompt (896 tiles, 5 whole-tile waves)
+    (28672, 4096, 2048, 384, False),
+    (28672, 4096, 2048, 384, True),
+    # a 16384-token product (1024 tiles)
+    (4096, 4096, 16384, 256, False),
+    # the 70B gate/up on a 1024-token prompt chunk (896 tiles)
+    (57344, 8192, 1024, 256, False),
+])
+def test_gemm_whole_tile_waves(ctx, rows, cols, tokens, sample, in_place):
+    """Launches large enough that CTAs take whole output tiles before the
+    stream-K split (dp_waves >= 1).  Large products are checked on a seeded
+    sample of weight rows (every token of each sampled row)."""
+    sm = ctx.lib.mlm_device_sm_count(ctx.handle)
+    plan = gemm_schedule(sm, rows, cols, tokens)
+    assert plan["dp_waves"] >= 1, plan
+    nb = rows * cols // 256
+    seed = 40 + rows % 7
+    blocks = O.gen_q4k(seed, 1, nb)
+    xb = bf16_bits(O.gen_f32(seed, 2, tokens * cols))
+    if in_place:
+        r = O.gen_f32(seed, 3, tokens * rows, 0.0, 100.0)
+        y = ctx.to_device(r)
+        res = y
+    else:
+        r = None
+        y = ctx.alloc(4 * rows * tokens)
+        res = None
+    ctx.call("mlm_q4k_gemm", ctx.to_device(blocks), rows, cols, ctx.to_device(xb), tokens, y, res)
+    got = y.download(np.float32, rows * tokens).reshape(tokens, rows)
+    bpr = cols // 256 * 144  # bytes of one weight row
+    sel = np.arange(rows) if sample == 0 else _sample_rows(rows, sample, seed)
+    wb = blocks.reshape(rows, bpr)[sel].reshape(-1)
+    w = bf16_value(bf16_bits(O.q4k_dequant_f32(wb, len(sel) * cols))).reshape(len(sel), cols)
+    x = bf16_value(xb).reshape(tokens, cols)
+    ref = x.astype(np.float64) @ w.astype(np.float64).T
+    if r is not None:
+        ref += r.reshape(tokens, rows)[:, sel]
+    g = got[:, sel]
+    assert np.all(np.isfinite(g))
+    err = rel_l2(g, ref)
+    assert err < TOL, (rows, cols, tokens, plan, err)
+
+
 def test_gemm_bad_args(ctx):
     from metallm_b200 import MLMError
     buf = ctx.alloc(1 << 16)

@@ -233,27 +233,13 @@ int mlm_q4k_gemv_batch(mlm_ctx *ctx, const void *W, int rows, int cols, const vo
 int mlm_q4k_gemm(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_bf16,
                  int tokens, float *y, const float *residual);
 
-/* Tiled Q4_K layout: the same 144-byte blocks, reordered once after upload
- * so that the decode GEMV streams them as contiguous 4608-byte units (32
- * rows of one block column, laid out in the GEMV's register order; rows past
- * the end zero).  Replaces the reference's load-time conversion of every
- * linear to fp16 (ModelLoader.swift:275-299, MetalService.swift:243-313)
- * with a conversion that keeps the weights packed.  mlm_q4k_tiled_bytes
- * gives the tiled size (0 for bad shapes); mlm_q4k_tile converts on the
- * context stream (W and W_tiled 16-byte aligned, not overlapping). */
-size_t mlm_q4k_tiled_bytes(int rows, int cols);
-int mlm_q4k_tile(mlm_ctx *ctx, const void *W, int rows, int cols, void *W_tiled);
-/* mlm_q4k_gemv on a tiled weight (same arguments, same results): the decode
- * linears of LlamaRunner.swift:563-609, 954-963, 1008-1034, 1059-1068,
- * 1169-1178.  Shares the context's split-K scratch with mlm_q4k_gemv. */
-int mlm_q4k_gemv_tiled(mlm_ctx *ctx, const void *W_tiled, int rows, int cols,
-                       const void *x_f16, float *y, const float *residual);
-
 /* No counterpart in the reference.  mlm_q4k_gemv with its split-K scratch
  * in a static 80 KB device array inside the library instead of the
  * context's allocation: the call allocates nothing, for hosts that own all
  * device memory through their own pool or enqueue from places where an
  * allocation may not happen.  rows <= 131072 (MLM_ERR_SHAPE beyond).  The
+ * calling thread's current device must be the context's device
+ * (MLM_ERR_STATE otherwise: the array's address is per device).  The
  * first call on a device looks up and clears the array (make it before any
  * stream capture); later calls clear only the arrival counters, on the
  * context stream.  All calls on a device share the array: calls that overlap

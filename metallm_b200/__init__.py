@@ -228,15 +228,6 @@ class Context:
     def q6k_gemv(self, W, rows: int, cols: int, x, y, residual=None) -> None:
         self.call("mlm_q6k_gemv", W, rows, cols, x, y, residual)
 
-    def q4k_tiled_bytes(self, rows: int, cols: int) -> int:
-        return int(self.lib.mlm_q4k_tiled_bytes(rows, cols))
-
-    def q4k_tile(self, W, rows: int, cols: int, W_tiled) -> None:
-        self.call("mlm_q4k_tile", W, rows, cols, W_tiled)
-
-    def q4k_gemv_tiled(self, W_tiled, rows: int, cols: int, x, y, residual=None) -> None:
-        self.call("mlm_q4k_gemv_tiled", W_tiled, rows, cols, x, y, residual)
-
 
 class Graph:
     """A captured op sequence (mlm_graph)."""

@@ -104,9 +104,6 @@ SIGNATURES = [
     ("mlm_q4k_gemm", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_int, c_vp, c_vp]),
     ("mlm_q4k_gemv_batch", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_int, c_vp, c_vp]),
     ("mlm_q4k_gemv_static", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_vp]),
-    ("mlm_q4k_tiled_bytes", ctypes.c_size_t, [c_int, c_int]),
-    ("mlm_q4k_tile", c_int, [c_vp, c_vp, c_int, c_int, c_vp]),
-    ("mlm_q4k_gemv_tiled", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_vp]),
     ("mlm_rmsnorm_f16", c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_float]),
     ("mlm_rmsnorm_f32", c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_float]),
     ("mlm_rope_f16", c_int, [c_vp, c_vp, c_vp, ctypes.POINTER(RopeArgs), c_int, c_int, c_int]),

@@ -19,7 +19,6 @@
 namespace mlm {
 
 int gemv_init(mlm_ctx *ctx);
-int gemv_tiled_init(mlm_ctx *ctx);
 int attn_init(mlm_ctx *ctx);
 int gemm_init(mlm_ctx *ctx);
 int prefill_init(mlm_ctx *ctx);
@@ -133,7 +132,7 @@ extern "C" int mlm_create(int device, mlm_ctx **out) {
     if (cudaHostGetDevicePointer(reinterpret_cast<void **>(&ctx->dev_status), hs, 0) != cudaSuccess)
       return fail(MLM_ERR_CUDA);
   }
-  if (gemv_init(ctx) != MLM_OK || gemv_tiled_init(ctx) != MLM_OK || attn_init(ctx) != MLM_OK ||
+  if (gemv_init(ctx) != MLM_OK || attn_init(ctx) != MLM_OK ||
       gemm_init(ctx) != MLM_OK || prefill_init(ctx) != MLM_OK ||
       gemv_batch_init(ctx) != MLM_OK || q6k_init(ctx) != MLM_OK)
     return fail(MLM_ERR_CUDA);

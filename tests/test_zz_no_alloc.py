@@ -52,6 +52,28 @@ def test_static_matches_gemv_two_calls(ctx, rows, cols):
         assert rel_l2(got, want) <= TOL, (rows, cols, i)
 
 
+def test_static_allocates_nothing(ctx):
+    """After the per-device set-up, calls leave the device's free memory
+    unchanged (cudaMemGetInfo before and after several calls)."""
+    import torch
+    rows, cols = 14336, 4096
+    nb = rows * cols // 256
+    W = ctx.alloc(nb * 144)
+    ctx.gen_q4k(33, 1, nb, W)
+    x = ctx.alloc(2 * cols)
+    ctx.gen_f16(33, 2, cols, x)
+    y = ctx.alloc(4 * rows)
+    torch.cuda.mem_get_info(ctx.device)  # torch's own lazy set-up, outside the window
+    _static(ctx, W, rows, cols, x, y)
+    ctx.wait()
+    free0, _ = torch.cuda.mem_get_info(ctx.device)
+    for _ in range(4):
+        _static(ctx, W, rows, cols, x, y)
+    ctx.wait()
+    free1, _ = torch.cuda.mem_get_info(ctx.device)
+    assert free1 == free0, (free0, free1)
+
+
 def test_static_rejects_rows_beyond_limit(ctx):
     cols = 256
     W = ctx.alloc(144 * 4)

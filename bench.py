@@ -317,7 +317,9 @@ def run_gpu(args, world, rank, local, pg) -> dict:
     x = ctx.alloc(2 * cols)
     ctx.gen_f16(7, 2, cols, x)
     out_elems = rows if is_gemv else nb * 256
-    outs = [ctx.alloc(4 * out_elems) for _ in range(2 if not is_gemv else 1)]
+    # the dequant writes 67 MB per step: four rotating outputs (268 MB, twice
+    # the L2) so each step's stores go out to HBM
+    outs = [ctx.alloc(4 * out_elems) for _ in range(4 if not is_gemv else 1)]
     ctx.wait()
 
     def step(i: int):
@@ -415,8 +417,10 @@ def run_gpu(args, world, rank, local, pg) -> dict:
         "config": {"workload": desc, "rows": rows, "cols": cols,
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "weight_copies": copies,
-                   "l2": f"inputs larger than L2: {copies} rotating weight copies "
-                         f"({copies * nb * 144 / 1e6:.0f} MB)",
+                   "l2": (f"inputs larger than L2: {copies} rotating weight copies "
+                          f"({copies * nb * 144 / 1e6:.0f} MB)" if is_gemv else
+                          f"outputs larger than L2: {len(outs)} rotating fp32 outputs "
+                          f"({len(outs) * 4 * out_elems / 1e6:.0f} MB)"),
                    "algorithmic_bytes_per_step": alg_bytes},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},

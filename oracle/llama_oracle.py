@@ -26,6 +26,15 @@ import numpy as np
 from . import oracle as O
 
 
+def _matvec(W: np.ndarray, rows: int, cols: int, x: np.ndarray) -> np.ndarray:
+    """y = W x for a Q4_K tensor (block bytes; fp64 sums over the bit-exact
+    dequantized rows) or for a tensor already dequantized to fp32 [rows][cols]
+    by dense() (fp32 BLAS sums)."""
+    if W.dtype == np.float32:
+        return W @ np.ascontiguousarray(x, dtype=np.float32)
+    return O.q4k_matvec_f32x(W, rows, cols, x)
+
+
 def layer_decode(w: Dict[str, np.ndarray], hidden: np.ndarray, kcache: np.ndarray,
                  vcache: np.ndarray, pos: int, cfg: dict) -> np.ndarray:
     """One decoder layer at position `pos`; appends K/V at row `pos` of the
@@ -34,20 +43,20 @@ def layer_decode(w: Dict[str, np.ndarray], hidden: np.ndarray, kcache: np.ndarra
                                                  "ffn_dim", "rms_eps"))
     kvd = nkv * hd
     xn = O.rmsnorm_f32(hidden, w["attn_norm"], 1, d, eps)
-    q = O.q4k_matvec_f32x(w["wq"], d, d, xn)
-    k = O.q4k_matvec_f32x(w["wk"], kvd, d, xn)
-    v = O.q4k_matvec_f32x(w["wv"], kvd, d, xn)
+    q = _matvec(w["wq"], d, d, xn)
+    k = _matvec(w["wk"], kvd, d, xn)
+    v = _matvec(w["wv"], kvd, d, xn)
     ra = O.rope_args(n_dims=hd, freq_base=cfg["rope_theta"], pos_offset=pos)
     q = O.rope_f32(ra, q, 1, nh, hd)
     k = O.rope_f32(ra, k, 1, nkv, hd)
     kcache[pos] = k.astype(np.float16).reshape(nkv, hd)
     vcache[pos] = v.astype(np.float16).reshape(nkv, hd)
     attn = O.attn_decode(q, kcache[: pos + 1], vcache[: pos + 1], nh, nkv, hd, pos + 1)
-    hidden = hidden + O.q4k_matvec_f32x(w["wo"], d, d, attn)
+    hidden = hidden + _matvec(w["wo"], d, d, attn)
     xn2 = O.rmsnorm_f32(hidden, w["ffn_norm"], 1, d, eps)
-    g = O.q4k_matvec_f32x(w["w_gate"], ffn, d, xn2)
-    u = O.q4k_matvec_f32x(w["w_up"], ffn, d, xn2)
-    return hidden + O.q4k_matvec_f32x(w["w_down"], d, ffn, O.silu_mul(g, u))
+    g = _matvec(w["w_gate"], ffn, d, xn2)
+    u = _matvec(w["w_up"], ffn, d, xn2)
+    return hidden + _matvec(w["w_down"], d, ffn, O.silu_mul(g, u))
 
 
 def model_forward(layers, glob: Dict[str, np.ndarray], caches, token: int, pos: int,
@@ -59,4 +68,14 @@ def model_forward(layers, glob: Dict[str, np.ndarray], caches, token: int, pos: 
     for w, (kc, vc) in zip(layers, caches):
         hidden = layer_decode(w, hidden, kc, vc, pos, cfg)
     xn = O.rmsnorm_f32(hidden, glob["output_norm"], 1, d, cfg["rms_eps"])
-    return O.q4k_matvec_f32x(glob["output"], cfg["vocab"], d, xn)
+    return _matvec(glob["output"], cfg["vocab"], d, xn)
+
+
+def dense(w: Dict[str, np.ndarray], shapes: Dict[str, tuple]) -> Dict[str, np.ndarray]:
+    """The same tensors with every Q4_K one dequantized once (bit-exact fp32,
+    DequantKernels.metal:63-92) to [rows][cols]: full-size models then run
+    through fp32 BLAS products instead of dequantizing per token."""
+    out = dict(w)
+    for name, (rows, cols) in shapes.items():
+        out[name] = O.q4k_dequant_f32(w[name], rows * cols).reshape(rows, cols)
+    return out

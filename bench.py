@@ -237,6 +237,83 @@ def barrier(pg, local):
         pg.barrier()
 
 
+L2_BYTES = 126 * 1024 * 1024
+
+
+def rotation_copies(steps: int, nbytes: int, requested: int = 0) -> int:
+    """Weight copies rotated through the K-step graph: a divisor of K (so a
+    replayed graph reuses each copy only after every other one) whose total
+    is at least 1.25x the L2; `requested` > 0 forces a count."""
+    if requested > 0:
+        return requested
+    need = -(-int(1.25 * L2_BYTES) // max(nbytes, 1))
+    for c in range(max(need, 1), steps + 1):
+        if steps % c == 0:
+            return c
+    return max(need, 1)
+
+
+def gemv_config(args, world: int, rows: int, cols: int, desc: str) -> dict:
+    """config of the GEMV / dequant workloads (the same keys in both arms)."""
+    nb = rows * cols // 256
+    is_gemv = args.workload.startswith("gemv")
+    copies = rotation_copies(args.steps, nb * 144, args.copies)
+    outs = 1 if is_gemv else 4
+    alg = gemv_bytes(rows, cols) if is_gemv else dequant_bytes(rows, cols)
+    return {"workload": desc, "rows": rows, "cols": cols,
+            "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+            "weight_copies": copies,
+            "l2": (f"inputs larger than L2: {copies} rotating weight copies "
+                   f"({copies * nb * 144 / 1e6:.0f} MB)" if is_gemv else
+                   f"outputs larger than L2: {outs} rotating fp32 outputs "
+                   f"({outs * 4 * nb * 256 / 1e6:.0f} MB)"),
+            "algorithmic_bytes_per_step": alg}
+
+
+TP70_PROMPT, TP70_GEN = 2048, 128
+
+
+def tp70b_steps(args) -> int:
+    return min(args.steps, TP70_GEN - args.warmup - 2)
+
+
+def tp70b_config(args, world: int) -> dict:
+    """config of the tensor-parallel 70B workload (the same keys in both arms);
+    timed steps start after the prompt and the warm-up steps."""
+    steps = tp70b_steps(args)
+    alg = llama70_rank_bytes(world, TP70_PROMPT + args.warmup + steps // 2, args.batch)
+    return {"workload": LLAMA_WORKLOADS["tp70b"], "batch": args.batch,
+            "prompt_tokens": TP70_PROMPT, "decode_steps_timed": steps,
+            "parallelism": f"tp{world}",
+            "l2": "inputs larger than L2: Q4_K weights of 39.1 GB / N per step",
+            "algorithmic_bytes_per_step_per_rank": alg}
+
+
+def replay_timed(graph_launch, tstream, target_s: float = 1.0, min_reps: int = 10,
+                 max_reps: int = 20000) -> dict:
+    """Replays a captured K-step graph R times back to back, each replay
+    bracketed by CUDA events on the launch stream, long enough (about
+    target_s) that the clock sampler sees the GPU under load; returns the
+    median replay time and the spread."""
+    import torch
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    ev[0].record(tstream)
+    graph_launch()
+    ev[1].record(tstream)
+    ev[1].synchronize()
+    one = max(ev[0].elapsed_time(ev[1]) * 1e-3, 1e-6)
+    reps = int(min(max_reps, max(min_reps, target_s / one)))
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(reps + 1)]
+    evs[0].record(tstream)
+    for i in range(reps):
+        graph_launch()
+        evs[i + 1].record(tstream)
+    evs[-1].synchronize()
+    ms = sorted(evs[i].elapsed_time(evs[i + 1]) for i in range(reps))
+    return {"median_ms": ms[reps // 2], "min_ms": ms[0], "max_ms": ms[-1], "replays": reps,
+            "total_ms": evs[0].elapsed_time(evs[-1])}
+
+
 # ----------------------------------------------------------------------------
 # CPU legs
 # ----------------------------------------------------------------------------
@@ -307,7 +384,7 @@ def run_gpu(args, world, rank, local, pg) -> dict:
     stream_ptr = ctx.stream()
     tstream = torch.cuda.ExternalStream(stream_ptr, device=f"cuda:{local}")
     nb = rows * cols // 256
-    copies = args.copies
+    copies = rotation_copies(args.steps, nb * 144, args.copies)
     is_gemv = args.workload.startswith("gemv")
     Ws = []
     for c in range(copies):
@@ -343,13 +420,8 @@ def run_gpu(args, world, rank, local, pg) -> dict:
     sampler = ClockSampler(local)
     sampler.start()
     time.sleep(0.3)
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
-    ev0.record(tstream)
-    graph.launch()
-    ev1.record(tstream)
-    ev1.synchronize()
-    dev_ms = ev0.elapsed_time(ev1)
+    rt = replay_timed(graph.launch, tstream)
+    dev_ms = rt["median_ms"]
     clocks = sampler.stop()
     graph.destroy()
     barrier(pg, local)
@@ -414,18 +486,16 @@ def run_gpu(args, world, rank, local, pg) -> dict:
         "vs_baseline": None,
         "dtype": "q4k x f16 -> f32" if is_gemv else "q4k -> f32",
         "data": "synthetic (seeded Q4_K blocks generated on device, as BASELINE config 0)",
-        "config": {"workload": desc, "rows": rows, "cols": cols,
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                   "weight_copies": copies,
-                   "l2": (f"inputs larger than L2: {copies} rotating weight copies "
-                          f"({copies * nb * 144 / 1e6:.0f} MB)" if is_gemv else
-                          f"outputs larger than L2: {len(outs)} rotating fp32 outputs "
-                          f"({len(outs) * 4 * out_elems / 1e6:.0f} MB)"),
-                   "algorithmic_bytes_per_step": alg_bytes},
+        "config": gemv_config(args, world, rows, cols, desc),
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": args.steps,
         "launch": "CUDA graph of K steps (programmatic dependent launch between GEMVs)",
+        "timing": {"replays": rt["replays"], "statistic": "median over replays of the K-step "
+                   "graph, each bracketed by CUDA events", "replay_ms_min": round(rt["min_ms"], 5),
+                   "replay_ms_median": round(rt["median_ms"], 5),
+                   "replay_ms_max": round(rt["max_ms"], 5),
+                   "timed_region_s": round(rt["total_ms"] * 1e-3, 3)},
         "roofline": {"bound": "hbm", "achieved": round(kernel_gbs, 1),
                      "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(kernel_gbs / peaks["hbm_gbs"], 4),
@@ -593,7 +663,7 @@ def run_gemm(args, world, rank, local, pg) -> dict:
     tstream = torch.cuda.ExternalStream(ctx.stream(), device=f"cuda:{local}")
     peaks = measured_peaks()
     nb = rows * cols // 256
-    copies = max(2, min(args.copies, 4))  # 4 x 66 MB > L2
+    copies = args.copies if args.copies > 0 else 4  # 4 x 66 MB > L2
     Ws = []
     for c in range(copies):
         W = ctx.alloc(nb * 144)
@@ -736,7 +806,7 @@ def run_llama(args, world, rank, local, pg) -> dict:
         alg = llama_token_bytes(1, pos, with_head=False) - 2 * 4096
         value = alg * args.steps * world / (ms_max * 1e-3) / 1e9
         unit, metric_value_desc = "GB/s", "one decoder layer per step"
-        launches = args.steps * 7  # state, QKV GEMV, RoPE, attention, 3 GEMVs
+        launches = args.steps * 6  # state, QKV GEMV, RoPE + append + attention, 3 GEMVs
         # e2e: hidden state in from pinned host memory, the layer, out again
         lib, h = ctx.lib, ctx.handle
         hbuf = ctypes.c_void_p()
@@ -849,7 +919,7 @@ def run_llama(args, world, rank, local, pg) -> dict:
         value = steps * world / (ms_max * 1e-3)
         unit = "tokens/s"
         alg = llama_token_bytes(32, pos0 + steps // 2)
-        launches = steps * (1 + 32 * 6 + 3)  # embed, 6 per layer, head, argmax, advance
+        launches = steps * (1 + 32 * 5 + 3)  # embed, 5 per layer, head, argmax, advance
         # e2e: forward(tokenID:) per token through the C ABI, the argmax read back
         m.set_position(prompt_len)
         lib, h = ctx.lib, ctx.handle
@@ -921,8 +991,8 @@ def run_tp70b(args, world, rank, local, pg) -> dict:
     peaks = measured_peaks()
     if world > 1:
         bootstrap(ctx)
-    B, prompt_len, gen_len = args.batch, 2048, 128
-    steps = min(args.steps, gen_len - args.warmup - 2)
+    B, prompt_len, gen_len = args.batch, TP70_PROMPT, TP70_GEN
+    steps = tp70b_steps(args)
     cfg = llama_config(max_seq=prompt_len + gen_len, **L70)
     m = Llama(ctx, cfg, batch=B)
     fill_llama(m, 1)
@@ -984,10 +1054,7 @@ def run_tp70b(args, world, rank, local, pg) -> dict:
         "dtype": "q4k -> bf16 x bf16 -> f32 (tcgen05 GEMM over the batch), fp16 KV cache",
         "data": "synthetic (seeded Q4_K weights, fp16 embedding, fp32 norms generated on device; "
                 "every rank its shard of one model; uniform random prompt ids)",
-        "config": {"workload": LLAMA_WORKLOADS["tp70b"], "batch": B, "prompt_tokens": prompt_len,
-                   "decode_steps_timed": steps, "parallelism": f"tp{world}",
-                   "l2": "inputs larger than L2: Q4_K weights of 39.1 GB / N per step",
-                   "algorithmic_bytes_per_step_per_rank": alg},
+        "config": dict(tp70b_config(args, world), algorithmic_bytes_per_step_per_rank=alg),
         "e2e": {"value": round(B * e2e_steps / e2e_s, 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B},
         # per step: embedding; per layer 2 RMSNorm rows, 3 GEMMs + 2 more, RoPE,
@@ -1237,7 +1304,8 @@ def run_reference(args, world, rank) -> dict | None:
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "q4k x f16 -> f32", "data": "synthetic (seeded Q4_K blocks)",
-                "config": {"workload": LLAMA_WORKLOADS[args.workload]},
+                "config": (tp70b_config(args, world) if args.workload == "tp70b" else
+                           {"workload": LLAMA_WORKLOADS[args.workload]}),
                 "cpu_baseline": dict(r, value=v, unit=unit),
                 "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
@@ -1265,11 +1333,35 @@ def run_reference(args, world, rank) -> dict | None:
         "vs_baseline": None,
         "dtype": "q4k x f16 -> f32" if is_gemv else "q4k -> f32",
         "data": "synthetic (seeded Q4_K blocks)",
-        "config": {"workload": desc, "rows": rows, "cols": cols},
+        "config": gemv_config(args, world, rows, cols, desc),
         "cpu_baseline": {"value": v, "unit": "GB/s", "cores": th, "kind": vals[0]["kind"],
                          "sample": vals[0]["sample"]},
         "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+
+
+SUB_KEYS = ("value", "unit", "ms_per_step", "steps", "warmup", "dtype", "config", "e2e",
+            "gpu_launches", "launch", "roofline", "prefill", "first_tokens", "clocks",
+            "cpu_baseline", "scaling", "n_gpus")
+
+
+def sub_measurements(args, local: int) -> dict:
+    """The second half of the metric and the sharded workload at one GPU,
+    measured in the same run as the headline: 'decode' = the Llama-3-8B-shape
+    model (512-token prompt pass, then timed greedy decode, tokens/s) and
+    'tp70b' = the 70B-shape batch of 8 on this one GPU through the same code
+    the multi-GPU lines run (the base of the scaling curve)."""
+    import copy
+    out = {}
+    sub = copy.copy(args)
+    sub.workload, sub.steps, sub.default_line = "decode", 128, False
+    d = run_llama(sub, 1, 0, local, None)
+    out["decode"] = {k: d[k] for k in SUB_KEYS if k in d}
+    sub = copy.copy(args)
+    sub.workload, sub.default_line = "tp70b", False
+    t = run_tp70b(sub, 1, 0, local, None)
+    out["tp70b"] = {k: t[k] for k in SUB_KEYS if k in t}
+    return out
 
 
 def main() -> None:
@@ -1277,16 +1369,25 @@ def main() -> None:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--workload", default="gemv_up",
+    ap.add_argument("--workload", default=None,
                     choices=sorted(WORKLOADS) + sorted(LLAMA_WORKLOADS) + sorted(FORMAT_WORKLOADS)
                     + ["gemm", "gemv_batch"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--copies", type=int, default=6, help="rotating weight copies (> L2)")
+    ap.add_argument("--copies", type=int, default=0,
+                    help="rotating weight copies (default: a divisor of --steps totalling > L2)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--batch", type=int, default=8, help="sequences of the tp70b workload")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="default line without its decode / tp70b sub-measurements")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    # No --workload: one GPU measures the headline GEMV (with the 8B decode and
+    # the one-GPU 70B batch as sub-objects); under torchrun the ranks run the
+    # 70B model tensor-parallel, the workload that shards.
+    args.default_line = args.workload is None
+    if args.workload is None:
+        args.workload = "tp70b" if int(os.environ.get("WORLD_SIZE", "1")) > 1 else "gemv_up"
 
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -1302,6 +1403,8 @@ def main() -> None:
                "gemv_q6k": run_formats, "repack": run_formats}.get(
             args.workload, run_llama if args.workload in LLAMA_WORKLOADS else run_gpu)
         line = run(args, world, rank, local, pg)
+        if args.default_line and world == 1 and not args.no_extras:
+            line.update(sub_measurements(args, local))
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:

@@ -12,8 +12,11 @@
 // a batch a second kernel merges them (one CTA per head and sequence), which
 // measured faster there (the merges of 8 sequences x 8 KV heads otherwise run
 // one per CTA at the kernel's tail).
+#include <algorithm>
+
 #include "mlm_device.cuh"
 #include "mlm_internal.h"
+#include "mlm_rope.cuh"
 
 namespace mlm {
 
@@ -259,6 +262,323 @@ __global__ void attn_decode_merge_kernel(const float *__restrict__ partials, int
   out[(size_t)h * kAttnD + dd] = from_float<OutT>(O / L);
 }
 
+// ---------------------------------------------------------------------------
+// One decode step's attention of one sequence with RoPE and the KV append
+// folded in (the runner's path: LlamaRunner.swift:612-952 -- applyRoPE on q
+// and k, the cache append, then attention).  Input: the QKV projection in
+// fp32 (q [n_heads][128], k and v [n_kv][128]) and the position in device
+// memory.  CTA (KV head, chunk): RoPE of its G query heads in fp32 (q is not
+// rounded to fp16), K/V rows of the chunk staged in shared memory; the chunk
+// holding the position also rotates k, rounds k and v to fp16, appends them
+// to the caches and uses them for that row.  The last CTA of a KV head to
+// finish merges the chunks from shared memory: every partial of the head is
+// copied in with one round of 16-byte loads.
+template <int G>
+__global__ void __launch_bounds__(kAttnThreads) attn_rope_decode_kernel(
+    const float *__restrict__ qkv, mlm_rope_args ra, RopeConsts rk,
+    const float *__restrict__ freqs, __half *__restrict__ kc, __half *__restrict__ vc,
+    int n_heads, int n_kv, int chunk_len, float scale, float *__restrict__ partials,
+    const int *__restrict__ pos_dev, __half *__restrict__ out, int *__restrict__ arrivals,
+    int staged_merge) {
+  __shared__ float s_scores[G][kAttnChunk * 2];
+  __shared__ float s_out[kAttnThreads / 32][G][kAttnD];
+  __shared__ float s_m[G], s_l[G];
+  extern __shared__ __align__(16) __half s_kv[];  // [2][2 * kAttnChunk][kAttnD]
+  pdl_wait_then_release();
+  const int kvh = blockIdx.x;
+  const int chunk = blockIdx.y;
+  const int pos = *pos_dev;
+  const int seq_len = pos + 1;
+  const int p0 = chunk * chunk_len;
+  if (p0 >= seq_len) return;
+  const int p1 = min(seq_len, p0 + chunk_len);
+  const bool has_new = p1 == seq_len;        // this chunk holds row `pos`
+  const int pc = has_new ? pos : p1;          // rows [p0, pc) come from the caches
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nwarp = kAttnThreads / 32;
+  const size_t row_stride = (size_t)n_kv * kAttnD;
+  const float *qf = qkv;
+  const float *kf = qkv + (size_t)n_heads * kAttnD;
+  const float *vf = kf + row_stride;
+
+  __half *s_k = s_kv, *s_v = s_kv + 2 * kAttnChunk * kAttnD;
+  {
+    constexpr int kPiecesPerRow = kAttnD * (int)sizeof(__half) / 16;  // 16
+    const int pieces = (pc - p0) * kPiecesPerRow;
+    const uint32_t sk = (uint32_t)__cvta_generic_to_shared(s_k);
+    const uint32_t sv = (uint32_t)__cvta_generic_to_shared(s_v);
+    for (int j = threadIdx.x; j < pieces; j += kAttnThreads) {
+      const int r = j / kPiecesPerRow, c = j - r * kPiecesPerRow;
+      cp_async16(sk + (uint32_t)(r * kAttnD + c * 8) * 2,
+                 kc + (size_t)(p0 + r) * row_stride + kvh * kAttnD + c * 8);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    for (int j = threadIdx.x; j < pieces; j += kAttnThreads) {
+      const int r = j / kPiecesPerRow, c = j - r * kPiecesPerRow;
+      cp_async16(sv + (uint32_t)(r * kAttnD + c * 8) * 2,
+                 vc + (size_t)(p0 + r) * row_stride + kvh * kAttnD + c * 8);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+
+  // the new row: thread t < 64 rotates pair t of k, thread 64 + t takes pair
+  // t of v; both rounded to fp16 into the caches and the stage
+  if (has_new) {
+    const int t = threadIdx.x & 63;
+    const size_t off = ((size_t)pos * n_kv + kvh) * kAttnD + 2 * t;
+    const int srow = (pos - p0) * kAttnD + 2 * t;
+    if (threadIdx.x < 64) {
+      float x0 = kf[kvh * kAttnD + 2 * t], x1 = kf[kvh * kAttnD + 2 * t + 1];
+      if (2 * t < (int)ra.n_dims) {
+        float c, sn;
+        rope_cos_sin(ra, rk, freqs, pos, t, c, sn);
+        const float r0 = x0 * c - x1 * sn, r1 = x0 * sn + x1 * c;
+        x0 = r0;
+        x1 = r1;
+      }
+      const __half2 h = __floats2half2_rn(x0, x1);
+      *reinterpret_cast<__half2 *>(kc + off) = h;
+      *reinterpret_cast<__half2 *>(s_k + srow) = h;
+    } else {
+      const __half2 h = __floats2half2_rn(vf[kvh * kAttnD + 2 * t], vf[kvh * kAttnD + 2 * t + 1]);
+      *reinterpret_cast<__half2 *>(vc + off) = h;
+      *reinterpret_cast<__half2 *>(s_v + srow) = h;
+    }
+  }
+
+  // q of the G heads, dims 4 lane .. 4 lane + 3 (pairs 2 lane, 2 lane + 1),
+  // rotated in fp32 and scaled by 1/sqrt(d)
+  float qv[G][4];
+  {
+    float c[2] = {1.f, 1.f}, sn[2] = {0.f, 0.f};
+#pragma unroll
+    for (int e = 0; e < 2; ++e)
+      if (2 * (2 * lane + e) < (int)ra.n_dims) rope_cos_sin(ra, rk, freqs, pos, 2 * lane + e, c[e], sn[e]);
+#pragma unroll
+    for (int gh = 0; gh < G; ++gh) {
+      const float4 x = *reinterpret_cast<const float4 *>(qf + (size_t)(kvh * G + gh) * kAttnD + 4 * lane);
+      qv[gh][0] = (x.x * c[0] - x.y * sn[0]) * scale;
+      qv[gh][1] = (x.x * sn[0] + x.y * c[0]) * scale;
+      qv[gh][2] = (x.z * c[1] - x.w * sn[1]) * scale;
+      qv[gh][3] = (x.z * sn[1] + x.w * c[1]) * scale;
+    }
+  }
+
+  asm volatile("cp.async.wait_group 1;" ::: "memory");  // K landed
+  __syncthreads();
+
+  for (int p = p0 + warp; p < p1; p += nwarp) {
+    const uint2 raw = *reinterpret_cast<const uint2 *>(s_k + (p - p0) * kAttnD + 4 * lane);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
+#pragma unroll
+    for (int gh = 0; gh < G; ++gh) {
+      float sc = qv[gh][0] * a.x + qv[gh][1] * a.y + qv[gh][2] * b.x + qv[gh][3] * b.y;
+      sc = warp_sum(sc);
+      if (lane == 0) s_scores[gh][p - p0] = sc;
+    }
+  }
+  __syncthreads();
+
+  for (int gh = warp; gh < G; gh += nwarp) {
+    float m = -INFINITY;
+    for (int i = lane; i < p1 - p0; i += 32) m = fmaxf(m, s_scores[gh][i]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (int i = lane; i < p1 - p0; i += 32) {
+      const float e = __expf(s_scores[gh][i] - m);
+      s_scores[gh][i] = e;
+      l += e;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      s_m[gh] = m;
+      s_l[gh] = l;
+    }
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");  // V landed
+  __syncthreads();
+
+  float o[G][4];
+#pragma unroll
+  for (int gh = 0; gh < G; ++gh) o[gh][0] = o[gh][1] = o[gh][2] = o[gh][3] = 0.f;
+  for (int p = p0 + warp; p < p1; p += nwarp) {
+    const uint2 raw = *reinterpret_cast<const uint2 *>(s_v + (p - p0) * kAttnD + 4 * lane);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
+#pragma unroll
+    for (int gh = 0; gh < G; ++gh) {
+      const float w = s_scores[gh][p - p0];
+      o[gh][0] += w * a.x;
+      o[gh][1] += w * a.y;
+      o[gh][2] += w * b.x;
+      o[gh][3] += w * b.y;
+    }
+  }
+#pragma unroll
+  for (int gh = 0; gh < G; ++gh)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) s_out[warp][gh][4 * lane + e] = o[gh][e];
+  __syncthreads();
+
+  for (int i = threadIdx.x; i < G * kAttnD; i += kAttnThreads) {
+    const int gh = i / kAttnD, dd = i - gh * kAttnD;
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < nwarp; ++w) acc += s_out[w][gh][dd];
+    float *pp = partials + ((size_t)chunk * n_heads + kvh * G + gh) * kAttnPartial;
+    pp[2 + dd] = acc;
+    if (dd == 0) {
+      pp[0] = s_m[gh];
+      pp[1] = s_l[gh];
+    }
+  }
+
+  // the last chunk of this KV head to finish merges the chunks, in order
+  __threadfence();
+  __syncthreads();
+  __shared__ bool s_last;
+  const int nlive = (seq_len + chunk_len - 1) / chunk_len;
+  if (threadIdx.x == 0) {
+    s_last = atomicAdd(arrivals + kvh, 1) == nlive - 1;
+    if (s_last) arrivals[kvh] = 0;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  static_assert(kAttnThreads == kAttnD, "one thread per output dimension");
+  float *s_cw = &s_out[0][0][0];            // [chunk][G] chunk weights exp(m - M)
+  __shared__ float s_L[G];
+  const int dd = threadIdx.x;
+  float O[G];
+#pragma unroll
+  for (int gh = 0; gh < G; ++gh) O[gh] = 0.f;
+  if (staged_merge) {
+    // the G partials of a chunk are contiguous (G * 520 bytes, G even:
+    // 16-byte pieces): all of the head's chunks into the free stage
+    float *sp = reinterpret_cast<float *>(s_kv);  // [chunk][G][kAttnPartial]
+    const int per = G * kAttnPartial / 4;         // 16-byte pieces per chunk
+    const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(sp);
+    for (int j = threadIdx.x; j < nlive * per; j += kAttnThreads) {
+      const int c = j / per, r = j - c * per;
+      const float *src = partials + ((size_t)c * n_heads + kvh * G) * kAttnPartial + 4 * r;
+      cp_async16(sbase + (uint32_t)((c * per + r) * 16), src);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    for (int gh = warp; gh < G; gh += nwarp) {
+      float m = -INFINITY;
+      for (int c = lane; c < nlive; c += 32) m = fmaxf(m, sp[(c * G + gh) * kAttnPartial]);
+      m = warp_max(m);
+      float l = 0.f;
+      for (int c = lane; c < nlive; c += 32) {
+        const float w = __expf(sp[(c * G + gh) * kAttnPartial] - m);
+        s_cw[c * G + gh] = w;
+        l += sp[(c * G + gh) * kAttnPartial + 1] * w;
+      }
+      l = warp_sum(l);
+      if (lane == 0) s_L[gh] = l;
+    }
+    __syncthreads();
+    for (int c = 0; c < nlive; ++c) {
+#pragma unroll
+      for (int gh = 0; gh < G; ++gh)
+        O[gh] += sp[(c * G + gh) * kAttnPartial + 2 + dd] * s_cw[c * G + gh];
+    }
+  } else {
+    float *s_cm = s_cw + kAttnMaxChunks * G;  // [chunk][G] chunk maxima
+    float *s_cl = s_cm + kAttnMaxChunks * G;  // [chunk][G] chunk sums
+    for (int i = threadIdx.x; i < nlive * G; i += kAttnThreads) {
+      const float *pp = partials + ((size_t)(i / G) * n_heads + kvh * G) * kAttnPartial +
+                        (i % G) * kAttnPartial;
+      s_cm[i] = __ldcg(pp);
+      s_cl[i] = __ldcg(pp + 1);
+    }
+    __syncthreads();
+    for (int gh = warp; gh < G; gh += nwarp) {
+      float m = -INFINITY;
+      for (int c = lane; c < nlive; c += 32) m = fmaxf(m, s_cm[c * G + gh]);
+      m = warp_max(m);
+      float l = 0.f;
+      for (int c = lane; c < nlive; c += 32) {
+        const float w = __expf(s_cm[c * G + gh] - m);
+        s_cw[c * G + gh] = w;
+        l += s_cl[c * G + gh] * w;
+      }
+      l = warp_sum(l);
+      if (lane == 0) s_L[gh] = l;
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int c = 0; c < nlive; ++c) {
+      const float *pcp = partials + ((size_t)c * n_heads + kvh * G) * kAttnPartial + 2 + dd;
+#pragma unroll
+      for (int gh = 0; gh < G; ++gh) O[gh] += __ldcg(pcp + gh * kAttnPartial) * s_cw[c * G + gh];
+    }
+  }
+#pragma unroll
+  for (int gh = 0; gh < G; ++gh)
+    out[(size_t)(kvh * G + gh) * kAttnD + dd] = __float2half_rn(O[gh] / s_L[gh]);
+}
+
+// Chunk length of the fused step for a cache of `capacity` positions: the
+// shortest (>= 32, a multiple of 16) whose chunk count lets the merge stage
+// all partials of a KV head in shared memory; else 128-position chunks and
+// the merge from L2.
+static void attn_rope_chunks(int capacity, int G, int &chunk_len, int &nchunks, bool &staged) {
+  const int fit = (G % 2 == 0) ? kAttnStageBytes / (G * kAttnPartial * 4) : 0;
+  const int nmax = std::min(kAttnMaxChunks, fit);
+  if (nmax > 0) {
+    int cl = (capacity + nmax - 1) / nmax;
+    cl = std::max(32, (cl + 15) / 16 * 16);
+    if (cl <= 2 * kAttnChunk) {
+      chunk_len = cl;
+      nchunks = (capacity + cl - 1) / cl;
+      staged = true;
+      return;
+    }
+  }
+  chunk_len = 2 * kAttnChunk;
+  nchunks = (capacity + chunk_len - 1) / chunk_len;
+  staged = false;
+}
+
+int attn_rope_decode_launch(mlm_ctx *ctx, const float *qkv, const float *freqs,
+                            const mlm_rope_args &ra, int n_heads, int n_kv, int head_dim,
+                            int capacity, void *kc, void *vc, void *out, float *partials,
+                            size_t partial_floats, cudaStream_t stream, const int *pos_dev) {
+  MLM_REQUIRE(ctx, head_dim == kAttnD, MLM_ERR_UNSUPPORTED,
+              "attention: head_dim=%d (this build handles %d)", head_dim, kAttnD);
+  MLM_REQUIRE(ctx, n_kv > 0 && n_heads % n_kv == 0, MLM_ERR_SHAPE,
+              "attention: %d query heads not a multiple of %d KV heads", n_heads, n_kv);
+  MLM_REQUIRE(ctx, n_kv <= kAttnMaxArrivals, MLM_ERR_SHAPE, "attention: %d KV heads", n_kv);
+  const int G = n_heads / n_kv;
+  MLM_REQUIRE(ctx, G == 1 || G == 2 || G == 4 || G == 8, MLM_ERR_UNSUPPORTED,
+              "attention: GQA group %d (supported 1, 2, 4, 8)", G);
+  int chunk_len, nchunks;
+  bool staged;
+  attn_rope_chunks(capacity, G, chunk_len, nchunks, staged);
+  MLM_REQUIRE(ctx, nchunks <= kAttnMaxChunks, MLM_ERR_SHAPE,
+              "attention: cache capacity %d exceeds %d positions", capacity,
+              2 * kAttnChunk * kAttnMaxChunks);
+  MLM_REQUIRE(ctx, (size_t)nchunks * n_heads * kAttnPartial <= partial_floats, MLM_ERR_SHAPE,
+              "attention: %d heads exceed the attention scratch", n_heads);
+  const RopeConsts rk = rope_consts(ra);
+  const float scale = 1.0f / sqrtf((float)head_dim);
+  auto kern = G == 1   ? attn_rope_decode_kernel<1>
+              : G == 2 ? attn_rope_decode_kernel<2>
+              : G == 4 ? attn_rope_decode_kernel<4>
+                       : attn_rope_decode_kernel<8>;
+  return check_launch_pdl(
+      ctx,
+      launch_pdl(kern, dim3(n_kv, nchunks), dim3(kAttnThreads), kAttnStageBytes, stream, qkv, ra,
+                 rk, freqs, reinterpret_cast<__half *>(kc), reinterpret_cast<__half *>(vc),
+                 n_heads, n_kv, chunk_len, scale, partials, pos_dev,
+                 reinterpret_cast<__half *>(out), ctx->attn_arrivals, staged ? 1 : 0),
+      "attention (RoPE, append, decode)");
+}
+
 // seq_len positions, or, when pos_dev is set, pos_dev[b] + 1 positions read
 // on the device out of a cache of capacity seq_len (a launch a captured graph
 // can replay at every step): fixed 128-position chunks covering the capacity.
@@ -367,6 +687,14 @@ static int attn_init_out(mlm_ctx *ctx) {
 }
 
 int attn_init(mlm_ctx *ctx) {
+  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_rope_decode_kernel<1>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnStageBytes));
+  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_rope_decode_kernel<2>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnStageBytes));
+  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_rope_decode_kernel<4>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnStageBytes));
+  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_rope_decode_kernel<8>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnStageBytes));
   int st = attn_init_out<__half, true>(ctx);
   if (st == MLM_OK) st = attn_init_out<__half, false>(ctx);
   if (st == MLM_OK) st = attn_init_out<__nv_bfloat16, true>(ctx);

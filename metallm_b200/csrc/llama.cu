@@ -49,7 +49,10 @@ namespace {
 
 struct LayerBuf {
   float *attn_norm, *ffn_norm;
-  uint8_t *qkv, *wo, *gu, *down;  // Q4_K
+  // Q4_K, except wv and down, which are Q6_K when v_type / down_type say so
+  // (Q4_K_M files); a Q4_K wv is the last rows of qkv, a Q6_K one separate
+  uint8_t *qkv, *wo, *gu, *down, *wv6 = nullptr;
+  int v_type = MLM_TYPE_Q4_K, down_type = MLM_TYPE_Q4_K;
   __half *kc, *vc;
 };
 
@@ -84,6 +87,11 @@ __global__ void advance_batch_kernel(int *st, int *pos, const int32_t *tok, int3
 }
 
 inline size_t q4k_row_bytes(int cols) { return (size_t)(cols / kQK) * kBlockBytes; }
+constexpr int kQ6BlockBytes = 210;
+inline size_t q6k_row_bytes(int cols) { return (size_t)(cols / kQK) * kQ6BlockBytes; }
+inline size_t row_bytes(int type, int cols) {
+  return type == MLM_TYPE_Q6_K ? q6k_row_bytes(cols) : q4k_row_bytes(cols);
+}
 
 }  // namespace
 }  // namespace mlm
@@ -98,15 +106,18 @@ struct mlm_llama {
   __half *tok_embd = nullptr;
   float *out_norm = nullptr;
   uint8_t *output = nullptr;
+  int output_type = MLM_TYPE_Q4_K;
+  void *q6_scratch = nullptr;  // bf16 copy of a Q6_K weight for the GEMMs
   float *rope_freqs = nullptr;
   // activations of one step
   float *hidden = nullptr, *qkv_out = nullptr, *gu_out = nullptr, *logits = nullptr;
-  __half *q16 = nullptr, *attn_out = nullptr;
+  __half *attn_out = nullptr;
   int *state = nullptr;
   int32_t *gen_tokens = nullptr;  // [max_seq] tokens of the captured greedy loop
   // batched prompt pass: activations of up to pf_chunk tokens
   int pf_chunk = 0;
   float *pf_hidden = nullptr, *pf_qkv = nullptr, *pf_gu = nullptr;
+  float *pf_tmp = nullptr;  // q/k rows and v rows apart when V is Q6_K
   void *pf_x = nullptr, *pf_q16 = nullptr, *pf_attn = nullptr;  // bf16 / fp16 / bf16
   int32_t *pf_tokens = nullptr;
   cudaGraph_t step_graph = nullptr;
@@ -142,6 +153,10 @@ struct mlm_llama {
   int qdim() const { return nh() * cfg.head_dim; }
   int kvdim() const { return nkv() * cfg.head_dim; }
   int qkv_rows() const { return qdim() + 2 * kvdim(); }
+  // rows of layer l's Q4_K QKV matrix (q, k and, when V is Q4_K, v)
+  int qkv4_rows(const LayerBuf &L) const {
+    return L.v_type == MLM_TYPE_Q6_K ? qdim() + kvdim() : qkv_rows();
+  }
 
   template <class T>
   int alloc(T **p, size_t bytes) {
@@ -173,17 +188,18 @@ struct mlm_llama {
     const LayerBuf &L = layers[l];
     const mlm_llama_config &c = cfg;
     cudaStream_t s = ctx->stream;
-    const int kvd = kvdim();
     int st;
     // RMSNorm runs inside the GEMV's x staging
-    if ((st = gemv(L.qkv, qkv_rows(), c.dim, normed(h, L.attn_norm), qkv_out, nullptr))) return st;
-    if ((st = rope_qk_kv_launch(ctx, qkv_out, qkv_out + qdim(), qkv_out + qdim() + kvd, rope_freqs,
-                                c.rope, nh(), nkv(), c.head_dim, q16, L.kc, L.vc, 0, s,
-                                state + kPos)))
+    if ((st = gemv(L.qkv, qkv4_rows(L), c.dim, normed(h, L.attn_norm), qkv_out, nullptr)))
       return st;
-    if ((st = attn_decode_launch(ctx, q16, L.kc, L.vc, nh(), nkv(), c.head_dim, c.max_seq,
-                                 attn_out, ctx->attn_partials, ctx->attn_partials_floats, s,
-                                 state + kPos)))
+    if (L.v_type == MLM_TYPE_Q6_K &&
+        (st = q6k_gemv_launch(ctx, L.wv6, kvdim(), c.dim, normed(h, L.attn_norm),
+                              qkv_out + qdim() + kvdim(), nullptr, s)))
+      return st;
+    // RoPE of q and k, the KV append and the attention in one launch
+    if ((st = attn_rope_decode_launch(ctx, qkv_out, rope_freqs, c.rope, nh(), nkv(), c.head_dim,
+                                      c.max_seq, L.kc, L.vc, attn_out, ctx->attn_partials,
+                                      ctx->attn_partials_floats, s, state + kPos)))
       return st;
     if ((st = row_parallel(L.wo, qdim(), gemv_half(attn_out), h))) return st;  // + residual
     if ((st = gemv(L.gu, 2 * ffn(), c.dim, normed(h, L.ffn_norm), gu_out, nullptr))) return st;
@@ -194,15 +210,23 @@ struct mlm_llama {
     sw.mode = GemvInput::kSwiGLU;
     sw.a = gu_out;
     sw.b = gu_out + ffn();
-    return row_parallel(L.down, ffn(), sw, h);  // + residual
+    return row_parallel(L.down, ffn(), sw, h, L.down_type);  // + residual
+  }
+
+  // a decode GEMV on a weight of either type
+  int gemv_t(int type, const uint8_t *W, int rows, int cols, const GemvInput &in, float *y,
+             const float *res) {
+    if (type == MLM_TYPE_Q6_K) return q6k_gemv_launch(ctx, W, rows, cols, in, y, res, ctx->stream);
+    return gemv(W, rows, cols, in, y, res);
   }
 
   // h += W x for a projection whose input columns are split over the ranks:
   // in place on one GPU; with TP, rank 0's partial carries the residual and
   // the sum all-reduce writes h on every rank
-  int row_parallel(const uint8_t *W, int cols, const GemvInput &in, float *h) {
-    if (!tp_on) return gemv(W, cfg.dim, cols, in, h, h);
-    int st = gemv(W, cfg.dim, cols, in, part, rank == 0 ? h : nullptr);
+  int row_parallel(const uint8_t *W, int cols, const GemvInput &in, float *h,
+                   int type = MLM_TYPE_Q4_K) {
+    if (!tp_on) return gemv_t(type, W, cfg.dim, cols, in, h, h);
+    int st = gemv_t(type, W, cfg.dim, cols, in, part, rank == 0 ? h : nullptr);
     if (st != MLM_OK) return st;
     return tp_allreduce_sum(ctx, part, h, cfg.dim, ctx->stream);
   }
@@ -213,10 +237,13 @@ struct mlm_llama {
     int st;
     if (!tp_on) {
       float *lg = lg_out ? lg_out : logits;
-      if ((st = gemv(output, cfg.vocab, cfg.dim, normed(h, out_norm), lg, nullptr))) return st;
+      if ((st = gemv_t(output_type, output, cfg.vocab, cfg.dim, normed(h, out_norm), lg, nullptr)))
+        return st;
       return argmax_launch(ctx, lg, cfg.vocab, state + kToken, ctx->stream);
     }
-    if ((st = gemv(output, vocab_l(), cfg.dim, normed(h, out_norm), logits_l, nullptr))) return st;
+    if ((st = gemv_t(output_type, output, vocab_l(), cfg.dim, normed(h, out_norm), logits_l,
+                     nullptr)))
+      return st;
     if ((st = argmax_key_launch(ctx, logits_l, vocab_l(), rank * vocab_l(), key_l, ctx->stream)))
       return st;
     if ((st = tp_allgather_bytes(ctx, key_l, keys, sizeof(unsigned long long), ctx->stream)))
@@ -252,7 +279,7 @@ struct mlm_llama {
       const LayerBuf &L = layers[l];
       if ((st = rmsnorm_rows_bf16_launch(ctx, pf_hidden, L.attn_norm, pf_x, T, c.dim, c.rms_eps, s)))
         return st;
-      if ((st = linear(L.qkv, qkv_rows(), c.dim, pf_x, T, pf_qkv, nullptr))) return st;
+      if ((st = qkv_rows_linear(L, pf_x, T))) return st;
       __half *kc = L.kc + cur * seq_elems(), *vc = L.vc + cur * seq_elems();
       if ((st = rope_kv_rows_launch(ctx, pf_qkv, rope_freqs, c.rope, nh(), nkv(), c.head_dim, pos,
                                     T, pf_q16, kc, vc, s)))
@@ -265,9 +292,23 @@ struct mlm_llama {
         return st;
       if ((st = linear(L.gu, 2 * ffn(), c.dim, pf_x, T, pf_gu, nullptr))) return st;
       if ((st = swiglu_rows_bf16_launch(ctx, pf_gu, ffn(), T, pf_x, s))) return st;
-      if ((st = row_parallel_rows(L.down, ffn(), pf_x, T))) return st;
+      if ((st = row_parallel_rows(L.down, ffn(), pf_x, T, L.down_type))) return st;
     }
     return MLM_OK;
+  }
+
+  // pf_qkv = X Wqkv^T over T rows [T][q | k | v]: one Q4_K linear, or the
+  // Q4_K q/k rows and the Q6_K v rows written beside them
+  int qkv_rows_linear(const LayerBuf &L, const void *x, int T) {
+    if (L.v_type != MLM_TYPE_Q6_K) return linear(L.qkv, qkv_rows(), cfg.dim, x, T, pf_qkv, nullptr);
+    const int r4 = qkv4_rows(L);
+    int st = linear(L.qkv, r4, cfg.dim, x, T, pf_tmp, nullptr);
+    if (st != MLM_OK) return st;
+    if ((st = linear_t(MLM_TYPE_Q6_K, L.wv6, kvdim(), cfg.dim, x, T, pf_tmp + (size_t)T * r4,
+                       nullptr)))
+      return st;
+    return interleave_rows_launch(ctx, pf_tmp, r4, pf_tmp + (size_t)T * r4, kvdim(), T, pf_qkv,
+                                  ctx->stream);
   }
 
   // one decode step of every sequence of the batch (token tok_b[b] at
@@ -285,7 +326,7 @@ struct mlm_llama {
       const LayerBuf &L = layers[l];
       if ((st = rmsnorm_rows_bf16_launch(ctx, pf_hidden, L.attn_norm, pf_x, B, c.dim, c.rms_eps, s)))
         return st;
-      if ((st = linear(L.qkv, qkv_rows(), c.dim, pf_x, B, pf_qkv, nullptr))) return st;
+      if ((st = qkv_rows_linear(L, pf_x, B))) return st;
       if ((st = rope_kv_batch_launch(ctx, pf_qkv, rope_freqs, c.rope, nh(), nkv(), c.head_dim, B,
                                      pos_b, seq_elems(), pf_q16, L.kc, L.vc, s)))
         return st;
@@ -298,11 +339,21 @@ struct mlm_llama {
         return st;
       if ((st = linear(L.gu, 2 * ffn(), c.dim, pf_x, B, pf_gu, nullptr))) return st;
       if ((st = swiglu_rows_bf16_launch(ctx, pf_gu, ffn(), B, pf_x, s))) return st;
-      if ((st = row_parallel_rows(L.down, ffn(), pf_x, B))) return st;
+      if ((st = row_parallel_rows(L.down, ffn(), pf_x, B, L.down_type))) return st;
     }
-    if ((st = rmsnorm_rows_bf16_launch(ctx, pf_hidden, out_norm, pf_x, B, c.dim, c.rms_eps, s)))
-      return st;
-    if ((st = linear(output, vocab_l(), c.dim, pf_x, B, b_logits, nullptr))) return st;
+    if (output_type == MLM_TYPE_Q6_K) {
+      // a Q6_K head: one GEMV per row, RMSNorm in its staging (a bf16 copy
+      // of the head would not fit the scratch)
+      for (int b = 0; b < B; ++b)
+        if ((st = q6k_gemv_launch(ctx, output, vocab_l(), c.dim,
+                                  normed(pf_hidden + (size_t)b * c.dim, out_norm),
+                                  b_logits + (size_t)b * vocab_l(), nullptr, s)))
+          return st;
+    } else {
+      if ((st = rmsnorm_rows_bf16_launch(ctx, pf_hidden, out_norm, pf_x, B, c.dim, c.rms_eps, s)))
+        return st;
+      if ((st = linear(output, vocab_l(), c.dim, pf_x, B, b_logits, nullptr))) return st;
+    }
     for (int b = 0; b < B; ++b) {
       st = tp_on ? argmax_key_launch(ctx, b_logits + (size_t)b * vocab_l(), vocab_l(),
                                      rank * vocab_l(), b_keys_l + b, s)
@@ -336,12 +387,19 @@ struct mlm_llama {
     if (T <= 8) return gemv_batch_launch(ctx, W, rows, cols, x, T, y, res, ctx->stream);
     return gemm_launch(ctx, W, rows, cols, x, T, y, res, ctx->stream);
   }
+  // a Q6_K weight goes through its bf16 copy in q6_scratch and the GEMM
+  int linear_t(int type, const uint8_t *W, int rows, int cols, const void *x, int T, float *y,
+               const float *res) {
+    if (type != MLM_TYPE_Q6_K) return linear(W, rows, cols, x, T, y, res);
+    return q6k_gemm_launch(ctx, W, rows, cols, x, T, y, res, q6_scratch, ctx->stream);
+  }
 
   // pf_hidden += X W^T over T rows for a projection with split input
   // columns (see row_parallel)
-  int row_parallel_rows(const uint8_t *W, int cols, const void *x, int T) {
-    if (!tp_on) return linear(W, cfg.dim, cols, x, T, pf_hidden, pf_hidden);
-    int st = linear(W, cfg.dim, cols, x, T, pf_part, rank == 0 ? pf_hidden : nullptr);
+  int row_parallel_rows(const uint8_t *W, int cols, const void *x, int T,
+                        int type = MLM_TYPE_Q4_K) {
+    if (!tp_on) return linear_t(type, W, cfg.dim, cols, x, T, pf_hidden, pf_hidden);
+    int st = linear_t(type, W, cfg.dim, cols, x, T, pf_part, rank == 0 ? pf_hidden : nullptr);
     if (st != MLM_OK) return st;
     return tp_allreduce_sum(ctx, pf_part, pf_hidden, (size_t)T * cfg.dim, ctx->stream);
   }
@@ -361,11 +419,20 @@ struct mlm_llama {
   }
 };
 
-static int llama_create(mlm_ctx *ctx, const mlm_llama_config *cfg, int batch, mlm_llama **out) {
+static bool known_type(int t) { return t == MLM_TYPE_Q4_K || t == MLM_TYPE_Q6_K; }
+
+static int llama_create(mlm_ctx *ctx, const mlm_llama_config *cfg, int batch,
+                        const mlm_llama_types *types, mlm_llama **out) {
   MLM_CHECK_CTX(ctx);
   MLM_REQUIRE(ctx, cfg && out, MLM_ERR_ARG, "mlm_llama_create: null argument");
   *out = nullptr;
   const mlm_llama_config &c = *cfg;
+  // tensor types: everything Q4_K unless types says otherwise
+  const int out_type = types ? types->output : MLM_TYPE_Q4_K;
+  auto v_type = [&](int l) { return types && types->attn_v ? types->attn_v[l] : MLM_TYPE_Q4_K; };
+  auto d_type = [&](int l) {
+    return types && types->ffn_down ? types->ffn_down[l] : MLM_TYPE_Q4_K;
+  };
   MLM_REQUIRE(ctx, batch >= 1 && batch <= 64 && batch <= std::min(c.max_seq, 1024), MLM_ERR_SHAPE,
               "mlm_llama_create_batch: batch %d (1 .. min(64, max_seq))", batch);
   MLM_REQUIRE(ctx, c.n_layers > 0 && c.vocab > 0 && c.max_seq > 0 && c.max_seq <= 8192,
@@ -384,6 +451,25 @@ static int llama_create(mlm_ctx *ctx, const mlm_llama_config *cfg, int batch, ml
   MLM_REQUIRE(ctx, 2 * c.ffn_dim <= ctx->gemv_max_tiles * 32 && c.vocab <= ctx->gemv_max_tiles * 32,
               MLM_ERR_SHAPE, "mlm_llama_create: matrices exceed the GEMV row limit");
   const int tp = ctx->tp_comm ? ctx->tp_size : 1;
+  bool any_v6 = false, any_d6 = false;
+  MLM_REQUIRE(ctx, known_type(out_type), MLM_ERR_UNSUPPORTED,
+              "mlm_llama_create: output type %d (Q4_K %d or Q6_K %d)", out_type, MLM_TYPE_Q4_K,
+              MLM_TYPE_Q6_K);
+  for (int l = 0; l < c.n_layers; ++l) {
+    MLM_REQUIRE(ctx, known_type(v_type(l)) && known_type(d_type(l)), MLM_ERR_UNSUPPORTED,
+                "mlm_llama_create: layer %d attn_v type %d / ffn_down type %d (Q4_K %d or Q6_K %d)",
+                l, v_type(l), d_type(l), MLM_TYPE_Q4_K, MLM_TYPE_Q6_K);
+    any_v6 |= v_type(l) == MLM_TYPE_Q6_K;
+    any_d6 |= d_type(l) == MLM_TYPE_Q6_K;
+  }
+  // the Q6_K decode GEMV reads whole 8-block (2048-column) chunks
+  MLM_REQUIRE(ctx,
+              ((!any_v6 && out_type != MLM_TYPE_Q6_K) || c.dim % 2048 == 0) &&
+                  (!any_d6 || (c.ffn_dim / tp) % 2048 == 0),
+              MLM_ERR_UNSUPPORTED,
+              "mlm_llama_create: Q6_K tensors need a multiple of 2048 input columns per rank "
+              "(dim %d, FFN %d over %d ranks)",
+              c.dim, c.ffn_dim, tp);
   if (ctx->tp_comm) {
     // heads, FFN rows and the vocabulary split evenly; the split input
     // columns of the output and down projections stay whole Q4_K blocks
@@ -411,27 +497,35 @@ static int llama_create(mlm_ctx *ctx, const mlm_llama_config *cfg, int batch, ml
     delete m;
     return code;
   };
-  const size_t rb_dim = q4k_row_bytes(c.dim), rb_ffn = q4k_row_bytes(m->ffn()),
-               rb_q = q4k_row_bytes(m->qdim());
+  const size_t rb_dim = q4k_row_bytes(c.dim), rb_q = q4k_row_bytes(m->qdim());
   const size_t cache_bytes = (size_t)batch * c.max_seq * m->kvdim() * sizeof(__half);
+  m->output_type = out_type;
   m->layers.resize(c.n_layers);
   for (int l = 0; l < c.n_layers; ++l) {
     LayerBuf &L = m->layers[l];
+    L.v_type = v_type(l);
+    L.down_type = d_type(l);
     if (m->alloc(&L.attn_norm, sizeof(float) * c.dim) || m->alloc(&L.ffn_norm, sizeof(float) * c.dim) ||
-        m->alloc(&L.qkv, (size_t)m->qkv_rows() * rb_dim) || m->alloc(&L.wo, (size_t)c.dim * rb_q) ||
-        m->alloc(&L.gu, (size_t)2 * m->ffn() * rb_dim) || m->alloc(&L.down, (size_t)c.dim * rb_ffn) ||
+        m->alloc(&L.qkv, (size_t)m->qkv4_rows(L) * rb_dim) || m->alloc(&L.wo, (size_t)c.dim * rb_q) ||
+        m->alloc(&L.gu, (size_t)2 * m->ffn() * rb_dim) ||
+        m->alloc(&L.down, (size_t)c.dim * row_bytes(L.down_type, m->ffn())) ||
+        (L.v_type == MLM_TYPE_Q6_K &&
+         m->alloc(&L.wv6, (size_t)m->kvdim() * q6k_row_bytes(c.dim))) ||
         m->alloc(&L.kc, cache_bytes) || m->alloc(&L.vc, cache_bytes))
       return fail(MLM_ERR_ALLOC);
   }
+  // bf16 copy of the largest Q6_K weight the prompt GEMMs read
+  const size_t scratch_elems = std::max(any_v6 ? (size_t)m->kvdim() * c.dim : 0,
+                                        any_d6 ? (size_t)c.dim * m->ffn() : 0);
+  if (scratch_elems && m->alloc(&m->q6_scratch, 2 * scratch_elems)) return fail(MLM_ERR_ALLOC);
   if (m->alloc(&m->tok_embd, (size_t)c.vocab * c.dim * sizeof(__half)) ||
       m->alloc(&m->out_norm, sizeof(float) * c.dim) ||
-      m->alloc(&m->output, (size_t)m->vocab_l() * rb_dim) ||
+      m->alloc(&m->output, (size_t)m->vocab_l() * row_bytes(out_type, c.dim)) ||
       m->alloc(&m->rope_freqs, sizeof(float) * (c.head_dim / 2)) ||
       m->alloc(&m->hidden, sizeof(float) * c.dim) ||
       m->alloc(&m->qkv_out, sizeof(float) * m->qkv_rows()) ||
       m->alloc(&m->gu_out, sizeof(float) * 2 * m->ffn()) ||
       m->alloc(&m->logits, sizeof(float) * c.vocab) ||
-      m->alloc(&m->q16, sizeof(__half) * m->qdim()) ||
       m->alloc(&m->attn_out, sizeof(__half) * m->qdim()) ||
       m->alloc(&m->state, sizeof(int) * kStateInts) ||
       m->alloc(&m->gen_tokens, sizeof(int32_t) * c.max_seq))
@@ -444,7 +538,8 @@ static int llama_create(mlm_ctx *ctx, const mlm_llama_config *cfg, int batch, ml
         m->alloc(&m->pf_qkv, sizeof(float) * T * m->qkv_rows()) ||
         m->alloc(&m->pf_gu, sizeof(float) * T * 2 * m->ffn()) ||
         m->alloc(&m->pf_x, 2 * T * xw) || m->alloc(&m->pf_q16, 2 * T * m->qdim()) ||
-        m->alloc(&m->pf_attn, 2 * T * m->qdim()) || m->alloc(&m->pf_tokens, sizeof(int32_t) * T))
+        m->alloc(&m->pf_attn, 2 * T * m->qdim()) || m->alloc(&m->pf_tokens, sizeof(int32_t) * T) ||
+        (any_v6 && m->alloc(&m->pf_tmp, sizeof(float) * T * m->qkv_rows())))
       return fail(MLM_ERR_ALLOC);
     m->b_partial_floats = (size_t)batch * attn_decode_partial_floats(m->nh(), c.max_seq);
     if (m->alloc(&m->pos_b, sizeof(int) * batch) || m->alloc(&m->tok_b, sizeof(int32_t) * batch) ||
@@ -469,12 +564,17 @@ static int llama_create(mlm_ctx *ctx, const mlm_llama_config *cfg, int batch, ml
 }
 
 extern "C" int mlm_llama_create(mlm_ctx *ctx, const mlm_llama_config *cfg, mlm_llama **out) {
-  return llama_create(ctx, cfg, 1, out);
+  return llama_create(ctx, cfg, 1, nullptr, out);
 }
 
 extern "C" int mlm_llama_create_batch(mlm_ctx *ctx, const mlm_llama_config *cfg, int batch,
                                       mlm_llama **out) {
-  return llama_create(ctx, cfg, batch, out);
+  return llama_create(ctx, cfg, batch, nullptr, out);
+}
+
+extern "C" int mlm_llama_create_typed(mlm_ctx *ctx, const mlm_llama_config *cfg, int batch,
+                                      const mlm_llama_types *types, mlm_llama **out) {
+  return llama_create(ctx, cfg, batch, types, out);
 }
 
 extern "C" void mlm_llama_destroy(mlm_llama *m) {
@@ -494,7 +594,9 @@ extern "C" int mlm_llama_layer_tensors(mlm_llama *m, int layer, mlm_llama_layer 
   out->ffn_norm = L.ffn_norm;
   out->wq = L.qkv;
   out->wk = L.qkv + (size_t)m->qdim() * rb;
-  out->wv = L.qkv + (size_t)(m->qdim() + m->kvdim()) * rb;
+  out->wv = L.v_type == MLM_TYPE_Q6_K ? L.wv6 : L.qkv + (size_t)(m->qdim() + m->kvdim()) * rb;
+  out->wv_type = L.v_type;
+  out->w_down_type = L.down_type;
   out->wo = L.wo;
   out->w_gate = L.gu;
   out->w_up = L.gu + (size_t)m->ffn() * rb;
@@ -510,6 +612,7 @@ extern "C" int mlm_llama_global_tensors(mlm_llama *m, mlm_llama_globals *out) {
   out->tok_embd = m->tok_embd;
   out->output_norm = m->out_norm;
   out->output = m->output;
+  out->output_type = m->output_type;
   out->rope_freqs = m->rope_freqs;
   return MLM_OK;
 }

@@ -67,6 +67,21 @@ int set_error(mlm_ctx *ctx, int code, const char *fmt, ...)
     __attribute__((format(printf, 3, 4)));
 int check_launch(mlm_ctx *ctx, const char *what);
 int q6k_init(mlm_ctx *ctx);  // q6k.cu: the GEMV's shared-memory limit
+struct GemvInput;
+// the Q6_K decode GEMV with the Q4_K GEMV's x modes (cols a multiple of 2048)
+int q6k_gemv_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const GemvInput &in,
+                    float *y, const float *residual, cudaStream_t stream);
+int q6k_dequant_bf16_launch(mlm_ctx *ctx, const void *blocks, void *out, uint64_t n,
+                            cudaStream_t stream);
+int interleave_rows_launch(mlm_ctx *ctx, const float *a, int ra, const float *b, int rb, int T,
+                           float *out, cudaStream_t stream);
+// the prompt GEMM on a bf16 weight [rows][cols] (tokens of bf16 x)
+int gemm_dense_launch(mlm_ctx *ctx, const void *W_bf16, int rows, int cols, const void *x_bf16,
+                      int tokens, float *y, const float *residual, cudaStream_t stream);
+// the same for a Q6_K weight, dequantized to bf16 into scratch (rows x cols)
+int q6k_gemm_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_bf16,
+                    int tokens, float *y, const float *residual, void *scratch_bf16,
+                    cudaStream_t stream);
 
 // Launch as a programmatic dependent of the previous kernel on the stream:
 // the grid may be scheduled once every CTA of that kernel has executed
@@ -135,6 +150,14 @@ int rope_qk_kv_launch(mlm_ctx *ctx, const float *q, const float *k, const float 
                       const float *freqs, const mlm_rope_args &a, int nq, int nkv, int d,
                       void *q_out, void *kc, void *vc, int pos, cudaStream_t stream,
                       const int *pos_dev);
+// one decode step of one sequence with RoPE and the KV append folded in:
+// qkv = the QKV projection in fp32 (q, then k, then v), the position at
+// pos_dev; appends row pos_dev[0] to kc/vc (capacity positions) and writes
+// the fp16 attention output [n_heads][128]
+int attn_rope_decode_launch(mlm_ctx *ctx, const float *qkv, const float *freqs,
+                            const mlm_rope_args &ra, int n_heads, int n_kv, int head_dim,
+                            int capacity, void *kc, void *vc, void *out, float *partials,
+                            size_t partial_floats, cudaStream_t stream, const int *pos_dev);
 int attn_decode_launch(mlm_ctx *ctx, const void *q, const void *kc, const void *vc, int n_heads,
                        int n_kv, int head_dim, int seq_len, void *out, float *partials,
                        size_t partial_floats, cudaStream_t stream, const int *pos_dev);

@@ -167,6 +167,17 @@ int mlm_q6k_dequant_bf16(mlm_ctx *ctx, const void *blocks, void *out_bf16, uint6
  * 16-byte aligned.  Stream-ordered. */
 int mlm_q6k_gemv(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_f16, float *y,
                  const float *residual);
+/* The same GEMV with the x stagings of the Q4_K GEMVs (mlm_q4k_gemv_xs,
+ * _rmsnorm, _swiglu below), for the Q6_K linears of Q4_K_M files: attn_v and
+ * ffn_down (read after RMSNorm and after the SiLU-gated product,
+ * LlamaRunner.swift:547-609, 1036-1068) and the output head
+ * (:1130-1178). */
+int mlm_q6k_gemv_xs(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_f16,
+                    const float *x_scale, float *y, const float *residual);
+int mlm_q6k_gemv_rmsnorm(mlm_ctx *ctx, const void *W, int rows, int cols, const float *hidden,
+                         const float *norm_w, float eps, float *y, const float *residual);
+int mlm_q6k_gemv_swiglu(mlm_ctx *ctx, const void *W, int rows, int cols, const float *gate,
+                        const float *up, float *y, const float *residual);
 
 /* MetalService.dequantizeQ4KM_to_f32 / _f16 (MetalService.swift:170, 243):
  * allocate the output, run, wait.  *out receives a device pointer to free
@@ -232,6 +243,13 @@ int mlm_q4k_gemv_batch(mlm_ctx *ctx, const void *W, int rows, int cols, const vo
 
 int mlm_q4k_gemm(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_bf16,
                  int tokens, float *y, const float *residual);
+/* The prompt linears on a Q6_K weight (encodeMPSMatrixMultiply on the
+ * weight ModelLoader.swift:282-287 dequantizes): W is dequantized into the
+ * caller's scratch (rows x cols bf16, 16-byte aligned: the fp32 value
+ * rounded once, as mlm_q6k_dequant_bf16) and the tensor-core GEMM reads it
+ * there; same X, Y and residual conventions as mlm_q4k_gemm. */
+int mlm_q6k_gemm(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_bf16,
+                 int tokens, float *y, const float *residual, void *scratch_bf16);
 
 /* No counterpart in the reference.  mlm_q4k_gemv with its split-K scratch
  * in a static 80 KB device array inside the library instead of the
@@ -383,14 +401,30 @@ typedef struct mlm_llama_layer {
   float *ffn_norm; /* fp32 [dim] */
   void *w_gate, *w_up, *w_down;
   void *k_cache, *v_cache;
+  int32_t wv_type, w_down_type; /* MLM_TYPE_Q4_K or MLM_TYPE_Q6_K (210-byte blocks) */
 } mlm_llama_layer;
 
 typedef struct mlm_llama_globals {
   void *tok_embd;     /* fp16 [vocab][dim] */
   float *output_norm; /* fp32 [dim] */
-  void *output;       /* Q4_K [vocab][dim/256] */
+  void *output;       /* Q4_K (or Q6_K) [vocab][dim/256] */
   float *rope_freqs;  /* fp32 [head_dim/2], read when rope.has_freq_factors */
+  int32_t output_type;
 } mlm_llama_globals;
+
+/* GGUF tensor types (the ggml_type values of the file's tensor table,
+ * GGUF.swift:63) a runner's linears may hold. */
+#define MLM_TYPE_Q4_K 12
+#define MLM_TYPE_Q6_K 14
+
+/* Per-tensor types of a Q4_K_M file: its output head and, per layer, attn_v
+ * and ffn_down may be Q6_K (ModelLoader.swift:274-296 dequantizes each
+ * tensor by its own type).  NULL arrays: every layer Q4_K. */
+typedef struct mlm_llama_types {
+  int32_t output;
+  const int32_t *attn_v;   /* [n_layers] */
+  const int32_t *ffn_down; /* [n_layers] */
+} mlm_llama_types;
 
 typedef struct mlm_llama mlm_llama;
 
@@ -456,6 +490,12 @@ int mlm_llama_decode_greedy(mlm_llama *m, int token, int steps, int32_t *tokens_
  * i-th token (one batched step captured once as a CUDA graph and replayed).
  * Every sequence advances by one position per step. */
 int mlm_llama_create_batch(mlm_ctx *ctx, const mlm_llama_config *cfg, int batch, mlm_llama **out);
+/* mlm_llama_create_batch with per-tensor types (mlm_llama_types; NULL: all
+ * Q4_K).  Q6_K tensors need a multiple of 2048 input columns per rank
+ * (MLM_ERR_UNSUPPORTED otherwise); the prompt pass reads them through a bf16
+ * copy the runner keeps for its largest Q6_K layer weight. */
+int mlm_llama_create_typed(mlm_ctx *ctx, const mlm_llama_config *cfg, int batch,
+                           const mlm_llama_types *types, mlm_llama **out);
 int mlm_llama_prefill_seq(mlm_llama *m, int seq, const int32_t *tokens, int n, float *logits,
                           int32_t *next_token_dev);
 int mlm_llama_seq_position(const mlm_llama *m, int seq);

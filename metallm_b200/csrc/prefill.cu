@@ -6,6 +6,8 @@
 // The reference has no batched prefill: it runs forward() once per prompt
 // token (LlamaRunner.swift:320-1210); these kernels are that per-token
 // arithmetic for many positions at once, around mlm_q4k_gemm.
+#include <algorithm>
+
 #include "mlm_device.cuh"
 #include "mlm_internal.h"
 #include "mlm_rope.cuh"
@@ -337,6 +339,28 @@ int swiglu_rows_bf16_launch(mlm_ctx *ctx, const float *gu, int ffn, int T, void 
   swiglu_rows_bf16_kernel<<<dim3((ffn + 255) / 256, T), 256, 0, stream>>>(
       gu, ffn, reinterpret_cast<__nv_bfloat16 *>(out));
   return check_launch(ctx, "prefill (swiglu)");
+}
+
+// out[t] = (a[t] | b[t]): two row-major blocks of T rows, ra and rb floats
+// wide, side by side (the q/k rows of a Q4_K QKV matrix beside the v rows of
+// a Q6_K one)
+__global__ void interleave_rows_kernel(const float *__restrict__ a, int ra,
+                                       const float *__restrict__ b, int rb, int T,
+                                       float *__restrict__ out) {
+  const size_t W = (size_t)ra + rb, n = (size_t)T * W;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t t = i / W, c = i - t * W;
+    out[i] = c < (size_t)ra ? a[t * ra + c] : b[t * rb + (c - ra)];
+  }
+}
+
+int interleave_rows_launch(mlm_ctx *ctx, const float *a, int ra, const float *b, int rb, int T,
+                           float *out, cudaStream_t stream) {
+  const size_t n = (size_t)T * (ra + rb);
+  const unsigned grid = (unsigned)std::min<size_t>((n + 255) / 256, (size_t)ctx->sm_count * 8);
+  interleave_rows_kernel<<<grid, 256, 0, stream>>>(a, ra, b, rb, T, out);
+  return check_launch(ctx, "interleave rows");
 }
 
 }  // namespace mlm

@@ -203,6 +203,11 @@ __device__ __forceinline__ void mbar_arrive1(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
+// kDense: W is already bf16 [N][K] (a weight dequantized ahead of the call):
+// the TMA warp loads each stage's A tile (256 rows x 32, the same 64-byte
+// swizzle) beside the X tile, and the dequantizing warps only run the
+// epilogues.
+template <bool kDense>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     q4k_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
                     const __grid_constant__ CUtensorMap tmap_x, GemmArgs p) {
@@ -224,7 +229,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int i = 0; i < kGemmStages; ++i) {
       mbar_init(bfull + 8 * i, 1);
-      mbar_init(afull + 8 * i, kWarpsPerGroup);
+      mbar_init(afull + 8 * i, kDense ? 1 : kWarpsPerGroup);
       mbar_init(sempty + 8 * i, 1);
     }
     mbar_init(done, 1);
@@ -252,7 +257,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       while (ok && parts.next(p, tile, k0, k1)) {
         const int n0 = (tile % p.tiles_n) * kGemmRows, t0 = (tile / p.tiles_n) * kGemmTok;
         for (int k = k0; k < k1; ++k) {
-          if (k == k0 || k % kStagesPerBlock == 0) {
+          if (!kDense && (k == k0 || k % kStagesPerBlock == 0)) {
             const uint32_t wb = wl & 1;
             if (wl >= 2 && !mbar_wait_bounded(wempty + 8 * wb, ((wl >> 1) - 1) & 1, p.status)) {
               ok = false;
@@ -268,6 +273,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               !mbar_wait_bounded(sempty + 8 * s, (it / kGemmStages - 1) & 1, p.status)) {
             ok = false;
             break;
+          }
+          if (kDense) {  // A: rows n0 .. n0 + 255 (past the end: zeros)
+            mbar_expect_tx(afull + 8 * s, kAStage);
+            tma2d(sbase + kOffA + s * kAStage, &tmap_w, k * kGemmKStep, n0, afull + 8 * s);
           }
           mbar_expect_tx(bfull + 8 * s, p.mma_n * kGemmKStep * 2);
           tma2d(sbase + kOffB + s * kBStage, &tmap_x, k * kGemmKStep, t0, bfull + 8 * s);
@@ -347,7 +356,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     PartIter parts(p);
     int tile, k0, k1;
     while (parts.next(p, tile, k0, k1)) {
-      for (int k = k0; k < k1; ++k) {
+      for (int k = k0; k < k1 && !kDense; ++k) {
         if (k == k0 || k % kStagesPerBlock == 0) {
           // done with the previous W block column (whether or not this warp
           // had a stage in it)
@@ -471,7 +480,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       ++seg;
     }
     // the last W block column's buffer is released (balances the arrivals)
-    if (wl > 0) {
+    if (!kDense && wl > 0) {
       __syncwarp();
       if (lane == 0) mbar_arrive1(wempty + 8 * ((wl - 1) & 1));
     }
@@ -514,7 +523,9 @@ EncodeFn tensor_map_encoder(mlm_ctx *ctx) {
 constexpr int kGemmMaxTiles = 65536;
 
 int gemm_init(mlm_ctx *ctx) {
-  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(q4k_gemm_kernel,
+  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(q4k_gemm_kernel<false>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
+  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(q4k_gemm_kernel<true>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
   if (!ctx->gemm_flags) {
     MLM_CUDA_TRY(ctx, cudaMalloc(&ctx->gemm_flags, sizeof(int) * kGemmMaxTiles));
@@ -529,8 +540,10 @@ int gemm_init(mlm_ctx *ctx) {
 using namespace mlm;
 
 namespace mlm {
-int gemm_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_bf16, int tokens,
-                float *y, const float *residual, cudaStream_t stream) {
+// dense: W is bf16 [rows][cols] instead of Q4_K blocks
+static int gemm_launch_impl(mlm_ctx *ctx, const void *W, bool dense, int rows, int cols,
+                            const void *x_bf16, int tokens, float *y, const float *residual,
+                            cudaStream_t stream) {
   MLM_CHECK_CTX(ctx);
   MLM_REQUIRE(ctx, W && x_bf16 && y, MLM_ERR_ARG, "mlm_q4k_gemm: null buffer");
   MLM_REQUIRE(ctx, rows > 0 && cols > 0 && tokens > 0 && cols % kQK == 0, MLM_ERR_SHAPE,
@@ -547,7 +560,17 @@ int gemm_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_b
   const int mma_n = tokens <= kGemmTok ? (tokens + 15) / 16 * 16 : kGemmTok;
   const int nb = cols / kQK;
   CUtensorMap mw, mx;
-  {
+  if (dense) {  // 32 x 256-row bf16 tiles in the 64-byte swizzle of the X tiles
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kGemmKStep, (cuuint32_t)kGemmRows};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode(&mw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(W), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    MLM_REQUIRE(ctx, r == CUDA_SUCCESS, MLM_ERR_CUDA, "gemm: bf16 W tensor map (%d)", (int)r);
+  } else {
     const cuuint64_t dims[2] = {(cuuint64_t)nb * kBlockBytes, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)nb * kBlockBytes};
     const cuuint32_t box[2] = {(cuuint32_t)kBlockBytes, (cuuint32_t)kGemmRows};
@@ -592,8 +615,33 @@ int gemm_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_b
   // whole-tile waves, leaving between one and two waves' worth to stream-K
   a.dp_waves = (int)std::max<long long>(0, tiles / ctas - 1);
   a.units = (tiles - (long long)a.dp_waves * ctas) * a.ks;
-  q4k_gemm_kernel<<<(unsigned)ctas, kGemmThreads, kGemmSmem, stream>>>(mw, mx, a);
+  if (dense)
+    q4k_gemm_kernel<true><<<(unsigned)ctas, kGemmThreads, kGemmSmem, stream>>>(mw, mx, a);
+  else
+    q4k_gemm_kernel<false><<<(unsigned)ctas, kGemmThreads, kGemmSmem, stream>>>(mw, mx, a);
   return check_launch(ctx, "mlm_q4k_gemm");
+}
+
+int gemm_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_bf16, int tokens,
+                float *y, const float *residual, cudaStream_t stream) {
+  return gemm_launch_impl(ctx, W, false, rows, cols, x_bf16, tokens, y, residual, stream);
+}
+
+int gemm_dense_launch(mlm_ctx *ctx, const void *W_bf16, int rows, int cols, const void *x_bf16,
+                      int tokens, float *y, const float *residual, cudaStream_t stream) {
+  return gemm_launch_impl(ctx, W_bf16, true, rows, cols, x_bf16, tokens, y, residual, stream);
+}
+
+// A Q6_K weight in the prompt pass: dequantized to bf16 (the fp32 value
+// rounded once) into the caller's scratch, then the GEMM on it.
+int q6k_gemm_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_bf16,
+                    int tokens, float *y, const float *residual, void *scratch_bf16,
+                    cudaStream_t stream) {
+  MLM_REQUIRE(ctx, W && scratch_bf16, MLM_ERR_ARG, "mlm_q6k_gemm: null buffer");
+  MLM_REQUIRE(ctx, aligned16(scratch_bf16), MLM_ERR_ALIGN, "mlm_q6k_gemm: scratch alignment");
+  int st = q6k_dequant_bf16_launch(ctx, W, scratch_bf16, (uint64_t)rows * cols, stream);
+  if (st != MLM_OK) return st;
+  return gemm_dense_launch(ctx, scratch_bf16, rows, cols, x_bf16, tokens, y, residual, stream);
 }
 }  // namespace mlm
 

@@ -135,7 +135,11 @@ constexpr int kQ6MaxCols = 32768;
 
 struct Q6GemvArgs {
   const uint8_t *W;
-  const __half *x;
+  const __half *x;       // kHalf: fp16 x
+  const float *x_scale;  // kHalf: per 32-element sub-block of x (NULL: 1)
+  const float *xa, *xb;  // fp32 sources of x in the kRmsNorm / kSwiGLU modes
+  float eps;
+  int x_mode;            // GemvInput::Mode
   float *y;
   const float *residual;
   int rows, nb, nchunk, tiles;
@@ -170,6 +174,9 @@ __device__ __forceinline__ void q6_to_f16x2(uint32_t q4, uint32_t &lo, uint32_t 
   asm("add.rn.f16x2 %0, %1, %2;" : "=r"(hi) : "r"(b), "r"(kBias));
 }
 
+// kScaled: x carries a scale per 32-element sub-block (fp16 x with x_scale,
+// or the kSwiGLU staging); the scale multiplies the sub-block's MMA sums.
+template <bool kScaled>
 __global__ void __launch_bounds__(kQ6Threads, 2) q6k_gemv_kernel(Q6GemvArgs p) {
   extern __shared__ __align__(16) uint8_t smem[];
   const int cols = p.nb * kQK;
@@ -177,6 +184,7 @@ __global__ void __launch_bounds__(kQ6Threads, 2) q6k_gemv_kernel(Q6GemvArgs p) {
   uint8_t *zero = xs + (size_t)cols * 2;                // kQ6ZeroBytes
   uint8_t *stages = zero + kQ6ZeroBytes;                // kQ6Stages x [16][1680]
   float *red = reinterpret_cast<float *>(stages + kQ6Stages * kQ6StageBytes);  // [8][16]
+  float *xscl = red + kQ6Warps * kQ6TileRows;           // [cols / 32] scales of x
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
   const uint32_t stages_s = (uint32_t)__cvta_generic_to_shared(stages);
@@ -207,11 +215,77 @@ __global__ void __launch_bounds__(kQ6Threads, 2) q6k_gemv_kernel(Q6GemvArgs p) {
   for (int q = 0; q < kQ6Stages - 1; ++q) issue(q);
   pdl_wait_then_release();
   {
-    const uint4 *xg = reinterpret_cast<const uint4 *>(p.x);
+    // x -> fp16 in shared memory (the modes of the Q4_K GEMV's staging):
+    // kHalf copies x (and its scales); kRmsNorm stores fp16(a * rms * w);
+    // kSwiGLU stores silu(g) * u with one power-of-two scale per sub-block,
+    // four consecutive lanes holding the four 8-element groups of one
     uint4 *xo = reinterpret_cast<uint4 *>(xs);
-    for (int i = threadIdx.x; i < cols / 8; i += kQ6Threads) xo[i] = __ldg(xg + i);
+    const int ngroups = cols / 8;
     for (int i = threadIdx.x; i < kQ6ZeroBytes / 16; i += kQ6Threads)
       reinterpret_cast<uint4 *>(zero)[i] = make_uint4(0, 0, 0, 0);
+    auto pack = [](const float (&f)[8]) {
+      uint4 v;
+      __half2 h;
+      h = __floats2half2_rn(f[0], f[1]); v.x = *reinterpret_cast<uint32_t *>(&h);
+      h = __floats2half2_rn(f[2], f[3]); v.y = *reinterpret_cast<uint32_t *>(&h);
+      h = __floats2half2_rn(f[4], f[5]); v.z = *reinterpret_cast<uint32_t *>(&h);
+      h = __floats2half2_rn(f[6], f[7]); v.w = *reinterpret_cast<uint32_t *>(&h);
+      return v;
+    };
+    auto load8 = [](const float *src, int i, float (&f)[8]) {
+      const float4 a = __ldg(reinterpret_cast<const float4 *>(src) + 2 * i);
+      const float4 b = __ldg(reinterpret_cast<const float4 *>(src) + 2 * i + 1);
+      f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+      f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+    };
+    if (p.x_mode == GemvInput::kHalf) {
+      const uint4 *xg = reinterpret_cast<const uint4 *>(p.x);
+      for (int i = threadIdx.x; i < ngroups; i += kQ6Threads) xo[i] = __ldg(xg + i);
+      if (kScaled)
+        for (int i = threadIdx.x; i < cols / 32; i += kQ6Threads) xscl[i] = __ldg(p.x_scale + i);
+    } else if (p.x_mode == GemvInput::kRmsNorm) {
+      float ss = 0.f;
+      const float4 *a4 = reinterpret_cast<const float4 *>(p.xa);
+      for (int k = threadIdx.x; k < cols / 4; k += kQ6Threads) {
+        const float4 v = __ldg(a4 + k);
+        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) red[warp] = ss;
+      __syncthreads();
+      float tot = 0.f;
+      for (int w = 0; w < kQ6Warps; ++w) tot += red[w];
+      const float scale = rms_scale(tot, cols, p.eps);
+      for (int i = threadIdx.x; i < ngroups; i += kQ6Threads) {
+        float a[8], w[8];
+        load8(p.xa, i, a);
+        load8(p.xb, i, w);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) a[e] = (a[e] * scale) * safe_weight(w[e]);
+        xo[i] = pack(a);
+      }
+      __syncthreads();  // red is reused by the tile sums
+    } else {  // kSwiGLU (ngroups is a multiple of 32: whole warps in the shuffles)
+      for (int i = threadIdx.x; i < ngroups; i += kQ6Threads) {
+        float gv[8], uv[8];
+        load8(p.xa, i, gv);
+        load8(p.xb, i, uv);
+        float m = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          gv[e] = swiglu(gv[e], uv[e]);
+          m = fmaxf(m, fabsf(gv[e]));
+        }
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+        const int ex = max(0, (int)((__float_as_uint(m) >> 23) & 0xFF) - 127 - 14);
+        const float inv = __uint_as_float((uint32_t)(127 - ex) << 23);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) gv[e] *= inv;
+        xo[i] = pack(gv);
+        if ((i & 3) == 0) xscl[i >> 2] = __uint_as_float((uint32_t)(127 + ex) << 23);
+      }
+    }
   }
 
   // B operands: words 0..3 of a half belong to group 2t (column 2t), words
@@ -261,7 +335,12 @@ __global__ void __launch_bounds__(kQ6Threads, 2) q6k_gemv_kernel(Q6GemvArgs p) {
       const uint32_t sc8 = lds32((blk_g8 + 192 + 8 * h + 2 * t) & ~3u) >> (((blk_g8 + 2 * t) & 2u) * 8u);
       const uint32_t dg = lds32((blk_g + 208) & ~3u) >> (((blk_g + 208) & 2u) * 8u);
       const uint32_t d8 = lds32((blk_g8 + 208) & ~3u) >> (((blk_g8 + 208) & 2u) * 8u);
-      const float fdg = half_bits_to_float(dg & 0xFFFFu), fd8 = half_bits_to_float(d8 & 0xFFFFu);
+      float fdg = half_bits_to_float(dg & 0xFFFFu), fd8 = half_bits_to_float(d8 & 0xFFFFu);
+      if (kScaled) {  // sub-block 4h + t of block c * 8 + warp
+        const float xsc = xscl[(c * kQ6ChunkBlocks + warp) * 8 + 4 * h + t];
+        fdg *= xsc;
+        fd8 *= xsc;
+      }
       acc[0] = fmaf(fdg * (float)(int8_t)(scg & 0xFF), cacc[0], acc[0]);
       acc[0] = fmaf(fdg * (float)(int8_t)((scg >> 8) & 0xFF), cacc[1], acc[0]);
       acc[1] = fmaf(fd8 * (float)(int8_t)(sc8 & 0xFF), cacc[2], acc[1]);
@@ -292,13 +371,51 @@ __global__ void __launch_bounds__(kQ6Threads, 2) q6k_gemv_kernel(Q6GemvArgs p) {
   asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
-size_t q6k_gemv_smem(int cols) { return (size_t)cols * 2 + kQ6FixedSmem; }
+size_t q6k_gemv_smem(int cols) { return (size_t)cols * 2 + kQ6FixedSmem + (size_t)cols / 8; }
 
 int q6k_init(mlm_ctx *ctx) {
-  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(q6k_gemv_kernel,
+  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(q6k_gemv_kernel<false>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)q6k_gemv_smem(kQ6MaxCols)));
+  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(q6k_gemv_kernel<true>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)q6k_gemv_smem(kQ6MaxCols)));
   return MLM_OK;
+}
+
+int q6k_gemv_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const GemvInput &in,
+                    float *y, const float *residual, cudaStream_t stream) {
+  const bool half = in.mode == GemvInput::kHalf;
+  const void *x = half ? in.x_f16 : in.a;
+  MLM_REQUIRE(ctx, W && x && y && (half || in.b), MLM_ERR_ARG, "mlm_q6k_gemv: null buffer");
+  MLM_REQUIRE(ctx, rows > 0 && cols > 0 && cols % (kQK * kQ6ChunkBlocks) == 0 && cols <= kQ6MaxCols,
+              MLM_ERR_SHAPE,
+              "mlm_q6k_gemv: rows=%d cols=%d (cols a multiple of 2048, at most %d)", rows, cols,
+              kQ6MaxCols);
+  MLM_REQUIRE(ctx, aligned16(W) && aligned16(x) && (half || aligned16(in.b)) &&
+                       (!residual || aligned4(residual)),
+              MLM_ERR_ALIGN, "mlm_q6k_gemv: W and x must be 16-byte aligned");
+  Q6GemvArgs a;
+  a.W = reinterpret_cast<const uint8_t *>(W);
+  a.x = reinterpret_cast<const __half *>(in.x_f16);
+  a.x_scale = in.x_scale;
+  a.xa = in.a;
+  a.xb = in.b;
+  a.eps = in.eps;
+  a.x_mode = in.mode;
+  a.y = y;
+  a.residual = residual;
+  a.rows = rows;
+  a.nb = cols / kQK;
+  a.nchunk = a.nb / kQ6ChunkBlocks;
+  a.tiles = (rows + kQ6TileRows - 1) / kQ6TileRows;
+  const int ctas = std::max(1, std::min(a.tiles, 2 * ctx->sm_count));
+  const bool scaled = in.mode == GemvInput::kSwiGLU || (half && in.x_scale != nullptr);
+  auto kern = scaled ? q6k_gemv_kernel<true> : q6k_gemv_kernel<false>;
+  return check_launch_pdl(ctx,
+                          launch_pdl(kern, dim3(ctas), dim3(kQ6Threads), q6k_gemv_smem(cols),
+                                     stream, a),
+                          "mlm_q6k_gemv");
 }
 
 template <class OutT>
@@ -319,6 +436,19 @@ static int q6k_dequant_entry(mlm_ctx *ctx, const void *blocks, OutT *out, uint64
   q6k_dequant_kernel<OutT><<<grid, 256, 0, ctx->stream>>>(
       reinterpret_cast<const uint8_t *>(blocks), out, nblocks);
   return check_launch(ctx, name);
+}
+
+int q6k_dequant_bf16_launch(mlm_ctx *ctx, const void *blocks, void *out, uint64_t n,
+                            cudaStream_t stream) {
+  MLM_REQUIRE(ctx, n % kQK == 0 && (reinterpret_cast<uintptr_t>(blocks) & 1) == 0,
+              MLM_ERR_SHAPE, "Q6_K dequant: n=%llu", (unsigned long long)n);
+  const uint64_t nblocks = n / kQK;
+  if (nblocks == 0) return MLM_OK;
+  const uint64_t warps = std::min<uint64_t>(nblocks, (uint64_t)ctx->sm_count * 64);
+  const unsigned grid = (unsigned)((warps * 32 + 255) / 256);
+  q6k_dequant_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
+      reinterpret_cast<const uint8_t *>(blocks), reinterpret_cast<__nv_bfloat16 *>(out), nblocks);
+  return check_launch(ctx, "Q6_K dequant");
 }
 
 }  // namespace mlm
@@ -355,25 +485,43 @@ extern "C" int mlm_q6k_dequant_bf16(mlm_ctx *ctx, const void *blocks, void *out,
 extern "C" int mlm_q6k_gemv(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_f16,
                             float *y, const float *residual) {
   MLM_CHECK_CTX(ctx);
-  MLM_REQUIRE(ctx, W && x_f16 && y, MLM_ERR_ARG, "mlm_q6k_gemv: null buffer");
-  MLM_REQUIRE(ctx, rows > 0 && cols > 0 && cols % (kQK * kQ6ChunkBlocks) == 0 && cols <= kQ6MaxCols,
-              MLM_ERR_SHAPE,
-              "mlm_q6k_gemv: rows=%d cols=%d (cols a multiple of 2048, at most %d)", rows, cols,
-              kQ6MaxCols);
-  MLM_REQUIRE(ctx, aligned16(W) && aligned16(x_f16) && (!residual || aligned4(residual)),
-              MLM_ERR_ALIGN, "mlm_q6k_gemv: W and x must be 16-byte aligned");
-  Q6GemvArgs a;
-  a.W = reinterpret_cast<const uint8_t *>(W);
-  a.x = reinterpret_cast<const __half *>(x_f16);
-  a.y = y;
-  a.residual = residual;
-  a.rows = rows;
-  a.nb = cols / kQK;
-  a.nchunk = a.nb / kQ6ChunkBlocks;
-  a.tiles = (rows + kQ6TileRows - 1) / kQ6TileRows;
-  const int ctas = std::max(1, std::min(a.tiles, 2 * ctx->sm_count));
-  return check_launch_pdl(ctx,
-                          launch_pdl(q6k_gemv_kernel, dim3(ctas), dim3(kQ6Threads),
-                                     q6k_gemv_smem(cols), ctx->stream, a),
-                          "mlm_q6k_gemv");
+  return q6k_gemv_launch(ctx, W, rows, cols, gemv_half(x_f16), y, residual, ctx->stream);
+}
+
+extern "C" int mlm_q6k_gemv_xs(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_f16,
+                               const float *x_scale, float *y, const float *residual) {
+  MLM_CHECK_CTX(ctx);
+  if (!x_scale) return set_error(ctx, MLM_ERR_ARG, "mlm_q6k_gemv_xs: null x_scale");
+  return q6k_gemv_launch(ctx, W, rows, cols, gemv_half(x_f16, x_scale), y, residual,
+                         ctx->stream);
+}
+
+extern "C" int mlm_q6k_gemv_rmsnorm(mlm_ctx *ctx, const void *W, int rows, int cols,
+                                    const float *hidden, const float *norm_w, float eps,
+                                    float *y, const float *residual) {
+  MLM_CHECK_CTX(ctx);
+  GemvInput in;
+  in.mode = GemvInput::kRmsNorm;
+  in.a = hidden;
+  in.b = norm_w;
+  in.eps = eps;
+  return q6k_gemv_launch(ctx, W, rows, cols, in, y, residual, ctx->stream);
+}
+
+extern "C" int mlm_q6k_gemv_swiglu(mlm_ctx *ctx, const void *W, int rows, int cols,
+                                   const float *gate, const float *up, float *y,
+                                   const float *residual) {
+  MLM_CHECK_CTX(ctx);
+  GemvInput in;
+  in.mode = GemvInput::kSwiGLU;
+  in.a = gate;
+  in.b = up;
+  return q6k_gemv_launch(ctx, W, rows, cols, in, y, residual, ctx->stream);
+}
+
+extern "C" int mlm_q6k_gemm(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_bf16,
+                            int tokens, float *y, const float *residual, void *scratch_bf16) {
+  MLM_CHECK_CTX(ctx);
+  return q6k_gemm_launch(ctx, W, rows, cols, x_bf16, tokens, y, residual, scratch_bf16,
+                         ctx->stream);
 }

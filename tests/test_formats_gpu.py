@@ -109,3 +109,93 @@ def test_gemv_on_repacked_gguf_weights(ctx):
     y = ctx.alloc(4 * rows)
     ctx.q4k_gemv(W, rows, cols, ctx.to_device(x), y)
     assert rel_l2(y.download(np.float32, rows), want) < GEMV_TOL
+
+
+# -- the Q6_K linears of Q4_K_M files inside the model ----------------------------
+
+def _q6_dense(W, rows, cols):
+    return O.q6k_dequant_f32(W, rows * cols).reshape(rows, cols).astype(np.float64)
+
+
+def test_q6k_gemv_scaled_x(ctx):
+    """x = x_f16 * x_scale[k/32] (the down projection's input format)."""
+    rows, cols = 1000, 14336
+    W = O.gen_q6k(41, 1, rows * cols // 256)
+    x16 = O.gen_f16(41, 2, cols)
+    scale = (2.0 ** (np.arange(cols // 32) % 9)).astype(np.float32)
+    r = O.gen_f32(41, 3, rows)
+    y = ctx.alloc(4 * rows)
+    ctx.call("mlm_q6k_gemv_xs", ctx.to_device(W), rows, cols, ctx.to_device(x16),
+             ctx.to_device(scale), y, ctx.to_device(r))
+    xtrue = x16.astype(np.float64) * np.repeat(scale, 32)
+    ref = _q6_dense(W, rows, cols) @ xtrue + r
+    assert rel_l2(y.download(np.float32), ref) < GEMV_TOL
+
+
+def test_q6k_gemv_rmsnorm_input(ctx):
+    """x = fp16(RMSNorm(hidden)) formed inside the Q6_K GEMV (attn_v, output)."""
+    import ctypes
+    rows, cols = 1024, 4096
+    W = O.gen_q6k(42, 1, rows * cols // 256)
+    h = O.gen_f32(42, 2, cols, 0.0, 3.0)
+    w = O.gen_f32(42, 3, cols, 1.0, 0.02)
+    y = ctx.alloc(4 * rows)
+    ctx.call("mlm_q6k_gemv_rmsnorm", ctx.to_device(W), rows, cols, ctx.to_device(h),
+             ctx.to_device(w), ctypes.c_float(1e-5), y, None)
+    xn = O.rmsnorm_f32(h, w, 1, cols, 1e-5).astype(np.float16)
+    ref = O.q6k_matvec(W, rows, cols, xn)
+    assert rel_l2(y.download(np.float32), ref) < GEMV_TOL
+
+
+def test_q6k_gemv_swiglu_input(ctx):
+    """x = silu(gate) * up formed inside the Q6_K GEMV (ffn_down), with the
+    residual; large values go to fp16 with a power-of-two scale."""
+    rows, cols = 4096, 14336
+    W = O.gen_q6k(43, 1, rows * cols // 256)
+    g = O.gen_f32(43, 2, cols, 0.0, 200.0)
+    u = O.gen_f32(43, 3, cols, 0.0, 200.0)
+    r = O.gen_f32(43, 4, rows)
+    y = ctx.alloc(4 * rows)
+    ctx.call("mlm_q6k_gemv_swiglu", ctx.to_device(W), rows, cols, ctx.to_device(g),
+             ctx.to_device(u), y, ctx.to_device(r))
+    ref = _q6_dense(W, rows, cols) @ O.silu_mul(g, u).astype(np.float64) + r
+    got = y.download(np.float32)
+    assert np.all(np.isfinite(got))
+    assert rel_l2(got, ref) < 1e-3  # x rounded to fp16 (2^-11 per element)
+
+
+def _bf16_round(a):
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    u = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint32) << 16
+    return u.view(np.float32)
+
+
+@pytest.mark.parametrize("rows,cols,tokens,in_place", [
+    (1024, 4096, 512, False), (4096, 14336, 64, True), (1000, 2048, 17, False),
+    (300, 4096, 1, True),
+    # 320 output tiles: whole-tile waves before the stream-K split
+    (20480, 2048, 1024, False)])
+def test_q6k_gemm(ctx, rows, cols, tokens, in_place):
+    """The prompt linears on a Q6_K weight: dequantized to bf16 into the
+    scratch, then the tensor-core GEMM on it; relative L2 <= 2e-3 against the
+    fp64 product of the same bf16 operands."""
+    W = O.gen_q6k(44, 1, rows * cols // 256)
+    xf = O.gen_f32(44, 2, tokens * cols)
+    xb = (_bf16_round(xf).view(np.uint32) >> 16).astype(np.uint16)
+    r = O.gen_f32(44, 3, tokens * rows, 0.0, 10.0)
+    scratch = ctx.alloc(2 * rows * cols)
+    if in_place:
+        y = ctx.to_device(r)
+        res = y
+    else:
+        y = ctx.alloc(4 * rows * tokens)
+        res = None
+    ctx.call("mlm_q6k_gemm", ctx.to_device(W), rows, cols, ctx.to_device(xb), tokens, y, res,
+             scratch)
+    got = y.download(np.float32, rows * tokens).reshape(tokens, rows)
+    w = _bf16_round(O.q6k_dequant_f32(W, rows * cols)).reshape(rows, cols).astype(np.float64)
+    ref = _bf16_round(xf).reshape(tokens, cols).astype(np.float64) @ w.T
+    if in_place:
+        ref += r.reshape(tokens, rows)
+    assert np.all(np.isfinite(got))
+    assert rel_l2(got, ref) < 2e-3

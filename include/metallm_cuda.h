@@ -113,6 +113,11 @@ int mlm_gen_q4k_sub(mlm_ctx *ctx, uint64_t seed, uint64_t stream, uint64_t nb_fu
  * 2-byte aligned */
 int mlm_gen_q6k(mlm_ctx *ctx, uint64_t seed, uint64_t stream, uint64_t first_block,
                 uint64_t nblocks, void *out);
+/* Block columns [kb0, kb0 + nkb) of rows [row0, row0 + rows) of the tensor
+ * mlm_gen_q6k generates with nb_full blocks per row: a rank's column shard
+ * of a generated weight. */
+int mlm_gen_q6k_sub(mlm_ctx *ctx, uint64_t seed, uint64_t stream, uint64_t nb_full,
+                    uint64_t row0, uint64_t rows, uint64_t kb0, uint64_t nkb, void *out);
 int mlm_gen_f16(mlm_ctx *ctx, uint64_t seed, uint64_t stream, uint64_t first,
                 uint64_t n, float mean, float std, void *out_f16);
 int mlm_gen_f32(mlm_ctx *ctx, uint64_t seed, uint64_t stream, uint64_t first,

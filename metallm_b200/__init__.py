@@ -14,8 +14,8 @@ from typing import Optional, Sequence
 
 import numpy as np
 
-from ._lib import (LIB_PATH, LlamaConfig, LlamaGlobals, LlamaLayer, MLMError,  # noqa: F401
-                   RopeArgs, load, rope_args)
+from ._lib import (LIB_PATH, TYPE_Q4_K, TYPE_Q6_K, LlamaConfig, LlamaGlobals,  # noqa: F401
+                   LlamaLayer, LlamaTypes, MLMError, RopeArgs, load, rope_args)
 
 QK_K = 256
 Q4K_BLOCK_BYTES = 144
@@ -182,6 +182,12 @@ class Context:
         self.call("mlm_gen_q4k_sub", seed, stream, nb_full, row0, rows, kb0, nkb,
                   ctypes.c_void_p(int(out)))
 
+    def gen_q6k_sub(self, seed: int, stream: int, nb_full: int, row0: int, rows: int, kb0: int,
+                    nkb: int, out) -> None:
+        """The same for a generated Q6_K tensor."""
+        self.call("mlm_gen_q6k_sub", seed, stream, nb_full, row0, rows, kb0, nkb,
+                  ctypes.c_void_p(int(out)))
+
     def gen_f16(self, seed: int, stream: int, n: int, out: DeviceBuffer, mean: float = 0.0,
                 std: float = 1.0, first: int = 0) -> DeviceBuffer:
         self.call("mlm_gen_f16", seed, stream, first, n, ctypes.c_float(mean),
@@ -260,12 +266,24 @@ class Llama:
     write the raw GGUF blocks straight into them.
     """
 
-    def __init__(self, ctx: Context, cfg: LlamaConfig, batch: int = 1):
+    def __init__(self, ctx: Context, cfg: LlamaConfig, batch: int = 1,
+                 types: Optional[dict] = None):
+        """types (a Q4_K_M file's per-tensor types): {"output": TYPE_Q6_K,
+        "attn_v": [type per layer], "ffn_down": [type per layer]}; missing
+        entries are Q4_K."""
         self.ctx = ctx
         self.cfg = cfg
         self.batch = batch
         h = ctypes.c_void_p()
-        if batch == 1:
+        if types:
+            arr = lambda v: ((ctypes.c_int32 * cfg.n_layers)(*v) if v is not None else None)
+            av, fd = arr(types.get("attn_v")), arr(types.get("ffn_down"))
+            t = LlamaTypes(int(types.get("output", TYPE_Q4_K)),
+                           ctypes.cast(av, ctypes.POINTER(ctypes.c_int32)) if av else None,
+                           ctypes.cast(fd, ctypes.POINTER(ctypes.c_int32)) if fd else None)
+            st = ctx.lib.mlm_llama_create_typed(ctx.handle, ctypes.byref(cfg), batch,
+                                                ctypes.byref(t), ctypes.byref(h))
+        elif batch == 1:
             st = ctx.lib.mlm_llama_create(ctx.handle, ctypes.byref(cfg), ctypes.byref(h))
         else:
             st = ctx.lib.mlm_llama_create_batch(ctx.handle, ctypes.byref(cfg), batch,

@@ -47,14 +47,27 @@ class LlamaConfig(ctypes.Structure):
 
 
 class LlamaLayer(ctypes.Structure):
-    """mlm_llama_layer: device pointers of one layer's tensors."""
+    """mlm_llama_layer: device pointers of one layer's tensors and the types
+    of attn_v and ffn_down."""
     _fields_ = [(n, ctypes.c_void_p) for n in ("attn_norm", "wq", "wk", "wv", "wo", "ffn_norm",
                                                "w_gate", "w_up", "w_down", "k_cache", "v_cache")]
+    _fields_ += [("wv_type", ctypes.c_int32), ("w_down_type", ctypes.c_int32)]
 
 
 class LlamaGlobals(ctypes.Structure):
     """mlm_llama_globals."""
     _fields_ = [(n, ctypes.c_void_p) for n in ("tok_embd", "output_norm", "output", "rope_freqs")]
+    _fields_ += [("output_type", ctypes.c_int32)]
+
+
+TYPE_Q4_K, TYPE_Q6_K = 12, 14  # MLM_TYPE_*: the ggml_type values
+
+
+class LlamaTypes(ctypes.Structure):
+    """mlm_llama_types: the output head's type and per-layer attn_v /
+    ffn_down types (NULL arrays: all Q4_K)."""
+    _fields_ = [("output", ctypes.c_int32), ("attn_v", ctypes.POINTER(ctypes.c_int32)),
+                ("ffn_down", ctypes.POINTER(ctypes.c_int32))]
 
 
 # (name, restype, argtypes) of every exported entry point
@@ -91,6 +104,7 @@ SIGNATURES = [
     ("mlm_q4k_dequant_bf16", c_int, [c_vp, c_vp, c_vp, c_u64]),
     ("mlm_q4k_repack_canonical", c_int, [c_vp, c_vp, c_vp, c_u64]),
     ("mlm_gen_q6k", c_int, [c_vp, c_u64, c_u64, c_u64, c_u64, c_vp]),
+    ("mlm_gen_q6k_sub", c_int, [c_vp, c_u64, c_u64, c_u64, c_u64, c_u64, c_u64, c_u64, c_vp]),
     ("mlm_q6k_dequant_f32", c_int, [c_vp, c_vp, c_vp, c_u64]),
     ("mlm_q6k_dequant_f16", c_int, [c_vp, c_vp, c_vp, c_u64]),
     ("mlm_q6k_dequant_bf16", c_int, [c_vp, c_vp, c_vp, c_u64]),
@@ -131,6 +145,7 @@ SIGNATURES = [
     ("mlm_llama_prefill", c_int, [c_vp, ctypes.POINTER(ctypes.c_int32), c_int, c_vp, c_vp]),
     ("mlm_llama_decode_greedy", c_int, [c_vp, c_int, c_int, c_vp]),
     ("mlm_llama_create_batch", c_int, [c_vp, c_vp, c_int, ctypes.POINTER(c_vp)]),
+    ("mlm_llama_create_typed", c_int, [c_vp, c_vp, c_int, c_vp, ctypes.POINTER(c_vp)]),
     ("mlm_llama_prefill_seq", c_int, [c_vp, c_int, c_vp, c_int, c_vp, c_vp]),
     ("mlm_llama_seq_position", c_int, [c_vp, c_int]),
     ("mlm_llama_forward_batch", c_int, [c_vp, c_vp, c_vp]),

@@ -304,8 +304,8 @@ struct mlm_llama {
     const int r4 = qkv4_rows(L);
     int st = linear(L.qkv, r4, cfg.dim, x, T, pf_tmp, nullptr);
     if (st != MLM_OK) return st;
-    if ((st = linear_t(MLM_TYPE_Q6_K, L.wv6, kvdim(), cfg.dim, x, T, pf_tmp + (size_t)T * r4,
-                       nullptr)))
+    if ((st = linear_q6(L.wv6, kvdim(), cfg.dim, x, T, pf_tmp + (size_t)T * r4, nullptr,
+                        [&](int t) { return rms_row(t, L.attn_norm); })))
       return st;
     return interleave_rows_launch(ctx, pf_tmp, r4, pf_tmp + (size_t)T * r4, kvdim(), T, pf_qkv,
                                   ctx->stream);
@@ -387,19 +387,44 @@ struct mlm_llama {
     if (T <= 8) return gemv_batch_launch(ctx, W, rows, cols, x, T, y, res, ctx->stream);
     return gemm_launch(ctx, W, rows, cols, x, T, y, res, ctx->stream);
   }
-  // a Q6_K weight goes through its bf16 copy in q6_scratch and the GEMM
-  int linear_t(int type, const uint8_t *W, int rows, int cols, const void *x, int T, float *y,
-               const float *res) {
-    if (type != MLM_TYPE_Q6_K) return linear(W, rows, cols, x, T, y, res);
-    return q6k_gemm_launch(ctx, W, rows, cols, x, T, y, res, q6_scratch, ctx->stream);
+  // A Q6_K weight over T token rows.  Up to 8 rows (a decode batch, a short
+  // prompt): one Q6_K GEMV per row with x staged from the fp32 source the
+  // single-token step uses (src(t): the RMSNorm or SiLU-gated input of row
+  // t), so these rows compute what the decode step computes.  More rows: the
+  // bf16 x through the weight's bf16 copy in q6_scratch and the GEMM.
+  template <class Src>
+  int linear_q6(const uint8_t *W, int rows, int cols, const void *x_bf16, int T, float *y,
+                const float *res, Src src) {
+    if (T > 8)
+      return q6k_gemm_launch(ctx, W, rows, cols, x_bf16, T, y, res, q6_scratch, ctx->stream);
+    for (int t = 0; t < T; ++t) {
+      int st = q6k_gemv_launch(ctx, W, rows, cols, src(t), y + (size_t)t * rows,
+                               res ? res + (size_t)t * rows : nullptr, ctx->stream);
+      if (st != MLM_OK) return st;
+    }
+    return MLM_OK;
+  }
+  GemvInput rms_row(int t, const float *norm_w) const {
+    return normed(pf_hidden + (size_t)t * cfg.dim, norm_w);
+  }
+  GemvInput swiglu_row(int t) const {
+    GemvInput in;
+    in.mode = GemvInput::kSwiGLU;
+    in.a = pf_gu + (size_t)t * 2 * ffn();
+    in.b = in.a + ffn();
+    return in;
   }
 
   // pf_hidden += X W^T over T rows for a projection with split input
-  // columns (see row_parallel)
+  // columns (see row_parallel); a Q6_K one is the down projection
   int row_parallel_rows(const uint8_t *W, int cols, const void *x, int T,
                         int type = MLM_TYPE_Q4_K) {
-    if (!tp_on) return linear_t(type, W, cfg.dim, cols, x, T, pf_hidden, pf_hidden);
-    int st = linear_t(type, W, cfg.dim, cols, x, T, pf_part, rank == 0 ? pf_hidden : nullptr);
+    auto lin = [&](float *y, const float *res) {
+      if (type != MLM_TYPE_Q6_K) return linear(W, cfg.dim, cols, x, T, y, res);
+      return linear_q6(W, cfg.dim, cols, x, T, y, res, [&](int t) { return swiglu_row(t); });
+    };
+    if (!tp_on) return lin(pf_hidden, pf_hidden);
+    int st = lin(pf_part, rank == 0 ? pf_hidden : nullptr);
     if (st != MLM_OK) return st;
     return tp_allreduce_sum(ctx, pf_part, pf_hidden, (size_t)T * cfg.dim, ctx->stream);
   }

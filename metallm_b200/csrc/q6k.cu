@@ -31,13 +31,10 @@ constexpr uint64_t kTagQ6K = 0x66ULL;
 
 // block b of a generated Q6_K tensor: 208 uniform bytes (ql, qh, scales),
 // then d = fp16(|N(0,1)| * 0.01) -- the arithmetic of orc_gen_q6k
-__global__ void gen_q6k_kernel(uint64_t seed, uint64_t stream, uint64_t first_block,
-                               uint64_t nblocks, uint8_t *out) {
-  const uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
-  if (i >= nblocks) return;
-  const uint64_t b = first_block + i;
+__device__ __forceinline__ void gen_q6k_block(uint64_t seed, uint64_t stream, uint64_t b,
+                                              uint8_t *out) {
   const uint64_t st = stream ^ (kTagQ6K << 56);
-  uint16_t *o = reinterpret_cast<uint16_t *>(out + i * kQ6Bytes);  // 2-byte aligned
+  uint16_t *o = reinterpret_cast<uint16_t *>(out);  // 2-byte aligned
 #pragma unroll 2
   for (int k = 0; k < 26; ++k) {
     const uint64_t r = rng_u64(seed, st, b * 26 + (uint64_t)k);
@@ -48,6 +45,24 @@ __global__ void gen_q6k_kernel(uint64_t seed, uint64_t stream, uint64_t first_bl
   }
   const float d = (float)fabs(rng_normal(seed, st, b));
   o[104] = __half_as_ushort(__float2half_rn(__fmul_rn(d, 0.01f)));
+}
+
+__global__ void gen_q6k_kernel(uint64_t seed, uint64_t stream, uint64_t first_block,
+                               uint64_t nblocks, uint8_t *out) {
+  const uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  if (i >= nblocks) return;
+  gen_q6k_block(seed, stream, first_block + i, out + i * kQ6Bytes);
+}
+
+// block columns [kb0, kb0 + nkb) of rows [row0, row0 + rows) of a generated
+// tensor with nb_full blocks per row (a column shard under tensor parallelism)
+__global__ void gen_q6k_sub_kernel(uint64_t seed, uint64_t stream, uint64_t nb_full,
+                                   uint64_t row0, uint64_t rows, uint64_t kb0, uint64_t nkb,
+                                   uint8_t *__restrict__ out) {
+  const uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  if (i >= rows * nkb) return;
+  const uint64_t r = i / nkb, c = i % nkb;
+  gen_q6k_block(seed, stream, (row0 + r) * nb_full + kb0 + c, out + i * kQ6Bytes);
 }
 
 // ---- dequantization ------------------------------------------------------------
@@ -466,6 +481,23 @@ extern "C" int mlm_gen_q6k(mlm_ctx *ctx, uint64_t seed, uint64_t stream, uint64_
   gen_q6k_kernel<<<grid, 128, 0, ctx->stream>>>(seed, stream, first_block, nblocks,
                                                 reinterpret_cast<uint8_t *>(out));
   return check_launch(ctx, "mlm_gen_q6k");
+}
+
+extern "C" int mlm_gen_q6k_sub(mlm_ctx *ctx, uint64_t seed, uint64_t stream, uint64_t nb_full,
+                               uint64_t row0, uint64_t rows, uint64_t kb0, uint64_t nkb,
+                               void *out) {
+  MLM_CHECK_CTX(ctx);
+  if (rows == 0 || nkb == 0) return MLM_OK;
+  MLM_REQUIRE(ctx, out, MLM_ERR_ARG, "mlm_gen_q6k_sub: null output");
+  MLM_REQUIRE(ctx, kb0 + nkb <= nb_full, MLM_ERR_SHAPE,
+              "mlm_gen_q6k_sub: block columns %llu..%llu of %llu", (unsigned long long)kb0,
+              (unsigned long long)(kb0 + nkb), (unsigned long long)nb_full);
+  MLM_REQUIRE(ctx, (reinterpret_cast<uintptr_t>(out) & 1) == 0, MLM_ERR_ALIGN,
+              "mlm_gen_q6k_sub: output must be 2-byte aligned");
+  const uint64_t n = rows * nkb;
+  gen_q6k_sub_kernel<<<(unsigned)((n + 127) / 128), 128, 0, ctx->stream>>>(
+      seed, stream, nb_full, row0, rows, kb0, nkb, reinterpret_cast<uint8_t *>(out));
+  return check_launch(ctx, "mlm_gen_q6k_sub");
 }
 
 extern "C" int mlm_q6k_dequant_f32(mlm_ctx *ctx, const void *blocks, float *out, uint64_t n) {

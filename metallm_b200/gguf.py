@@ -13,9 +13,11 @@ then moves every block from the GGUF element order into the order the
 kernels read.  Norm weights go up as fp32; the token embedding is converted
 to the runner's fp16 table on the device (F16 as is, F32 rounded, Q4_K and
 Q6_K dequantized).  With tensor parallelism each rank uploads its shard
-(``metallm_b200.tp``).  The runner's linears and output head are Q4_K: a
-file holding another type there (a Q4_K_M file's Q6_K attn_v / ffn_down /
-output tensors) is rejected with the tensor's name.
+(``metallm_b200.tp``).  The linears are Q4_K, except that attn_v,
+ffn_down and the output head may be Q6_K, as Q4_K_M files store them: the
+runner is created with those per-tensor types (``tensor_types``) and the
+Q6_K blocks go up unchanged (their GGUF order is the one the kernels read).
+A file holding any other type there is rejected with the tensor's name.
 
 ``write_gguf`` writes the same format (used by the tests to build files).
 """
@@ -306,11 +308,36 @@ def _upload(ctx, dptr: int, data: np.ndarray) -> None:
                "mlm_upload")
 
 
-def _q4k_shard(f: GGUFFile, name: str, rows: int, cols: int, sh: dict) -> np.ndarray:
-    """The (row0, rows, kb0, nkb) part of a Q4_K tensor, [rows][nkb] blocks."""
-    _check_tensor(f, name, (Q4_K,), rows, cols)
-    full = f.tensor_data(name).reshape(rows, cols // 256, 144)
+BLOCK_BYTES = {Q4_K: 144, Q6_K: 210}
+
+# linears a Q4_K_M file may store as Q6_K (the runner's typed tensors)
+Q6K_OK = ("wv", "w_down")
+
+
+def _block_shard(f: GGUFFile, name: str, rows: int, cols: int, sh: dict,
+                 types: Sequence[int] = (Q4_K,)) -> np.ndarray:
+    """The (row0, rows, kb0, nkb) part of a Q4_K (or Q6_K) tensor, [rows][nkb]
+    blocks."""
+    t = _check_tensor(f, name, types, rows, cols)
+    full = f.tensor_data(name).reshape(rows, cols // 256, BLOCK_BYTES[t.type])
     return full[sh["row0"]:sh["row0"] + sh["rows"], sh["kb0"]:sh["kb0"] + sh["nkb"]]
+
+
+def tensor_types(f: GGUFFile, n_layers: int) -> Optional[dict]:
+    """The runner's per-tensor types for the file (None: all Q4_K): Q6_K
+    attn_v / ffn_down / output as Q4_K_M files store them."""
+    def ty(name):
+        t = f.tensors.get(name)
+        return t.type if t is not None else Q4_K
+    out_name = "output.weight" if "output.weight" in f.tensors else "token_embd.weight"
+    types = {"output": Q6_K if ty(out_name) == Q6_K else Q4_K,
+             "attn_v": [Q6_K if ty(f"blk.{l}.attn_v.weight") == Q6_K else Q4_K
+                        for l in range(n_layers)],
+             "ffn_down": [Q6_K if ty(f"blk.{l}.ffn_down.weight") == Q6_K else Q4_K
+                          for l in range(n_layers)]}
+    if types["output"] == Q4_K and Q6_K not in types["attn_v"] + types["ffn_down"]:
+        return None
+    return types
 
 
 def load_llama(ctx, path: str, max_seq: Optional[int] = None, batch: int = 1):
@@ -321,7 +348,7 @@ def load_llama(ctx, path: str, max_seq: Optional[int] = None, batch: int = 1):
     from .tp import Shard, layer_shards, output_shard
     with GGUFFile(path) as f:
         cfg = llama_config_from_gguf(f, max_seq)
-        m = Llama(ctx, cfg, batch)
+        m = Llama(ctx, cfg, batch, types=tensor_types(f, cfg.n_layers))
         try:
             rank, size = ctx.tp_info()
             shard = Shard(rank, max(size, 1))
@@ -333,9 +360,11 @@ def load_llama(ctx, path: str, max_seq: Optional[int] = None, batch: int = 1):
                     name = f"blk.{layer}.{theirs}.weight"
                     if ours in shapes:
                         rows, cols = shapes[ours]
-                        blocks = _q4k_shard(f, name, rows, cols, shards[ours])
+                        ok = (Q4_K, Q6_K) if ours in Q6K_OK else (Q4_K,)
+                        blocks = _block_shard(f, name, rows, cols, shards[ours], ok)
                         _upload(ctx, t[ours], blocks)
-                        ctx.q4k_repack_canonical(t[ours], t[ours], blocks.size // 144)
+                        if blocks.shape[-1] == 144:  # Q6_K needs no reordering
+                            ctx.q4k_repack_canonical(t[ours], t[ours], blocks.size // 144)
                     else:
                         _check_tensor(f, name, (F32, F16), 1, cfg.dim)
                         _upload(ctx, t[ours], _as_f32(f, name))
@@ -345,11 +374,12 @@ def load_llama(ctx, path: str, max_seq: Optional[int] = None, batch: int = 1):
             _upload(ctx, g["output_norm"], _as_f32(f, "output_norm.weight"))
             out_name = "output.weight" if "output.weight" in f.tensors else "token_embd.weight"
             osh = output_shard(cfg, shard)
-            blocks = _q4k_shard(f, out_name, cfg.vocab, cfg.dim,
-                                dict(row0=osh["row0"], rows=osh["rows"], kb0=0,
-                                     nkb=cfg.dim // 256))
+            blocks = _block_shard(f, out_name, cfg.vocab, cfg.dim,
+                                  dict(row0=osh["row0"], rows=osh["rows"], kb0=0,
+                                       nkb=cfg.dim // 256), (Q4_K, Q6_K))
             _upload(ctx, g["output"], blocks)
-            ctx.q4k_repack_canonical(g["output"], g["output"], blocks.size // 144)
+            if blocks.shape[-1] == 144:
+                ctx.q4k_repack_canonical(g["output"], g["output"], blocks.size // 144)
             if cfg.rope.has_freq_factors:
                 t = _check_tensor(f, "rope_freqs.weight", (F32,), 1, cfg.rope.n_dims // 2)
                 _upload(ctx, g["rope_freqs"], f.tensor_data(t.name).view(np.float32))

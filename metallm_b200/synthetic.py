@@ -46,12 +46,29 @@ def q4k_shapes(cfg: LlamaConfig) -> Dict[str, tuple]:
             "w_up": (cfg.ffn_dim, cfg.dim), "w_down": (cfg.dim, cfg.ffn_dim)}
 
 
-def _fill_q4k(ctx, seed: int, stream: int, sh: dict, out) -> None:
-    """The (row0, rows, kb0, nkb) part of generated tensor `stream`."""
+def _fill_q4k(ctx, seed: int, stream: int, sh: dict, out, q6: bool = False) -> None:
+    """The (row0, rows, kb0, nkb) part of generated tensor `stream` (Q4_K, or
+    Q6_K when q6)."""
     if sh["kb0"] == 0 and sh["nkb"] == sh["nb"]:
-        ctx.gen_q4k(seed, stream, sh["rows"] * sh["nb"], out, first_block=sh["row0"] * sh["nb"])
+        gen = ctx.gen_q6k if q6 else ctx.gen_q4k
+        gen(seed, stream, sh["rows"] * sh["nb"], out, first_block=sh["row0"] * sh["nb"])
     else:
-        ctx.gen_q4k_sub(seed, stream, sh["nb"], sh["row0"], sh["rows"], sh["kb0"], sh["nkb"], out)
+        sub = ctx.gen_q6k_sub if q6 else ctx.gen_q4k_sub
+        sub(seed, stream, sh["nb"], sh["row0"], sh["rows"], sh["kb0"], sh["nkb"], out)
+
+
+# tensors of a layer whose type the runner reports (a Q4_K_M file's Q6_K ones)
+TYPED = {"wv": "wv_type", "w_down": "w_down_type"}
+
+
+def q4k_m_types(n_layers: int) -> dict:
+    """The per-tensor types llama.cpp's Q4_K_M recipe gives a Llama model:
+    Q6_K output head, Q6_K attn_v and ffn_down in the first and last eighth
+    of the layers and in every third layer between, Q4_K elsewhere."""
+    def q6(l):
+        return l < n_layers // 8 or l >= 7 * n_layers // 8 or (l - n_layers // 8) % 3 == 2
+    t = [14 if q6(l) else 12 for l in range(n_layers)]
+    return {"output": 14, "attn_v": t, "ffn_down": list(t)}
 
 
 def fill_llama(llama, seed: int, cache_positions: int = 0, layers=None) -> None:
@@ -70,7 +87,8 @@ def fill_llama(llama, seed: int, cache_positions: int = 0, layers=None) -> None:
     for layer in (range(cfg.n_layers) if layers is None else layers):
         t = llama.layer_tensors(layer)
         for name in q4k_shapes(cfg):
-            _fill_q4k(ctx, seed, layer_stream(layer, name), shards[name], t[name])
+            q6 = name in TYPED and t[TYPED[name]] == 14
+            _fill_q4k(ctx, seed, layer_stream(layer, name), shards[name], t[name], q6)
         for name in ("attn_norm", "ffn_norm"):
             ctx.gen_f32(seed, layer_stream(layer, name), cfg.dim, t[name], 1.0, 0.02)
         if cache_positions:
@@ -79,4 +97,5 @@ def fill_llama(llama, seed: int, cache_positions: int = 0, layers=None) -> None:
     g = llama.global_tensors()
     ctx.gen_f16(seed, global_stream("tok_embd"), cfg.vocab * cfg.dim, g["tok_embd"], 0.0, 0.02)
     ctx.gen_f32(seed, global_stream("output_norm"), cfg.dim, g["output_norm"], 1.0, 0.02)
-    _fill_q4k(ctx, seed, global_stream("output"), output_shard(cfg, shard), g["output"])
+    _fill_q4k(ctx, seed, global_stream("output"), output_shard(cfg, shard), g["output"],
+              g["output_type"] == 14)

@@ -26,12 +26,21 @@ import numpy as np
 from . import oracle as O
 
 
+def _is_q6k(W: np.ndarray, rows: int, cols: int) -> bool:
+    """Q6_K block bytes (210 per 256 elements) rather than Q4_K (144)."""
+    return W.dtype == np.uint8 and W.size == rows * cols // 256 * 210
+
+
 def _matvec(W: np.ndarray, rows: int, cols: int, x: np.ndarray) -> np.ndarray:
     """y = W x for a Q4_K tensor (block bytes; fp64 sums over the bit-exact
-    dequantized rows) or for a tensor already dequantized to fp32 [rows][cols]
-    by dense() (fp32 BLAS sums)."""
+    dequantized rows), a Q6_K tensor (the bit-exact dequantization of
+    DequantKernels.metal:131-172, fp64 sums) or a tensor already dequantized
+    to fp32 [rows][cols] by dense() (fp32 BLAS sums)."""
     if W.dtype == np.float32:
         return W @ np.ascontiguousarray(x, dtype=np.float32)
+    if _is_q6k(W, rows, cols):
+        w = O.q6k_dequant_f32(W, rows * cols).reshape(rows, cols).astype(np.float64)
+        return (w @ np.asarray(x, dtype=np.float64)).astype(np.float32)
     return O.q4k_matvec_f32x(W, rows, cols, x)
 
 
@@ -77,5 +86,6 @@ def dense(w: Dict[str, np.ndarray], shapes: Dict[str, tuple]) -> Dict[str, np.nd
     through fp32 BLAS products instead of dequantizing per token."""
     out = dict(w)
     for name, (rows, cols) in shapes.items():
-        out[name] = O.q4k_dequant_f32(w[name], rows * cols).reshape(rows, cols)
+        deq = O.q6k_dequant_f32 if _is_q6k(w[name], rows, cols) else O.q4k_dequant_f32
+        out[name] = deq(w[name], rows * cols).reshape(rows, cols)
     return out

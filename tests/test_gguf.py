@@ -119,7 +119,7 @@ def test_loader_shards_tile_each_tensor(tmp_path, size):
             seen = np.zeros(full.shape[:2], dtype=np.int32)
             for r in range(size):
                 sh = layer_shards(cfg, Shard(r, size))[name]
-                part = G._q4k_shard(f, f"blk.0.{G.LAYER_TENSORS[name]}.weight", rows, cols, sh)
+                part = G._block_shard(f, f"blk.0.{G.LAYER_TENSORS[name]}.weight", rows, cols, sh)
                 sl = (slice(sh["row0"], sh["row0"] + sh["rows"]), slice(sh["kb0"], sh["kb0"] + sh["nkb"]))
                 assert np.array_equal(part, full[sl])
                 seen[sl] += 1
@@ -128,7 +128,7 @@ def test_loader_shards_tile_each_tensor(tmp_path, size):
         parts = []
         for r in range(size):
             osh = output_shard(cfg, Shard(r, size))
-            parts.append(G._q4k_shard(f, "output.weight", cfg.vocab, cfg.dim,
+            parts.append(G._block_shard(f, "output.weight", cfg.vocab, cfg.dim,
                                       dict(row0=osh["row0"], rows=osh["rows"], kb0=0,
                                            nkb=cfg.dim // 256)))
         assert np.array_equal(np.concatenate(parts), out)
@@ -148,3 +148,20 @@ def test_failed_parse_closes_the_file(tmp_path):
     gc.collect()
     if before is not None:
         assert len(os.listdir(fd_dir)) <= before + 1
+
+
+def test_tensor_types_of_a_q4_k_m_file(tmp_path):
+    """Per-tensor types as the runner takes them: Q6_K attn_v / ffn_down /
+    output found by name; an all-Q4_K file gives None."""
+    path = str(tmp_path / "types.gguf")
+    G.write_gguf(path, _meta(), [
+        ("blk.0.attn_v.weight", G.Q6_K, (1024, 256), O.gen_q6k(3, 1, 1024)),
+        ("blk.0.ffn_down.weight", G.Q4_K, (1024, 256), O.gen_q4k(3, 2, 1024)),
+        ("output.weight", G.Q6_K, (1024, 256), O.gen_q6k(3, 3, 1024))])
+    with G.GGUFFile(path) as f:
+        t = G.tensor_types(f, 2)
+    assert t == {"output": G.Q6_K, "attn_v": [G.Q6_K, G.Q4_K], "ffn_down": [G.Q4_K, G.Q4_K]}
+    path2 = str(tmp_path / "plain.gguf")
+    G.write_gguf(path2, _meta(), [("output.weight", G.Q4_K, (1024, 256), O.gen_q4k(3, 3, 1024))])
+    with G.GGUFFile(path2) as f:
+        assert G.tensor_types(f, 2) is None

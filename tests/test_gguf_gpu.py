@@ -45,7 +45,9 @@ def interleaved_to_gguf(blocks: np.ndarray) -> np.ndarray:
     return b.reshape(-1)
 
 
-def write_model(path: str, cfg, embd_q4k: bool = False) -> None:
+def write_model(path: str, cfg, embd_q4k: bool = False, types: dict | None = None) -> None:
+    """A Llama GGUF file from the fill_llama streams; `types` (as given to the
+    runner) stores attn_v / ffn_down / output as Q6_K where it says so."""
     meta = {"general.architecture": "llama", "llama.block_count": cfg.n_layers,
             "llama.embedding_length": cfg.dim, "llama.feed_forward_length": cfg.ffn_dim,
             "llama.attention.head_count": cfg.n_heads,
@@ -57,6 +59,11 @@ def write_model(path: str, cfg, embd_q4k: bool = False) -> None:
     names = dict(G.LAYER_TENSORS)
     for l in range(cfg.n_layers):
         for ours, (rows, cols) in q4k_shapes(cfg).items():
+            key = {"wv": "attn_v", "w_down": "ffn_down"}.get(ours)
+            if types and key and types[key][l] == G.Q6_K:
+                w = O.gen_q6k(SEED, layer_stream(l, ours), rows * cols // 256)
+                tensors.append((f"blk.{l}.{names[ours]}.weight", G.Q6_K, (cols, rows), w))
+                continue
             w = O.gen_q4k(SEED, layer_stream(l, ours), rows * cols // 256)
             tensors.append((f"blk.{l}.{names[ours]}.weight", G.Q4_K, (cols, rows),
                             interleaved_to_gguf(w)))
@@ -72,8 +79,12 @@ def write_model(path: str, cfg, embd_q4k: bool = False) -> None:
                                   0.02)))
     tensors.append(("output_norm.weight", G.F32, (cfg.dim,),
                     O.gen_f32(SEED, global_stream("output_norm"), cfg.dim, 1.0, 0.02)))
-    out = O.gen_q4k(SEED, global_stream("output"), cfg.vocab * cfg.dim // 256)
-    tensors.append(("output.weight", G.Q4_K, (cfg.dim, cfg.vocab), interleaved_to_gguf(out)))
+    if types and types["output"] == G.Q6_K:
+        out = O.gen_q6k(SEED, global_stream("output"), cfg.vocab * cfg.dim // 256)
+        tensors.append(("output.weight", G.Q6_K, (cfg.dim, cfg.vocab), out))
+    else:
+        out = O.gen_q4k(SEED, global_stream("output"), cfg.vocab * cfg.dim // 256)
+        tensors.append(("output.weight", G.Q4_K, (cfg.dim, cfg.vocab), interleaved_to_gguf(out)))
     G.write_gguf(path, meta, tensors)
 
 
@@ -97,6 +108,31 @@ def test_loaded_runner_equals_filled_runner(ctx, tmp_path):
     got = _run(ctx, m, cfg)
     m.close()
     ref = Llama(ctx, cfg)
+    fill_llama(ref, SEED)
+    want = _run(ctx, ref, cfg)
+    ref.close()
+    assert np.array_equal(got[0], want[0])
+    assert np.array_equal(got[1], want[1])
+
+
+def test_q4_k_m_file_loads_with_its_types(ctx, tmp_path):
+    """A Q4_K_M-style file (Q6_K output head, Q6_K attn_v / ffn_down in some
+    layers): the loader creates the runner with those types, uploads the
+    Q6_K blocks unchanged and repacks only the Q4_K ones; the loaded runner
+    equals the directly filled typed runner bit for bit."""
+    cfg = llama_config(n_layers=3, dim=2048, n_heads=16, n_kv_heads=4, ffn_dim=4096,
+                       vocab=4096, max_seq=64)
+    types = {"output": G.Q6_K, "attn_v": [G.Q6_K, G.Q4_K, G.Q6_K],
+             "ffn_down": [G.Q6_K, G.Q6_K, G.Q4_K]}
+    path = str(tmp_path / "q4km.gguf")
+    write_model(path, cfg, types=types)
+    with G.GGUFFile(path) as f:
+        assert G.tensor_types(f, cfg.n_layers) == types
+    m = G.load_llama(ctx, path, max_seq=64)
+    assert m.layer_tensors(0)["wv_type"] == G.Q6_K and m.global_tensors()["output_type"] == G.Q6_K
+    got = _run(ctx, m, cfg)
+    m.close()
+    ref = Llama(ctx, cfg, types=types)
     fill_llama(ref, SEED)
     want = _run(ctx, ref, cfg)
     ref.close()

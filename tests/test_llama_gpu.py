@@ -27,9 +27,15 @@ def cfg_dict(cfg) -> dict:
             "rope_theta": cfg.rope.freq_base, "vocab": cfg.vocab}
 
 
-def oracle_layer(cfg, layer: int) -> dict:
-    w = {name: O.gen_q4k(SEED, layer_stream(layer, name), rows * cols // 256)
-         for name, (rows, cols) in q4k_shapes(cfg).items()}
+def oracle_layer(cfg, layer: int, types: dict | None = None) -> dict:
+    """The layer's tensors as fill_llama generates them; `types` as given to
+    the runner (Q6_K attn_v / ffn_down per layer)."""
+    def gen(name, rows, cols):
+        key = {"wv": "attn_v", "w_down": "ffn_down"}.get(name)
+        q6 = types is not None and key is not None and types.get(key) is not None and \
+            types[key][layer] == 14
+        return (O.gen_q6k if q6 else O.gen_q4k)(SEED, layer_stream(layer, name), rows * cols // 256)
+    w = {name: gen(name, rows, cols) for name, (rows, cols) in q4k_shapes(cfg).items()}
     for name in ("attn_norm", "ffn_norm"):
         w[name] = O.gen_f32(SEED, layer_stream(layer, name), cfg.dim, 1.0, 0.02)
     return w
@@ -47,10 +53,12 @@ def oracle_cache(cfg, layer: int, filled: int):
     return caches
 
 
-def oracle_globals(cfg) -> dict:
+def oracle_globals(cfg, types: dict | None = None) -> dict:
+    q6 = types is not None and types.get("output") == 14
     return {"tok_embd": O.gen_f16(SEED, global_stream("tok_embd"), cfg.vocab * cfg.dim, 0.0, 0.02),
             "output_norm": O.gen_f32(SEED, global_stream("output_norm"), cfg.dim, 1.0, 0.02),
-            "output": O.gen_q4k(SEED, global_stream("output"), cfg.vocab * cfg.dim // 256)}
+            "output": (O.gen_q6k if q6 else O.gen_q4k)(SEED, global_stream("output"),
+                                                      cfg.vocab * cfg.dim // 256)}
 
 
 def test_layer_decode_llama8b_shape(ctx):
@@ -134,9 +142,10 @@ def test_model_forward_and_greedy(ctx):
     m.close()
 
 
-def _oracle_model(cfg):
-    layers = [oracle_layer(cfg, l) for l in range(cfg.n_layers)]
-    return layers, oracle_globals(cfg), [oracle_cache(cfg, l, 0) for l in range(cfg.n_layers)]
+def _oracle_model(cfg, types: dict | None = None):
+    layers = [oracle_layer(cfg, l, types) for l in range(cfg.n_layers)]
+    return (layers, oracle_globals(cfg, types),
+            [oracle_cache(cfg, l, 0) for l in range(cfg.n_layers)])
 
 
 def _layer0_top2_gap(cfg, w0, glob, kcache, prompt, t: int) -> float:

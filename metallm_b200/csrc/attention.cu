@@ -243,6 +243,7 @@ __global__ void attn_decode_merge_kernel(const float *__restrict__ partials, int
                                          int nchunks, OutT *__restrict__ out,
                                          const int *__restrict__ pos_dev, int chunk_len,
                                          size_t part_bs, size_t out_bs) {
+  pdl_wait_then_release();
   const int h = blockIdx.x;
   const int dd = threadIdx.x;  // kAttnD threads
   const int bz = blockIdx.y;
@@ -640,14 +641,19 @@ static int attn_decode_impl(mlm_ctx *ctx, const void *q, const void *kc, const v
               : G == 2 ? attn_decode_partial_kernel<2, OutT, false>
               : G == 4 ? attn_decode_partial_kernel<4, OutT, false>
                        : attn_decode_partial_kernel<8, OutT, false>;
-  kern<<<grid, kAttnThreads, kAttnStageBytes, stream>>>(qh, kh, vh, n_heads, n_kv, seq_len,
-                                                        chunk_len, scale, partials, pos_dev, q_bs,
-                                                        kv_bs, part_bs, out, out_bs, nullptr);
-  int st = check_launch(ctx, "mlm_attn_decode (partial)");
+  int st = check_launch_pdl(
+      ctx,
+      launch_pdl(kern, grid, dim3(kAttnThreads), kAttnStageBytes, stream, qh, kh, vh, n_heads,
+                 n_kv, seq_len, chunk_len, scale, partials, pos_dev, q_bs, kv_bs, part_bs, out,
+                 out_bs, static_cast<int *>(nullptr)),
+      "mlm_attn_decode (partial)");
   if (st != MLM_OK) return st;
-  attn_decode_merge_kernel<OutT><<<dim3(n_heads, batch), kAttnD, 0, stream>>>(
-      partials, n_heads, nchunks, out, pos_dev, chunk_len, part_bs, out_bs);
-  return check_launch(ctx, "mlm_attn_decode (merge)");
+  return check_launch_pdl(
+      ctx,
+      launch_pdl(attn_decode_merge_kernel<OutT>, dim3(n_heads, batch), dim3(kAttnD), 0, stream,
+                 static_cast<const float *>(partials), n_heads, nchunks, out, pos_dev, chunk_len,
+                 part_bs, out_bs),
+      "mlm_attn_decode (merge)");
 }
 
 int attn_decode_launch(mlm_ctx *ctx, const void *q, const void *kc, const void *vc, int n_heads,

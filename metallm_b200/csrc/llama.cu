@@ -277,9 +277,11 @@ struct mlm_llama {
     if ((st = embed_rows_launch(ctx, tok_embd, c.vocab, c.dim, pf_tokens, T, pf_hidden, s))) return st;
     for (int l = 0; l < c.n_layers; ++l) {
       const LayerBuf &L = layers[l];
-      if ((st = rmsnorm_rows_bf16_launch(ctx, pf_hidden, L.attn_norm, pf_x, T, c.dim, c.rms_eps, s)))
+      const bool zq = T <= 8 && L.v_type != MLM_TYPE_Q6_K;  // batched GEMV: accumulates
+      if ((st = rmsnorm_rows_bf16_launch(ctx, pf_hidden, L.attn_norm, pf_x, T, c.dim, c.rms_eps, s,
+                                         zq ? pf_qkv : nullptr, (size_t)T * qkv_rows())))
         return st;
-      if ((st = qkv_rows_linear(L, pf_x, T))) return st;
+      if ((st = qkv_rows_linear(L, pf_x, T, zq))) return st;
       __half *kc = L.kc + cur * seq_elems(), *vc = L.vc + cur * seq_elems();
       if ((st = rope_kv_rows_launch(ctx, pf_qkv, rope_freqs, c.rope, nh(), nkv(), c.head_dim, pos,
                                     T, pf_q16, kc, vc, s)))
@@ -288,9 +290,10 @@ struct mlm_llama {
                                     pf_attn, s)))
         return st;
       if ((st = row_parallel_rows(L.wo, qdim(), pf_attn, T))) return st;
-      if ((st = rmsnorm_rows_bf16_launch(ctx, pf_hidden, L.ffn_norm, pf_x, T, c.dim, c.rms_eps, s)))
+      if ((st = rmsnorm_rows_bf16_launch(ctx, pf_hidden, L.ffn_norm, pf_x, T, c.dim, c.rms_eps, s,
+                                         T <= 8 ? pf_gu : nullptr, (size_t)T * 2 * ffn())))
         return st;
-      if ((st = linear(L.gu, 2 * ffn(), c.dim, pf_x, T, pf_gu, nullptr))) return st;
+      if ((st = linear(L.gu, 2 * ffn(), c.dim, pf_x, T, pf_gu, nullptr, T <= 8))) return st;
       if ((st = swiglu_rows_bf16_launch(ctx, pf_gu, ffn(), T, pf_x, s))) return st;
       if ((st = row_parallel_rows(L.down, ffn(), pf_x, T, L.down_type))) return st;
     }
@@ -299,8 +302,9 @@ struct mlm_llama {
 
   // pf_qkv = X Wqkv^T over T rows [T][q | k | v]: one Q4_K linear, or the
   // Q4_K q/k rows and the Q6_K v rows written beside them
-  int qkv_rows_linear(const LayerBuf &L, const void *x, int T) {
-    if (L.v_type != MLM_TYPE_Q6_K) return linear(L.qkv, qkv_rows(), cfg.dim, x, T, pf_qkv, nullptr);
+  int qkv_rows_linear(const LayerBuf &L, const void *x, int T, bool y_zeroed = false) {
+    if (L.v_type != MLM_TYPE_Q6_K)
+      return linear(L.qkv, qkv_rows(), cfg.dim, x, T, pf_qkv, nullptr, y_zeroed);
     const int r4 = qkv4_rows(L);
     int st = linear(L.qkv, r4, cfg.dim, x, T, pf_tmp, nullptr);
     if (st != MLM_OK) return st;
@@ -324,9 +328,11 @@ struct mlm_llama {
     if ((st = embed_rows_launch(ctx, tok_embd, c.vocab, c.dim, tok_b, B, pf_hidden, s))) return st;
     for (int l = 0; l < c.n_layers; ++l) {
       const LayerBuf &L = layers[l];
-      if ((st = rmsnorm_rows_bf16_launch(ctx, pf_hidden, L.attn_norm, pf_x, B, c.dim, c.rms_eps, s)))
+      const bool zq = L.v_type != MLM_TYPE_Q6_K;  // the batched GEMV accumulates into pf_qkv
+      if ((st = rmsnorm_rows_bf16_launch(ctx, pf_hidden, L.attn_norm, pf_x, B, c.dim, c.rms_eps, s,
+                                         zq ? pf_qkv : nullptr, (size_t)B * qkv_rows())))
         return st;
-      if ((st = qkv_rows_linear(L, pf_x, B))) return st;
+      if ((st = qkv_rows_linear(L, pf_x, B, zq))) return st;
       if ((st = rope_kv_batch_launch(ctx, pf_qkv, rope_freqs, c.rope, nh(), nkv(), c.head_dim, B,
                                      pos_b, seq_elems(), pf_q16, L.kc, L.vc, s)))
         return st;
@@ -335,9 +341,10 @@ struct mlm_llama {
                                          b_partial_floats, s, pos_b)))
         return st;
       if ((st = row_parallel_rows(L.wo, qdim(), pf_attn, B))) return st;
-      if ((st = rmsnorm_rows_bf16_launch(ctx, pf_hidden, L.ffn_norm, pf_x, B, c.dim, c.rms_eps, s)))
+      if ((st = rmsnorm_rows_bf16_launch(ctx, pf_hidden, L.ffn_norm, pf_x, B, c.dim, c.rms_eps, s,
+                                         pf_gu, (size_t)B * 2 * ffn())))
         return st;
-      if ((st = linear(L.gu, 2 * ffn(), c.dim, pf_x, B, pf_gu, nullptr))) return st;
+      if ((st = linear(L.gu, 2 * ffn(), c.dim, pf_x, B, pf_gu, nullptr, true))) return st;
       if ((st = swiglu_rows_bf16_launch(ctx, pf_gu, ffn(), B, pf_x, s))) return st;
       if ((st = row_parallel_rows(L.down, ffn(), pf_x, B, L.down_type))) return st;
     }
@@ -382,9 +389,12 @@ struct mlm_llama {
   // Y = X W^T (+ residual) over T token rows of bf16 X: up to 8 rows (a
   // decode batch) stream the weights through the batched GEMV, more through
   // the tensor-core GEMM
+  // y_zeroed: y was cleared by the kernel before (the RMSNorm rows feeding
+  // this linear), so the batched GEMV needs no memset of its own
   int linear(const uint8_t *W, int rows, int cols, const void *x, int T, float *y,
-             const float *res) {
-    if (T <= 8) return gemv_batch_launch(ctx, W, rows, cols, x, T, y, res, ctx->stream);
+             const float *res, bool y_zeroed = false) {
+    if (T <= 8)
+      return gemv_batch_launch(ctx, W, rows, cols, x, T, y, res, ctx->stream, y_zeroed);
     return gemm_launch(ctx, W, rows, cols, x, T, y, res, ctx->stream);
   }
   // A Q6_K weight over T token rows.  Up to 8 rows (a decode batch, a short

@@ -174,15 +174,18 @@ int silu_mul_launch(mlm_ctx *ctx, const float *g, const float *u, void *out, int
                     cudaStream_t stream);
 // decode linears of a batch of up to 8 tokens (q4k_gemv_batch.cu): Y[t] =
 // W X[t] (+ residual, which may be Y itself), X bf16 [tokens][cols]
+// y_zeroed: y is known to be zero already (no residual): skips the memset
 int gemv_batch_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_bf16,
-                      int tokens, float *y, const float *residual, cudaStream_t stream);
+                      int tokens, float *y, const float *residual, cudaStream_t stream,
+                      bool y_zeroed = false);
 // batched prompt pass (prefill.cu, q4k_gemm.cu)
 int gemm_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_bf16, int tokens,
                 float *y, const float *residual, cudaStream_t stream);
 int embed_rows_launch(mlm_ctx *ctx, const void *table, int vocab, int dim, const int32_t *tokens,
                       int T, float *out, cudaStream_t stream);
 int rmsnorm_rows_bf16_launch(mlm_ctx *ctx, const float *x, const float *w, void *y, int rows,
-                             int n, float eps, cudaStream_t stream);
+                             int n, float eps, cudaStream_t stream, float *zero = nullptr,
+                             size_t zero_n = 0);
 int rope_kv_rows_launch(mlm_ctx *ctx, const float *qkv, const float *freqs, const mlm_rope_args &a,
                         int nq, int nkv, int d, int pos0, int T, void *q_out, void *kc, void *vc,
                         cudaStream_t stream);

@@ -18,6 +18,7 @@ namespace {
 // hidden[t] = float(table[tokens[t]]) (tokens clamped into the vocabulary)
 __global__ void embed_rows_kernel(const __half *__restrict__ table, int vocab, int dim,
                                   const int32_t *__restrict__ tokens, float *__restrict__ out) {
+  pdl_wait_then_release();
   const int t = blockIdx.y;
   int tok = tokens[t];
   tok = tok < 0 ? 0 : (tok >= vocab ? vocab - 1 : tok);
@@ -26,23 +27,60 @@ __global__ void embed_rows_kernel(const __half *__restrict__ table, int vocab, i
     out[(size_t)t * dim + i] = __half2float(row[i]);
 }
 
-// one row per CTA: bf16(x * rms_scale(x) * w) (NormalizationKernels.metal:31-79)
-__global__ void __launch_bounds__(512) rmsnorm_rows_bf16_kernel(const float *__restrict__ x,
-                                                               const float *__restrict__ w,
-                                                               __nv_bfloat16 *__restrict__ y,
-                                                               int n, float eps) {
-  __shared__ float red[32];
-  const float *xr = x + (size_t)blockIdx.x * n;
+// one row per CTA: bf16(x * rms_scale(x) * w) (NormalizationKernels.metal:31-79).
+// The row is read once: each thread keeps its float4 pieces in registers
+// across the reduction (rows of up to 512 x 4 x kRmsPer elements).  When
+// zero is set the CTAs also clear zero[0 .. zero_n) (the output of the
+// accumulating GEMV that consumes these rows).
+constexpr int kRmsThreads = 512;
+constexpr int kRmsPer = 8;  // float4 pieces per thread: rows up to 16384
+__global__ void __launch_bounds__(kRmsThreads) rmsnorm_rows_bf16_kernel(
+    const float *__restrict__ x, const float *__restrict__ w, __nv_bfloat16 *__restrict__ y, int n,
+    float eps, float *__restrict__ zero, size_t zero_n, int rows) {
+  __shared__ float red[kRmsThreads / 32];
+  pdl_wait_then_release();
+  if (zero) {
+    float4 *z4 = reinterpret_cast<float4 *>(zero);
+    const size_t n4 = zero_n / 4;
+    for (size_t i = (size_t)blockIdx.x * kRmsThreads + threadIdx.x; i < n4;
+         i += (size_t)gridDim.x * kRmsThreads)
+      z4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  if ((int)blockIdx.x >= rows) return;  // CTAs beyond the rows only clear
+  const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)blockIdx.x * n);
+  const float4 *w4 = reinterpret_cast<const float4 *>(w);
+  const int n4 = n / 4;
+  float4 v[kRmsPer];
   float ss = 0.f;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) ss += xr[i] * xr[i];
+#pragma unroll
+  for (int k = 0; k < kRmsPer; ++k) {
+    const int i = threadIdx.x + k * kRmsThreads;
+    v[k] = i < n4 ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int k = 0; k < kRmsPer; ++k)
+    ss += v[k].x * v[k].x + v[k].y * v[k].y + v[k].z * v[k].z + v[k].w * v[k].w;
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
   float tot = 0.f;
-  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += red[i];
+#pragma unroll
+  for (int i = 0; i < kRmsThreads / 32; ++i) tot += red[i];
   const float scale = rms_scale(tot, n, eps);
-  for (int i = threadIdx.x; i < n; i += blockDim.x)
-    y[(size_t)blockIdx.x * n + i] = __float2bfloat16_rn((xr[i] * scale) * safe_weight(w[i]));
+  uint2 *yr = reinterpret_cast<uint2 *>(y + (size_t)blockIdx.x * n);
+#pragma unroll
+  for (int k = 0; k < kRmsPer; ++k) {
+    const int i = threadIdx.x + k * kRmsThreads;
+    if (i < n4) {
+      const float4 ww = __ldg(w4 + i);
+      const __nv_bfloat162 lo = __floats2bfloat162_rn((v[k].x * scale) * safe_weight(ww.x),
+                                                      (v[k].y * scale) * safe_weight(ww.y));
+      const __nv_bfloat162 hi = __floats2bfloat162_rn((v[k].z * scale) * safe_weight(ww.z),
+                                                      (v[k].w * scale) * safe_weight(ww.w));
+      yr[i] = make_uint2(*reinterpret_cast<const uint32_t *>(&lo),
+                         *reinterpret_cast<const uint32_t *>(&hi));
+    }
+  }
 }
 
 // RoPE of q and k of token t at position pos0 + t; q -> fp16 q_out, rotated
@@ -97,6 +135,7 @@ __global__ void rope_kv_rows_kernel(mlm_rope_args a, RopeConsts k, const float *
 // out[t][i] = bf16(silu(gu[t][i]) * gu[t][ffn + i])
 __global__ void swiglu_rows_bf16_kernel(const float *__restrict__ gu, int ffn,
                                         __nv_bfloat16 *__restrict__ out) {
+  pdl_wait_then_release();
   const int t = blockIdx.y;
   const float *row = gu + (size_t)t * 2 * ffn;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ffn; i += gridDim.x * blockDim.x)
@@ -284,16 +323,25 @@ int prefill_init(mlm_ctx *ctx) {
 
 int embed_rows_launch(mlm_ctx *ctx, const void *table, int vocab, int dim, const int32_t *tokens,
                       int T, float *out, cudaStream_t stream) {
-  embed_rows_kernel<<<dim3((dim + 255) / 256, T), 256, 0, stream>>>(
-      reinterpret_cast<const __half *>(table), vocab, dim, tokens, out);
-  return check_launch(ctx, "prefill (embedding)");
+  return check_launch_pdl(
+      ctx,
+      launch_pdl(embed_rows_kernel, dim3((dim + 255) / 256, T), dim3(256), 0, stream,
+                 reinterpret_cast<const __half *>(table), vocab, dim, tokens, out),
+      "prefill (embedding)");
 }
 
 int rmsnorm_rows_bf16_launch(mlm_ctx *ctx, const float *x, const float *w, void *y, int rows,
-                             int n, float eps, cudaStream_t stream) {
-  rmsnorm_rows_bf16_kernel<<<rows, 512, 0, stream>>>(x, w, reinterpret_cast<__nv_bfloat16 *>(y), n,
-                                                     eps);
-  return check_launch(ctx, "prefill (rmsnorm)");
+                             int n, float eps, cudaStream_t stream, float *zero, size_t zero_n) {
+  MLM_REQUIRE(ctx, n % 4 == 0 && n <= 4 * kRmsThreads * kRmsPer && zero_n % 4 == 0,
+              MLM_ERR_SHAPE, "rmsnorm rows: n=%d", n);
+  // a few rows clearing a large output get extra CTAs for the clearing
+  const size_t zero_ctas = zero ? std::min<size_t>(148, (zero_n / 4 + 4095) / 4096) : 0;
+  const int grid = (int)std::max<size_t>(rows, zero_ctas);
+  return check_launch_pdl(
+      ctx,
+      launch_pdl(rmsnorm_rows_bf16_kernel, dim3(grid), dim3(kRmsThreads), 0, stream, x, w,
+                 reinterpret_cast<__nv_bfloat16 *>(y), n, eps, zero, zero_n, rows),
+      "prefill (rmsnorm)");
 }
 
 int rope_kv_rows_launch(mlm_ctx *ctx, const float *qkv, const float *freqs, const mlm_rope_args &a,
@@ -336,9 +384,10 @@ int attn_prefill_launch(mlm_ctx *ctx, const void *q16, const void *kc, const voi
 
 int swiglu_rows_bf16_launch(mlm_ctx *ctx, const float *gu, int ffn, int T, void *out,
                             cudaStream_t stream) {
-  swiglu_rows_bf16_kernel<<<dim3((ffn + 255) / 256, T), 256, 0, stream>>>(
-      gu, ffn, reinterpret_cast<__nv_bfloat16 *>(out));
-  return check_launch(ctx, "prefill (swiglu)");
+  return check_launch_pdl(ctx,
+                          launch_pdl(swiglu_rows_bf16_kernel, dim3((ffn + 255) / 256, T), dim3(256),
+                                     0, stream, gu, ffn, reinterpret_cast<__nv_bfloat16 *>(out)),
+                          "prefill (swiglu)");
 }
 
 // out[t] = (a[t] | b[t]): two row-major blocks of T rows, ra and rb floats

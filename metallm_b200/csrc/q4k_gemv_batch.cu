@@ -97,6 +97,27 @@ __global__ void __launch_bounds__(kBgThreads, 2) q4k_gemv_batch_kernel(BgArgs p)
   const int kb0 = chunk * kBgChunk, nkb = min(kBgChunk, p.nb - kb0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
+  uint8_t *mystage = wstage + warp * 2 * kBgStage;
+  const uint32_t stage_addr = (uint32_t)__cvta_generic_to_shared(mystage);
+  // block column kb of tile's 16 rows -> stage buf (rows past the end are
+  // zero-filled)
+  auto issue = [&](int tile, int kb, int buf) {
+    for (int c = lane; c < kBgRows * 9; c += 32) {
+      const int row = c / 9, part = c - row * 9;
+      const int gr = tile * kBgRows + row;
+      const bool live = gr < p.rows;
+      const uint8_t *src =
+          p.W + ((size_t)(live ? gr : 0) * p.nb + kb0 + kb) * kBlockBytes + part * 16;
+      cp_async16(stage_addr + buf * kBgStage + row * kBlockBytes + part * 16, src,
+                 live ? 16u : 0u);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  // the weights do not depend on the kernel before this one: the warp's
+  // first block column is in flight before waiting for it (x, y)
+  const int first_tile = cj + p.ctas_per_chunk * warp;
+  if (first_tile < p.tiles) issue(first_tile, 0, 0);
+  pdl_wait_then_release();
 
   // ---- stage x: one thread per (token, sub-block, t): elements 8t .. 8t+7 --
   if (threadIdx.x < kBgMaxT) tokmax[threadIdx.x] = 0;
@@ -159,33 +180,16 @@ __global__ void __launch_bounds__(kBgThreads, 2) q4k_gemv_batch_kernel(BgArgs p)
 
   // ---- tiles of this chunk, round-robin over the CTA's warps ---------------
   const uint32_t M = 0x000F000Fu, MH = 0x00F000F0u;
-  uint8_t *mystage = wstage + warp * 2 * kBgStage;
-  const uint32_t stage_addr = (uint32_t)__cvta_generic_to_shared(mystage);
-  for (int tile = cj + p.ctas_per_chunk * warp; tile < p.tiles;
-       tile += p.ctas_per_chunk * kBgWarps) {
+  for (int tile = first_tile; tile < p.tiles; tile += p.ctas_per_chunk * kBgWarps) {
     const int r0 = tile * kBgRows + g, r1 = r0 + 8;
     const bool ok0 = r0 < p.rows, ok1 = r1 < p.rows;
-    // block column kb of the tile's 16 rows -> stage buf (rows past the end
-    // are zero-filled)
-    auto issue = [&](int kb, int buf) {
-      for (int c = lane; c < kBgRows * 9; c += 32) {
-        const int row = c / 9, part = c - row * 9;
-        const int gr = tile * kBgRows + row;
-        const bool live = gr < p.rows;
-        const uint8_t *src =
-            p.W + ((size_t)(live ? gr : 0) * p.nb + kb0 + kb) * kBlockBytes + part * 16;
-        cp_async16(stage_addr + buf * kBgStage + row * kBlockBytes + part * 16, src,
-                   live ? 16u : 0u);
-      }
-      asm volatile("cp.async.commit_group;" ::: "memory");
-    };
     // (r0, 2t) (r0, 2t+1) (r1, 2t) (r1, 2t+1): the scaled-x products and the
     // min terms
     float aq[4] = {0.f, 0.f, 0.f, 0.f}, am[4] = {0.f, 0.f, 0.f, 0.f};
-    issue(0, 0);
+    if (tile != first_tile) issue(tile, 0, 0);
     for (int kb = 0; kb < nkb; ++kb) {
       if (kb + 1 < nkb) {
-        issue(kb + 1, (kb + 1) & 1);
+        issue(tile, kb + 1, (kb + 1) & 1);
         asm volatile("cp.async.wait_group 1;" ::: "memory");
       } else {
         asm volatile("cp.async.wait_group 0;" ::: "memory");
@@ -252,7 +256,8 @@ int gemv_batch_init(mlm_ctx *ctx) {
 }
 
 int gemv_batch_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_bf16,
-                      int tokens, float *y, const float *residual, cudaStream_t stream) {
+                      int tokens, float *y, const float *residual, cudaStream_t stream,
+                      bool y_zeroed) {
   MLM_CHECK_CTX(ctx);
   MLM_REQUIRE(ctx, W && x_bf16 && y, MLM_ERR_ARG, "mlm_q4k_gemv_batch: null buffer");
   MLM_REQUIRE(ctx, rows > 0 && cols > 0 && cols % kQK == 0 && tokens >= 1 && tokens <= kBgMaxT,
@@ -263,9 +268,9 @@ int gemv_batch_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const voi
   MLM_REQUIRE(ctx, aligned16(W) && aligned16(x_bf16), MLM_ERR_ALIGN,
               "mlm_q4k_gemv_batch: W and X must be 16-byte aligned");
   const size_t ybytes = sizeof(float) * (size_t)rows * tokens;
-  if (!residual)
-    MLM_CUDA_TRY(ctx, cudaMemsetAsync(y, 0, ybytes, stream));
-  else if (residual != y)
+  if (!residual) {
+    if (!y_zeroed) MLM_CUDA_TRY(ctx, cudaMemsetAsync(y, 0, ybytes, stream));
+  } else if (residual != y)
     MLM_CUDA_TRY(ctx, cudaMemcpyAsync(y, residual, ybytes, cudaMemcpyDeviceToDevice, stream));
   BgArgs a;
   a.W = reinterpret_cast<const uint8_t *>(W);
@@ -280,8 +285,10 @@ int gemv_batch_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const voi
   // about two CTAs per SM over all chunks; never more CTAs than tiles
   a.ctas_per_chunk =
       std::max(1, std::min(a.tiles / kBgWarps + 1, (2 * ctx->sm_count + nchunks - 1) / nchunks));
-  q4k_gemv_batch_kernel<<<nchunks * a.ctas_per_chunk, kBgThreads, kBgSmem, stream>>>(a);
-  return check_launch(ctx, "mlm_q4k_gemv_batch");
+  return check_launch_pdl(ctx,
+                          launch_pdl(q4k_gemv_batch_kernel, dim3(nchunks * a.ctas_per_chunk),
+                                     dim3(kBgThreads), kBgSmem, stream, a),
+                          "mlm_q4k_gemv_batch");
 }
 
 }  // namespace mlm

@@ -237,6 +237,22 @@ def barrier(pg, local):
         pg.barrier()
 
 
+class nvtx_range:
+    """An NVTX range around a timed region, so a profiler can select its
+    kernels (ncu --nvtx --nvtx-include "timed/"); no effect otherwise."""
+
+    def __init__(self, name: str):
+        self.name = name
+
+    def __enter__(self):
+        import torch
+        torch.cuda.nvtx.range_push(self.name)
+
+    def __exit__(self, *exc):
+        import torch
+        torch.cuda.nvtx.range_pop()
+
+
 L2_BYTES = 126 * 1024 * 1024
 
 
@@ -911,7 +927,8 @@ def run_llama(args, world, rank, local, pg) -> dict:
         sampler.start()
         time.sleep(0.3)
         pos0 = m.position
-        dev_ms = timed(lambda: m.decode_greedy(last, steps, out))
+        with nvtx_range("timed"):
+            dev_ms = timed(lambda: m.decode_greedy(last, steps, out))
         clocks = sampler.stop()
         toks = out.download(np.int32, steps)
         ms_max = max_over_ranks(dev_ms, pg, local)
@@ -1029,7 +1046,8 @@ def run_tp70b(args, world, rank, local, pg) -> dict:
     sampler.start()
     time.sleep(0.3)
     pos0 = m.seq_position(0)
-    dev_ms = timed(lambda: m.decode_greedy_batch(last, steps, out))
+    with nvtx_range("timed"):
+        dev_ms = timed(lambda: m.decode_greedy_batch(last, steps, out))
     clocks = sampler.stop()
     toks = out.download(np.int32, steps * B).reshape(steps, B)
     ms_max = max_over_ranks(dev_ms, pg, local)

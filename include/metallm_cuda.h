@@ -222,6 +222,15 @@ int mlm_q4k_gemv_rmsnorm(mlm_ctx *ctx, const void *W, int rows, int cols, const 
  * in one launch. */
 int mlm_q4k_gemv_swiglu(mlm_ctx *ctx, const void *W, int rows, int cols, const float *gate,
                         const float *up, float *y, const float *residual);
+/* The decode FFN's gate and up projections as one GEMV over W = [gate rows;
+ * up rows] (rows = 2F, F a multiple of 32) on x = RMSNorm(hidden), whose
+ * epilogue also forms h = silu(gate) * up (LlamaRunner.swift:1008-1058:
+ * gate, up, applySILU, multiply) in the scaled fp16 form of
+ * mlm_silu_mul_scaled: h_f16 [F], h_scale [F/32], bit-identical to that op on
+ * y.  h is the x of the down projection through mlm_q4k_gemv_xs; no CTA
+ * evaluates the SiLU of an element more than once. */
+int mlm_q4k_gemv_gate_up(mlm_ctx *ctx, const void *W, int rows, int cols, const float *hidden,
+                         const float *norm_w, float eps, float *y, void *h_f16, float *h_scale);
 
 /* Prefill GEMM on packed Q4_K weights: y[t][n] = sum_k x[t][k] * W[n][k] for
  * `tokens` rows of x at once (bf16 [tokens][cols] row-major; y fp32

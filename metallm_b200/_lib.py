@@ -119,6 +119,8 @@ SIGNATURES = [
     ("mlm_q4k_gemv_xs", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_vp]),
     ("mlm_q4k_gemv_rmsnorm", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_float, c_vp, c_vp]),
     ("mlm_q4k_gemv_swiglu", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_vp, c_vp]),
+    ("mlm_q4k_gemv_gate_up", c_int,
+     [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_float, c_vp, c_vp, c_vp]),
     ("mlm_q4k_gemm", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_int, c_vp, c_vp]),
     ("mlm_q4k_gemv_batch", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_int, c_vp, c_vp]),
     ("mlm_q4k_gemv_static", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_vp]),

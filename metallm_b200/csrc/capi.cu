@@ -112,10 +112,12 @@ extern "C" int mlm_create(int device, mlm_ctx **out) {
 
   ctx->gemv_max_tiles = kMaxGemvRows / 32;
   ctx->gemv_max_ctas = gemv_max_ctas(ctx->sm_count);
-  if (cudaMalloc(&ctx->gemv_counters, sizeof(int) * ctx->gemv_max_tiles) != cudaSuccess ||
+  // split-K tile counters, then the gate/up pairing counters (half as many)
+  const size_t counter_bytes = sizeof(int) * (ctx->gemv_max_tiles + ctx->gemv_max_tiles / 2);
+  if (cudaMalloc(&ctx->gemv_counters, counter_bytes) != cudaSuccess ||
       cudaMalloc(&ctx->gemv_partials, sizeof(float) * 64 * ctx->gemv_max_ctas) != cudaSuccess)
     return fail(MLM_ERR_ALLOC);
-  if (cudaMemset(ctx->gemv_counters, 0, sizeof(int) * ctx->gemv_max_tiles) != cudaSuccess)
+  if (cudaMemset(ctx->gemv_counters, 0, counter_bytes) != cudaSuccess)
     return fail(MLM_ERR_CUDA);
   ctx->attn_partials_floats = attn_partial_floats_max(kMaxAttnHeads);
   if (cudaMalloc(&ctx->attn_partials, sizeof(float) * ctx->attn_partials_floats) != cudaSuccess)

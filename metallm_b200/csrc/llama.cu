@@ -112,6 +112,8 @@ struct mlm_llama {
   // activations of one step
   float *hidden = nullptr, *qkv_out = nullptr, *gu_out = nullptr, *logits = nullptr;
   __half *attn_out = nullptr;
+  __half *ffn_h = nullptr;  // silu(gate) * up as scaled fp16, from the gate/up GEMV
+  float *ffn_h_scale = nullptr;
   int *state = nullptr;
   int32_t *gen_tokens = nullptr;  // [max_seq] tokens of the captured greedy loop
   // batched prompt pass: activations of up to pf_chunk tokens
@@ -202,15 +204,18 @@ struct mlm_llama {
                                       ctx->attn_partials_floats, s, state + kPos)))
       return st;
     if ((st = row_parallel(L.wo, qdim(), gemv_half(attn_out), h))) return st;  // + residual
-    if ((st = gemv(L.gu, 2 * ffn(), c.dim, normed(h, L.ffn_norm), gu_out, nullptr))) return st;
-    // the SiLU-gated product is formed in the down projection's x staging,
-    // as fp16 with per-32 power-of-two scales (it exceeds the fp16 range on
-    // large activations)
-    GemvInput sw;
-    sw.mode = GemvInput::kSwiGLU;
-    sw.a = gu_out;
-    sw.b = gu_out + ffn();
-    return row_parallel(L.down, ffn(), sw, h, L.down_type);  // + residual
+    // the gate/up GEMV's epilogue forms the SiLU-gated product once per
+    // element, as fp16 with per-32 power-of-two scales (it exceeds the fp16
+    // range on large activations); the down projection stages it as is
+    GemvPair pair;
+    pair.h_f16 = ffn_h;
+    pair.h_scale = ffn_h_scale;
+    pair.counters = ctx->gemv_counters + ctx->gemv_max_tiles;
+    if ((st = gemv_launch(ctx, L.gu, 2 * ffn(), c.dim, normed(h, L.ffn_norm), gu_out, nullptr,
+                          ctx->gemv_partials, ctx->gemv_counters, ctx->gemv_max_ctas,
+                          ctx->gemv_max_tiles, s, &pair)))
+      return st;
+    return row_parallel(L.down, ffn(), gemv_half(ffn_h, ffn_h_scale), h, L.down_type);
   }
 
   // a decode GEMV on a weight of either type
@@ -562,6 +567,8 @@ static int llama_create(mlm_ctx *ctx, const mlm_llama_config *cfg, int batch,
       m->alloc(&m->gu_out, sizeof(float) * 2 * m->ffn()) ||
       m->alloc(&m->logits, sizeof(float) * c.vocab) ||
       m->alloc(&m->attn_out, sizeof(__half) * m->qdim()) ||
+      m->alloc(&m->ffn_h, sizeof(__half) * m->ffn()) ||
+      m->alloc(&m->ffn_h_scale, sizeof(float) * (m->ffn() / 32)) ||
       m->alloc(&m->state, sizeof(int) * kStateInts) ||
       m->alloc(&m->gen_tokens, sizeof(int32_t) * c.max_seq))
     return fail(MLM_ERR_ALLOC);

@@ -103,8 +103,6 @@ __device__ __forceinline__ float rms_scale(float sum_sq, int n, float eps) {
 __device__ __forceinline__ float safe_weight(float w) {
   return (isnan(w) || isinf(w)) ? 1.0f : w;
 }
-// SiLU-gated product of the decode FFN (kernel_silu_f16 then kernel_mul_f16,
-// ActivationKernels.metal:6-27, in fp32)
 // round an fp32 value to the storage type of an output (round to nearest even)
 template <class T>
 __device__ __forceinline__ T from_float(float v);
@@ -117,8 +115,17 @@ __device__ __forceinline__ __nv_bfloat16 from_float<__nv_bfloat16>(float v) {
   return __float2bfloat16_rn(v);
 }
 
+// SiLU-gated product of the decode FFN (kernel_silu_f16 then kernel_mul_f16,
+// ActivationKernels.metal:6-27, in fp32)
 __device__ __forceinline__ float swiglu(float g, float u) {
   return g * (1.0f / (1.0f + expf(-g))) * u;
+}
+
+// Exponent e of the scaled fp16 form of a 32-element sub-block whose largest
+// magnitude is m: its values are stored as fp16(v * 2^-e) with scale 2^e, so
+// the largest stays below 2^15 (e = 0 when it already does).
+__device__ __forceinline__ int silu_scale_exp(float m) {
+  return max(0, (int)((__float_as_uint(m) >> 23) & 0xFF) - 127 - 14);
 }
 
 // 128-bit streaming load that does not allocate in L1 (weights are read once)

@@ -26,7 +26,7 @@ struct mlm_ctx {
   // and one arrival counter per row tile; counters return to zero after
   // every launch.
   float *gemv_partials = nullptr;
-  int *gemv_counters = nullptr;
+  int *gemv_counters = nullptr;  // [gemv_max_tiles] split-K, then [gemv_max_tiles / 2] pairing
   int gemv_max_ctas = 0;
   int gemv_max_tiles = 0;
 
@@ -141,9 +141,20 @@ inline GemvInput gemv_half(const void *x, const float *x_scale = nullptr) {
 }
 int gemv_validate(mlm_ctx *ctx, const void *W, int rows, int cols, const GemvInput &in,
                   float *y);
+// Gate/up pairing of a decode GEMV over [gate rows; up rows]: once both
+// tiles t and t + rows / 64 of y are stored, the warp that stores the second
+// one also writes h = silu(gate) * up of those 32 elements in the scaled fp16
+// form of mlm_silu_mul_scaled (h_f16, one scale per 32), so the down
+// projection stages a plain fp16 x.  counters: rows / 64 ints, zero between
+// launches (the second arrival re-zeroes its own).
+struct GemvPair {
+  void *h_f16 = nullptr;  // fp16 [rows / 2]
+  float *h_scale = nullptr;
+  int *counters = nullptr;
+};
 int gemv_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const GemvInput &in, float *y,
                 const float *residual, float *partials, int *counters, int max_ctas,
-                int max_tiles, cudaStream_t stream);
+                int max_tiles, cudaStream_t stream, const GemvPair *pair = nullptr);
 int rmsnorm_f32_launch(mlm_ctx *ctx, const float *x, const float *w, float *y32, void *y16,
                        int rows, int n, float eps, cudaStream_t stream);
 int rope_qk_kv_launch(mlm_ctx *ctx, const float *q, const float *k, const float *v,

@@ -80,6 +80,10 @@ struct GemvArgs {
   const float *residual;
   float *partials;  // [ctas][2][32]
   int *counters;    // [tiles]
+  __half *pair_h;   // gate/up pairing (GemvPair; NULL: off)
+  float *pair_scale;
+  int *pair_ctr;    // [rows / 64]
+  int pair_tiles;   // tiles of the gate half: tile t pairs with t + pair_tiles
   int *status;      // device-visible error word (0 = ok)
   unsigned long long nb_magic;  // ceil(2^40 / nb): u / nb == (u * magic) >> 40
   int rows;
@@ -355,10 +359,28 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, MLM_GEMV_MIN_BLOCKS)
 
   float acc[4] = {0.f, 0.f, 0.f, 0.f};  // rows g, g+8, g+16, g+24 of the current tile
 
-  // store a finished row sum (lane = row in tile)
+  // store a finished row sum (lane = row in tile); with gate/up pairing, the
+  // second of tiles t and t +- pair_tiles to be stored also forms
+  // h = silu(gate) * up of their 32 rows (the scaled fp16 form)
   auto store_row = [&](int t, float s) {
     const int r = t * kTileRows + lane;
     if (r < p.rows) p.y[r] = s + (p.residual ? p.residual[r] : 0.f);
+    if (p.pair_h == nullptr) return;
+    const int pt = t < p.pair_tiles ? t : t - p.pair_tiles;
+    __threadfence();  // this tile's rows are visible before it is counted
+    __syncwarp();
+    int old = 0;
+    if (lane == 0) old = atomicAdd(p.pair_ctr + pt, 1);
+    if (__shfl_sync(0xffffffffu, old, 0) == 0) return;
+    __threadfence();
+    const int e = pt * kTileRows + lane;
+    const float h = swiglu(__ldcg(p.y + e), __ldcg(p.y + (size_t)p.pair_tiles * kTileRows + e));
+    const int ex = silu_scale_exp(warp_max(fabsf(h)));
+    p.pair_h[e] = __float2half_rn(h * __uint_as_float((uint32_t)(127 - ex) << 23));
+    if (lane == 0) {
+      p.pair_scale[pt] = __uint_as_float((uint32_t)(127 + ex) << 23);
+      p.pair_ctr[pt] = 0;
+    }
   };
 
   // A tile shared with neighbouring CTAs: publish this CTA's part; the last
@@ -610,12 +632,16 @@ static int encode_weight_map(mlm_ctx *ctx, const void *W, int rows, int nb, CUte
 
 int gemv_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const GemvInput &in, float *y,
                 const float *residual, float *partials, int *counters, int max_ctas,
-                int max_tiles, cudaStream_t stream) {
+                int max_tiles, cudaStream_t stream, const GemvPair *pair) {
   const int nb = cols / kQK;
   const int tiles = (rows + kTileRows - 1) / kTileRows;
   MLM_REQUIRE(ctx, tiles <= max_tiles, MLM_ERR_SHAPE,
               "mlm_q4k_gemv: %d rows exceed the %d-row scratch limit", rows,
               max_tiles * kTileRows);
+  MLM_REQUIRE(ctx, !pair || (rows % (2 * kTileRows) == 0 && pair->h_f16 && pair->h_scale &&
+                             pair->counters && !residual),
+              MLM_ERR_SHAPE, "mlm_q4k_gemv: gate/up pairing needs rows=%d a multiple of %d",
+              rows, 2 * kTileRows);
   GemvPlan pl;
   // 228 KB of shared memory per SM, 1 KB of it reserved per resident CTA
   const size_t smem_cap = std::min((size_t)ctx->max_smem_optin,
@@ -638,6 +664,10 @@ int gemv_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const GemvInput
   a.residual = residual;
   a.partials = partials;
   a.counters = counters;
+  a.pair_h = pair ? reinterpret_cast<__half *>(pair->h_f16) : nullptr;
+  a.pair_scale = pair ? pair->h_scale : nullptr;
+  a.pair_ctr = pair ? pair->counters : nullptr;
+  a.pair_tiles = rows / (2 * kTileRows);
   a.status = ctx->dev_status;
   a.nb_magic = ((1ull << 40) + (unsigned long long)nb - 1) / (unsigned long long)nb;
   a.rows = rows;
@@ -724,6 +754,26 @@ extern "C" int mlm_q4k_gemv_swiglu(mlm_ctx *ctx, const void *W, int rows, int co
   in.a = gate;
   in.b = up;
   return gemv_entry(ctx, W, rows, cols, in, y, residual);
+}
+
+extern "C" int mlm_q4k_gemv_gate_up(mlm_ctx *ctx, const void *W, int rows, int cols,
+                                    const float *hidden, const float *norm_w, float eps,
+                                    float *y, void *h_f16, float *h_scale) {
+  MLM_CHECK_CTX(ctx);
+  MLM_REQUIRE(ctx, h_f16 && h_scale, MLM_ERR_ARG, "mlm_q4k_gemv_gate_up: null h buffer");
+  GemvInput in;
+  in.mode = GemvInput::kRmsNorm;
+  in.a = hidden;
+  in.b = norm_w;
+  in.eps = eps;
+  int st = gemv_validate(ctx, W, rows, cols, in, y);
+  if (st != MLM_OK) return st;
+  GemvPair pair;
+  pair.h_f16 = h_f16;
+  pair.h_scale = h_scale;
+  pair.counters = ctx->gemv_counters + ctx->gemv_max_tiles;
+  return gemv_launch(ctx, W, rows, cols, in, y, nullptr, ctx->gemv_partials, ctx->gemv_counters,
+                     ctx->gemv_max_ctas, ctx->gemv_max_tiles, ctx->stream, &pair);
 }
 
 // ---------------------------------------------------------------------------

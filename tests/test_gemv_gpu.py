@@ -198,3 +198,45 @@ def test_gemv_swiglu_input(ctx):
     got = y.download(np.float32)
     assert np.all(np.isfinite(got))
     assert rel_l2(got, ref) < 1e-3  # x rounded to fp16 (2^-11 per element)
+
+
+@pytest.mark.parametrize("F,cols", [(14336, 4096), (2816, 1024)])
+def test_gemv_gate_up_pairs(ctx, F, cols):
+    """mlm_q4k_gemv_gate_up over [gate; up] rows: y equals mlm_q4k_gemv_rmsnorm's
+    bit for bit, the h / h_scale its epilogue forms equal mlm_silu_mul_scaled
+    on that y bit for bit, and the down projection on h (mlm_q4k_gemv_xs)
+    equals mlm_q4k_gemv_swiglu on y bit for bit.  Three launches in a row:
+    the pairing counters re-zero themselves."""
+    rows = 2 * F
+    nb = rows * cols // 256
+    W = ctx.alloc(nb * 144)
+    ctx.gen_q4k(31, 1, nb, W)
+    h = ctx.to_device(O.gen_f32(31, 2, cols, 0.0, 3.0))
+    # large norm weights: some sub-blocks of silu(gate) * up pass 2^15 and
+    # take a scale above 1
+    w = ctx.to_device(O.gen_f32(31, 3, cols, 40.0, 10.0))
+    eps = ctypes.c_float(1e-5)
+    y_ref = ctx.alloc(4 * rows)
+    ctx.call("mlm_q4k_gemv_rmsnorm", W, rows, cols, h, w, eps, y_ref, None)
+    hs_ref, sc_ref = ctx.alloc(2 * F), ctx.alloc(4 * (F // 32))
+    ctx.call("mlm_silu_mul_scaled", y_ref, int(y_ref) + 4 * F, hs_ref, sc_ref, F)
+    want_y = y_ref.download(np.float32)
+    want_h = hs_ref.download(np.uint16)
+    want_s = sc_ref.download(np.float32)
+    assert np.any(want_s > 1.0)
+    for _ in range(3):
+        y, hs, sc = ctx.alloc(4 * rows), ctx.alloc(2 * F), ctx.alloc(4 * (F // 32))
+        ctx.call("mlm_q4k_gemv_gate_up", W, rows, cols, h, w, eps, y, hs, sc)
+        assert np.array_equal(y.download(np.float32), want_y)
+        assert np.array_equal(hs.download(np.uint16), want_h)
+        assert np.array_equal(sc.download(np.float32), want_s)
+    # the down projection: staged fp16 h against the SwiGLU staging
+    dn = 4096 if cols == 4096 else 1024
+    nbd = dn * F // 256
+    Wd = ctx.alloc(nbd * 144)
+    ctx.gen_q4k(32, 1, nbd, Wd)
+    r = ctx.to_device(O.gen_f32(32, 4, dn))
+    a, b = ctx.alloc(4 * dn), ctx.alloc(4 * dn)
+    ctx.call("mlm_q4k_gemv_xs", Wd, dn, F, hs, sc, a, r)
+    ctx.call("mlm_q4k_gemv_swiglu", Wd, dn, F, y_ref, int(y_ref) + 4 * F, b, r)
+    assert np.array_equal(a.download(np.float32), b.download(np.float32))

@@ -268,316 +268,301 @@ __global__ void attn_decode_merge_kernel(const float *__restrict__ partials, int
 // folded in (the runner's path: LlamaRunner.swift:612-952 -- applyRoPE on q
 // and k, the cache append, then attention).  Input: the QKV projection in
 // fp32 (q [n_heads][128], k and v [n_kv][128]) and the position in device
-// memory.  CTA (KV head, chunk): RoPE of its G query heads in fp32 (q is not
-// rounded to fp16), K/V rows of the chunk staged in shared memory; the chunk
-// holding the position also rotates k, rounds k and v to fp16, appends them
-// to the caches and uses them for that row.  The last CTA of a KV head to
-// finish merges the chunks from shared memory: every partial of the head is
-// copied in with one round of 16-byte loads.
+// memory.
+//
+// One thread-block cluster of kClusterCtas CTAs per KV head; CTA r of the
+// cluster owns positions [r * chunk_len, (r + 1) * chunk_len), staged in
+// shared memory by cp.async in phases of up to kPhaseRows rows (K rows
+// padded to 272 bytes so that a lane per row reads without bank conflicts).
+// Per phase, lane j of warp w scores rows j, j + 32, ... against query head
+// w (and w + 4, ...) of the KV head's group, with q rotated in fp32 and
+// scaled by 1/sqrt(d); the warp keeps that head's running max and sum
+// (online softmax across phases); thread t accumulates output dimension t
+// of every head.  The CTA holding the position also rotates k, rounds k and
+// v to fp16, appends them to the caches and uses them for that row.  The
+// CTAs' (max, sum, output) triples are merged through distributed shared
+// memory after a cluster barrier: CTA h of the cluster finishes head h of
+// the group from the other CTAs' partials, so no partial goes through global
+// memory and no arrival counter is needed.
+#ifndef MLM_ATTN_CLUSTER
+#define MLM_ATTN_CLUSTER 8
+#endif
+constexpr int kClusterCtas = MLM_ATTN_CLUSTER;  // CTAs per KV head
+// rows staged at once: 96 rows (51 KB) let a CTA sit beside a decode GEMV's
+// CTA on one SM, so it is resident, with its first rows in flight, before
+// the QKV GEMV it depends on has finished
+constexpr int kPhaseRows = 96;
+constexpr int kKPitch = kAttnD + 8;             // K row pitch in halves (272 bytes)
+constexpr int kRowBytes = kKPitch * 2 + kAttnD * 2;  // shared memory per staged row
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// the float at the same shared-memory address in CTA `rank` of the cluster
+__device__ __forceinline__ float ld_cluster_f32(const float *local, uint32_t rank) {
+  uint32_t a = (uint32_t)__cvta_generic_to_shared(local), ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
+  return v;
+}
+
 template <int G>
 __global__ void __launch_bounds__(kAttnThreads) attn_rope_decode_kernel(
     const float *__restrict__ qkv, mlm_rope_args ra, RopeConsts rk,
     const float *__restrict__ freqs, __half *__restrict__ kc, __half *__restrict__ vc,
-    int n_heads, int n_kv, int chunk_len, float scale, float *__restrict__ partials,
-    const int *__restrict__ pos_dev, __half *__restrict__ out, int *__restrict__ arrivals,
-    int staged_merge) {
-  __shared__ float s_scores[G][kAttnChunk * 2];
-  __shared__ float s_out[kAttnThreads / 32][G][kAttnD];
-  __shared__ float s_m[G], s_l[G];
-  extern __shared__ __align__(16) __half s_kv[];  // [2][2 * kAttnChunk][kAttnD]
-  pdl_wait_then_release();
-  const int kvh = blockIdx.x;
-  const int chunk = blockIdx.y;
+    int n_heads, int n_kv, int chunk_len, float scale, const int *__restrict__ pos_dev,
+    __half *__restrict__ out) {
+  static_assert(kAttnThreads == kAttnD && kAttnThreads == 128, "thread t = output dimension t");
+  constexpr int HW = (G + 3) / 4;          // heads per warp: w, w + 4, ...
+  constexpr int NR = kPhaseRows / 32;      // rows per lane, at most
+  extern __shared__ __align__(16) uint8_t s_dyn[];
+  __shared__ __align__(16) float s_q[G][kAttnD];  // q, then this CTA's output
+  __shared__ __align__(16) float s_p[kPhaseRows][G];
+  __shared__ float s_corr[G], s_m[G], s_l[G];
+  const uint32_t rank = cluster_ctarank();
+  const int kvh = blockIdx.x / kClusterCtas;
+  // the position and the cached rows before it were written by earlier
+  // steps, not by the kernel this one depends on: read them before the wait
   const int pos = *pos_dev;
   const int seq_len = pos + 1;
-  const int p0 = chunk * chunk_len;
-  if (p0 >= seq_len) return;
-  const int p1 = min(seq_len, p0 + chunk_len);
-  const bool has_new = p1 == seq_len;        // this chunk holds row `pos`
-  const int pc = has_new ? pos : p1;          // rows [p0, pc) come from the caches
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int nwarp = kAttnThreads / 32;
   const size_t row_stride = (size_t)n_kv * kAttnD;
-  const float *qf = qkv;
   const float *kf = qkv + (size_t)n_heads * kAttnD;
   const float *vf = kf + row_stride;
+  const int p_begin = (int)rank * chunk_len;
+  const int p_end = min(p_begin + chunk_len, seq_len);
+  const int rows_cap = min(chunk_len, kPhaseRows);
+  const int nphase = p_end > p_begin ? (p_end - p_begin + rows_cap - 1) / rows_cap : 0;
+  const bool has_new = nphase > 0 && p_end == seq_len;  // this CTA holds row `pos`
+  __half *s_k = reinterpret_cast<__half *>(s_dyn);        // [rows_cap][kKPitch]
+  __half *s_v = s_k + (size_t)rows_cap * kKPitch;         // [rows_cap][128]
 
-  __half *s_k = s_kv, *s_v = s_kv + 2 * kAttnChunk * kAttnD;
-  {
-    constexpr int kPiecesPerRow = kAttnD * (int)sizeof(__half) / 16;  // 16
-    const int pieces = (pc - p0) * kPiecesPerRow;
+  // cached rows of phase ph by cp.async (row pos, when it falls in the
+  // phase, comes from registers once q, k and v are available)
+  auto load_phase = [&](int ph) {
+    const int a = p_begin + ph * rows_cap;
+    const int n = min(rows_cap, p_end - a);
+    const int cached = (has_new && a + n == p_end) ? n - 1 : n;
+    constexpr int kPieces = kAttnD * (int)sizeof(__half) / 16;  // 16 per row
     const uint32_t sk = (uint32_t)__cvta_generic_to_shared(s_k);
     const uint32_t sv = (uint32_t)__cvta_generic_to_shared(s_v);
-    for (int j = threadIdx.x; j < pieces; j += kAttnThreads) {
-      const int r = j / kPiecesPerRow, c = j - r * kPiecesPerRow;
-      cp_async16(sk + (uint32_t)(r * kAttnD + c * 8) * 2,
-                 kc + (size_t)(p0 + r) * row_stride + kvh * kAttnD + c * 8);
+    for (int j = threadIdx.x; j < cached * kPieces; j += kAttnThreads) {
+      const int r = j / kPieces, c = j - r * kPieces;
+      const size_t g = (size_t)(a + r) * row_stride + kvh * kAttnD + c * 8;
+      cp_async16(sk + (uint32_t)(r * kKPitch + c * 8) * 2, kc + g);
+      cp_async16(sv + (uint32_t)(r * kAttnD + c * 8) * 2, vc + g);
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
-    for (int j = threadIdx.x; j < pieces; j += kAttnThreads) {
-      const int r = j / kPiecesPerRow, c = j - r * kPiecesPerRow;
-      cp_async16(sv + (uint32_t)(r * kAttnD + c * 8) * 2,
-                 vc + (size_t)(p0 + r) * row_stride + kvh * kAttnD + c * 8);
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-  }
+  };
+  if (nphase > 0) load_phase(0);
 
-  // the new row: thread t < 64 rotates pair t of k, thread 64 + t takes pair
-  // t of v; both rounded to fp16 into the caches and the stage
-  if (has_new) {
-    const int t = threadIdx.x & 63;
-    const size_t off = ((size_t)pos * n_kv + kvh) * kAttnD + 2 * t;
-    const int srow = (pos - p0) * kAttnD + 2 * t;
-    if (threadIdx.x < 64) {
-      float x0 = kf[kvh * kAttnD + 2 * t], x1 = kf[kvh * kAttnD + 2 * t + 1];
-      if (2 * t < (int)ra.n_dims) {
-        float c, sn;
-        rope_cos_sin(ra, rk, freqs, pos, t, c, sn);
-        const float r0 = x0 * c - x1 * sn, r1 = x0 * sn + x1 * c;
-        x0 = r0;
-        x1 = r1;
-      }
-      const __half2 h = __floats2half2_rn(x0, x1);
-      *reinterpret_cast<__half2 *>(kc + off) = h;
-      *reinterpret_cast<__half2 *>(s_k + srow) = h;
-    } else {
-      const __half2 h = __floats2half2_rn(vf[kvh * kAttnD + 2 * t], vf[kvh * kAttnD + 2 * t + 1]);
-      *reinterpret_cast<__half2 *>(vc + off) = h;
-      *reinterpret_cast<__half2 *>(s_v + srow) = h;
-    }
-  }
+  // q, k and v of this step come from the QKV GEMV before this kernel
+  pdl_wait_then_release();
 
-  // q of the G heads, dims 4 lane .. 4 lane + 3 (pairs 2 lane, 2 lane + 1),
-  // rotated in fp32 and scaled by 1/sqrt(d)
-  float qv[G][4];
+  // q of the group rotated in fp32 (pair t of every head by thread t < 64),
+  // the new k row rotated likewise, the new v row by threads 64..127
+  __half2 kv_new = __floats2half2_rn(0.f, 0.f);
   {
-    float c[2] = {1.f, 1.f}, sn[2] = {0.f, 0.f};
+    const int t = threadIdx.x & 63;
+    if (threadIdx.x < 64) {
+      float c = 1.f, sn = 0.f;
+      if (2 * t < (int)ra.n_dims) rope_cos_sin(ra, rk, freqs, pos, t, c, sn);
 #pragma unroll
-    for (int e = 0; e < 2; ++e)
-      if (2 * (2 * lane + e) < (int)ra.n_dims) rope_cos_sin(ra, rk, freqs, pos, 2 * lane + e, c[e], sn[e]);
-#pragma unroll
-    for (int gh = 0; gh < G; ++gh) {
-      const float4 x = *reinterpret_cast<const float4 *>(qf + (size_t)(kvh * G + gh) * kAttnD + 4 * lane);
-      qv[gh][0] = (x.x * c[0] - x.y * sn[0]) * scale;
-      qv[gh][1] = (x.x * sn[0] + x.y * c[0]) * scale;
-      qv[gh][2] = (x.z * c[1] - x.w * sn[1]) * scale;
-      qv[gh][3] = (x.z * sn[1] + x.w * c[1]) * scale;
-    }
-  }
-
-  asm volatile("cp.async.wait_group 1;" ::: "memory");  // K landed
-  __syncthreads();
-
-  for (int p = p0 + warp; p < p1; p += nwarp) {
-    const uint2 raw = *reinterpret_cast<const uint2 *>(s_k + (p - p0) * kAttnD + 4 * lane);
-    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
-    const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
-#pragma unroll
-    for (int gh = 0; gh < G; ++gh) {
-      float sc = qv[gh][0] * a.x + qv[gh][1] * a.y + qv[gh][2] * b.x + qv[gh][3] * b.y;
-      sc = warp_sum(sc);
-      if (lane == 0) s_scores[gh][p - p0] = sc;
-    }
-  }
-  __syncthreads();
-
-  for (int gh = warp; gh < G; gh += nwarp) {
-    float m = -INFINITY;
-    for (int i = lane; i < p1 - p0; i += 32) m = fmaxf(m, s_scores[gh][i]);
-    m = warp_max(m);
-    float l = 0.f;
-    for (int i = lane; i < p1 - p0; i += 32) {
-      const float e = __expf(s_scores[gh][i] - m);
-      s_scores[gh][i] = e;
-      l += e;
-    }
-    l = warp_sum(l);
-    if (lane == 0) {
-      s_m[gh] = m;
-      s_l[gh] = l;
-    }
-  }
-  asm volatile("cp.async.wait_group 0;" ::: "memory");  // V landed
-  __syncthreads();
-
-  float o[G][4];
-#pragma unroll
-  for (int gh = 0; gh < G; ++gh) o[gh][0] = o[gh][1] = o[gh][2] = o[gh][3] = 0.f;
-  for (int p = p0 + warp; p < p1; p += nwarp) {
-    const uint2 raw = *reinterpret_cast<const uint2 *>(s_v + (p - p0) * kAttnD + 4 * lane);
-    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
-    const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
-#pragma unroll
-    for (int gh = 0; gh < G; ++gh) {
-      const float w = s_scores[gh][p - p0];
-      o[gh][0] += w * a.x;
-      o[gh][1] += w * a.y;
-      o[gh][2] += w * b.x;
-      o[gh][3] += w * b.y;
-    }
-  }
-#pragma unroll
-  for (int gh = 0; gh < G; ++gh)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) s_out[warp][gh][4 * lane + e] = o[gh][e];
-  __syncthreads();
-
-  for (int i = threadIdx.x; i < G * kAttnD; i += kAttnThreads) {
-    const int gh = i / kAttnD, dd = i - gh * kAttnD;
-    float acc = 0.f;
-#pragma unroll
-    for (int w = 0; w < nwarp; ++w) acc += s_out[w][gh][dd];
-    float *pp = partials + ((size_t)chunk * n_heads + kvh * G + gh) * kAttnPartial;
-    pp[2 + dd] = acc;
-    if (dd == 0) {
-      pp[0] = s_m[gh];
-      pp[1] = s_l[gh];
-    }
-  }
-
-  // the last chunk of this KV head to finish merges the chunks, in order
-  __threadfence();
-  __syncthreads();
-  __shared__ bool s_last;
-  const int nlive = (seq_len + chunk_len - 1) / chunk_len;
-  if (threadIdx.x == 0) {
-    s_last = atomicAdd(arrivals + kvh, 1) == nlive - 1;
-    if (s_last) arrivals[kvh] = 0;
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  static_assert(kAttnThreads == kAttnD, "one thread per output dimension");
-  float *s_cw = &s_out[0][0][0];            // [chunk][G] chunk weights exp(m - M)
-  __shared__ float s_L[G];
-  const int dd = threadIdx.x;
-  float O[G];
-#pragma unroll
-  for (int gh = 0; gh < G; ++gh) O[gh] = 0.f;
-  if (staged_merge) {
-    // the G partials of a chunk are contiguous (G * 520 bytes, G even:
-    // 16-byte pieces): all of the head's chunks into the free stage
-    float *sp = reinterpret_cast<float *>(s_kv);  // [chunk][G][kAttnPartial]
-    const int per = G * kAttnPartial / 4;         // 16-byte pieces per chunk
-    const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(sp);
-    for (int j = threadIdx.x; j < nlive * per; j += kAttnThreads) {
-      const int c = j / per, r = j - c * per;
-      const float *src = partials + ((size_t)c * n_heads + kvh * G) * kAttnPartial + 4 * r;
-      cp_async16(sbase + (uint32_t)((c * per + r) * 16), src);
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-    __syncthreads();
-    for (int gh = warp; gh < G; gh += nwarp) {
-      float m = -INFINITY;
-      for (int c = lane; c < nlive; c += 32) m = fmaxf(m, sp[(c * G + gh) * kAttnPartial]);
-      m = warp_max(m);
-      float l = 0.f;
-      for (int c = lane; c < nlive; c += 32) {
-        const float w = __expf(sp[(c * G + gh) * kAttnPartial] - m);
-        s_cw[c * G + gh] = w;
-        l += sp[(c * G + gh) * kAttnPartial + 1] * w;
+      for (int h = 0; h < G; ++h) {
+        const float2 x =
+            *reinterpret_cast<const float2 *>(qkv + (size_t)(kvh * G + h) * kAttnD + 2 * t);
+        s_q[h][2 * t] = (x.x * c - x.y * sn) * scale;
+        s_q[h][2 * t + 1] = (x.x * sn + x.y * c) * scale;
       }
-      l = warp_sum(l);
-      if (lane == 0) s_L[gh] = l;
-    }
-    __syncthreads();
-    for (int c = 0; c < nlive; ++c) {
-#pragma unroll
-      for (int gh = 0; gh < G; ++gh)
-        O[gh] += sp[(c * G + gh) * kAttnPartial + 2 + dd] * s_cw[c * G + gh];
-    }
-  } else {
-    float *s_cm = s_cw + kAttnMaxChunks * G;  // [chunk][G] chunk maxima
-    float *s_cl = s_cm + kAttnMaxChunks * G;  // [chunk][G] chunk sums
-    for (int i = threadIdx.x; i < nlive * G; i += kAttnThreads) {
-      const float *pp = partials + ((size_t)(i / G) * n_heads + kvh * G) * kAttnPartial +
-                        (i % G) * kAttnPartial;
-      s_cm[i] = __ldcg(pp);
-      s_cl[i] = __ldcg(pp + 1);
-    }
-    __syncthreads();
-    for (int gh = warp; gh < G; gh += nwarp) {
-      float m = -INFINITY;
-      for (int c = lane; c < nlive; c += 32) m = fmaxf(m, s_cm[c * G + gh]);
-      m = warp_max(m);
-      float l = 0.f;
-      for (int c = lane; c < nlive; c += 32) {
-        const float w = __expf(s_cm[c * G + gh] - m);
-        s_cw[c * G + gh] = w;
-        l += s_cl[c * G + gh] * w;
+      if (has_new) {
+        const float2 x = *reinterpret_cast<const float2 *>(kf + kvh * kAttnD + 2 * t);
+        kv_new = __floats2half2_rn(x.x * c - x.y * sn, x.x * sn + x.y * c);
+        *reinterpret_cast<__half2 *>(kc + ((size_t)pos * n_kv + kvh) * kAttnD + 2 * t) = kv_new;
       }
-      l = warp_sum(l);
-      if (lane == 0) s_L[gh] = l;
-    }
-    __syncthreads();
-#pragma unroll 4
-    for (int c = 0; c < nlive; ++c) {
-      const float *pcp = partials + ((size_t)c * n_heads + kvh * G) * kAttnPartial + 2 + dd;
-#pragma unroll
-      for (int gh = 0; gh < G; ++gh) O[gh] += __ldcg(pcp + gh * kAttnPartial) * s_cw[c * G + gh];
+    } else if (has_new) {
+      const float2 x = *reinterpret_cast<const float2 *>(vf + kvh * kAttnD + 2 * t);
+      kv_new = __floats2half2_rn(x.x, x.y);
+      *reinterpret_cast<__half2 *>(vc + ((size_t)pos * n_kv + kvh) * kAttnD + 2 * t) = kv_new;
     }
   }
+
+  float m_run[HW], l_run[HW];
 #pragma unroll
-  for (int gh = 0; gh < G; ++gh)
-    out[(size_t)(kvh * G + gh) * kAttnD + dd] = __float2half_rn(O[gh] / s_L[gh]);
+  for (int i = 0; i < HW; ++i) {
+    m_run[i] = -INFINITY;
+    l_run[i] = 0.f;
+  }
+  float o[G];
+#pragma unroll
+  for (int h = 0; h < G; ++h) o[h] = 0.f;
+
+  for (int ph = 0; ph < nphase; ++ph) {
+    const int a = p_begin + ph * rows_cap;
+    const int n = min(rows_cap, p_end - a);
+    if (ph > 0) load_phase(ph);
+    {
+      const int cached = (has_new && a + n == p_end) ? n - 1 : n;
+      if (cached < n) {
+        const int t = threadIdx.x & 63;
+        if (threadIdx.x < 64)
+          *reinterpret_cast<__half2 *>(s_k + (size_t)cached * kKPitch + 2 * t) = kv_new;
+        else
+          *reinterpret_cast<__half2 *>(s_v + (size_t)cached * kAttnD + 2 * t) = kv_new;
+      }
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();
+
+    // scores of rows lane + 32 i for the warp's heads, then the online softmax
+#pragma unroll
+    for (int hi = 0; hi < HW; ++hi) {
+      const int h = warp + 4 * hi;
+      if (h >= G) break;
+      float acc[NR];
+#pragma unroll
+      for (int i = 0; i < NR; ++i) acc[i] = 0.f;
+#pragma unroll 2
+      for (int d = 0; d < kAttnD; d += 8) {
+        const float4 qa = *reinterpret_cast<const float4 *>(&s_q[h][d]);
+        const float4 qb = *reinterpret_cast<const float4 *>(&s_q[h][d + 4]);
+#pragma unroll
+        for (int i = 0; i < NR; ++i) {
+          if (32 * i < n) {
+            const uint4 raw =
+                *reinterpret_cast<const uint4 *>(s_k + (size_t)(lane + 32 * i) * kKPitch + d);
+            const float2 k0 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
+            const float2 k1 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
+            const float2 k2 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.z));
+            const float2 k3 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.w));
+            acc[i] += ((qa.x * k0.x + qa.y * k0.y) + (qa.z * k1.x + qa.w * k1.y)) +
+                      ((qb.x * k2.x + qb.y * k2.y) + (qb.z * k3.x + qb.w * k3.y));
+          }
+        }
+      }
+      float mloc = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < NR; ++i) {
+        if (lane + 32 * i >= n) acc[i] = -INFINITY;
+        mloc = fmaxf(mloc, acc[i]);
+      }
+      const float m_new = fmaxf(m_run[hi], warp_max(mloc));
+      float lsum = 0.f;
+#pragma unroll
+      for (int i = 0; i < NR; ++i) {
+        const float p = __expf(acc[i] - m_new);  // 0 for rows past n
+        if (32 * i < n) s_p[lane + 32 * i][h] = p;
+        lsum += p;
+      }
+      const float corr = __expf(m_run[hi] - m_new);
+      l_run[hi] = l_run[hi] * corr + warp_sum(lsum);
+      m_run[hi] = m_new;
+      if (lane == 0) s_corr[h] = corr;
+    }
+    __syncthreads();
+
+    // output dimension t of every head
+    {
+      const int t = threadIdx.x;
+#pragma unroll
+      for (int h = 0; h < G; ++h) o[h] *= s_corr[h];
+#pragma unroll 8
+      for (int j = 0; j < n; ++j) {
+        const float v = __half2float(s_v[(size_t)j * kAttnD + t]);
+#pragma unroll
+        for (int h = 0; h < G; ++h) o[h] += s_p[j][h] * v;
+      }
+    }
+    __syncthreads();  // the stage and s_p are free for the next phase
+  }
+
+  // this CTA's partials: output in place of q, max and sum per head
+#pragma unroll
+  for (int h = 0; h < G; ++h) s_q[h][threadIdx.x] = o[h];
+#pragma unroll
+  for (int hi = 0; hi < HW; ++hi) {
+    const int h = warp + 4 * hi;
+    if (h < G && lane == 0) {
+      s_m[h] = m_run[hi];
+      s_l[h] = l_run[hi];
+    }
+  }
+  cluster_sync_all();
+
+  // CTA r finishes heads r, r + kClusterCtas, ... of the group from every
+  // CTA's partials (CTA 0 always holds rows, so M is finite)
+  for (int h = (int)rank; h < G; h += kClusterCtas) {
+    float mc[kClusterCtas];
+    float M = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < kClusterCtas; ++c) {
+      mc[c] = ld_cluster_f32(&s_m[h], c);
+      M = fmaxf(M, mc[c]);
+    }
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int c = 0; c < kClusterCtas; ++c) {
+      const float w = __expf(mc[c] - M);
+      L += ld_cluster_f32(&s_l[h], c) * w;
+      O += ld_cluster_f32(&s_q[h][threadIdx.x], c) * w;
+    }
+    out[(size_t)(kvh * G + h) * kAttnD + threadIdx.x] = __float2half_rn(O / L);
+  }
+  cluster_sync_all();  // no CTA leaves while another reads its shared memory
 }
 
-// Chunk length of the fused step for a cache of `capacity` positions: the
-// shortest (>= 32, a multiple of 16) whose chunk count lets the merge stage
-// all partials of a KV head in shared memory; else 128-position chunks and
-// the merge from L2.
-static void attn_rope_chunks(int capacity, int G, int &chunk_len, int &nchunks, bool &staged) {
-  const int fit = (G % 2 == 0) ? kAttnStageBytes / (G * kAttnPartial * 4) : 0;
-  const int nmax = std::min(kAttnMaxChunks, fit);
-  if (nmax > 0) {
-    int cl = (capacity + nmax - 1) / nmax;
-    cl = std::max(32, (cl + 15) / 16 * 16);
-    if (cl <= 2 * kAttnChunk) {
-      chunk_len = cl;
-      nchunks = (capacity + cl - 1) / cl;
-      staged = true;
-      return;
-    }
-  }
-  chunk_len = 2 * kAttnChunk;
-  nchunks = (capacity + chunk_len - 1) / chunk_len;
-  staged = false;
+// positions per CTA of the fused kernel: the capacity over the cluster,
+// rounded up to whole 32-row groups
+static int attn_rope_chunk_len(int capacity) {
+  const int per = (capacity + kClusterCtas - 1) / kClusterCtas;
+  return (per + 31) / 32 * 32;
 }
 
 int attn_rope_decode_launch(mlm_ctx *ctx, const float *qkv, const float *freqs,
                             const mlm_rope_args &ra, int n_heads, int n_kv, int head_dim,
-                            int capacity, void *kc, void *vc, void *out, float *partials,
-                            size_t partial_floats, cudaStream_t stream, const int *pos_dev) {
+                            int capacity, void *kc, void *vc, void *out, cudaStream_t stream,
+                            const int *pos_dev) {
   MLM_REQUIRE(ctx, head_dim == kAttnD, MLM_ERR_UNSUPPORTED,
               "attention: head_dim=%d (this build handles %d)", head_dim, kAttnD);
   MLM_REQUIRE(ctx, n_kv > 0 && n_heads % n_kv == 0, MLM_ERR_SHAPE,
               "attention: %d query heads not a multiple of %d KV heads", n_heads, n_kv);
-  MLM_REQUIRE(ctx, n_kv <= kAttnMaxArrivals, MLM_ERR_SHAPE, "attention: %d KV heads", n_kv);
   const int G = n_heads / n_kv;
   MLM_REQUIRE(ctx, G == 1 || G == 2 || G == 4 || G == 8, MLM_ERR_UNSUPPORTED,
               "attention: GQA group %d (supported 1, 2, 4, 8)", G);
-  int chunk_len, nchunks;
-  bool staged;
-  attn_rope_chunks(capacity, G, chunk_len, nchunks, staged);
-  MLM_REQUIRE(ctx, nchunks <= kAttnMaxChunks, MLM_ERR_SHAPE,
-              "attention: cache capacity %d exceeds %d positions", capacity,
-              2 * kAttnChunk * kAttnMaxChunks);
-  MLM_REQUIRE(ctx, (size_t)nchunks * n_heads * kAttnPartial <= partial_floats, MLM_ERR_SHAPE,
-              "attention: %d heads exceed the attention scratch", n_heads);
+  MLM_REQUIRE(ctx, capacity > 0, MLM_ERR_SHAPE, "attention: cache capacity %d", capacity);
+  const int chunk_len = attn_rope_chunk_len(capacity);
+  const int rows_cap = std::min(chunk_len, kPhaseRows);
   const RopeConsts rk = rope_consts(ra);
   const float scale = 1.0f / sqrtf((float)head_dim);
   auto kern = G == 1   ? attn_rope_decode_kernel<1>
               : G == 2 ? attn_rope_decode_kernel<2>
               : G == 4 ? attn_rope_decode_kernel<4>
                        : attn_rope_decode_kernel<8>;
-  return check_launch_pdl(
-      ctx,
-      launch_pdl(kern, dim3(n_kv, nchunks), dim3(kAttnThreads), kAttnStageBytes, stream, qkv, ra,
-                 rk, freqs, reinterpret_cast<__half *>(kc), reinterpret_cast<__half *>(vc),
-                 n_heads, n_kv, chunk_len, scale, partials, pos_dev,
-                 reinterpret_cast<__half *>(out), ctx->attn_arrivals, staged ? 1 : 0),
-      "attention (RoPE, append, decode)");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(n_kv * kClusterCtas);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = (size_t)rows_cap * kRowBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kClusterCtas;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t e = cudaLaunchKernelEx(
+      &cfg, kern, qkv, ra, rk, freqs, reinterpret_cast<__half *>(kc),
+      reinterpret_cast<__half *>(vc), n_heads, n_kv, chunk_len, scale, pos_dev,
+      reinterpret_cast<__half *>(out));
+  return check_launch_pdl(ctx, e, "attention (RoPE, append, decode)");
 }
 
 // seq_len positions, or, when pos_dev is set, pos_dev[b] + 1 positions read
@@ -692,16 +677,24 @@ static int attn_init_out(mlm_ctx *ctx) {
   return MLM_OK;
 }
 
+template <int G>
+static int attn_rope_init(mlm_ctx *ctx) {
+  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_rope_decode_kernel<G>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kPhaseRows * kRowBytes));
+  if (kClusterCtas > 8)
+    MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_rope_decode_kernel<G>,
+                                           cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  return MLM_OK;
+}
+
 int attn_init(mlm_ctx *ctx) {
-  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_rope_decode_kernel<1>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnStageBytes));
-  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_rope_decode_kernel<2>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnStageBytes));
-  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_rope_decode_kernel<4>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnStageBytes));
-  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_rope_decode_kernel<8>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnStageBytes));
-  int st = attn_init_out<__half, true>(ctx);
+  int st = attn_rope_init<1>(ctx);
+  if (st == MLM_OK) st = attn_rope_init<2>(ctx);
+  if (st == MLM_OK) st = attn_rope_init<4>(ctx);
+  if (st == MLM_OK) st = attn_rope_init<8>(ctx);
+  if (st != MLM_OK) return st;
+  st = attn_init_out<__half, true>(ctx);
   if (st == MLM_OK) st = attn_init_out<__half, false>(ctx);
   if (st == MLM_OK) st = attn_init_out<__nv_bfloat16, true>(ctx);
   if (st != MLM_OK) return st;

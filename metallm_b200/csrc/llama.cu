@@ -200,8 +200,7 @@ struct mlm_llama {
       return st;
     // RoPE of q and k, the KV append and the attention in one launch
     if ((st = attn_rope_decode_launch(ctx, qkv_out, rope_freqs, c.rope, nh(), nkv(), c.head_dim,
-                                      c.max_seq, L.kc, L.vc, attn_out, ctx->attn_partials,
-                                      ctx->attn_partials_floats, s, state + kPos)))
+                                      c.max_seq, L.kc, L.vc, attn_out, s, state + kPos)))
       return st;
     if ((st = row_parallel(L.wo, qdim(), gemv_half(attn_out), h))) return st;  // + residual
     // the gate/up GEMV's epilogue forms the SiLU-gated product once per

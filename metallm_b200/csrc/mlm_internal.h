@@ -167,8 +167,8 @@ int rope_qk_kv_launch(mlm_ctx *ctx, const float *q, const float *k, const float 
 // the fp16 attention output [n_heads][128]
 int attn_rope_decode_launch(mlm_ctx *ctx, const float *qkv, const float *freqs,
                             const mlm_rope_args &ra, int n_heads, int n_kv, int head_dim,
-                            int capacity, void *kc, void *vc, void *out, float *partials,
-                            size_t partial_floats, cudaStream_t stream, const int *pos_dev);
+                            int capacity, void *kc, void *vc, void *out, cudaStream_t stream,
+                            const int *pos_dev);
 int attn_decode_launch(mlm_ctx *ctx, const void *q, const void *kc, const void *vc, int n_heads,
                        int n_kv, int head_dim, int seq_len, void *out, float *partials,
                        size_t partial_floats, cudaStream_t stream, const int *pos_dev);

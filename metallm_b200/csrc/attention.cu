@@ -362,6 +362,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_rope_decode_kernel(
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
   if (nphase > 0) load_phase(0);
+  // the rotation of pair t at this position (threads t < 64)
+  float c = 1.f, sn = 0.f;
+  if (threadIdx.x < 64 && 2 * (int)threadIdx.x < (int)ra.n_dims)
+    rope_cos_sin(ra, rk, freqs, pos, threadIdx.x, c, sn);
 
   // q, k and v of this step come from the QKV GEMV before this kernel
   pdl_wait_then_release();
@@ -372,8 +376,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_rope_decode_kernel(
   {
     const int t = threadIdx.x & 63;
     if (threadIdx.x < 64) {
-      float c = 1.f, sn = 0.f;
-      if (2 * t < (int)ra.n_dims) rope_cos_sin(ra, rk, freqs, pos, t, c, sn);
 #pragma unroll
       for (int h = 0; h < G; ++h) {
         const float2 x =

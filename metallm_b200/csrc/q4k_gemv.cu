@@ -580,14 +580,34 @@ struct GemvPlan {
 };
 
 // The most warps whose shared-memory footprint fits.
+// The most units a warp takes when a CTA holds s units over `warps` warps.
+static long long units_per_warp(long long s, int warps) {
+  const long long nwe = std::min<long long>(warps, s);
+  return (s + nwe - 1) / nwe;
+}
+
+// CTA count: the grid holds every SM, and each CTA a contiguous run of units
+// (its first and last tiles shared with its neighbours, their partial sums
+// handed over through global memory) -- unless a count between half and all
+// of the SMs divides the tiles without raising the most units a warp takes:
+// then every CTA owns whole tiles and no partial sum leaves a CTA.
+static int pick_ctas(int tiles, int nb, int sm_count, int warps) {
+  const long long units = (long long)tiles * nb;
+  const int split = (int)std::min<long long>(sm_count, units);
+  const long long cost = units_per_warp((units + split - 1) / split, warps);
+  for (int d = std::min(sm_count, tiles); 2 * d >= sm_count; --d)
+    if (tiles % d == 0 && units_per_warp((long long)(tiles / d) * nb, warps) <= cost) return d;
+  return split;
+}
+
 static bool plan_gemv(int rows, int nb, int sm_count, size_t smem_max, GemvPlan &pl) {
   const int tiles = (rows + kTileRows - 1) / kTileRows;
   const long long units = (long long)tiles * nb;
-  const int ctas = (int)std::min<long long>(sm_count, units);
-  if (units * ctas >= (1LL << 31) || units >= (1LL << 24)) return false;
-  const int umax = (int)((units + ctas - 1) / ctas);
-  const int ntile = ((umax / nb + 2) + 3) & ~3;
+  if (units * sm_count >= (1LL << 31) || units >= (1LL << 24)) return false;
   for (int warps = kGemvMaxWarps; warps >= 2; --warps) {
+    const int ctas = pick_ctas(tiles, nb, sm_count, warps);
+    const int umax = (int)((units + ctas - 1) / ctas);
+    const int ntile = ((umax / nb + 2) + 3) & ~3;
     const size_t smem_bar = (size_t)warps * kGemvStages * kStageBytes;
     const size_t smem_x = smem_bar + (((size_t)warps * kGemvStages * 8 + 15) & ~(size_t)15);
     const size_t smem = smem_x + 64 + (size_t)nb * 32 * 16 + (size_t)nb * 8 * 4 * 2 +

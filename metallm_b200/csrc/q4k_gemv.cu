@@ -261,8 +261,47 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, MLM_GEMV_MIN_BLOCKS)
           if (i < ngroups) stage(i, xv[u], p.x_scale ? p.x_scale[i >> 2] : 1.0f);
         }
       }
+    } else if (p.x_mode == GemvInput::kRmsNorm && ngroups <= 4 * (int)blockDim.x) {
+      // every CTA reduces the sum of squares of the whole hidden state
+      // itself; hidden state and weights are read once, into registers, so
+      // the norm costs one round trip to L2
+      constexpr int XU = 4;
+      float a[XU][8], w[XU][8];
+      float ss = 0.f;
+#pragma unroll
+      for (int u = 0; u < XU; ++u) {
+        const int i = threadIdx.x + u * blockDim.x;
+        if (i < ngroups) {
+          load8(p.xa, i, a[u]);
+          load8(p.xb, i, w[u]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < XU; ++u) {
+        const int i = threadIdx.x + u * blockDim.x;
+        if (i < ngroups) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) ss += a[u][e] * a[u][e];
+        }
+      }
+      ss = warp_sum(ss);
+      float *red = parts;  // free until the main loop
+      if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+      __syncthreads();
+      float tot = 0.f;
+      for (int wi = 0; wi < nwarps; ++wi) tot += red[wi];
+      const float scale = rms_scale(tot, ngroups * 8, p.eps);
+#pragma unroll
+      for (int u = 0; u < XU; ++u) {
+        const int i = threadIdx.x + u * blockDim.x;
+        if (i < ngroups) {  // whole warps: ngroups is a multiple of 32
+#pragma unroll
+          for (int e = 0; e < 8; ++e) a[u][e] = (a[u][e] * scale) * safe_weight(w[u][e]);
+          stage(i, pack(a[u]), 1.0f);
+        }
+      }
     } else if (p.x_mode == GemvInput::kRmsNorm) {
-      // every CTA reduces the sum of squares of the whole hidden state itself
+      // the same over hidden states of more than 4 groups per thread
       float ss = 0.f;
       const float4 *a4 = reinterpret_cast<const float4 *>(p.xa);
       for (int k = threadIdx.x; k < ngroups * 2; k += blockDim.x) {

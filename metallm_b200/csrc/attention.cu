@@ -272,28 +272,38 @@ __global__ void attn_decode_merge_kernel(const float *__restrict__ partials, int
 //
 // One thread-block cluster of kClusterCtas CTAs per KV head; CTA r of the
 // cluster owns positions [r * chunk_len, (r + 1) * chunk_len), staged in
-// shared memory by cp.async in phases of up to kPhaseRows rows (K rows
-// padded to 272 bytes so that a lane per row reads without bank conflicts).
-// Per phase, lane j of warp w scores rows j, j + 32, ... against query head
-// w (and w + 4, ...) of the KV head's group, with q rotated in fp32 and
-// scaled by 1/sqrt(d); the warp keeps that head's running max and sum
-// (online softmax across phases); thread t accumulates output dimension t
-// of every head.  The CTA holding the position also rotates k, rounds k and
-// v to fp16, appends them to the caches and uses them for that row.  The
-// CTAs' (max, sum, output) triples are merged through distributed shared
-// memory after a cluster barrier: CTA h of the cluster finishes head h of
-// the group from the other CTAs' partials, so no partial goes through global
-// memory and no arrival counter is needed.
+// shared memory by cp.async in phases of up to kPhaseRows rows (K and V rows
+// padded to 272 bytes, so every ldmatrix below is free of bank conflicts).
+// The first phase's rows are put in flight before the dependent wait: they
+// were written by earlier steps, not by the QKV GEMV this kernel follows.
+//
+// Both products run on the tensor cores (mma.sync m16n8k16, fp32
+// accumulators) with fp16 operands split in two so that they carry fp32
+// accuracy: q (rotated in fp32, scaled by 1/sqrt(d) and by a power of two
+// 2^-e that keeps it inside the fp16 range) as q_hi + q_lo, the softmax
+// weights as p_hi + p_lo; K and V are fp16 already.  Scores: A = 16 cached
+// rows x 16 dimensions, B = the group's heads (padded to 8); the warp owning
+// a head then takes the max, the exponentials and the running sum over the
+// phase's rows (online softmax across phases).  Output: A = the weights of
+// the group's heads (padded to 16) x 16 rows, B = V^T through ldmatrix.trans,
+// warp w holding dimensions [32w, 32w + 32).  The CTA holding the position
+// also rotates k, rounds k and v to fp16, appends them to the caches and
+// uses them for that row.  The CTAs' (max, sum, output) triples are merged
+// through distributed shared memory after a cluster barrier: CTA h of the
+// cluster finishes head h of the group from the other CTAs' partials.
 #ifndef MLM_ATTN_CLUSTER
 #define MLM_ATTN_CLUSTER 8
 #endif
 constexpr int kClusterCtas = MLM_ATTN_CLUSTER;  // CTAs per KV head
-// rows staged at once: 96 rows (51 KB) let a CTA sit beside a decode GEMV's
+// rows staged at once: 96 rows keep the CTA (about 65 KB of shared memory,
+// at most 64 registers a thread) small enough to sit beside a decode GEMV's
 // CTA on one SM, so it is resident, with its first rows in flight, before
 // the QKV GEMV it depends on has finished
 constexpr int kPhaseRows = 96;
-constexpr int kKPitch = kAttnD + 8;             // K row pitch in halves (272 bytes)
-constexpr int kRowBytes = kKPitch * 2 + kAttnD * 2;  // shared memory per staged row
+constexpr int kKPitch = kAttnD + 8;            // K and V row pitch in halves (272 bytes)
+constexpr int kRowBytes = 2 * kKPitch * 2;     // shared memory per staged row (K and V)
+constexpr int kSPitch = kPhaseRows + 4;        // score rows (fp32) per head
+constexpr int kPPitch = kPhaseRows + 8;        // weight rows (fp16) per head: 208 bytes
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -312,20 +322,48 @@ __device__ __forceinline__ float ld_cluster_f32(const float *local, uint32_t ran
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
   return v;
 }
+// four 8x8 fp16 matrices; lane l gives the address of row (l & 7) of
+// matrix l >> 3 (.trans: each lane receives the transposed elements)
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
+                                          uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// v as fp16 hi + lo (hi = fp16(v), lo = fp16(v - hi))
+__device__ __forceinline__ void split_f16(float v, __half &hi, __half &lo) {
+  hi = __float2half_rn(v);
+  lo = __float2half_rn(v - __half2float(hi));
+}
 
 template <int G>
-__global__ void __launch_bounds__(kAttnThreads) attn_rope_decode_kernel(
+__global__ void __launch_bounds__(kAttnThreads, 8) attn_rope_decode_kernel(
     const float *__restrict__ qkv, mlm_rope_args ra, RopeConsts rk,
     const float *__restrict__ freqs, __half *__restrict__ kc, __half *__restrict__ vc,
     int n_heads, int n_kv, int chunk_len, float scale, const int *__restrict__ pos_dev,
     __half *__restrict__ out) {
-  static_assert(kAttnThreads == kAttnD && kAttnThreads == 128, "thread t = output dimension t");
-  constexpr int HW = (G + 3) / 4;          // heads per warp: w, w + 4, ...
-  constexpr int NR = kPhaseRows / 32;      // rows per lane, at most
+  static_assert(kAttnThreads == 128 && kAttnD == 128, "4 warps; warp w outputs dims 32w..32w+31");
+  static_assert(G <= 8, "a group's heads are padded to 8 (scores) and 16 (output)");
+  constexpr int HW = (G + 3) / 4;  // heads per warp in the softmax: w, w + 4
   extern __shared__ __align__(16) uint8_t s_dyn[];
-  __shared__ __align__(16) float s_q[G][kAttnD];  // q, then this CTA's output
-  __shared__ __align__(16) float s_p[kPhaseRows][G];
-  __shared__ float s_corr[G], s_m[G], s_l[G];
+  // q as fp16 hi / lo [head][dim] (heads padded to 8); after the last phase
+  // the same bytes hold this CTA's output [G][128] in fp32
+  __shared__ __align__(16) __half s_q[2][8][kKPitch];
+  __shared__ __align__(16) float s_s[G][kSPitch];       // the phase's scores
+  __shared__ __align__(16) __half s_p[2][16][kPPitch];  // weights hi / lo [head][row]
+  __shared__ float s_corr[G], s_m[G], s_l[G], s_qmax[2];
   const uint32_t rank = cluster_ctarank();
   const int kvh = blockIdx.x / kClusterCtas;
   // the position and the cached rows before it were written by earlier
@@ -333,6 +371,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_rope_decode_kernel(
   const int pos = *pos_dev;
   const int seq_len = pos + 1;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, tq = lane & 3;
   const size_t row_stride = (size_t)n_kv * kAttnD;
   const float *kf = qkv + (size_t)n_heads * kAttnD;
   const float *vf = kf + row_stride;
@@ -342,7 +381,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_rope_decode_kernel(
   const int nphase = p_end > p_begin ? (p_end - p_begin + rows_cap - 1) / rows_cap : 0;
   const bool has_new = nphase > 0 && p_end == seq_len;  // this CTA holds row `pos`
   __half *s_k = reinterpret_cast<__half *>(s_dyn);        // [rows_cap][kKPitch]
-  __half *s_v = s_k + (size_t)rows_cap * kKPitch;         // [rows_cap][128]
+  __half *s_v = s_k + (size_t)rows_cap * kKPitch;         // [rows_cap][kKPitch]
 
   // cached rows of phase ph by cp.async (row pos, when it falls in the
   // phase, comes from registers once q, k and v are available)
@@ -355,13 +394,23 @@ __global__ void __launch_bounds__(kAttnThreads) attn_rope_decode_kernel(
     const uint32_t sv = (uint32_t)__cvta_generic_to_shared(s_v);
     for (int j = threadIdx.x; j < cached * kPieces; j += kAttnThreads) {
       const int r = j / kPieces, c = j - r * kPieces;
-      const size_t g = (size_t)(a + r) * row_stride + kvh * kAttnD + c * 8;
-      cp_async16(sk + (uint32_t)(r * kKPitch + c * 8) * 2, kc + g);
-      cp_async16(sv + (uint32_t)(r * kAttnD + c * 8) * 2, vc + g);
+      const size_t gi = (size_t)(a + r) * row_stride + kvh * kAttnD + c * 8;
+      const uint32_t off = (uint32_t)(r * kKPitch + c * 8) * 2;
+      cp_async16(sk + off, kc + gi);
+      cp_async16(sv + off, vc + gi);
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
   if (nphase > 0) load_phase(0);
+  // padding: weight rows of heads G..15 and q rows of heads G..7 are zero
+  for (int i = threadIdx.x; i < 2 * (16 - G) * kPPitch; i += kAttnThreads) {
+    const int hl = i / ((16 - G) * kPPitch), rem = i - hl * (16 - G) * kPPitch;
+    s_p[hl][G + rem / kPPitch][rem % kPPitch] = __float2half_rn(0.f);
+  }
+  for (int i = threadIdx.x; i < 2 * (8 - G) * kKPitch; i += kAttnThreads) {
+    const int hl = i / ((8 - G) * kKPitch), rem = i - hl * (8 - G) * kKPitch;
+    s_q[hl][G + rem / kKPitch][rem % kKPitch] = __float2half_rn(0.f);
+  }
   // the rotation of pair t at this position (threads t < 64)
   float c = 1.f, sn = 0.f;
   if (threadIdx.x < 64 && 2 * (int)threadIdx.x < (int)ra.n_dims)
@@ -370,9 +419,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_rope_decode_kernel(
   // q, k and v of this step come from the QKV GEMV before this kernel
   pdl_wait_then_release();
 
-  // q of the group rotated in fp32 (pair t of every head by thread t < 64),
-  // the new k row rotated likewise, the new v row by threads 64..127
+  // q of the group rotated in fp32 (pair t of every head by thread t < 64)
+  // and scaled by 1/sqrt(d), the new k row rotated likewise, the new v row
+  // by threads 64..127
   __half2 kv_new = __floats2half2_rn(0.f, 0.f);
+  float qr[G][2];
+  float qm = 0.f;
   {
     const int t = threadIdx.x & 63;
     if (threadIdx.x < 64) {
@@ -380,8 +432,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_rope_decode_kernel(
       for (int h = 0; h < G; ++h) {
         const float2 x =
             *reinterpret_cast<const float2 *>(qkv + (size_t)(kvh * G + h) * kAttnD + 2 * t);
-        s_q[h][2 * t] = (x.x * c - x.y * sn) * scale;
-        s_q[h][2 * t + 1] = (x.x * sn + x.y * c) * scale;
+        qr[h][0] = (x.x * c - x.y * sn) * scale;
+        qr[h][1] = (x.x * sn + x.y * c) * scale;
+        qm = fmaxf(qm, fmaxf(fabsf(qr[h][0]), fabsf(qr[h][1])));
       }
       if (has_new) {
         const float2 x = *reinterpret_cast<const float2 *>(kf + kvh * kAttnD + 2 * t);
@@ -394,6 +447,34 @@ __global__ void __launch_bounds__(kAttnThreads) attn_rope_decode_kernel(
       *reinterpret_cast<__half2 *>(vc + ((size_t)pos * n_kv + kvh) * kAttnD + 2 * t) = kv_new;
     }
   }
+  qm = warp_max(qm);
+  if (lane == 0 && warp < 2) s_qmax[warp] = qm;
+  __syncthreads();
+  // q * 2^-qe stays below 2^15 (fp16); the scores are multiplied back
+  const int qe = silu_scale_exp(fmaxf(s_qmax[0], s_qmax[1]));
+  const float sback = __uint_as_float((uint32_t)(127 + qe) << 23);
+  if (threadIdx.x < 64) {
+    const float qinv = __uint_as_float((uint32_t)(127 - qe) << 23);
+    const int t = threadIdx.x;
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      __half h0, l0, h1, l1;
+      split_f16(qr[h][0] * qinv, h0, l0);
+      split_f16(qr[h][1] * qinv, h1, l1);
+      *reinterpret_cast<__half2 *>(&s_q[0][h][2 * t]) = __halves2half2(h0, h1);
+      *reinterpret_cast<__half2 *>(&s_q[1][h][2 * t]) = __halves2half2(l0, l1);
+    }
+  }
+
+  const uint32_t sq = (uint32_t)__cvta_generic_to_shared(&s_q[0][0][0]);
+  const uint32_t sp = (uint32_t)__cvta_generic_to_shared(&s_p[0][0][0]);
+  const uint32_t skb = (uint32_t)__cvta_generic_to_shared(s_k);
+  const uint32_t svb = (uint32_t)__cvta_generic_to_shared(s_v);
+  // ldmatrix row addresses of this lane: A tiles (rows r0 + (lane & 15)),
+  // B tiles of q (head lane & 7, 8-column block lane >> 3)
+  const int a_row = (lane & 7) + ((lane >> 3) & 1) * 8, a_col = (lane >> 4) * 8;
+  const int b_row = lane & 7, b_col = (lane >> 3) * 8;
+  constexpr uint32_t kQBytes = 8 * kKPitch * 2, kPBytes = 16 * kPPitch * 2;
 
   float m_run[HW], l_run[HW];
 #pragma unroll
@@ -401,66 +482,83 @@ __global__ void __launch_bounds__(kAttnThreads) attn_rope_decode_kernel(
     m_run[i] = -INFINITY;
     l_run[i] = 0.f;
   }
-  float o[G];
+  float o[4][4];  // output dims 32w + 8nt + 2tq (+1) of head g (rows g + 8: padding)
 #pragma unroll
-  for (int h = 0; h < G; ++h) o[h] = 0.f;
+  for (int nt = 0; nt < 4; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
 
   for (int ph = 0; ph < nphase; ++ph) {
     const int a = p_begin + ph * rows_cap;
     const int n = min(rows_cap, p_end - a);
+    const int n16 = (n + 15) & ~15;
     if (ph > 0) load_phase(ph);
-    {
-      const int cached = (has_new && a + n == p_end) ? n - 1 : n;
-      if (cached < n) {
-        const int t = threadIdx.x & 63;
-        if (threadIdx.x < 64)
-          *reinterpret_cast<__half2 *>(s_k + (size_t)cached * kKPitch + 2 * t) = kv_new;
-        else
-          *reinterpret_cast<__half2 *>(s_v + (size_t)cached * kAttnD + 2 * t) = kv_new;
+    const int cached = (has_new && a + n == p_end) ? n - 1 : n;
+    if (cached < n) {
+      const int t = threadIdx.x & 63;
+      __half *row = (threadIdx.x < 64 ? s_k : s_v) + (size_t)cached * kKPitch;
+      *reinterpret_cast<__half2 *>(row + 2 * t) = kv_new;
+    }
+    // V rows n..n16-1 meet zero weights; stale rows may hold NaN: zero them
+    for (int i = threadIdx.x; i < (n16 - n) * (kAttnD / 2); i += kAttnThreads)
+      reinterpret_cast<uint32_t *>(s_v + (size_t)(n + i / (kAttnD / 2)) * kKPitch)[i % (kAttnD / 2)] =
+          0u;
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+
+    // scores of 16-row tiles w, w + 4, ...: S = K (q_hi + q_lo)^T
+    for (int j0 = 16 * warp; j0 < n; j0 += 64) {
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int s = 0; s < kAttnD / 16; s += 2) {
+        uint32_t qh[4], ql[4], ka[4];
+        const uint32_t qo = (uint32_t)(b_row * kKPitch + 16 * s + b_col) * 2;
+        ldsm_x4(sq + qo, qh);
+        ldsm_x4(sq + kQBytes + qo, ql);
+        ldsm_x4(skb + (uint32_t)((j0 + a_row) * kKPitch + 16 * s + a_col) * 2, ka);
+        mma_16816(acc, ka, qh[0], qh[1]);
+        mma_16816(acc, ka, ql[0], ql[1]);
+        ldsm_x4(skb + (uint32_t)((j0 + a_row) * kKPitch + 16 * (s + 1) + a_col) * 2, ka);
+        mma_16816(acc, ka, qh[2], qh[3]);
+        mma_16816(acc, ka, ql[2], ql[3]);
       }
-      asm volatile("cp.async.wait_group 0;" ::: "memory");
+      // C: rows j0 + g (acc 0, 1) and j0 + g + 8 (acc 2, 3), heads 2tq, 2tq + 1
+      if (2 * tq < G) {
+        s_s[2 * tq][j0 + g] = acc[0] * sback;
+        s_s[2 * tq][j0 + g + 8] = acc[2] * sback;
+      }
+      if (2 * tq + 1 < G) {
+        s_s[2 * tq + 1][j0 + g] = acc[1] * sback;
+        s_s[2 * tq + 1][j0 + g + 8] = acc[3] * sback;
+      }
     }
     __syncthreads();
 
-    // scores of rows lane + 32 i for the warp's heads, then the online softmax
+    // softmax of head h by warp h % 4 over rows lane + 32 i; weights as
+    // fp16 hi / lo (zero for rows n..n16-1)
 #pragma unroll
     for (int hi = 0; hi < HW; ++hi) {
       const int h = warp + 4 * hi;
       if (h >= G) break;
-      float acc[NR];
-#pragma unroll
-      for (int i = 0; i < NR; ++i) acc[i] = 0.f;
-#pragma unroll 2
-      for (int d = 0; d < kAttnD; d += 8) {
-        const float4 qa = *reinterpret_cast<const float4 *>(&s_q[h][d]);
-        const float4 qb = *reinterpret_cast<const float4 *>(&s_q[h][d + 4]);
-#pragma unroll
-        for (int i = 0; i < NR; ++i) {
-          if (32 * i < n) {
-            const uint4 raw =
-                *reinterpret_cast<const uint4 *>(s_k + (size_t)(lane + 32 * i) * kKPitch + d);
-            const float2 k0 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
-            const float2 k1 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
-            const float2 k2 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.z));
-            const float2 k3 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.w));
-            acc[i] += ((qa.x * k0.x + qa.y * k0.y) + (qa.z * k1.x + qa.w * k1.y)) +
-                      ((qb.x * k2.x + qb.y * k2.y) + (qb.z * k3.x + qb.w * k3.y));
-          }
-        }
-      }
+      float sv[kPhaseRows / 32];
       float mloc = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < NR; ++i) {
-        if (lane + 32 * i >= n) acc[i] = -INFINITY;
-        mloc = fmaxf(mloc, acc[i]);
+      for (int i = 0; i < kPhaseRows / 32; ++i) {
+        const int j = lane + 32 * i;
+        sv[i] = j < n ? s_s[h][j] : -INFINITY;
+        mloc = fmaxf(mloc, sv[i]);
       }
       const float m_new = fmaxf(m_run[hi], warp_max(mloc));
       float lsum = 0.f;
 #pragma unroll
-      for (int i = 0; i < NR; ++i) {
-        const float p = __expf(acc[i] - m_new);  // 0 for rows past n
-        if (32 * i < n) s_p[lane + 32 * i][h] = p;
+      for (int i = 0; i < kPhaseRows / 32; ++i) {
+        const int j = lane + 32 * i;
+        const float p = j < n ? __expf(sv[i] - m_new) : 0.f;
         lsum += p;
+        if (j < n16) {
+          __half ph16, pl16;
+          split_f16(p, ph16, pl16);
+          s_p[0][h][j] = ph16;
+          s_p[1][h][j] = pl16;
+        }
       }
       const float corr = __expf(m_run[hi] - m_new);
       l_run[hi] = l_run[hi] * corr + warp_sum(lsum);
@@ -469,24 +567,44 @@ __global__ void __launch_bounds__(kAttnThreads) attn_rope_decode_kernel(
     }
     __syncthreads();
 
-    // output dimension t of every head
+    // output: O[h][d] = corr O + (p_hi + p_lo) V over the phase's rows,
+    // dims [32w, 32w + 32) of warp w
     {
-      const int t = threadIdx.x;
+      const float cr = g < G ? s_corr[g] : 0.f;
 #pragma unroll
-      for (int h = 0; h < G; ++h) o[h] *= s_corr[h];
-#pragma unroll 8
-      for (int j = 0; j < n; ++j) {
-        const float v = __half2float(s_v[(size_t)j * kAttnD + t]);
+      for (int nt = 0; nt < 4; ++nt) {
+        o[nt][0] *= cr;
+        o[nt][1] *= cr;
+      }
+      for (int j0 = 0; j0 < n16; j0 += 16) {
+        uint32_t pa[4], pl[4];
+        const uint32_t po = (uint32_t)(a_row * kPPitch + j0 + a_col) * 2;
+        ldsm_x4(sp + po, pa);
+        ldsm_x4(sp + kPBytes + po, pl);
 #pragma unroll
-        for (int h = 0; h < G; ++h) o[h] += s_p[j][h] * v;
+        for (int half = 0; half < 2; ++half) {
+          uint32_t vb[4];
+          ldsm_x4_t(svb + (uint32_t)((j0 + a_row) * kKPitch + 32 * warp + 16 * half + a_col) * 2, vb);
+          mma_16816(o[2 * half], pa, vb[0], vb[1]);
+          mma_16816(o[2 * half], pl, vb[0], vb[1]);
+          mma_16816(o[2 * half + 1], pa, vb[2], vb[3]);
+          mma_16816(o[2 * half + 1], pl, vb[2], vb[3]);
+        }
       }
     }
-    __syncthreads();  // the stage and s_p are free for the next phase
+    __syncthreads();  // stages, scores and weights are free for the next phase
   }
 
-  // this CTA's partials: output in place of q, max and sum per head
+  // this CTA's partials: output in place of q, max and sum per head (the
+  // barrier also orders the q stores of a CTA without rows before these)
+  __syncthreads();
+  float *s_o = reinterpret_cast<float *>(&s_q[0][0][0]);  // [G][128]
+  if (g < G) {
 #pragma unroll
-  for (int h = 0; h < G; ++h) s_q[h][threadIdx.x] = o[h];
+    for (int nt = 0; nt < 4; ++nt)
+      *reinterpret_cast<float2 *>(&s_o[g * kAttnD + 32 * warp + 8 * nt + 2 * tq]) =
+          make_float2(o[nt][0], o[nt][1]);
+  }
 #pragma unroll
   for (int hi = 0; hi < HW; ++hi) {
     const int h = warp + 4 * hi;
@@ -503,16 +621,16 @@ __global__ void __launch_bounds__(kAttnThreads) attn_rope_decode_kernel(
     float mc[kClusterCtas];
     float M = -INFINITY;
 #pragma unroll
-    for (int c = 0; c < kClusterCtas; ++c) {
-      mc[c] = ld_cluster_f32(&s_m[h], c);
-      M = fmaxf(M, mc[c]);
+    for (int cc = 0; cc < kClusterCtas; ++cc) {
+      mc[cc] = ld_cluster_f32(&s_m[h], cc);
+      M = fmaxf(M, mc[cc]);
     }
     float L = 0.f, O = 0.f;
 #pragma unroll
-    for (int c = 0; c < kClusterCtas; ++c) {
-      const float w = __expf(mc[c] - M);
-      L += ld_cluster_f32(&s_l[h], c) * w;
-      O += ld_cluster_f32(&s_q[h][threadIdx.x], c) * w;
+    for (int cc = 0; cc < kClusterCtas; ++cc) {
+      const float w = __expf(mc[cc] - M);
+      L += ld_cluster_f32(&s_l[h], cc) * w;
+      O += ld_cluster_f32(&s_o[h * kAttnD + threadIdx.x], cc) * w;
     }
     out[(size_t)(kvh * G + h) * kAttnD + threadIdx.x] = __float2half_rn(O / L);
   }

@@ -322,6 +322,13 @@ __device__ __forceinline__ float ld_cluster_f32(const float *local, uint32_t ran
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
   return v;
 }
+// two floats to the same shared-memory address in CTA `rank` of the cluster
+__device__ __forceinline__ void st_cluster_f32x2(const float *local, uint32_t rank, float a,
+                                                 float b) {
+  uint32_t la = (uint32_t)__cvta_generic_to_shared(local), ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(la), "r"(rank));
+  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(ra), "f"(a), "f"(b) : "memory");
+}
 // four 8x8 fp16 matrices; lane l gives the address of row (l & 7) of
 // matrix l >> 3 (.trans: each lane receives the transposed elements)
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
@@ -355,15 +362,16 @@ __global__ void __launch_bounds__(kAttnThreads, 8) attn_rope_decode_kernel(
     int n_heads, int n_kv, int chunk_len, float scale, const int *__restrict__ pos_dev,
     __half *__restrict__ out) {
   static_assert(kAttnThreads == 128 && kAttnD == 128, "4 warps; warp w outputs dims 32w..32w+31");
-  static_assert(G <= 8, "a group's heads are padded to 8 (scores) and 16 (output)");
+  static_assert(G <= 8 && G <= kClusterCtas,
+                "a group's heads are padded to 8 (scores) and 16 (output); CTA h finishes head h");
   constexpr int HW = (G + 3) / 4;  // heads per warp in the softmax: w, w + 4
   extern __shared__ __align__(16) uint8_t s_dyn[];
-  // q as fp16 hi / lo [head][dim] (heads padded to 8); after the last phase
-  // the same bytes hold this CTA's output [G][128] in fp32
+  // q as fp16 hi / lo [head][dim] (heads padded to 8)
   __shared__ __align__(16) __half s_q[2][8][kKPitch];
   __shared__ __align__(16) float s_s[G][kSPitch];       // the phase's scores
   __shared__ __align__(16) __half s_p[2][16][kPPitch];  // weights hi / lo [head][row]
-  __shared__ float s_corr[G], s_m[G], s_l[G], s_qmax[2];
+  __shared__ __align__(16) float s_recv[kClusterCtas][kAttnD + 4];  // partials of head rank
+  __shared__ float s_corr[G], s_qmax[2];
   const uint32_t rank = cluster_ctarank();
   const int kvh = blockIdx.x / kClusterCtas;
   // the position and the cached rows before it were written by earlier
@@ -506,7 +514,7 @@ __global__ void __launch_bounds__(kAttnThreads, 8) attn_rope_decode_kernel(
 
     // scores of 16-row tiles w, w + 4, ...: S = K (q_hi + q_lo)^T
     for (int j0 = 16 * warp; j0 < n; j0 += 64) {
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      float acc[4] = {0.f, 0.f, 0.f, 0.f}, acl[4] = {0.f, 0.f, 0.f, 0.f};  // q_hi, q_lo
 #pragma unroll
       for (int s = 0; s < kAttnD / 16; s += 2) {
         uint32_t qh[4], ql[4], ka[4];
@@ -515,11 +523,13 @@ __global__ void __launch_bounds__(kAttnThreads, 8) attn_rope_decode_kernel(
         ldsm_x4(sq + kQBytes + qo, ql);
         ldsm_x4(skb + (uint32_t)((j0 + a_row) * kKPitch + 16 * s + a_col) * 2, ka);
         mma_16816(acc, ka, qh[0], qh[1]);
-        mma_16816(acc, ka, ql[0], ql[1]);
+        mma_16816(acl, ka, ql[0], ql[1]);
         ldsm_x4(skb + (uint32_t)((j0 + a_row) * kKPitch + 16 * (s + 1) + a_col) * 2, ka);
         mma_16816(acc, ka, qh[2], qh[3]);
-        mma_16816(acc, ka, ql[2], ql[3]);
+        mma_16816(acl, ka, ql[2], ql[3]);
       }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[e] += acl[e];
       // C: rows j0 + g (acc 0, 1) and j0 + g + 8 (acc 2, 3), heads 2tq, 2tq + 1
       if (2 * tq < G) {
         s_s[2 * tq][j0 + g] = acc[0] * sback;
@@ -595,46 +605,38 @@ __global__ void __launch_bounds__(kAttnThreads, 8) attn_rope_decode_kernel(
     __syncthreads();  // stages, scores and weights are free for the next phase
   }
 
-  // this CTA's partials: output in place of q, max and sum per head (the
-  // barrier also orders the q stores of a CTA without rows before these)
-  __syncthreads();
-  float *s_o = reinterpret_cast<float *>(&s_q[0][0][0]);  // [G][128]
+  // this CTA's partials go straight into the shared memory of the CTA that
+  // finishes each head (CTA h of the cluster for head h), in slot `rank`:
+  // (max, sum, output[128]); the cluster barrier makes them visible there,
+  // and after it no CTA touches another's shared memory
   if (g < G) {
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt)
-      *reinterpret_cast<float2 *>(&s_o[g * kAttnD + 32 * warp + 8 * nt + 2 * tq]) =
-          make_float2(o[nt][0], o[nt][1]);
+      st_cluster_f32x2(&s_recv[rank][2 + 32 * warp + 8 * nt + 2 * tq], g, o[nt][0], o[nt][1]);
   }
 #pragma unroll
   for (int hi = 0; hi < HW; ++hi) {
     const int h = warp + 4 * hi;
-    if (h < G && lane == 0) {
-      s_m[h] = m_run[hi];
-      s_l[h] = l_run[hi];
-    }
+    if (h < G && lane == 0) st_cluster_f32x2(&s_recv[rank][0], h, m_run[hi], l_run[hi]);
   }
   cluster_sync_all();
 
-  // CTA r finishes heads r, r + kClusterCtas, ... of the group from every
-  // CTA's partials (CTA 0 always holds rows, so M is finite)
-  for (int h = (int)rank; h < G; h += kClusterCtas) {
-    float mc[kClusterCtas];
+  // CTA h < G finishes head h from every CTA's partials (CTA 0 always holds
+  // rows, so M is finite)
+  if ((int)rank < G) {
+    const int h = (int)rank;
     float M = -INFINITY;
 #pragma unroll
-    for (int cc = 0; cc < kClusterCtas; ++cc) {
-      mc[cc] = ld_cluster_f32(&s_m[h], cc);
-      M = fmaxf(M, mc[cc]);
-    }
+    for (int cc = 0; cc < kClusterCtas; ++cc) M = fmaxf(M, s_recv[cc][0]);
     float L = 0.f, O = 0.f;
 #pragma unroll
     for (int cc = 0; cc < kClusterCtas; ++cc) {
-      const float w = __expf(mc[cc] - M);
-      L += ld_cluster_f32(&s_l[h], cc) * w;
-      O += ld_cluster_f32(&s_o[h * kAttnD + threadIdx.x], cc) * w;
+      const float w = __expf(s_recv[cc][0] - M);
+      L += s_recv[cc][1] * w;
+      O += s_recv[cc][2 + threadIdx.x] * w;
     }
     out[(size_t)(kvh * G + h) * kAttnD + threadIdx.x] = __float2half_rn(O / L);
   }
-  cluster_sync_all();  // no CTA leaves while another reads its shared memory
 }
 
 // positions per CTA of the fused kernel: the capacity over the cluster,

@@ -8,10 +8,10 @@
 // of positions and serves all n_heads/n_kv_heads query heads of that KV head,
 // so each K and V row is read from HBM exactly once.  Softmax is fp32 with a
 // running max; each CTA writes (max, sum, unnormalised output) for its chunk.
-// For one sequence the last CTA of a KV head to finish merges the chunks; for
-// a batch a second kernel merges them (one CTA per head and sequence), which
-// measured faster there (the merges of 8 sequences x 8 KV heads otherwise run
-// one per CTA at the kernel's tail).
+// The last CTA of a KV head to finish merges the chunks (mlm_attn_decode).
+// The runner's decode steps, one sequence or a batch, use the fused kernel
+// further down: RoPE and the KV append folded in, both products on the
+// tensor cores, chunks merged through distributed shared memory.
 #include <algorithm>
 
 #include "mlm_device.cuh"
@@ -35,7 +35,7 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
 
-template <int G, class OutT, bool kMerge>
+template <int G, class OutT>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_partial_kernel(
     const __half *__restrict__ q, const __half *__restrict__ kc, const __half *__restrict__ vc,
     int n_heads, int n_kv, int seq_len, int chunk_len, float scale,
@@ -174,8 +174,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_partial_kernel(
     }
   }
 
-  if (!kMerge) return;  // attn_decode_merge_kernel combines the chunks
-
   // The last chunk of this (sequence, KV head) to finish merges the chunks
   // of its G query heads, in chunk order; it re-zeroes the arrival counter
   // for the next launch.
@@ -234,33 +232,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_partial_kernel(
 #pragma unroll
   for (int gh = 0; gh < G; ++gh)
     out[(size_t)(kvh * G + gh) * kAttnD + dd] = from_float<OutT>(O[gh] / s_L[gh]);
-}
-
-// chunk merge of a batch: one CTA per (head, sequence), thread dd = output
-// dimension dd; the chunks in order
-template <class OutT>
-__global__ void attn_decode_merge_kernel(const float *__restrict__ partials, int n_heads,
-                                         int nchunks, OutT *__restrict__ out,
-                                         const int *__restrict__ pos_dev, int chunk_len,
-                                         size_t part_bs, size_t out_bs) {
-  pdl_wait_then_release();
-  const int h = blockIdx.x;
-  const int dd = threadIdx.x;  // kAttnD threads
-  const int bz = blockIdx.y;
-  partials += bz * part_bs;
-  out += bz * out_bs;
-  if (pos_dev) nchunks = (pos_dev[bz] + chunk_len) / chunk_len;
-  float M = -INFINITY;
-  for (int c = 0; c < nchunks; ++c)
-    M = fmaxf(M, partials[((size_t)c * n_heads + h) * kAttnPartial]);
-  float L = 0.f, O = 0.f;
-  for (int c = 0; c < nchunks; ++c) {
-    const float *pp = partials + ((size_t)c * n_heads + h) * kAttnPartial;
-    const float w = __expf(pp[0] - M);
-    L += pp[1] * w;
-    O += pp[2 + dd] * w;
-  }
-  out[(size_t)h * kAttnD + dd] = from_float<OutT>(O / L);
 }
 
 // ---------------------------------------------------------------------------
@@ -355,12 +326,14 @@ __device__ __forceinline__ void split_f16(float v, __half &hi, __half &lo) {
   lo = __float2half_rn(v - __half2float(hi));
 }
 
-template <int G>
+// Sequence b = blockIdx.y of a batch reads qkv + b qkv_bs, the caches at
+// b kv_bs elements, its position pos_dev[b], and writes out + b out_bs.
+template <int G, class OutT>
 __global__ void __launch_bounds__(kAttnThreads, 8) attn_rope_decode_kernel(
     const float *__restrict__ qkv, mlm_rope_args ra, RopeConsts rk,
     const float *__restrict__ freqs, __half *__restrict__ kc, __half *__restrict__ vc,
     int n_heads, int n_kv, int chunk_len, float scale, const int *__restrict__ pos_dev,
-    __half *__restrict__ out) {
+    OutT *__restrict__ out, size_t qkv_bs, size_t kv_bs, size_t out_bs) {
   static_assert(kAttnThreads == 128 && kAttnD == 128, "4 warps; warp w outputs dims 32w..32w+31");
   static_assert(G <= 8 && G <= kClusterCtas,
                 "a group's heads are padded to 8 (scores) and 16 (output); CTA h finishes head h");
@@ -374,9 +347,13 @@ __global__ void __launch_bounds__(kAttnThreads, 8) attn_rope_decode_kernel(
   __shared__ float s_corr[G], s_qmax[2];
   const uint32_t rank = cluster_ctarank();
   const int kvh = blockIdx.x / kClusterCtas;
+  qkv += blockIdx.y * qkv_bs;
+  kc += blockIdx.y * kv_bs;
+  vc += blockIdx.y * kv_bs;
+  out += blockIdx.y * out_bs;
   // the position and the cached rows before it were written by earlier
   // steps, not by the kernel this one depends on: read them before the wait
-  const int pos = *pos_dev;
+  const int pos = pos_dev[blockIdx.y];
   const int seq_len = pos + 1;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, tq = lane & 3;
@@ -635,7 +612,7 @@ __global__ void __launch_bounds__(kAttnThreads, 8) attn_rope_decode_kernel(
       L += s_recv[cc][1] * w;
       O += s_recv[cc][2 + threadIdx.x] * w;
     }
-    out[(size_t)(kvh * G + h) * kAttnD + threadIdx.x] = __float2half_rn(O / L);
+    out[(size_t)(kvh * G + h) * kAttnD + threadIdx.x] = from_float<OutT>(O / L);
   }
 }
 
@@ -646,9 +623,11 @@ static int attn_rope_chunk_len(int capacity) {
   return (per + 31) / 32 * 32;
 }
 
-int attn_rope_decode_launch(mlm_ctx *ctx, const float *qkv, const float *freqs,
+template <class OutT>
+static int attn_rope_launch(mlm_ctx *ctx, const float *qkv, const float *freqs,
                             const mlm_rope_args &ra, int n_heads, int n_kv, int head_dim,
-                            int capacity, void *kc, void *vc, void *out, cudaStream_t stream,
+                            int capacity, void *kc, void *vc, OutT *out, int batch,
+                            size_t qkv_bs, size_t kv_bs, size_t out_bs, cudaStream_t stream,
                             const int *pos_dev) {
   MLM_REQUIRE(ctx, head_dim == kAttnD, MLM_ERR_UNSUPPORTED,
               "attention: head_dim=%d (this build handles %d)", head_dim, kAttnD);
@@ -657,17 +636,18 @@ int attn_rope_decode_launch(mlm_ctx *ctx, const float *qkv, const float *freqs,
   const int G = n_heads / n_kv;
   MLM_REQUIRE(ctx, G == 1 || G == 2 || G == 4 || G == 8, MLM_ERR_UNSUPPORTED,
               "attention: GQA group %d (supported 1, 2, 4, 8)", G);
-  MLM_REQUIRE(ctx, capacity > 0, MLM_ERR_SHAPE, "attention: cache capacity %d", capacity);
+  MLM_REQUIRE(ctx, capacity > 0 && batch > 0 && batch <= 65535, MLM_ERR_SHAPE,
+              "attention: cache capacity %d, batch %d", capacity, batch);
   const int chunk_len = attn_rope_chunk_len(capacity);
   const int rows_cap = std::min(chunk_len, kPhaseRows);
   const RopeConsts rk = rope_consts(ra);
   const float scale = 1.0f / sqrtf((float)head_dim);
-  auto kern = G == 1   ? attn_rope_decode_kernel<1>
-              : G == 2 ? attn_rope_decode_kernel<2>
-              : G == 4 ? attn_rope_decode_kernel<4>
-                       : attn_rope_decode_kernel<8>;
+  auto kern = G == 1   ? attn_rope_decode_kernel<1, OutT>
+              : G == 2 ? attn_rope_decode_kernel<2, OutT>
+              : G == 4 ? attn_rope_decode_kernel<4, OutT>
+                       : attn_rope_decode_kernel<8, OutT>;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(n_kv * kClusterCtas);
+  cfg.gridDim = dim3(n_kv * kClusterCtas, batch);
   cfg.blockDim = dim3(kAttnThreads);
   cfg.dynamicSmemBytes = (size_t)rows_cap * kRowBytes;
   cfg.stream = stream;
@@ -682,16 +662,35 @@ int attn_rope_decode_launch(mlm_ctx *ctx, const float *qkv, const float *freqs,
   cfg.numAttrs = 2;
   const cudaError_t e = cudaLaunchKernelEx(
       &cfg, kern, qkv, ra, rk, freqs, reinterpret_cast<__half *>(kc),
-      reinterpret_cast<__half *>(vc), n_heads, n_kv, chunk_len, scale, pos_dev,
-      reinterpret_cast<__half *>(out));
+      reinterpret_cast<__half *>(vc), n_heads, n_kv, chunk_len, scale, pos_dev, out, qkv_bs,
+      kv_bs, out_bs);
   return check_launch_pdl(ctx, e, "attention (RoPE, append, decode)");
+}
+
+int attn_rope_decode_launch(mlm_ctx *ctx, const float *qkv, const float *freqs,
+                            const mlm_rope_args &ra, int n_heads, int n_kv, int head_dim,
+                            int capacity, void *kc, void *vc, void *out, cudaStream_t stream,
+                            const int *pos_dev) {
+  return attn_rope_launch(ctx, qkv, freqs, ra, n_heads, n_kv, head_dim, capacity, kc, vc,
+                          reinterpret_cast<__half *>(out), 1, 0, 0, 0, stream, pos_dev);
+}
+
+int attn_rope_decode_batch_launch(mlm_ctx *ctx, const float *qkv, size_t qkv_bs,
+                                  const float *freqs, const mlm_rope_args &ra, int n_heads,
+                                  int n_kv, int head_dim, int capacity, int batch, size_t kv_bs,
+                                  void *kc, void *vc, void *out_bf16, cudaStream_t stream,
+                                  const int *pos_dev) {
+  return attn_rope_launch(ctx, qkv, freqs, ra, n_heads, n_kv, head_dim, capacity, kc, vc,
+                          reinterpret_cast<__nv_bfloat16 *>(out_bf16), batch, qkv_bs, kv_bs,
+                          (size_t)n_heads * head_dim, stream, pos_dev);
 }
 
 // seq_len positions, or, when pos_dev is set, pos_dev[b] + 1 positions read
 // on the device out of a cache of capacity seq_len (a launch a captured graph
 // can replay at every step): fixed 128-position chunks covering the capacity.
-// `batch` sequences (grid z): sequence b reads q + b q_bs, caches + b kv_bs,
-// uses partials + b part_bs and writes out + b out_bs (as OutT).
+// `batch` sequences (grid z; mlm_attn_decode passes one): sequence b reads
+// q + b q_bs, caches + b kv_bs, uses partials + b part_bs and writes
+// out + b out_bs (as OutT).
 template <class OutT>
 static int attn_decode_impl(mlm_ctx *ctx, const void *q, const void *kc, const void *vc,
                             int n_heads, int n_kv, int head_dim, int seq_len, OutT *out,
@@ -731,36 +730,16 @@ static int attn_decode_impl(mlm_ctx *ctx, const void *q, const void *kc, const v
   const __half *qh = reinterpret_cast<const __half *>(q);
   const __half *kh = reinterpret_cast<const __half *>(kc);
   const __half *vh = reinterpret_cast<const __half *>(vc);
-  if (batch == 1) {  // one sequence: chunks merged in the kernel, dependent launch
-    auto kern = G == 1   ? attn_decode_partial_kernel<1, OutT, true>
-                : G == 2 ? attn_decode_partial_kernel<2, OutT, true>
-                : G == 4 ? attn_decode_partial_kernel<4, OutT, true>
-                         : attn_decode_partial_kernel<8, OutT, true>;
-    return check_launch_pdl(
-        ctx,
-        launch_pdl(kern, grid, dim3(kAttnThreads), kAttnStageBytes, stream, qh, kh, vh, n_heads,
-                   n_kv, seq_len, chunk_len, scale, partials, pos_dev, q_bs, kv_bs, part_bs, out,
-                   out_bs, ctx->attn_arrivals),
-        "mlm_attn_decode");
-  }
-  // a batch: the partials, then one merge CTA per (head, sequence)
-  auto kern = G == 1   ? attn_decode_partial_kernel<1, OutT, false>
-              : G == 2 ? attn_decode_partial_kernel<2, OutT, false>
-              : G == 4 ? attn_decode_partial_kernel<4, OutT, false>
-                       : attn_decode_partial_kernel<8, OutT, false>;
-  int st = check_launch_pdl(
+  auto kern = G == 1   ? attn_decode_partial_kernel<1, OutT>
+              : G == 2 ? attn_decode_partial_kernel<2, OutT>
+              : G == 4 ? attn_decode_partial_kernel<4, OutT>
+                       : attn_decode_partial_kernel<8, OutT>;
+  return check_launch_pdl(
       ctx,
       launch_pdl(kern, grid, dim3(kAttnThreads), kAttnStageBytes, stream, qh, kh, vh, n_heads,
                  n_kv, seq_len, chunk_len, scale, partials, pos_dev, q_bs, kv_bs, part_bs, out,
-                 out_bs, static_cast<int *>(nullptr)),
-      "mlm_attn_decode (partial)");
-  if (st != MLM_OK) return st;
-  return check_launch_pdl(
-      ctx,
-      launch_pdl(attn_decode_merge_kernel<OutT>, dim3(n_heads, batch), dim3(kAttnD), 0, stream,
-                 static_cast<const float *>(partials), n_heads, nchunks, out, pos_dev, chunk_len,
-                 part_bs, out_bs),
-      "mlm_attn_decode (merge)");
+                 out_bs, ctx->attn_arrivals),
+      "mlm_attn_decode");
 }
 
 int attn_decode_launch(mlm_ctx *ctx, const void *q, const void *kc, const void *vc, int n_heads,
@@ -771,56 +750,45 @@ int attn_decode_launch(mlm_ctx *ctx, const void *q, const void *kc, const void *
                           pos_dev, 1, 0, 0, 0);
 }
 
-int attn_decode_batch_launch(mlm_ctx *ctx, const void *q, const void *kc, const void *vc,
-                             int n_heads, int n_kv, int head_dim, int capacity, int batch,
-                             size_t kv_bs, void *out_bf16, float *partials,
-                             size_t partial_floats, cudaStream_t stream, const int *pos_dev) {
-  const size_t qd = (size_t)n_heads * head_dim;
-  return attn_decode_impl(ctx, q, kc, vc, n_heads, n_kv, head_dim, capacity,
-                          reinterpret_cast<__nv_bfloat16 *>(out_bf16), partials, partial_floats,
-                          stream, pos_dev, batch, qd, kv_bs, qd);
-}
-
-size_t attn_decode_partial_floats(int n_heads, int capacity) {
-  return (size_t)((capacity + 2 * kAttnChunk - 1) / (2 * kAttnChunk)) * n_heads * kAttnPartial;
-}
-
 // called once per context, with its device current
-template <class OutT, bool kMerge>
+template <class OutT>
 static int attn_init_out(mlm_ctx *ctx) {
-  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_partial_kernel<1, OutT, kMerge>,
+  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_partial_kernel<1, OutT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnStageBytes));
-  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_partial_kernel<2, OutT, kMerge>,
+  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_partial_kernel<2, OutT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnStageBytes));
-  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_partial_kernel<4, OutT, kMerge>,
+  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_partial_kernel<4, OutT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnStageBytes));
-  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_partial_kernel<8, OutT, kMerge>,
+  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_decode_partial_kernel<8, OutT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnStageBytes));
   return MLM_OK;
 }
 
-template <int G>
+template <int G, class OutT>
 static int attn_rope_init(mlm_ctx *ctx) {
-  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_rope_decode_kernel<G>,
+  MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_rope_decode_kernel<G, OutT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          kPhaseRows * kRowBytes));
   if (kClusterCtas > 8)
-    MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_rope_decode_kernel<G>,
+    MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(attn_rope_decode_kernel<G, OutT>,
                                            cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
   return MLM_OK;
 }
 
+template <class OutT>
+static int attn_rope_init_all(mlm_ctx *ctx) {
+  int st = attn_rope_init<1, OutT>(ctx);
+  if (st == MLM_OK) st = attn_rope_init<2, OutT>(ctx);
+  if (st == MLM_OK) st = attn_rope_init<4, OutT>(ctx);
+  if (st == MLM_OK) st = attn_rope_init<8, OutT>(ctx);
+  return st;
+}
+
 int attn_init(mlm_ctx *ctx) {
-  int st = attn_rope_init<1>(ctx);
-  if (st == MLM_OK) st = attn_rope_init<2>(ctx);
-  if (st == MLM_OK) st = attn_rope_init<4>(ctx);
-  if (st == MLM_OK) st = attn_rope_init<8>(ctx);
+  int st = attn_rope_init_all<__half>(ctx);
+  if (st == MLM_OK) st = attn_rope_init_all<__nv_bfloat16>(ctx);
   if (st != MLM_OK) return st;
-  st = attn_init_out<__half, true>(ctx);
-  if (st == MLM_OK) st = attn_init_out<__half, false>(ctx);
-  if (st == MLM_OK) st = attn_init_out<__nv_bfloat16, true>(ctx);
-  if (st != MLM_OK) return st;
-  st = attn_init_out<__nv_bfloat16, false>(ctx);
+  st = attn_init_out<__half>(ctx);
   if (st != MLM_OK) return st;
   // arrival counters of the chunk merge, zero between launches
   if (cudaMalloc(&ctx->attn_arrivals, sizeof(int) * kAttnMaxArrivals) != cudaSuccess)

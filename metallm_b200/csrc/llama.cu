@@ -139,8 +139,6 @@ struct mlm_llama {
   int32_t *tok_b = nullptr;                     // device tokens [batch]
   int32_t *gen_b = nullptr;                     // [max_seq][batch] greedy tokens
   float *b_logits = nullptr;                    // [batch][vocab / tp]
-  float *b_partials = nullptr;                  // attention scratch of the batch
-  size_t b_partial_floats = 0;
   unsigned long long *b_keys_l = nullptr, *b_keys = nullptr;  // [batch], [tp][batch]
   cudaGraph_t bstep_graph = nullptr;
   cudaGraphExec_t bstep_exec = nullptr;
@@ -337,12 +335,10 @@ struct mlm_llama {
                                          zq ? pf_qkv : nullptr, (size_t)B * qkv_rows())))
         return st;
       if ((st = qkv_rows_linear(L, pf_x, B, zq))) return st;
-      if ((st = rope_kv_batch_launch(ctx, pf_qkv, rope_freqs, c.rope, nh(), nkv(), c.head_dim, B,
-                                     pos_b, seq_elems(), pf_q16, L.kc, L.vc, s)))
-        return st;
-      if ((st = attn_decode_batch_launch(ctx, pf_q16, L.kc, L.vc, nh(), nkv(), c.head_dim,
-                                         c.max_seq, B, seq_elems(), pf_attn, b_partials,
-                                         b_partial_floats, s, pos_b)))
+      // RoPE of q and k, the KV append and the attention of every sequence
+      if ((st = attn_rope_decode_batch_launch(ctx, pf_qkv, qkv_rows(), rope_freqs, c.rope, nh(),
+                                              nkv(), c.head_dim, c.max_seq, B, seq_elems(),
+                                              L.kc, L.vc, pf_attn, s, pos_b)))
         return st;
       if ((st = row_parallel_rows(L.wo, qdim(), pf_attn, B))) return st;
       if ((st = rmsnorm_rows_bf16_launch(ctx, pf_hidden, L.ffn_norm, pf_x, B, c.dim, c.rms_eps, s,
@@ -582,11 +578,9 @@ static int llama_create(mlm_ctx *ctx, const mlm_llama_config *cfg, int batch,
         m->alloc(&m->pf_attn, 2 * T * m->qdim()) || m->alloc(&m->pf_tokens, sizeof(int32_t) * T) ||
         (any_v6 && m->alloc(&m->pf_tmp, sizeof(float) * T * m->qkv_rows())))
       return fail(MLM_ERR_ALLOC);
-    m->b_partial_floats = (size_t)batch * attn_decode_partial_floats(m->nh(), c.max_seq);
     if (m->alloc(&m->pos_b, sizeof(int) * batch) || m->alloc(&m->tok_b, sizeof(int32_t) * batch) ||
         m->alloc(&m->gen_b, sizeof(int32_t) * c.max_seq * batch) ||
         m->alloc(&m->b_logits, sizeof(float) * batch * m->vocab_l()) ||
-        m->alloc(&m->b_partials, sizeof(float) * m->b_partial_floats) ||
         m->alloc(&m->b_keys_l, sizeof(unsigned long long) * batch) ||
         m->alloc(&m->b_keys, sizeof(unsigned long long) * batch * tp))
       return fail(MLM_ERR_ALLOC);

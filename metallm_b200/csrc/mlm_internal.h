@@ -169,18 +169,17 @@ int attn_rope_decode_launch(mlm_ctx *ctx, const float *qkv, const float *freqs,
                             const mlm_rope_args &ra, int n_heads, int n_kv, int head_dim,
                             int capacity, void *kc, void *vc, void *out, cudaStream_t stream,
                             const int *pos_dev);
+// the same for a batch of sequences, one new token each: sequence b reads
+// qkv + b qkv_bs, the caches at b kv_bs elements, position pos_dev[b], and
+// writes its bf16 output [n_heads][128] at out_bf16 + b n_heads 128
+int attn_rope_decode_batch_launch(mlm_ctx *ctx, const float *qkv, size_t qkv_bs,
+                                  const float *freqs, const mlm_rope_args &ra, int n_heads,
+                                  int n_kv, int head_dim, int capacity, int batch, size_t kv_bs,
+                                  void *kc, void *vc, void *out_bf16, cudaStream_t stream,
+                                  const int *pos_dev);
 int attn_decode_launch(mlm_ctx *ctx, const void *q, const void *kc, const void *vc, int n_heads,
                        int n_kv, int head_dim, int seq_len, void *out, float *partials,
                        size_t partial_floats, cudaStream_t stream, const int *pos_dev);
-// decode attention of `batch` sequences at once (one new token each, at
-// position pos_dev[b]): q fp16 [batch][n_heads][128], caches of sequence b at
-// kc/vc + b * kv_bs elements (capacity positions each), out bf16
-// [batch][n_heads][128]; partials hold batch * attn_decode_partial_floats
-int attn_decode_batch_launch(mlm_ctx *ctx, const void *q, const void *kc, const void *vc,
-                             int n_heads, int n_kv, int head_dim, int capacity, int batch,
-                             size_t kv_bs, void *out_bf16, float *partials,
-                             size_t partial_floats, cudaStream_t stream, const int *pos_dev);
-size_t attn_decode_partial_floats(int n_heads, int capacity);
 int silu_mul_launch(mlm_ctx *ctx, const float *g, const float *u, void *out, int n,
                     cudaStream_t stream);
 // decode linears of a batch of up to 8 tokens (q4k_gemv_batch.cu): Y[t] =
@@ -200,10 +199,6 @@ int rmsnorm_rows_bf16_launch(mlm_ctx *ctx, const float *x, const float *w, void 
 int rope_kv_rows_launch(mlm_ctx *ctx, const float *qkv, const float *freqs, const mlm_rope_args &a,
                         int nq, int nkv, int d, int pos0, int T, void *q_out, void *kc, void *vc,
                         cudaStream_t stream);
-int rope_kv_batch_launch(mlm_ctx *ctx, const float *qkv, const float *freqs,
-                         const mlm_rope_args &a, int nq, int nkv, int d, int batch,
-                         const int *pos_dev, size_t kv_bs, void *q_out, void *kc, void *vc,
-                         cudaStream_t stream);
 int attn_prefill_launch(mlm_ctx *ctx, const void *q16, const void *kc, const void *vc, int pos0,
                         int T, int n_heads, int n_kv, int head_dim, void *out, cudaStream_t stream);
 int swiglu_rows_bf16_launch(mlm_ctx *ctx, const float *gu, int ffn, int T, void *out,

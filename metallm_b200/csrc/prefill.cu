@@ -355,20 +355,6 @@ int rope_kv_rows_launch(mlm_ctx *ctx, const float *qkv, const float *freqs, cons
   return check_launch(ctx, "prefill (rope)");
 }
 
-int rope_kv_batch_launch(mlm_ctx *ctx, const float *qkv, const float *freqs,
-                         const mlm_rope_args &a, int nq, int nkv, int d, int batch,
-                         const int *pos_dev, size_t kv_bs, void *q_out, void *kc, void *vc,
-                         cudaStream_t stream) {
-  const RopeConsts k = rope_consts(a);
-  const int total = nq * (d / 2) + 2 * nkv * (d / 2);
-  return check_launch_pdl(
-      ctx,
-      launch_pdl(rope_kv_rows_kernel, dim3((total + 255) / 256, batch), dim3(256), 0, stream, a,
-                 k, freqs, qkv, nq, nkv, d, 0, reinterpret_cast<__half *>(q_out),
-                 reinterpret_cast<__half *>(kc), reinterpret_cast<__half *>(vc), pos_dev, kv_bs),
-      "batched decode (rope)");
-}
-
 int attn_prefill_launch(mlm_ctx *ctx, const void *q16, const void *kc, const void *vc, int pos0,
                         int T, int n_heads, int n_kv, int head_dim, void *out, cudaStream_t stream) {
   MLM_REQUIRE(ctx, head_dim == kFaD && n_kv > 0 && n_heads % n_kv == 0, MLM_ERR_UNSUPPORTED,

@@ -250,15 +250,19 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, MLM_GEMV_MIN_BLOCKS)
       constexpr int XB = 8;  // x loads in flight per thread
       for (int base = threadIdx.x; base < ngroups; base += XB * blockDim.x) {
         uint4 xv[XB];
+        float xs[XB];  // sub-block scales, loaded with x (one round trip)
 #pragma unroll
         for (int u = 0; u < XB; ++u) {
           const int i = base + u * blockDim.x;
-          if (i < ngroups) xv[u] = __ldg(xg + i);
+          if (i < ngroups) {
+            xv[u] = __ldg(xg + i);
+            xs[u] = p.x_scale ? __ldg(p.x_scale + (i >> 2)) : 1.0f;
+          }
         }
 #pragma unroll
         for (int u = 0; u < XB; ++u) {
           const int i = base + u * blockDim.x;
-          if (i < ngroups) stage(i, xv[u], p.x_scale ? p.x_scale[i >> 2] : 1.0f);
+          if (i < ngroups) stage(i, xv[u], xs[u]);
         }
       }
     } else if (p.x_mode == GemvInput::kRmsNorm && ngroups <= 4 * (int)blockDim.x) {

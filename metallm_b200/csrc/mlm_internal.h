@@ -2,6 +2,7 @@
 // translation units of libmetallm_cuda.so.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdarg>
@@ -152,6 +153,10 @@ struct GemvPair {
   float *h_scale = nullptr;
   int *counters = nullptr;
 };
+// TMA map of a Q4_K weight as a 2D byte tensor [rows][cols / 256 * 144] with
+// boxes of one block column x box_rows rows (rows past the end read as zero)
+int encode_q4k_rows_map(mlm_ctx *ctx, const void *W, int rows, int nb, int box_rows,
+                        CUtensorMap *map);
 int gemv_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const GemvInput &in, float *y,
                 const float *residual, float *partials, int *counters, int max_ctas,
                 int max_tiles, cudaStream_t stream, const GemvPair *pair = nullptr);

@@ -95,16 +95,6 @@ struct GemvArgs {
   uint32_t smem_x;    // byte offset of the x region
 };
 
-// One unit (a 144-byte x 32-row box at byte column x, row y of W) into
-// shared memory, completing on `bar`.
-__device__ __forceinline__ void tma_unit(uint32_t dst, const CUtensorMap *tmap, int x, int y,
-                                         uint32_t bar, uint64_t pol) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar), "l"(pol)
-      : "memory");
-}
 
 __global__ void __launch_bounds__(kGemvMaxWarps * 32, MLM_GEMV_MIN_BLOCKS)
     q4k_gemv_kernel(const __grid_constant__ CUtensorMap tmap, GemvArgs p) {
@@ -663,9 +653,10 @@ static bool plan_gemv(int rows, int nb, int sm_count, size_t smem_max, GemvPlan 
   return false;
 }
 
-// W viewed as a 2D byte tensor [rows][nb * 144]; box = one unit (144 bytes
-// of 32 rows).  Rows past the end read as zeros.
-static int encode_weight_map(mlm_ctx *ctx, const void *W, int rows, int nb, CUtensorMap *map) {
+// W viewed as a 2D byte tensor [rows][nb * 144]; box = one block column of
+// box_rows rows (144 bytes each).  Rows past the end read as zeros.
+int encode_q4k_rows_map(mlm_ctx *ctx, const void *W, int rows, int nb, int box_rows,
+                        CUtensorMap *map) {
   using EncodeFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
                                 const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
                                 const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -682,7 +673,7 @@ static int encode_weight_map(mlm_ctx *ctx, const void *W, int rows, int nb, CUte
   }
   const cuuint64_t dims[2] = {(cuuint64_t)nb * kBlockBytes, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)nb * kBlockBytes};
-  const cuuint32_t box[2] = {(cuuint32_t)kBlockBytes, (cuuint32_t)kTileRows};
+  const cuuint32_t box[2] = {(cuuint32_t)kBlockBytes, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(W), dims,
                             strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -713,7 +704,7 @@ int gemv_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const GemvInput
   MLM_REQUIRE(ctx, ok, MLM_ERR_UNSUPPORTED,
               "mlm_q4k_gemv: rows=%d cols=%d does not fit the shared-memory plan", rows, cols);
   CUtensorMap tmap;
-  int st = encode_weight_map(ctx, W, rows, nb, &tmap);
+  int st = encode_q4k_rows_map(ctx, W, rows, nb, kTileRows, &tmap);
   if (st != MLM_OK) return st;
   GemvArgs a;
   a.W = reinterpret_cast<const uint8_t *>(W);

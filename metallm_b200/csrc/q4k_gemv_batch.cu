@@ -21,15 +21,17 @@
 // high-nibble positions is also divided by 16, an exact exponent shift, so
 // both nibble MMAs of a sub-block add into one accumulator) and its warps
 // take the chunk's tiles.  A warp copies its tile's 16 blocks of each
-// block column into a two-deep shared-memory stage with coalesced 16-byte
-// cp.async (the next column's copy overlaps the current column's MMAs); with
-// the 144-byte row stride every fragment load is conflict-free.  Each
+// block column into a two-deep shared-memory stage with one TMA box (16 rows
+// x 144 bytes, an mbarrier per stage, bounded waits), the next column's copy
+// overlapping the current column's MMAs; with the 144-byte row stride every
+// fragment load is conflict-free.  Each
 // (tile, chunk) adds its partial into Y with fp32 atomics; Y starts from the
 // residual (or zero).
 #include <algorithm>
 
 #include "mlm_device.cuh"
 #include "mlm_internal.h"
+#include "q4k_gemv_common.cuh"
 
 namespace mlm {
 namespace {
@@ -45,9 +47,9 @@ constexpr int kBgStage = kBgRows * kBlockBytes;  // one block column of a tile: 
 constexpr int kBgSmem = kBgWarps * 2 * kBgStage;  // dynamic: the warps' weight stages
 
 struct BgArgs {
-  const uint8_t *W;
   const __nv_bfloat16 *x;  // [T][cols]
   float *y;                // [T][rows]
+  int *status;             // device-visible error word (0 = ok)
   int rows, cols, T, nb, tiles, ctas_per_chunk;
 };
 
@@ -80,15 +82,11 @@ __device__ __forceinline__ float byte_plus_2p23(uint32_t w, int b) {
   return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u + b));
 }
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes)
-               : "memory");
-}
-
-__global__ void __launch_bounds__(kBgThreads, 2) q4k_gemv_batch_kernel(BgArgs p) {
+__global__ void __launch_bounds__(kBgThreads, 2)
+    q4k_gemv_batch_kernel(const __grid_constant__ CUtensorMap tmap, BgArgs p) {
   // x of the chunk: [token][sub-block][lane t] -> 8 fp16 in mask order
   __shared__ uint4 xperm[kBgMaxT * kBgXStride];
-  extern __shared__ __align__(16) uint8_t wstage[];
+  extern __shared__ __align__(128) uint8_t wstage[];  // TMA destinations: 128-byte aligned
   __shared__ float xsum[kBgSub][kBgMaxT];    // per (sub-block, token): sum of the x
   __shared__ uint32_t tokmax[kBgMaxT];       // per token: bits of the chunk's max |x|
   __shared__ float tokscale[kBgMaxT];        // per token: the power of two x was divided by
@@ -99,19 +97,32 @@ __global__ void __launch_bounds__(kBgThreads, 2) q4k_gemv_batch_kernel(BgArgs p)
   const int g = lane >> 2, t = lane & 3;
   uint8_t *mystage = wstage + warp * 2 * kBgStage;
   const uint32_t stage_addr = (uint32_t)__cvta_generic_to_shared(mystage);
-  // block column kb of tile's 16 rows -> stage buf (rows past the end are
-  // zero-filled)
+  __shared__ __align__(8) uint64_t bars[kBgWarps * 2];  // one per stage of each warp
+  const uint32_t my_bar = (uint32_t)__cvta_generic_to_shared(&bars[warp * 2]);
+  if (lane == 0) {
+    mbar_init(my_bar, 1);
+    mbar_init(my_bar + 8, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncwarp();
+  const uint64_t pol = evict_first_policy();
+  uint32_t phases = 0, pending = 0;  // bit b: parity of stage b's next completion / a copy in flight
+  // block column kb of tile's 16 rows -> stage buf, one TMA box (rows past
+  // the end read as zeros)
   auto issue = [&](int tile, int kb, int buf) {
-    for (int c = lane; c < kBgRows * 9; c += 32) {
-      const int row = c / 9, part = c - row * 9;
-      const int gr = tile * kBgRows + row;
-      const bool live = gr < p.rows;
-      const uint8_t *src =
-          p.W + ((size_t)(live ? gr : 0) * p.nb + kb0 + kb) * kBlockBytes + part * 16;
-      cp_async16(stage_addr + buf * kBgStage + row * kBlockBytes + part * 16, src,
-                 live ? 16u : 0u);
+    if (lane == 0) {
+      mbar_expect_tx(my_bar + 8 * buf, kBgStage);
+      tma_unit(stage_addr + buf * kBgStage, &tmap, (kb0 + kb) * kBlockBytes, tile * kBgRows,
+               my_bar + 8 * buf, pol);
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
+    pending |= 1u << buf;
+  };
+  // bounded wait for stage buf; false (and the error word set) on timeout
+  auto wait_stage = [&](int buf) {
+    if (!mbar_wait_bounded(my_bar + 8 * buf, (phases >> buf) & 1, p.status)) return false;
+    phases ^= 1u << buf;
+    pending &= ~(1u << buf);
+    return true;
   };
   // the weights do not depend on the kernel before this one: the warp's
   // first block column is in flight before waiting for it (x, y)
@@ -180,6 +191,7 @@ __global__ void __launch_bounds__(kBgThreads, 2) q4k_gemv_batch_kernel(BgArgs p)
 
   // ---- tiles of this chunk, round-robin over the CTA's warps ---------------
   const uint32_t M = 0x000F000Fu, MH = 0x00F000F0u;
+  bool ok = true;
   for (int tile = first_tile; tile < p.tiles; tile += p.ctas_per_chunk * kBgWarps) {
     const int r0 = tile * kBgRows + g, r1 = r0 + 8;
     const bool ok0 = r0 < p.rows, ok1 = r1 < p.rows;
@@ -188,13 +200,11 @@ __global__ void __launch_bounds__(kBgThreads, 2) q4k_gemv_batch_kernel(BgArgs p)
     float aq[4] = {0.f, 0.f, 0.f, 0.f}, am[4] = {0.f, 0.f, 0.f, 0.f};
     if (tile != first_tile) issue(tile, 0, 0);
     for (int kb = 0; kb < nkb; ++kb) {
-      if (kb + 1 < nkb) {
-        issue(tile, kb + 1, (kb + 1) & 1);
-        asm volatile("cp.async.wait_group 1;" ::: "memory");
-      } else {
-        asm volatile("cp.async.wait_group 0;" ::: "memory");
+      if (kb + 1 < nkb) issue(tile, kb + 1, (kb + 1) & 1);
+      if (!wait_stage(kb & 1)) {
+        ok = false;
+        break;
       }
-      __syncwarp();
       const uint8_t *s0 = mystage + (kb & 1) * kBgStage + g * kBlockBytes;
       const uint8_t *s1 = s0 + 8 * kBlockBytes;
       const uint4 h0 = *reinterpret_cast<const uint4 *>(s0);
@@ -236,6 +246,7 @@ __global__ void __launch_bounds__(kBgThreads, 2) q4k_gemv_batch_kernel(BgArgs p)
       }
       __syncwarp();  // the stage is read before the next copy overwrites it
     }
+    if (!ok) break;
     const int n0 = 2 * t, n1 = 2 * t + 1;
     const float xs0 = tokscale[n0], xs1 = tokscale[n1];
     const float acc[4] = {aq[0] * xs0 - am[0], aq[1] * xs1 - am[1], aq[2] * xs0 - am[2],
@@ -244,6 +255,12 @@ __global__ void __launch_bounds__(kBgThreads, 2) q4k_gemv_batch_kernel(BgArgs p)
     if (ok0 && n1 < p.T) atomicAdd(p.y + (size_t)n1 * p.rows + r0, acc[1]);
     if (ok1 && n0 < p.T) atomicAdd(p.y + (size_t)n0 * p.rows + r1, acc[2]);
     if (ok1 && n1 < p.T) atomicAdd(p.y + (size_t)n1 * p.rows + r1, acc[3]);
+  }
+  if (!ok) {
+    // a stage wait ran out of budget: let the copies still in flight land
+    // (bounded again) before this warp's shared memory is released
+    for (int b = 0; b < 2; ++b)
+      if ((pending >> b) & 1) wait_stage(b);
   }
 }
 
@@ -273,9 +290,9 @@ int gemv_batch_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const voi
   } else if (residual != y)
     MLM_CUDA_TRY(ctx, cudaMemcpyAsync(y, residual, ybytes, cudaMemcpyDeviceToDevice, stream));
   BgArgs a;
-  a.W = reinterpret_cast<const uint8_t *>(W);
   a.x = reinterpret_cast<const __nv_bfloat16 *>(x_bf16);
   a.y = y;
+  a.status = ctx->dev_status;
   a.rows = rows;
   a.cols = cols;
   a.T = tokens;
@@ -285,9 +302,12 @@ int gemv_batch_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const voi
   // about two CTAs per SM over all chunks; never more CTAs than tiles
   a.ctas_per_chunk =
       std::max(1, std::min(a.tiles / kBgWarps + 1, (2 * ctx->sm_count + nchunks - 1) / nchunks));
+  CUtensorMap tmap;
+  const int st = encode_q4k_rows_map(ctx, W, rows, a.nb, kBgRows, &tmap);
+  if (st != MLM_OK) return st;
   return check_launch_pdl(ctx,
                           launch_pdl(q4k_gemv_batch_kernel, dim3(nchunks * a.ctas_per_chunk),
-                                     dim3(kBgThreads), kBgSmem, stream, a),
+                                     dim3(kBgThreads), kBgSmem, stream, tmap, a),
                           "mlm_q4k_gemv_batch");
 }
 

@@ -21,6 +21,17 @@ __device__ __forceinline__ void mma_f16_16816(float (&c)[4], uint32_t a0, uint32
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// One box of W (144 bytes of each of its rows at byte column x, from row y)
+// into shared memory, completing on `bar`.
+__device__ __forceinline__ void tma_unit(uint32_t dst, const CUtensorMap *tmap, int x, int y,
+                                         uint32_t bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar), "l"(pol)
+      : "memory");
+}
+
 // Weights are read exactly once: copy them with an L2 evict-first policy so
 // they do not push x, y and the KV cache out of L2.
 __device__ __forceinline__ uint64_t evict_first_policy() {

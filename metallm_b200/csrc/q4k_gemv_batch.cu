@@ -20,11 +20,13 @@
 // activations in range and is undone in fp32 after the chunk; the x of the
 // high-nibble positions is also divided by 16, an exact exponent shift, so
 // both nibble MMAs of a sub-block add into one accumulator) and its warps
-// take the chunk's tiles.  A warp copies its tile's 16 blocks of each
-// block column into a two-deep shared-memory stage with one TMA box (16 rows
-// x 144 bytes, an mbarrier per stage, bounded waits), the next column's copy
-// overlapping the current column's MMAs; with the 144-byte row stride every
-// fragment load is conflict-free.  Each
+// take the chunk's tiles.  A warp walks its (tile, block column) items
+// through a ring of kBgStages shared-memory stages, one TMA box per item (16
+// rows x 144 bytes, an mbarrier per stage, bounded waits), the next items'
+// copies overlapping the current one's MMAs across tile boundaries; with the
+// 144-byte row stride every fragment load is conflict-free.  One CTA of 16
+// warps per SM with a 3-deep ring measured faster than two CTAs with 2-deep
+// rings (more bytes in flight per SM).  Each
 // (tile, chunk) adds its partial into Y with fp32 atomics; Y starts from the
 // residual (or zero).
 #include <algorithm>
@@ -44,7 +46,15 @@ constexpr int kBgThreads = kBgWarps * 32;
 constexpr int kBgMaxT = 8;
 constexpr int kBgXStride = kBgSub * 4 + 1;  // uint4 per token, padded against bank conflicts
 constexpr int kBgStage = kBgRows * kBlockBytes;  // one block column of a tile: 2304 bytes
-constexpr int kBgSmem = kBgWarps * 2 * kBgStage;  // dynamic: the warps' weight stages
+#ifndef MLM_BG_STAGES
+#define MLM_BG_STAGES 3
+#endif
+#ifndef MLM_BG_MIN_BLOCKS
+#define MLM_BG_MIN_BLOCKS 1
+#endif
+constexpr int kBgStages = MLM_BG_STAGES;         // ring depth per warp
+constexpr int kBgBlocks = MLM_BG_MIN_BLOCKS;     // resident CTAs per SM
+constexpr int kBgSmem = kBgWarps * kBgStages * kBgStage;  // dynamic: the warps' weight stages
 
 struct BgArgs {
   const __nv_bfloat16 *x;  // [T][cols]
@@ -82,7 +92,7 @@ __device__ __forceinline__ float byte_plus_2p23(uint32_t w, int b) {
   return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u + b));
 }
 
-__global__ void __launch_bounds__(kBgThreads, 2)
+__global__ void __launch_bounds__(kBgThreads, kBgBlocks)
     q4k_gemv_batch_kernel(const __grid_constant__ CUtensorMap tmap, BgArgs p) {
   // x of the chunk: [token][sub-block][lane t] -> 8 fp16 in mask order
   __shared__ uint4 xperm[kBgMaxT * kBgXStride];
@@ -95,27 +105,38 @@ __global__ void __launch_bounds__(kBgThreads, 2)
   const int kb0 = chunk * kBgChunk, nkb = min(kBgChunk, p.nb - kb0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
-  uint8_t *mystage = wstage + warp * 2 * kBgStage;
+  uint8_t *mystage = wstage + warp * kBgStages * kBgStage;
   const uint32_t stage_addr = (uint32_t)__cvta_generic_to_shared(mystage);
-  __shared__ __align__(8) uint64_t bars[kBgWarps * 2];  // one per stage of each warp
-  const uint32_t my_bar = (uint32_t)__cvta_generic_to_shared(&bars[warp * 2]);
+  __shared__ __align__(8) uint64_t bars[kBgWarps * kBgStages];  // one per stage of each warp
+  const uint32_t my_bar = (uint32_t)__cvta_generic_to_shared(&bars[warp * kBgStages]);
   if (lane == 0) {
-    mbar_init(my_bar, 1);
-    mbar_init(my_bar + 8, 1);
+#pragma unroll
+    for (int b = 0; b < kBgStages; ++b) mbar_init(my_bar + 8 * b, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncwarp();
   const uint64_t pol = evict_first_policy();
   uint32_t phases = 0, pending = 0;  // bit b: parity of stage b's next completion / a copy in flight
-  // block column kb of tile's 16 rows -> stage buf, one TMA box (rows past
-  // the end read as zeros)
-  auto issue = [&](int tile, int kb, int buf) {
+  // The warp's work items: block column kb of tiles first_tile + j stride,
+  // item i = (j, kb) with j = i / nkb, in a ring of kBgStages stages.
+  const int stride = p.ctas_per_chunk * kBgWarps;
+  const int first_tile = cj + p.ctas_per_chunk * warp;
+  const int nitems = first_tile < p.tiles ? ((p.tiles - 1 - first_tile) / stride + 1) * nkb : 0;
+  int in_j = 0, in_kb = 0, in_buf = 0;  // the next item to put in flight
+  // the next item's 16 rows of one block column -> its stage, one TMA box
+  // (rows past the end read as zeros)
+  auto issue_next = [&]() {
     if (lane == 0) {
-      mbar_expect_tx(my_bar + 8 * buf, kBgStage);
-      tma_unit(stage_addr + buf * kBgStage, &tmap, (kb0 + kb) * kBlockBytes, tile * kBgRows,
-               my_bar + 8 * buf, pol);
+      mbar_expect_tx(my_bar + 8 * in_buf, kBgStage);
+      tma_unit(stage_addr + in_buf * kBgStage, &tmap, (kb0 + in_kb) * kBlockBytes,
+               (first_tile + in_j * stride) * kBgRows, my_bar + 8 * in_buf, pol);
     }
-    pending |= 1u << buf;
+    pending |= 1u << in_buf;
+    if (++in_kb == nkb) {
+      in_kb = 0;
+      ++in_j;
+    }
+    in_buf = in_buf + 1 == kBgStages ? 0 : in_buf + 1;
   };
   // bounded wait for stage buf; false (and the error word set) on timeout
   auto wait_stage = [&](int buf) {
@@ -125,9 +146,10 @@ __global__ void __launch_bounds__(kBgThreads, 2)
     return true;
   };
   // the weights do not depend on the kernel before this one: the warp's
-  // first block column is in flight before waiting for it (x, y)
-  const int first_tile = cj + p.ctas_per_chunk * warp;
-  if (first_tile < p.tiles) issue(first_tile, 0, 0);
+  // first items are in flight before waiting for it (x, y)
+#pragma unroll
+  for (int i = 0; i < kBgStages - 1; ++i)
+    if (i < nitems) issue_next();
   pdl_wait_then_release();
 
   // ---- stage x: one thread per (token, sub-block, t): elements 8t .. 8t+7 --
@@ -192,61 +214,61 @@ __global__ void __launch_bounds__(kBgThreads, 2)
   // ---- tiles of this chunk, round-robin over the CTA's warps ---------------
   const uint32_t M = 0x000F000Fu, MH = 0x00F000F0u;
   bool ok = true;
-  for (int tile = first_tile; tile < p.tiles; tile += p.ctas_per_chunk * kBgWarps) {
+  // (r0, 2t) (r0, 2t+1) (r1, 2t) (r1, 2t+1): the scaled-x products and the
+  // min terms of the current tile
+  float aq[4] = {0.f, 0.f, 0.f, 0.f}, am[4] = {0.f, 0.f, 0.f, 0.f};
+  int buf = 0, kb = 0, tile = first_tile;
+  for (int i = 0; i < nitems; ++i) {
+    if (i + kBgStages - 1 < nitems) issue_next();
+    if (!wait_stage(buf)) {
+      ok = false;
+      break;
+    }
+    const uint8_t *s0 = mystage + buf * kBgStage + g * kBlockBytes;
+    const uint8_t *s1 = s0 + 8 * kBlockBytes;
+    const uint4 h0 = *reinterpret_cast<const uint4 *>(s0);
+    const uint4 h1 = *reinterpret_cast<const uint4 *>(s1);
+    // d 2^24 (undoes the subnormal scale of the nibbles) and dmin; with
+    // f = 2^23 + sc, fma(D, f, -D 2^23) is D sc exactly (at most 17
+    // significant bits), so the 6-bit values need no conversion
+    const float D0 = half_bits_to_float(h0.x) * 16777216.0f, Dm0 = half_bits_to_float(h0.x >> 16);
+    const float D1 = half_bits_to_float(h1.x) * 16777216.0f, Dm1 = half_bits_to_float(h1.x >> 16);
+    const float nD0 = -D0 * 8388608.0f, nDm0 = -Dm0 * 8388608.0f;
+    const float nD1 = -D1 * 8388608.0f, nDm1 = -Dm1 * 8388608.0f;
+    uint32_t scl0, sch0, ml0, mh0, scl1, sch1, ml1, mh1;
+    q4k_scales_packed(h0, scl0, sch0, ml0, mh0);
+    q4k_scales_packed(h1, scl1, sch1, ml1, mh1);
+#pragma unroll
+    for (int sb = 0; sb < 8; ++sb) {
+      const int s = kb * 8 + sb;
+      const uint4 xv = xperm[g * kBgXStride + s * 4 + t];
+      const uint32_t w0 = *reinterpret_cast<const uint32_t *>(s0 + 16 + 16 * sb + 4 * t);
+      const uint32_t w1 = *reinterpret_cast<const uint32_t *>(s1 + 16 + 16 * sb + 4 * t);
+      const uint32_t u0 = w0 >> 8, u1 = w1 >> 8;
+      float c[4] = {0.f, 0.f, 0.f, 0.f};
+      mma16816(c, w0 & M, w1 & M, u0 & M, u1 & M, xv.x, xv.y);
+      mma16816(c, w0 & MH, w1 & MH, u0 & MH, u1 & MH, xv.z, xv.w);
+      const int bsel = sb & 3;
+      const float ds0 = fmaf(D0, byte_plus_2p23(sb < 4 ? scl0 : sch0, bsel), nD0);
+      const float dm0 = fmaf(Dm0, byte_plus_2p23(sb < 4 ? ml0 : mh0, bsel), nDm0);
+      const float ds1 = fmaf(D1, byte_plus_2p23(sb < 4 ? scl1 : sch1, bsel), nD1);
+      const float dm1 = fmaf(Dm1, byte_plus_2p23(sb < 4 ? ml1 : mh1, bsel), nDm1);
+      const float2 xm = *reinterpret_cast<const float2 *>(&xsum[s][2 * t]);
+      aq[0] = fmaf(ds0, c[0], aq[0]);
+      aq[1] = fmaf(ds0, c[1], aq[1]);
+      aq[2] = fmaf(ds1, c[2], aq[2]);
+      aq[3] = fmaf(ds1, c[3], aq[3]);
+      am[0] = fmaf(dm0, xm.x, am[0]);
+      am[1] = fmaf(dm0, xm.y, am[1]);
+      am[2] = fmaf(dm1, xm.x, am[2]);
+      am[3] = fmaf(dm1, xm.y, am[3]);
+    }
+    __syncwarp();  // the stage is read before the next copy overwrites it
+    buf = buf + 1 == kBgStages ? 0 : buf + 1;
+    if (++kb < nkb) continue;
+    // the tile's last block column: add its partial into Y
     const int r0 = tile * kBgRows + g, r1 = r0 + 8;
     const bool ok0 = r0 < p.rows, ok1 = r1 < p.rows;
-    // (r0, 2t) (r0, 2t+1) (r1, 2t) (r1, 2t+1): the scaled-x products and the
-    // min terms
-    float aq[4] = {0.f, 0.f, 0.f, 0.f}, am[4] = {0.f, 0.f, 0.f, 0.f};
-    if (tile != first_tile) issue(tile, 0, 0);
-    for (int kb = 0; kb < nkb; ++kb) {
-      if (kb + 1 < nkb) issue(tile, kb + 1, (kb + 1) & 1);
-      if (!wait_stage(kb & 1)) {
-        ok = false;
-        break;
-      }
-      const uint8_t *s0 = mystage + (kb & 1) * kBgStage + g * kBlockBytes;
-      const uint8_t *s1 = s0 + 8 * kBlockBytes;
-      const uint4 h0 = *reinterpret_cast<const uint4 *>(s0);
-      const uint4 h1 = *reinterpret_cast<const uint4 *>(s1);
-      // d 2^24 (undoes the subnormal scale of the nibbles) and dmin; with
-      // f = 2^23 + sc, fma(D, f, -D 2^23) is D sc exactly (at most 17
-      // significant bits), so the 6-bit values need no conversion
-      const float D0 = half_bits_to_float(h0.x) * 16777216.0f, Dm0 = half_bits_to_float(h0.x >> 16);
-      const float D1 = half_bits_to_float(h1.x) * 16777216.0f, Dm1 = half_bits_to_float(h1.x >> 16);
-      const float nD0 = -D0 * 8388608.0f, nDm0 = -Dm0 * 8388608.0f;
-      const float nD1 = -D1 * 8388608.0f, nDm1 = -Dm1 * 8388608.0f;
-      uint32_t scl0, sch0, ml0, mh0, scl1, sch1, ml1, mh1;
-      q4k_scales_packed(h0, scl0, sch0, ml0, mh0);
-      q4k_scales_packed(h1, scl1, sch1, ml1, mh1);
-#pragma unroll
-      for (int sb = 0; sb < 8; ++sb) {
-        const int s = kb * 8 + sb;
-        const uint4 xv = xperm[g * kBgXStride + s * 4 + t];
-        const uint32_t w0 = *reinterpret_cast<const uint32_t *>(s0 + 16 + 16 * sb + 4 * t);
-        const uint32_t w1 = *reinterpret_cast<const uint32_t *>(s1 + 16 + 16 * sb + 4 * t);
-        const uint32_t u0 = w0 >> 8, u1 = w1 >> 8;
-        float c[4] = {0.f, 0.f, 0.f, 0.f};
-        mma16816(c, w0 & M, w1 & M, u0 & M, u1 & M, xv.x, xv.y);
-        mma16816(c, w0 & MH, w1 & MH, u0 & MH, u1 & MH, xv.z, xv.w);
-        const int bsel = sb & 3;
-        const float ds0 = fmaf(D0, byte_plus_2p23(sb < 4 ? scl0 : sch0, bsel), nD0);
-        const float dm0 = fmaf(Dm0, byte_plus_2p23(sb < 4 ? ml0 : mh0, bsel), nDm0);
-        const float ds1 = fmaf(D1, byte_plus_2p23(sb < 4 ? scl1 : sch1, bsel), nD1);
-        const float dm1 = fmaf(Dm1, byte_plus_2p23(sb < 4 ? ml1 : mh1, bsel), nDm1);
-        const float2 xm = *reinterpret_cast<const float2 *>(&xsum[s][2 * t]);
-        aq[0] = fmaf(ds0, c[0], aq[0]);
-        aq[1] = fmaf(ds0, c[1], aq[1]);
-        aq[2] = fmaf(ds1, c[2], aq[2]);
-        aq[3] = fmaf(ds1, c[3], aq[3]);
-        am[0] = fmaf(dm0, xm.x, am[0]);
-        am[1] = fmaf(dm0, xm.y, am[1]);
-        am[2] = fmaf(dm1, xm.x, am[2]);
-        am[3] = fmaf(dm1, xm.y, am[3]);
-      }
-      __syncwarp();  // the stage is read before the next copy overwrites it
-    }
-    if (!ok) break;
     const int n0 = 2 * t, n1 = 2 * t + 1;
     const float xs0 = tokscale[n0], xs1 = tokscale[n1];
     const float acc[4] = {aq[0] * xs0 - am[0], aq[1] * xs1 - am[1], aq[2] * xs0 - am[2],
@@ -255,11 +277,15 @@ __global__ void __launch_bounds__(kBgThreads, 2)
     if (ok0 && n1 < p.T) atomicAdd(p.y + (size_t)n1 * p.rows + r0, acc[1]);
     if (ok1 && n0 < p.T) atomicAdd(p.y + (size_t)n0 * p.rows + r1, acc[2]);
     if (ok1 && n1 < p.T) atomicAdd(p.y + (size_t)n1 * p.rows + r1, acc[3]);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) aq[e] = am[e] = 0.f;
+    kb = 0;
+    tile += stride;
   }
   if (!ok) {
     // a stage wait ran out of budget: let the copies still in flight land
     // (bounded again) before this warp's shared memory is released
-    for (int b = 0; b < 2; ++b)
+    for (int b = 0; b < kBgStages; ++b)
       if ((pending >> b) & 1) wait_stage(b);
   }
 }
@@ -299,9 +325,9 @@ int gemv_batch_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const voi
   a.nb = cols / kQK;
   a.tiles = (rows + kBgRows - 1) / kBgRows;
   const int nchunks = (a.nb + kBgChunk - 1) / kBgChunk;
-  // about two CTAs per SM over all chunks; never more CTAs than tiles
-  a.ctas_per_chunk =
-      std::max(1, std::min(a.tiles / kBgWarps + 1, (2 * ctx->sm_count + nchunks - 1) / nchunks));
+  // about kBgBlocks CTAs per SM over all chunks; never more CTAs than tiles
+  a.ctas_per_chunk = std::max(
+      1, std::min(a.tiles / kBgWarps + 1, (kBgBlocks * ctx->sm_count + nchunks - 1) / nchunks));
   CUtensorMap tmap;
   const int st = encode_q4k_rows_map(ctx, W, rows, a.nb, kBgRows, &tmap);
   if (st != MLM_OK) return st;

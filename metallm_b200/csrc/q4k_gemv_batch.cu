@@ -44,7 +44,9 @@ constexpr int kBgSub = kBgChunk * 8;  // sub-blocks per chunk
 constexpr int kBgWarps = 16;
 constexpr int kBgThreads = kBgWarps * 32;
 constexpr int kBgMaxT = 8;
-constexpr int kBgXStride = kBgSub * 4 + 1;  // uint4 per token, padded against bank conflicts
+// uint4 per token: a quarter warp reads tokens g, g + 1 at lanes t = 0..3, so
+// the token pitch is 64 bytes past a multiple of 128 (no bank conflicts)
+constexpr int kBgXStride = kBgSub * 4 + 4;
 constexpr int kBgStage = kBgRows * kBlockBytes;  // one block column of a tile: 2304 bytes
 #ifndef MLM_BG_STAGES
 #define MLM_BG_STAGES 3

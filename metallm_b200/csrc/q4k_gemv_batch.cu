@@ -327,9 +327,10 @@ int gemv_batch_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const voi
   a.nb = cols / kQK;
   a.tiles = (rows + kBgRows - 1) / kBgRows;
   const int nchunks = (a.nb + kBgChunk - 1) / kBgChunk;
-  // about kBgBlocks CTAs per SM over all chunks; never more CTAs than tiles
-  a.ctas_per_chunk = std::max(
-      1, std::min(a.tiles / kBgWarps + 1, (kBgBlocks * ctx->sm_count + nchunks - 1) / nchunks));
+  // at most kBgBlocks CTAs per SM over all chunks (one wave: a CTA past it
+  // would run alone after the others), never more CTAs than tiles
+  a.ctas_per_chunk =
+      std::max(1, std::min(a.tiles / kBgWarps + 1, kBgBlocks * ctx->sm_count / nchunks));
   CUtensorMap tmap;
   const int st = encode_q4k_rows_map(ctx, W, rows, a.nb, kBgRows, &tmap);
   if (st != MLM_OK) return st;

@@ -368,25 +368,31 @@ __global__ void __launch_bounds__(kAttnThreads, 8) attn_rope_decode_kernel(
   __half *s_k = reinterpret_cast<__half *>(s_dyn);        // [rows_cap][kKPitch]
   __half *s_v = s_k + (size_t)rows_cap * kKPitch;         // [rows_cap][kKPitch]
 
-  // cached rows of phase ph by cp.async (row pos, when it falls in the
-  // phase, comes from registers once q, k and v are available)
-  auto load_phase = [&](int ph) {
-    const int a = p_begin + ph * rows_cap;
-    const int n = min(rows_cap, p_end - a);
-    const int cached = (has_new && a + n == p_end) ? n - 1 : n;
+  // Cached rows of phase ph by cp.async, K and V as separate groups, so the
+  // next phase's K is in flight during this phase's softmax and P.V and its
+  // V after this phase's P.V (row pos, when it falls in a phase, comes from
+  // registers once q, k and v are available).
+  auto phase_rows = [&](int ph, int &a, int &n, int &cached) {
+    a = p_begin + ph * rows_cap;
+    n = min(rows_cap, p_end - a);
+    cached = (has_new && a + n == p_end) ? n - 1 : n;
+  };
+  auto load_rows = [&](int ph, const __half *src, __half *dst) {
+    int a, n, cached;
+    phase_rows(ph, a, n, cached);
     constexpr int kPieces = kAttnD * (int)sizeof(__half) / 16;  // 16 per row
-    const uint32_t sk = (uint32_t)__cvta_generic_to_shared(s_k);
-    const uint32_t sv = (uint32_t)__cvta_generic_to_shared(s_v);
+    const uint32_t sd = (uint32_t)__cvta_generic_to_shared(dst);
     for (int j = threadIdx.x; j < cached * kPieces; j += kAttnThreads) {
       const int r = j / kPieces, c = j - r * kPieces;
-      const size_t gi = (size_t)(a + r) * row_stride + kvh * kAttnD + c * 8;
-      const uint32_t off = (uint32_t)(r * kKPitch + c * 8) * 2;
-      cp_async16(sk + off, kc + gi);
-      cp_async16(sv + off, vc + gi);
+      cp_async16(sd + (uint32_t)(r * kKPitch + c * 8) * 2,
+                 src + (size_t)(a + r) * row_stride + kvh * kAttnD + c * 8);
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  if (nphase > 0) load_phase(0);
+  if (nphase > 0) {
+    load_rows(0, kc, s_k);
+    load_rows(0, vc, s_v);
+  }
   // padding: weight rows of heads G..15 and q rows of heads G..7 are zero
   for (int i = threadIdx.x; i < 2 * (16 - G) * kPPitch; i += kAttnThreads) {
     const int hl = i / ((16 - G) * kPPitch), rem = i - hl * (16 - G) * kPPitch;
@@ -471,22 +477,34 @@ __global__ void __launch_bounds__(kAttnThreads, 8) attn_rope_decode_kernel(
 #pragma unroll
   for (int nt = 0; nt < 4; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
 
-  for (int ph = 0; ph < nphase; ++ph) {
-    const int a = p_begin + ph * rows_cap;
-    const int n = min(rows_cap, p_end - a);
+  // the new row of phase ph into its K (threads < 64) or V (64..127) stage,
+  // and (V) zero rows n..n16-1, which meet zero weights but may hold NaN
+  auto fill_k = [&](int ph) {
+    int a, n, cached;
+    phase_rows(ph, a, n, cached);
+    if (cached < n && threadIdx.x < 64)
+      *reinterpret_cast<__half2 *>(s_k + (size_t)cached * kKPitch + 2 * threadIdx.x) = kv_new;
+  };
+  auto fill_v = [&](int ph) {
+    int a, n, cached;
+    phase_rows(ph, a, n, cached);
+    if (cached < n && threadIdx.x >= 64)
+      *reinterpret_cast<__half2 *>(s_v + (size_t)cached * kKPitch + 2 * (threadIdx.x - 64)) =
+          kv_new;
     const int n16 = (n + 15) & ~15;
-    if (ph > 0) load_phase(ph);
-    const int cached = (has_new && a + n == p_end) ? n - 1 : n;
-    if (cached < n) {
-      const int t = threadIdx.x & 63;
-      __half *row = (threadIdx.x < 64 ? s_k : s_v) + (size_t)cached * kKPitch;
-      *reinterpret_cast<__half2 *>(row + 2 * t) = kv_new;
-    }
-    // V rows n..n16-1 meet zero weights; stale rows may hold NaN: zero them
     for (int i = threadIdx.x; i < (n16 - n) * (kAttnD / 2); i += kAttnThreads)
       reinterpret_cast<uint32_t *>(s_v + (size_t)(n + i / (kAttnD / 2)) * kKPitch)[i % (kAttnD / 2)] =
           0u;
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
+  };
+  if (nphase > 0) {
+    fill_k(0);
+    fill_v(0);
+  }
+  for (int ph = 0; ph < nphase; ++ph) {
+    const int n = min(rows_cap, p_end - (p_begin + ph * rows_cap));
+    const int n16 = (n + 15) & ~15;
+    const bool more = ph + 1 < nphase;
+    asm volatile("cp.async.wait_group 1;" ::: "memory");  // this phase's K (its V may fly)
     __syncthreads();
 
     // scores of 16-row tiles w, w + 4, ...: S = K (q_hi + q_lo)^T
@@ -518,6 +536,10 @@ __global__ void __launch_bounds__(kAttnThreads, 8) attn_rope_decode_kernel(
       }
     }
     __syncthreads();
+    if (more) {  // the K stage is free: the next phase's K
+      load_rows(ph + 1, kc, s_k);
+      fill_k(ph + 1);
+    }
 
     // softmax of head h by warp h % 4 over rows lane + 32 i; weights as
     // fp16 hi / lo (zero for rows n..n16-1)
@@ -552,6 +574,11 @@ __global__ void __launch_bounds__(kAttnThreads, 8) attn_rope_decode_kernel(
       m_run[hi] = m_new;
       if (lane == 0) s_corr[h] = corr;
     }
+    // this phase's V (the next phase's K, if any, may still fly)
+    if (more)
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    else
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
 
     // output: O[h][d] = corr O + (p_hi + p_lo) V over the phase's rows,
@@ -579,7 +606,11 @@ __global__ void __launch_bounds__(kAttnThreads, 8) attn_rope_decode_kernel(
         }
       }
     }
-    __syncthreads();  // stages, scores and weights are free for the next phase
+    __syncthreads();  // the V stage, scores and weights are free for the next phase
+    if (more) {
+      load_rows(ph + 1, vc, s_v);
+      fill_v(ph + 1);
+    }
   }
 
   // this CTA's partials go straight into the shared memory of the CTA that

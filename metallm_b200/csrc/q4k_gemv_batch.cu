@@ -39,8 +39,8 @@ namespace mlm {
 namespace {
 
 constexpr int kBgRows = 16;      // rows per tile (the MMA's M)
-constexpr int kBgChunk = 8;      // Q4_K block columns per chunk
-constexpr int kBgSub = kBgChunk * 8;  // sub-blocks per chunk
+constexpr int kBgChunk = 8;      // Q4_K block columns per chunk, at most
+constexpr int kBgSub = kBgChunk * 8;  // sub-blocks per chunk, at most
 constexpr int kBgWarps = 16;
 constexpr int kBgThreads = kBgWarps * 32;
 constexpr int kBgMaxT = 8;
@@ -63,6 +63,7 @@ struct BgArgs {
   float *y;                // [T][rows]
   int *status;             // device-visible error word (0 = ok)
   int rows, cols, T, nb, tiles, ctas_per_chunk;
+  int chunk;  // block columns per chunk (1..kBgChunk)
 };
 
 __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
@@ -104,7 +105,7 @@ __global__ void __launch_bounds__(kBgThreads, kBgBlocks)
   __shared__ float tokscale[kBgMaxT];        // per token: the power of two x was divided by
 
   const int chunk = blockIdx.x / p.ctas_per_chunk, cj = blockIdx.x % p.ctas_per_chunk;
-  const int kb0 = chunk * kBgChunk, nkb = min(kBgChunk, p.nb - kb0);
+  const int kb0 = chunk * p.chunk, nkb = min(p.chunk, p.nb - kb0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   uint8_t *mystage = wstage + warp * kBgStages * kBgStage;
@@ -326,7 +327,18 @@ int gemv_batch_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const voi
   a.T = tokens;
   a.nb = cols / kQK;
   a.tiles = (rows + kBgRows - 1) / kBgRows;
-  const int nchunks = (a.nb + kBgChunk - 1) / kBgChunk;
+  // Chunk width: the widest (fewest partial sums per output) whose grid
+  // fills the SMs -- narrow weights (a rank's share of a row-parallel
+  // projection) otherwise leave most SMs idle, since a warp takes whole
+  // 16-row tiles of a chunk
+  int nchunks = 0;
+  for (int c = kBgChunk; c >= 1; c /= 2) {
+    a.chunk = c;
+    nchunks = (a.nb + c - 1) / c;
+    const int per = std::max(
+        1, std::min(a.tiles / kBgWarps + 1, kBgBlocks * ctx->sm_count / nchunks));
+    if (nchunks * per >= kBgBlocks * ctx->sm_count * 3 / 4) break;
+  }
   // at most kBgBlocks CTAs per SM over all chunks (one wave: a CTA past it
   // would run alone after the others), never more CTAs than tiles
   a.ctas_per_chunk =

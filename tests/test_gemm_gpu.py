@@ -155,6 +155,11 @@ GEMV_TOL = 1e-5
 @pytest.mark.parametrize("rows,cols,tokens,scale", [(4096, 4096, 8, 1.0), (1000, 2048, 3, 1.0),
                                                     (6144, 4096, 5, 1.0), (300, 512, 1, 1.0),
                                                     (4096, 14336, 8, 1.0),
+                                                    # a 70B rank's shares at 4 GPUs: narrower
+                                                    # K chunks (2 block columns), and a last
+                                                    # chunk of 4 of 8 columns
+                                                    (8192, 2048, 8, 1.0), (2560, 8192, 8, 1.0),
+                                                    (8192, 7168, 8, 1.0),
                                                     # beyond the fp16 range: the scales hold it
                                                     (2048, 1024, 4, 3.0e5)])
 def test_gemv_batch(ctx, rows, cols, tokens, scale):

@@ -30,8 +30,11 @@
 // zero region instead.
 //
 // Work split.  A unit is one block column of a 32-row tile (4608 bytes).
-// Each CTA owns a contiguous range of units in tile-major order, so every SM
-// streams the same number of bytes (to one unit) whatever the shape.  The
+// Each CTA owns a contiguous range of units in tile-major order.  When a CTA
+// count between half and all of the SMs divides the tiles without raising
+// the most units a warp takes, every CTA owns whole tiles (no partial sum
+// leaves a CTA); otherwise every SM gets a CTA and every SM streams the same
+// number of bytes (to one unit).  The
 // CTA walks its units boundary tiles first (the tiles it shares with its
 // neighbours), so the cross-CTA exchange overlaps the interior work; each
 // warp takes a contiguous run of that sequence and advances (tile, block)

@@ -332,8 +332,9 @@ template <int G, class OutT>
 __global__ void __launch_bounds__(kAttnThreads, 8) attn_rope_decode_kernel(
     const float *__restrict__ qkv, mlm_rope_args ra, RopeConsts rk,
     const float *__restrict__ freqs, __half *__restrict__ kc, __half *__restrict__ vc,
-    int n_heads, int n_kv, int chunk_len, float scale, const int *__restrict__ pos_dev,
-    OutT *__restrict__ out, size_t qkv_bs, size_t kv_bs, size_t out_bs) {
+    int n_heads, int n_kv, int chunk_len, int rows_cap, float scale,
+    const int *__restrict__ pos_dev, OutT *__restrict__ out, size_t qkv_bs, size_t kv_bs,
+    size_t out_bs) {
   static_assert(kAttnThreads == 128 && kAttnD == 128, "4 warps; warp w outputs dims 32w..32w+31");
   static_assert(G <= 8 && G <= kClusterCtas,
                 "a group's heads are padded to 8 (scores) and 16 (output); CTA h finishes head h");
@@ -362,7 +363,7 @@ __global__ void __launch_bounds__(kAttnThreads, 8) attn_rope_decode_kernel(
   const float *vf = kf + row_stride;
   const int p_begin = (int)rank * chunk_len;
   const int p_end = min(p_begin + chunk_len, seq_len);
-  const int rows_cap = min(chunk_len, kPhaseRows);
+  // rows staged per phase: rows_cap (a multiple of 32, at most kPhaseRows)
   const int nphase = p_end > p_begin ? (p_end - p_begin + rows_cap - 1) / rows_cap : 0;
   const bool has_new = nphase > 0 && p_end == seq_len;  // this CTA holds row `pos`
   __half *s_k = reinterpret_cast<__half *>(s_dyn);        // [rows_cap][kKPitch]
@@ -670,7 +671,10 @@ static int attn_rope_launch(mlm_ctx *ctx, const float *qkv, const float *freqs,
   MLM_REQUIRE(ctx, capacity > 0 && batch > 0 && batch <= 65535, MLM_ERR_SHAPE,
               "attention: cache capacity %d, batch %d", capacity, batch);
   const int chunk_len = attn_rope_chunk_len(capacity);
-  const int rows_cap = std::min(chunk_len, kPhaseRows);
+  // A grid past three CTAs per SM (a batch) stages 64-row phases: at
+  // 53 KB four CTAs fit an SM, so the grid runs in one wave
+  const int ctas = n_kv * kClusterCtas * batch;
+  const int rows_cap = std::min(chunk_len, ctas > 3 * ctx->sm_count ? 64 : kPhaseRows);
   const RopeConsts rk = rope_consts(ra);
   const float scale = 1.0f / sqrtf((float)head_dim);
   auto kern = G == 1   ? attn_rope_decode_kernel<1, OutT>
@@ -693,8 +697,8 @@ static int attn_rope_launch(mlm_ctx *ctx, const float *qkv, const float *freqs,
   cfg.numAttrs = 2;
   const cudaError_t e = cudaLaunchKernelEx(
       &cfg, kern, qkv, ra, rk, freqs, reinterpret_cast<__half *>(kc),
-      reinterpret_cast<__half *>(vc), n_heads, n_kv, chunk_len, scale, pos_dev, out, qkv_bs,
-      kv_bs, out_bs);
+      reinterpret_cast<__half *>(vc), n_heads, n_kv, chunk_len, rows_cap, scale, pos_dev, out,
+      qkv_bs, kv_bs, out_bs);
   return check_launch_pdl(ctx, e, "attention (RoPE, append, decode)");
 }
 

@@ -1075,11 +1075,10 @@ def run_tp70b(args, world, rank, local, pg) -> dict:
         "config": dict(tp70b_config(args, world), algorithmic_bytes_per_step_per_rank=alg),
         "e2e": {"value": round(B * e2e_steps / e2e_s, 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B},
-        # per step: embedding; per layer 2 RMSNorm rows, 3 GEMMs + 2 more, RoPE,
-        # attention (partials + merge for a batch), SwiGLU (+ 2 one-shot
-        # all-reduces with TP); head: RMSNorm, GEMM, B argmaxes (+ key reduce
-        # with TP); advance
-        "gpu_launches": steps * (1 + 80 * (9 + (1 if B > 1 else 0) + (2 if world > 1 else 0)) + 2 + B
+        # per step: embedding; per layer 2 RMSNorm rows, 4 batched GEMVs, the
+        # fused attention, SwiGLU rows (+ 2 one-shot all-reduces with TP);
+        # head: RMSNorm, GEMV, B argmaxes (+ the key reduce with TP); advance
+        "gpu_launches": steps * (1 + 80 * (8 + (2 if world > 1 else 0)) + 2 + B
                                  + (1 if world > 1 else 0) + 1),
         "launch": "CUDA graph (one batched decode step, all-reduces included, replayed per step)",
         "roofline": {"bound": "hbm", "achieved": round(kernel_gbs, 1), "peak": peaks["hbm_gbs"],

@@ -86,7 +86,7 @@ int nccl_check(mlm_ctx *ctx, ncclResult_t r, const char *what) {
 
 constexpr int kArMaxRanks = 8;
 constexpr int kArMaxFloats = 64 * 1024;  // per call: 256 KB of fp32
-constexpr int kArCtas = 16;
+constexpr int kArCtas = 64;  // CTAs storing to the peers: a batch's 256 KB needs the store rate
 constexpr int kArThreads = 256;
 // receive area: [2 parities][ranks][kArMaxFloats] 8-byte words, each the
 // value's bits and the epoch that wrote it

@@ -279,6 +279,14 @@ int mlm_q6k_gemm(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_
 int mlm_q4k_gemv_static(mlm_ctx *ctx, const void *W, int rows, int cols, const void *x_f16,
                         float *y, const float *residual);
 
+/* Launch plans, computed on the host alone (no GPU call, no context): the
+ * decode GEMV's CTAs and warps per CTA for a rows x cols weight on a GPU of
+ * sm_count SMs, and whether every CTA owns whole 32-row tiles (no partial
+ * sum crosses CTAs); the batched GEMV's K chunk (block columns) and CTAs. */
+int mlm_q4k_gemv_plan(int rows, int cols, int sm_count, int *ctas, int *warps,
+                      int *whole_tiles);
+int mlm_q4k_gemv_batch_plan(int rows, int cols, int sm_count, int *chunk, int *ctas);
+
 /* ---------------------------------------------------------------------------
  * Normalisation, RoPE, activations
  * ------------------------------------------------------------------------ */

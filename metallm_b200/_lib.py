@@ -124,6 +124,8 @@ SIGNATURES = [
     ("mlm_q4k_gemm", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_int, c_vp, c_vp]),
     ("mlm_q4k_gemv_batch", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_int, c_vp, c_vp]),
     ("mlm_q4k_gemv_static", c_int, [c_vp, c_vp, c_int, c_int, c_vp, c_vp, c_vp]),
+    ("mlm_q4k_gemv_plan", c_int, [c_int, c_int, c_int, c_i32p, c_i32p, c_i32p]),
+    ("mlm_q4k_gemv_batch_plan", c_int, [c_int, c_int, c_int, c_i32p, c_i32p]),
     ("mlm_rmsnorm_f16", c_int, [c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_float]),
     ("mlm_rmsnorm_f32", c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_float]),
     ("mlm_rope_f16", c_int, [c_vp, c_vp, c_vp, ctypes.POINTER(RopeArgs), c_int, c_int, c_int]),

@@ -833,6 +833,22 @@ extern "C" int mlm_q4k_gemv_gate_up(mlm_ctx *ctx, const void *W, int rows, int c
                      ctx->gemv_max_ctas, ctx->gemv_max_tiles, ctx->stream, &pair);
 }
 
+extern "C" int mlm_q4k_gemv_plan(int rows, int cols, int sm_count, int *ctas, int *warps,
+                                 int *whole_tiles) {
+  if (rows <= 0 || cols <= 0 || cols % kQK != 0 || sm_count <= 0 || !ctas || !warps ||
+      !whole_tiles)
+    return MLM_ERR_ARG;
+  GemvPlan pl;
+  // the opt-in limit of a B200 (227 KB), 1 KB of an SM's 228 KB reserved per CTA
+  const size_t smem_cap = std::min((size_t)232448, (size_t)233472 / MLM_GEMV_MIN_BLOCKS - 1024);
+  if (!plan_gemv(rows, cols / kQK, sm_count, smem_cap, pl)) return MLM_ERR_UNSUPPORTED;
+  const int tiles = (rows + kTileRows - 1) / kTileRows;
+  *ctas = pl.ctas;
+  *warps = pl.warps;
+  *whole_tiles = tiles % pl.ctas == 0 ? 1 : 0;
+  return MLM_OK;
+}
+
 // ---------------------------------------------------------------------------
 // mlm_q4k_gemv_static: the same kernel with its split-K scratch in a
 // file-scope device array instead of the context's allocation.

@@ -295,6 +295,24 @@ __global__ void __launch_bounds__(kBgThreads, kBgBlocks)
 
 }  // namespace
 
+// Chunk width: the widest (fewest partial sums per output) whose grid fills
+// the SMs -- narrow weights (a rank's share of a row-parallel projection)
+// otherwise leave most SMs idle, since a warp takes whole 16-row tiles of a
+// chunk; then at most kBgBlocks CTAs per SM over all chunks (one wave: a CTA
+// past it would run alone after the others), never more CTAs than tiles.
+static void batch_plan(int tiles, int nb, int sm_count, int &chunk, int &nchunks,
+                       int &ctas_per_chunk) {
+  auto per_chunk = [&](int nch) {
+    return std::max(1, std::min(tiles / kBgWarps + 1, kBgBlocks * sm_count / nch));
+  };
+  for (int c = kBgChunk; c >= 1; c /= 2) {
+    chunk = c;
+    nchunks = (nb + c - 1) / c;
+    if (nchunks * per_chunk(nchunks) >= kBgBlocks * sm_count * 3 / 4) break;
+  }
+  ctas_per_chunk = per_chunk(nchunks);
+}
+
 int gemv_batch_init(mlm_ctx *ctx) {
   MLM_CUDA_TRY(ctx, cudaFuncSetAttribute(q4k_gemv_batch_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kBgSmem));
@@ -327,22 +345,8 @@ int gemv_batch_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const voi
   a.T = tokens;
   a.nb = cols / kQK;
   a.tiles = (rows + kBgRows - 1) / kBgRows;
-  // Chunk width: the widest (fewest partial sums per output) whose grid
-  // fills the SMs -- narrow weights (a rank's share of a row-parallel
-  // projection) otherwise leave most SMs idle, since a warp takes whole
-  // 16-row tiles of a chunk
   int nchunks = 0;
-  for (int c = kBgChunk; c >= 1; c /= 2) {
-    a.chunk = c;
-    nchunks = (a.nb + c - 1) / c;
-    const int per = std::max(
-        1, std::min(a.tiles / kBgWarps + 1, kBgBlocks * ctx->sm_count / nchunks));
-    if (nchunks * per >= kBgBlocks * ctx->sm_count * 3 / 4) break;
-  }
-  // at most kBgBlocks CTAs per SM over all chunks (one wave: a CTA past it
-  // would run alone after the others), never more CTAs than tiles
-  a.ctas_per_chunk =
-      std::max(1, std::min(a.tiles / kBgWarps + 1, kBgBlocks * ctx->sm_count / nchunks));
+  batch_plan(a.tiles, a.nb, ctx->sm_count, a.chunk, nchunks, a.ctas_per_chunk);
   CUtensorMap tmap;
   const int st = encode_q4k_rows_map(ctx, W, rows, a.nb, kBgRows, &tmap);
   if (st != MLM_OK) return st;
@@ -355,6 +359,16 @@ int gemv_batch_launch(mlm_ctx *ctx, const void *W, int rows, int cols, const voi
 }  // namespace mlm
 
 using namespace mlm;
+
+extern "C" int mlm_q4k_gemv_batch_plan(int rows, int cols, int sm_count, int *chunk,
+                                       int *ctas) {
+  if (rows <= 0 || cols <= 0 || cols % kQK != 0 || sm_count <= 0 || !chunk || !ctas)
+    return MLM_ERR_ARG;
+  int nchunks = 0, per = 0;
+  batch_plan((rows + kBgRows - 1) / kBgRows, cols / kQK, sm_count, *chunk, nchunks, per);
+  *ctas = nchunks * per;
+  return MLM_OK;
+}
 
 extern "C" int mlm_q4k_gemv_batch(mlm_ctx *ctx, const void *W, int rows, int cols,
                                   const void *x_bf16, int tokens, float *y,

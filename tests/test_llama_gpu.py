@@ -324,3 +324,37 @@ def test_llama_errors(ctx):
         m.decode_greedy(1, 3, out)
     assert e.value.status == -8
     m.close()
+
+
+@pytest.mark.parametrize("dim,n_heads", [(1024, 8), (2048, 16)])
+def test_batch_of_eight_small_groups(ctx, dim, n_heads):
+    """GQA groups of 1 and 2 query heads (8 KV heads) and a batch of 8 with
+    caches of 1024 positions: the fused attention's grid (8 KV heads x 8
+    CTAs x 8 sequences) passes three CTAs per SM, so it stages 64-row
+    phases, and the longer prompts span two phases in a CTA.  One batched
+    step's logits of every sequence against the oracle's per-sequence run."""
+    from metallm_b200.synthetic import fill_llama
+    cfg = llama_config(n_layers=1, dim=dim, n_heads=n_heads, n_kv_heads=8, ffn_dim=1024,
+                       vocab=512, max_seq=1024)
+    B = 8
+    m = Llama(ctx, cfg, batch=B)
+    fill_llama(m, SEED)
+    rng = np.random.default_rng(8)
+    prompts = [rng.integers(0, cfg.vocab, size=n).tolist()
+               for n in (300, 130, 70, 40, 20, 9, 3, 1)]
+    nxt = ctx.alloc(16)
+    firsts = []
+    for b, pr in enumerate(prompts):
+        m.prefill(pr, nxt, None, seq=b)
+        firsts.append(int(nxt.download(np.int32)[0]))
+    logits = ctx.alloc(4 * B * cfg.vocab)
+    m.forward_batch(firsts, logits)
+    got = logits.download(np.float32).reshape(B, cfg.vocab)
+    m.close()
+    for b, pr in enumerate(prompts):
+        layers, glob, caches = _oracle_model(cfg)
+        for pos, tok in enumerate(pr):
+            LO.model_forward(layers, glob, caches, tok, pos, cfg_dict(cfg))
+        w = LO.model_forward(layers, glob, caches, firsts[b], len(pr), cfg_dict(cfg))
+        assert rel_l2(got[b], w) < TOL, (b, rel_l2(got[b], w))
+        assert int(np.argmax(got[b])) == int(np.argmax(w)), b

@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl reference]
 
-Default workload (the headline): the fused Q4_K x fp16
+Default workload (the headline GEMV): the fused Q4_K x fp16
 decode GEMV y = W x with W = 14336 x 4096 Q4_K (Llama-3-8B FFN up/gate shape),
 x = 4096 fp16 ~ N(0,1), fp32 accumulation.  A step is one GEMV.  Six seeded
 weight copies (198 MB > the 126 MB L2) rotate between steps, so every step
@@ -53,14 +53,13 @@ WORKLOADS = {
 # FFN 14336, vocab 128256, RoPE theta 500000)
 LLAMA_WORKLOADS = {
     "layer": "one Llama-3-8B-shape decoder layer, single-token decode at position 2047 over a "
-             "2047-token fp16 cache (BASELINE config 2)",
-    "decode": "Llama-3-8B-shape Q4_K model, batch 1: 512 prompt tokens then greedy decode "
-              "(BASELINE config 3)",
+             "2047-token fp16 cache",
+    "decode": "Llama-3-8B-shape Q4_K model, batch 1: 512 prompt tokens then greedy decode",
     "prefill": "Llama-3-8B-shape Q4_K model, batch 1: the 512-token prompt pass (tcgen05 Q4_K "
-               "GEMM, bf16 activations) up to the first generated token (BASELINE config 3)",
+               "GEMM, bf16 activations) up to the first generated token",
     "tp70b": "Llama-3-70B-shape Q4_K model (80 layers, hidden 8192, 64/8 heads of 128, FFN 28672, "
              "vocab 128256), a batch of 8 sequences: each a 2048-token prompt, then greedy "
-             "decode of all 8 together, tensor-parallel over the N GPUs (BASELINE config 4)",
+             "decode of all 8 together, tensor-parallel over the N GPUs",
 }
 
 L70 = dict(n_layers=80, dim=8192, n_heads=64, n_kv_heads=8, ffn_dim=28672, vocab=128256)
@@ -501,7 +500,7 @@ def run_gpu(args, world, rank, local, pg) -> dict:
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "q4k x f16 -> f32" if is_gemv else "q4k -> f32",
-        "data": "synthetic (seeded Q4_K blocks generated on device, as BASELINE config 0)",
+        "data": "synthetic (seeded Q4_K blocks generated on device)",
         "config": gemv_config(args, world, rows, cols, desc),
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
@@ -567,7 +566,7 @@ def cpu_decode_rate(budget_s: float, threads: int, big: bool = False) -> dict:
 
 GEMM_SHAPE = (28672, 4096, 512)
 GEMM_DESC = ("Q4_K x bf16 GEMM on tcgen05: the fused gate/up weights of a Llama-3-8B layer "
-             "(28672 x 4096 Q4_K) on a 512-token prompt (BASELINE config 3 prefill)")
+             "(28672 x 4096 Q4_K) on a 512-token prompt of the 8B shape")
 
 
 def cpu_gemm_rate(budget_s: float, threads: int) -> dict:
@@ -582,7 +581,7 @@ def cpu_gemm_rate(budget_s: float, threads: int) -> dict:
 
 GEMV_BATCH_SHAPE = (57344, 8192, 8)
 GEMV_BATCH_DESC = ("Q4_K batched decode GEMV: the fused gate/up weights of a Llama-3-70B layer "
-                   "(57344 x 8192 Q4_K) on the 8 tokens of a decode batch (BASELINE config 4)")
+                   "(57344 x 8192 Q4_K) on the 8 tokens of a 70B-shape decode batch")
 
 
 def run_gemv_batch(args, world, rank, local, pg) -> dict:
@@ -775,7 +774,7 @@ def gemm_kernel_time(ctx, m, n_layers: int, T: int, reps: int, tstream) -> dict:
 
 
 def run_llama(args, world, rank, local, pg) -> dict:
-    """BASELINE configs 2 (one layer) and 3 (the model: prefill, greedy decode)."""
+    """The 8B-shape decoder workloads: one layer, and the model (prompt pass, greedy decode)."""
     import torch
 
     from metallm_b200 import Context, Llama
@@ -975,7 +974,7 @@ def run_llama(args, world, rank, local, pg) -> dict:
         "ms_per_step": round(per_step_ms, 5), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "q4k x f16 -> f32 (fp16 KV cache)",
         "data": "synthetic (seeded Q4_K weights, fp16 embedding, fp32 norms generated on "
-                "device, as BASELINE configs 2/3)",
+                "device)",
         "config": config, "e2e": e2e, "gpu_launches": launches,
         "launch": ("stream-ordered launches, one per kernel" if args.workload == "prefill" else
                    "CUDA graph (one decode step captured, replayed per token)"),
